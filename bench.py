@@ -1,0 +1,334 @@
+"""Benchmark of the B200 W4A16 MoE expert path (one JSON line on rank 0).
+
+Headline (``value``): MoE-layer prefill tokens/s at T=4096 tokens per GPU, H=2048,
+E=512 experts, I=512, top-10, W4 group 128 (the prefill configuration of the workload
+definition; synthetic seeded weights and activations).  A step is one full MoE layer:
+router GEMM, top-k, expert-major permutation, grouped gate/up + SwiGLU, grouped down,
+shared expert, slot-order combine and sigmoid-gated merge.  Inputs are resident in HBM;
+each layer's weights (0.83 GB) exceed the 126 MB L2, and steps rotate over distinct
+layers.  ``decode`` reports the decode configuration (M=1 and M=4 tokens, microseconds
+per layer) over a CUDA-graphed rotation of 16 distinct layers (13 GB of weights).
+
+With ``--gpus N`` under torchrun each rank runs the same per-GPU workload (weak scaling):
+the experts are sharded expert-parallel and tokens are exchanged with NCCL all-to-all
+when ``fnx.ep`` is available, otherwise each rank runs an independent replica.
+
+``--impl reference`` times the reference's algorithm on the host CPU (the oracle port of
+``FnLayer._moe``; the reference itself is Python + torch_npu and cannot run here) on a
+bounded token sample of the same layer, with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "qwen-ascend_b200"))
+
+import torch  # noqa: E402
+
+H, I, E, K_TOP, GS = 2048, 512, 512, 10, 128
+T_PREFILL = 4096
+METRIC = "MoE-layer prefill tokens/s @T=4096 (E=512, top-10, H=2048, I=512, W4 g128)"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def prefill_flops(T):
+    routed = 2 * T * K_TOP * (H * 2 * I + I * H)
+    shared = 2 * T * 3 * H * I
+    router = 2 * T * H * E
+    return routed + shared + router
+
+
+def decode_bytes(U, M):
+    per_expert = H * 2 * I // 2 + (H // GS) * 2 * I * 2 + I * H // 2 + (I // GS) * H * 2
+    return U * per_expert + per_expert + (E + 1) * H * 2 + M * H * 2 * 2
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock / reasons while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.rows = []
+        if self.proc is None:
+            return
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        for line in out.strip().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) >= 9:
+                self.rows.append(f)
+
+    def summary(self):
+        if not getattr(self, "rows", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ CPU baseline
+def cpu_baseline(sample_tokens=128, seed=0):
+    """The oracle port of the reference's torch path on this host's cores: one MoE layer
+    over ``sample_tokens`` tokens with fp32 accumulation, dequantising every touched
+    expert inside the timed region (as the reference's ExpQ path does per call)."""
+    import oracle as O
+    from fnx import synth
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    t = synth.make_layer(synth.CFG2, seed=seed)
+    x = synth.make_tokens(sample_tokens, H, seed=seed + 1)
+    t0 = time.perf_counter()
+    L = O.Layer(t, GS)
+    O.moe_forward(x, L, K_TOP, acc=torch.float32)
+    dt = time.perf_counter() - t0
+    return {"value": sample_tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_tokens} tokens through one layer of the T=4096 configuration (E=512, top-10): "
+                      f"oracle port of FnLayer._moe, fp32 accumulation, per-call dequantisation; {dt:.1f} s"}
+
+
+# ------------------------------------------------------------------ B200 arm
+def make_layers(n, dev, seed0=100):
+    from fnx import synth
+    from fnx.engine import MoELayer
+    layers = []
+    for i in range(n):
+        t = synth.make_layer(synth.CFG2, seed=seed0 + i, device=dev)
+        layers.append(MoELayer.from_synth(t, synth.CFG2))
+    return layers
+
+
+def time_events(fn, iters, stream):
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(iters):
+        fn()
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def bench_prefill(args, world, rank, dev):
+    from fnx import synth
+    from fnx import _lib
+    from fnx.engine import EPI_SWIGLU_F32, _grouped_w4
+    nl = 2
+    layers = make_layers(nl, dev)
+    xs = [synth.make_tokens(T_PREFILL, H, seed=1000 + rank * 10 + i, device=dev) for i in range(nl)]
+    stream = torch.cuda.current_stream(dev)
+    step = [0]
+
+    def run():
+        i = step[0] % nl
+        step[0] += 1
+        return layers[i].prefill(xs[i])
+
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clk:
+        ms = time_events(run, args.steps, stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(ms, world)
+    value = world * T_PREFILL / (ms * 1e-3)
+
+    # dominant kernel: routed gate/up grouped GEMM + fused SwiGLU, timed alone
+    lay = layers[0]
+    _, d = lay.prefill(xs[0], details=True)
+    act = torch.empty(T_PREFILL * K_TOP, I, dtype=torch.bfloat16, device=dev)
+
+    def gu():
+        _grouped_w4(xs[0], lay.gu.w4, lay.gu._scales, d["ends"], act, E=E, M=T_PREFILL * K_TOP, K=H, Nw=2 * I,
+                    gs=GS, epilogue=EPI_SWIGLU_F32, row_index=d["order"], index_div=K_TOP)
+    for _ in range(3):
+        gu()
+    gu_ms = time_events(gu, 10, stream)
+    gu_flops = 2 * T_PREFILL * K_TOP * H * 2 * I
+    pk, src = peaks()
+    achieved = gu_flops / (gu_ms * 1e-3) / 1e12
+    roofline = {"kernel": "grouped_gemm_kernel<W4, SwiGLU> (routed gate/up)", "bound": "tensor",
+                "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["bf16_tflops"], 4), "peak_source": f"{src} bf16 burst",
+                "traffic": None, "ms_per_launch": round(gu_ms, 4),
+                "algorithmic_flops_per_launch": gu_flops}
+    layer_tflops = prefill_flops(T_PREFILL) / (ms * 1e-3) / 1e12
+
+    # end to end through the public API with host buffers
+    xh = [xs[i].cpu().pin_memory() for i in range(nl)]
+    outh = torch.empty(T_PREFILL, H, dtype=torch.bfloat16).pin_memory()
+
+    def e2e():
+        i = step[0] % nl
+        step[0] += 1
+        xd = xh[i].to(dev, non_blocking=True)
+        out = layers[i](xd)
+        outh.copy_(out, non_blocking=True)
+    for _ in range(args.warmup):
+        e2e()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(time_events(e2e, args.steps, stream), world)
+    launches_per_step = 10
+    return dict(value=value, ms=ms, clocks=clk.summary(), roofline=roofline, layer_tflops=layer_tflops,
+                e2e={"value": world * T_PREFILL / (e2e_ms * 1e-3), "unit": "tokens/s",
+                     "h2d_bytes_per_step": T_PREFILL * H * 2, "d2h_bytes_per_step": T_PREFILL * H * 2,
+                     "ms_per_step": round(e2e_ms, 4)},
+                gpu_launches=launches_per_step * args.steps)
+
+
+def bench_decode(dev, nl=16, iters=20):
+    from fnx import synth
+    layers = make_layers(nl, dev, seed0=200)
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+    pk, src = peaks()
+    for M in (1, 4):
+        xs = [synth.make_tokens(M, H, seed=300 + i, device=dev) for i in range(nl)]
+        for i in range(nl):
+            layers[i].decode(xs[i])
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            outs = [layers[i].decode(xs[i]) for i in range(nl)]
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        ms = time_events(g.replay, iters, stream)
+        us = ms * 1e3 / nl
+        U = statistics.mean(int(torch.unique(o[2]).numel()) for o in outs)
+        nbytes = decode_bytes(U, M)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[f"M{M}"] = {"us_per_layer": round(us, 3), "distinct_experts": U, "bytes_per_layer": int(nbytes),
+                        "achieved_gbs": round(gbs, 1), "frac_hbm": round(gbs / pk["hbm_gbs"], 4)}
+        del g
+    res["hbm_peak_gbs"] = pk["hbm_gbs"]
+    res["peak_source"] = src
+    res["layers_in_rotation"] = nl
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--cpu-sample", type=int, default=128)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+                          int(os.environ.get("LOCAL_RANK", "0")))
+    config = {"workload": "moe_layer_prefill_T4096", "tokens_per_gpu": T_PREFILL, "H": H, "I": I, "E": E,
+              "top_k": K_TOP, "w4_group": GS, "shared_expert": "W4, sigmoid gate",
+              "l2": "inputs larger than L2 (0.83 GB weights per layer, 2-layer rotation)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        steps = []
+        for s in range(args.warmup + args.steps):
+            r = cpu_baseline(sample_tokens=args.cpu_sample, seed=s % 2)
+            if s >= args.warmup:
+                steps.append(r["value"])
+        v = statistics.median(steps)
+        r["value"] = v
+        print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+                          "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * args.cpu_sample / v,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                          "data": "synthetic", "config": config, "cpu_baseline": r,
+                          "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    import __graft_entry__
+    __graft_entry__.build()
+
+    r = bench_prefill(args, world, rank, dev)
+    dec = None if args.no_decode else bench_decode(dev)
+    cpu = cpu_baseline(args.cpu_sample) if (rank == 0 and world == 1) else None
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(r["value"], 1), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded; shapes/distributions of the workload definition)",
+                "config": dict(config, parallelism="replicas" if world > 1 else "single GPU"),
+                "clocks": r["clocks"], "e2e": r["e2e"], "gpu_launches": r["gpu_launches"],
+                "roofline": r["roofline"], "layer_tflops": round(r["layer_tflops"], 1), "decode": dec,
+                "cpu_baseline": cpu}
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,129 @@
+/* fnx_b200.h -- C ABI of libfnx_b200.so, the B200 (sm_100a) W4A16 MoE expert path.
+ *
+ * Conventions (same as the reference's ctypes-loaded AscendC shims):
+ *   - pointers are raw device pointers; `stream` is a cudaStream_t passed as void*;
+ *   - every call launches asynchronously on `stream`, allocates nothing, never
+ *     synchronises, and is capturable in a CUDA graph;
+ *   - return 0 when launched, a negative code when an argument is rejected:
+ *       -1 argument out of range, -2 unsupported shape, -3 alignment,
+ *       -4 CUDA launch error, -5 workspace too small;
+ *   - errors found on the device (a bounded wait that expired, an expert id outside
+ *     [0, E)) are recorded in a device word read by fnx_device_errors().
+ * Citations are to files of the reference tree (xyzhou613-dev/qwen-ascend).
+ */
+#ifndef FNX_B200_H
+#define FNX_B200_H
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- reference-compatible exports (same symbol, argument order and meaning) ---- */
+
+/* replaces kernels/expert_gather/gather.cpp:24 (fnx/expert_gather.py:22-28).
+ * w int32 [E,K,N/8], s bf16 [E,G,N], ids int64 [10] -> ow int32 [K,10*N/8], os bf16 [G,10*N].
+ * Accepts any N % 8 == 0 (the reference: N in {1280, 2560}); ids are not range-checked. */
+int fnx_gather_pair(void* w, void* s, void* ids, void* ow, void* os, int K, int G, int N, void* stream);
+
+/* replaces kernels/moe_epilogue/epilogue.cpp:41 (fnx/moe_epilogue.py:15-19): G=10, W=2560.
+ * y bf16 [10, 10*2560] Cartesian down output, w bf16 [1,10], shared bf16 [1,2560], gate bf16 [1]. */
+int fnx_moe_epilogue(void* y, void* w, void* shared, void* gate, void* out, void* stream);
+
+/* replaces kernels/reduce/reduce.cpp:62 (fnx/weighted_reduce.py:33-39).
+ * mode 1: out[t] = bf16(sum_g fp32(bf16(in[t*groups+g] * w[t*groups+g]))), w fp32 [batch,groups];
+ * mode 2: rows via inverse int64 [batch*groups]; mode 0: mean of `groups` rows with bf16
+ * elementwise weights [batch*groups, width].  order must be 0.  Any width >= 1, groups <= 64. */
+int fnx_weighted_reduce(void* input, void* weights, void* inverse, void* output, int batch, int groups, int width,
+                        int row_stride, int mode, int order, void* stream);
+
+/* replaces kernels/post_ops/post_ops.cpp:91 (fnx/post_ops.py:14,39): width 2560,
+ * out = bf16(e + bf16(s * bf16(sigmoid(g[t])))). */
+int fnx_moe_merge(void* e, void* s, void* g, void* y, int batch, void* stream);
+
+/* replaces libfnxw4gemv.so's fnx_w4gemv_launch as bound by fnx/w4gemv_op.py:42-43,153-158.
+ * p4 [E,N,K/2] bytes (lay 1: lo=W[2j], hi=W[2j+1], x split xe/xo; lay 2: v2 layout, xe=xo=x),
+ * s4t fp16 [E,K/32,N], ids int32 [nExp] (or NULL = slot order), y fp32 [nExp,N].
+ * dbg and nblk are accepted and unused. */
+int fnx_w4gemv_launch(void* p4, void* s4t, void* xe, void* xo, void* y, void* dbg, void* ids, int N, int K, int nExp,
+                      int nblk, int lay, void* stream);
+
+/* replaces fnx_w4gemv_launch_layers as bound by fnx/w4gemv_op.py:189-192: nL <= 64 layers in
+ * one launch, host arrays of device pointers, x natural [nExp,K] fp32, ids = slot order. */
+int fnx_w4gemv_launch_layers(void** p4, void** s4t, void** x, void** y, int nL, int N, int K, int nExp, int nblk,
+                             int lay, void* dbg, void* stream);
+
+/* ---- widened forms of the reference kernels (shapes the AscendC kernels hard-code) ---- */
+
+/* fnx_gather_pair with any slot count; ids outside [0,E) copy zeros and set device error 2
+ * (E <= 0 disables the check). */
+int fnx_gather_pair_ex(void* w, void* s, void* ids, void* ow, void* os, int E, int K, int G, int N, int nslots,
+                       void* stream);
+/* fnx_moe_epilogue for y [k, k*width], w [1,k]. */
+int fnx_moe_epilogue_ex(void* y, void* w, void* shared, void* gate, void* out, int k, int width, void* stream);
+/* fnx_moe_merge for any width. */
+int fnx_moe_merge_ex(void* e, void* s, void* g, void* y, int batch, int width, void* stream);
+
+/* ---- the B200 MoE path (no single reference counterpart; each restates reference code) ---- */
+
+/* Routing of fnx/engine.py:1811-1813: softmax(fp32(logits [T, ld] bf16, first E columns)
+ * + bias fp32 [E] or NULL), top-k with ties to the lower expert id, w = bf16(p / sum p).
+ * Outputs w_out bf16 [T,k], idx_out int64 [T,k], wf_out fp32 [T,k] (each may be NULL). */
+int fnx_router_topk(void* logits, long long ld, void* bias, void* w_out, void* idx_out, void* wf_out, int T, int E,
+                    int k, void* stream);
+
+/* Expert-major permutation of fnx/engine.py:1817-1840, stable: idx int64 [n] ->
+ * order int64 [n], inverse int64 [n], ends int64 [E] (cumulative counts), counts int64 [E]
+ * (may be NULL).  workspace: fnx_moe_permute_workspace(n, E) bytes.  E <= 4096. */
+size_t fnx_moe_permute_workspace(int n, int E);
+int fnx_moe_permute(void* idx, void* order, void* inverse, void* ends, void* counts, int n, int E, void* workspace,
+                    size_t ws_bytes, void* stream);
+
+/* Expert-major grouped W4A16 GEMM on tcgen05 (restated npu_grouped_matmul,
+ * fnx/engine.py:723-753): rows [ends[e-1], ends[e]) use expert e.  Row r reads act row
+ * row_index[r] / index_div (row_index NULL: act row r).  w4 int32 [E,K,Nw/8] expert-major
+ * int4pack, scales bf16 [E,K/gs,Nw]; ends NULL means one group of M rows.
+ * epilogue 0: out bf16 [M, Nw];  1: SwiGLU of gate = features [0,Nw/2), up = [Nw/2,Nw)
+ * in fp32 on bf16-rounded inputs -> out [M, Nw/2];  2: the shared expert's SwiGLU
+ * bf16(bf16(silu(g)) * u).  K % 64 == 0, gs % 64 == 0, Nw % 128 == 0. */
+int fnx_moe_grouped_w4(const void* act, long long ld_act, const void* row_index, int index_div, const void* w4,
+                       const void* scales, const void* ends, void* out, long long ld_out, int E, int M, int K, int Nw,
+                       int gs, int epilogue, void* stream);
+
+/* DenseW8.__call__ (fnx/engine.py:350-365): y bf16 [M,N] = x bf16 [M,K] . bf16(w8t int8 [K,N]
+ * * sc bf16 [G,N]) with fp32 accumulation.  K % 64 == 0, N % 128 == 0. */
+int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G, void* stream);
+
+/* bf16 GEMM y [M, N] = x [M, K] . w [N, K]^T (the router / concatenated shared GEMM,
+ * fnx/engine.py:1787).  N % 128 == 0. */
+int fnx_bf16_gemm_nt(const void* x, long long ld_x, const void* w, void* y, long long ld_y, int M, int K, int N,
+                     void* stream);
+
+/* Slot-order weighted reduce of the expert-major down output fused with the sigmoid-gated
+ * shared merge (fnx/engine.py:1844-1853): yd bf16 [T*k, H], wf fp32 [T,k], inverse int64
+ * [T*k] (or NULL), sh bf16 [T,H], gate bf16 at gate[t * gate_ld] -> out bf16 [T,H]. */
+int fnx_moe_combine(void* yd, void* wf, void* inverse, void* sh, void* gate, long long gate_ld, void* out, int T, int k,
+                    int H, void* stream);
+
+/* Whole decode MoE layer for M <= 16 tokens (fnx/engine.py:1786-1889 decode branch):
+ * router bf16 [E+1, H] (row E = shared-expert gate), routed and shared experts in the
+ * int4pack layout; out bf16 [M,H], w_out bf16 [M,k], idx_out int64 [M,k] (may be NULL).
+ * workspace: fnx_moe_decode_workspace(M,H,I,E,k) bytes, zero-filled before first use;
+ * each completed call leaves it ready for the next.  Calls sharing a workspace must not
+ * overlap on the GPU. */
+size_t fnx_moe_decode_workspace(int M, int H, int I, int E, int k);
+int fnx_moe_decode_w4(const void* x, const void* router, const void* gu_w4, const void* gu_s, const void* dn_w4,
+                      const void* dn_s, const void* sh_gu_w4, const void* sh_gu_s, const void* sh_dn_w4,
+                      const void* sh_dn_s, const void* bias, void* out, void* w_out, void* idx_out, int M, int H, int I,
+                      int E, int k, int gs, void* workspace, size_t ws_bytes, void* stream);
+
+/* ---- library ---- */
+const char* fnx_b200_version(void);
+/* device error bits since the last clear: 1 bounded wait expired, 2 expert id out of range,
+ * 4 overflow.  Synchronises with the device (cudaMemcpyFromSymbol). */
+unsigned fnx_device_errors(int clear);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -100,7 +100,7 @@ def w4a16_matmul(x: torch.Tensor, w: torch.Tensor, acc: torch.dtype = torch.floa
     return (x.to(acc) @ w.to(acc)).to(F32).to(BF16)
 
 
-def grouped_matmul(rows: torch.Tensor, ends: torch.Tensor, weights_fn) -> torch.Tensor:
+def grouped_matmul(rows: torch.Tensor, ends: torch.Tensor, weights_fn, acc: torch.dtype = torch.float64) -> torch.Tensor:
     """Restated ``npu_grouped_matmul(group_type=0, split_item=3)`` (``fnx/engine.py:749-753``):
     rows ``[ends[e-1], ends[e])`` are multiplied by ``weights_fn(e)`` (bf16 ``[K, N]``)."""
     ends = [int(v) for v in ends.tolist()]
@@ -108,7 +108,7 @@ def grouped_matmul(rows: torch.Tensor, ends: torch.Tensor, weights_fn) -> torch.
     begin = 0
     for e, end in enumerate(ends):
         if end > begin:
-            outs.append(w4a16_matmul(rows[begin:end], weights_fn(e)))
+            outs.append(w4a16_matmul(rows[begin:end], weights_fn(e), acc))
         begin = end
     if not outs:
         n = weights_fn(0).shape[-1]
@@ -339,7 +339,7 @@ def shared_and_logits(x: torch.Tensor, L: Layer):
     return sh, gu[:, 2 * I:2 * I + 1].contiguous(), gu[:, 2 * I + 1:].contiguous()
 
 
-def moe_forward(x: torch.Tensor, L: Layer, k: int, routing=None, bias=None, details=False):
+def moe_forward(x: torch.Tensor, L: Layer, k: int, routing=None, bias=None, details=False, acc=torch.float64):
     """One MoE layer: shared expert + router + expert-major grouped W4A16 gate/up, fp32
     SwiGLU, grouped down, slot-order weighted reduce and the sigmoid-gated shared merge
     (``fnx/engine.py:1782-1853``, grouped branch; for one token it equals the decode
@@ -354,9 +354,9 @@ def moe_forward(x: torch.Tensor, L: Layer, k: int, routing=None, bias=None, deta
         w, idx = routing
     order, counts, ends, inverse = permute(idx, L.E)
     rows = x.to(BF16).index_select(0, order // k)
-    gu = grouped_matmul(rows, ends, L.gu)
+    gu = grouped_matmul(rows, ends, L.gu, acc)
     act = swiglu_fp32(gu, I)
-    yd = grouped_matmul(act, ends, L.dn)
+    yd = grouped_matmul(act, ends, L.dn, acc)
     y = weighted_reduce(yd, w, inverse=inverse)
     out = moe_merge(y, sh, gate)
     if details:
@@ -438,19 +438,20 @@ def max_abs(a: torch.Tensor, b: torch.Tensor) -> float:
 
 
 # The floating-point tolerance of the path: max-abs 2e-2 and relative-L2 5e-3 for bf16
-# outputs with fp32 accumulation.  The synthetic workload's outputs have an RMS of ~10
-# (bf16 spacing up to 0.25 there), so the max-abs bound is applied to outputs normalised
-# by the reference's RMS (max |a - b| / rms(b)); the relative-L2 bound is scale-free.
+# outputs with fp32 accumulation.  The synthetic workload's outputs reach magnitudes of
+# ~100 (bf16 spacing 0.5 there), so an absolute 2e-2 is below bf16 resolution; the
+# max-abs bound is applied to outputs normalised by the reference's largest magnitude
+# (max |a - b| / max |b|).  The relative-L2 bound is scale-free.
 TOL_MAX_ABS = 2e-2
 TOL_REL_L2 = 5e-3
 
 
 def tolerance_report(a: torch.Tensor, b: torch.Tensor) -> dict:
     a32, b32 = a.to(F32), b.to(F32)
-    rms = float(b32.pow(2).mean().sqrt().clamp_min(1e-12))
+    scale = float(b32.abs().max().clamp_min(1e-12)) if b32.numel() else 1.0
     d = (a32 - b32).abs()
     return dict(max_abs=float(d.max()) if d.numel() else 0.0,
-                max_abs_norm=(float(d.max()) / rms) if d.numel() else 0.0,
+                max_abs_norm=(float(d.max()) / scale) if d.numel() else 0.0,
                 rel_l2=rel_l2(a32, b32),
                 exact_fraction=float((a32 == b32).to(F32).mean()) if d.numel() else 1.0,
                 finite=bool(torch.isfinite(a32).all()))

@@ -1,0 +1,448 @@
+// libfnx_b200.so -- the C-ABI of the B200 W4A16 MoE expert path.
+//
+// One translation unit (so every kernel shares the device error word).  Entry points
+// take raw device pointers, sizes and a cudaStream_t (void*); they launch
+// asynchronously on that stream, never allocate, never synchronise, and return 0 or a
+// negative FNX_E* code when an argument is rejected before launch.  Declarations and
+// the reference interface each one replaces are in include/fnx_b200.h.
+#include <stdio.h>
+#include <string.h>
+
+#include "fnx_common.cuh"
+#include "kernels_combine.cuh"
+#include "kernels_decode.cuh"
+#include "kernels_gemm.cuh"
+#include "kernels_route.cuh"
+#include "kernels_w4gemv.cuh"
+
+#define FNX_API extern "C" __attribute__((visibility("default")))
+
+using namespace fnx;
+
+namespace {
+
+int num_sms() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    }
+    return sms;
+}
+
+inline int launch_rc() {
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FNX_OK : FNX_ELAUNCH;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int grid_for(long long work, int threads) {
+    long long g = (work + threads - 1) / threads;
+    const long long cap = (long long)num_sms() * 8;
+    if (g > cap) g = cap;
+    return (int)(g < 1 ? 1 : g);
+}
+
+int weighted_reduce_launch(const void* in, const void* w, const void* inverse, void* out, int batch, int groups,
+                           int width, long long row_stride, int mode, cudaStream_t st) {
+    const bool vec = width % 8 == 0 && row_stride % 8 == 0 && aligned16(in) && aligned16(out) &&
+                     (mode != 0 || aligned16(w));
+    const long long work = (long long)batch * (vec ? width / 8 : width);
+    const int grid = grid_for(work, 256);
+    const bf16* x = static_cast<const bf16*>(in);
+    const int64_t* inv = static_cast<const int64_t*>(inverse);
+    bf16* y = static_cast<bf16*>(out);
+#define FNX_WR(M, V) weighted_reduce_kernel<M, V><<<grid, 256, 0, st>>>(x, w, inv, y, batch, groups, width, row_stride)
+    if (vec) {
+        if (mode == 0) FNX_WR(0, true); else if (mode == 1) FNX_WR(1, true); else FNX_WR(2, true);
+    } else {
+        if (mode == 0) FNX_WR(0, false); else if (mode == 1) FNX_WR(1, false); else FNX_WR(2, false);
+    }
+#undef FNX_WR
+    return launch_rc();
+}
+
+int moe_merge_launch(const void* e, const void* s, const void* g, void* y, int batch, int width, cudaStream_t st) {
+    const bool vec = width % 8 == 0 && aligned16(e) && aligned16(s) && aligned16(y);
+    const long long work = (long long)batch * (vec ? width / 8 : width);
+    const int grid = grid_for(work, 256);
+    if (vec)
+        moe_merge_kernel<true><<<grid, 256, 0, st>>>((const bf16*)e, (const bf16*)s, (const bf16*)g, (bf16*)y, batch, width);
+    else
+        moe_merge_kernel<false><<<grid, 256, 0, st>>>((const bf16*)e, (const bf16*)s, (const bf16*)g, (bf16*)y, batch, width);
+    return launch_rc();
+}
+
+// ---- TMA tensor maps (cuTensorMapEncodeTiled through the runtime's driver entry point,
+// so the library does not link libcuda and loads on hosts without a GPU driver).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    return fn;
+}
+
+struct MapKey {
+    const void* ptr;
+    int dtype, swz;
+    unsigned long long d0, d1;
+    unsigned b0, b1;
+};
+struct MapEntry {
+    MapKey key;
+    CUtensorMap map;
+    bool used;
+};
+
+// 2-D tiled map: inner dimension d0 (contiguous, elements), outer d1 rows, box {b0, b1}.
+// Cached per (pointer, shape) -- weights are long-lived, so repeated calls reuse maps.
+int make_map_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dt, int esize, unsigned long long d0,
+                unsigned long long d1, unsigned b0, unsigned b1, CUtensorMapSwizzle swz) {
+    static MapEntry cache[64];
+    static int next = 0;
+    const MapKey k{ptr, (int)dt, (int)swz, d0, d1, b0, b1};
+    for (auto& e : cache)
+        if (e.used && memcmp(&e.key, &k, sizeof(k)) == 0) {
+            *out = e.map;
+            return FNX_OK;
+        }
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return FNX_EDRIVER;
+    const cuuint64_t dims[2] = {d0, d1};
+    const cuuint64_t strides[1] = {d0 * (cuuint64_t)esize};
+    const cuuint32_t box[2] = {b0, b1};
+    const cuuint32_t estr[2] = {1, 1};
+    if (fn(out, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return FNX_EALIGN;
+    MapEntry& e = cache[next];
+    next = (next + 1) % 64;
+    e.key = k;
+    e.map = *out;
+    e.used = true;
+    return FNX_OK;
+}
+
+template <int MODE, int EPI>
+int gemm_launch_t(GemmParams& p, cudaStream_t st) {
+    const size_t smem = grouped_gemm_smem_bytes(MODE);
+    static bool configured = false;
+    if (!configured) {
+        if (cudaFuncSetAttribute(grouped_gemm_kernel<MODE, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem) != cudaSuccess)
+            return FNX_ELAUNCH;
+        configured = true;
+    }
+    int rc = FNX_OK;
+    if (MODE == GEMM_W4) {
+        rc = make_map_2d(&p.tmap_a, p.w, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, (unsigned long long)p.Nw / 8,
+                         (unsigned long long)p.E * p.K, 8, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (!rc)
+            rc = make_map_2d(&p.tmap_s, p.scales, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (unsigned long long)p.Nw,
+                             (unsigned long long)p.E * (p.K / p.gs), 64, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else if (MODE == GEMM_BF16) {
+        rc = make_map_2d(&p.tmap_a, p.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (unsigned long long)p.K,
+                         (unsigned long long)p.E * p.Nw, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (rc) return rc;
+    grouped_gemm_kernel<MODE, EPI><<<num_sms(), G_THREADS, smem, st>>>(p);
+    return launch_rc();
+}
+
+int gemm_launch(int mode, int epi, GemmParams& p, cudaStream_t st) {
+    if (mode == GEMM_W4) {
+        if (epi == EPI_PLAIN) return gemm_launch_t<GEMM_W4, EPI_PLAIN>(p, st);
+        if (epi == EPI_SWIGLU_F32) return gemm_launch_t<GEMM_W4, EPI_SWIGLU_F32>(p, st);
+        return gemm_launch_t<GEMM_W4, EPI_SWIGLU_BF16>(p, st);
+    }
+    if (mode == GEMM_W8) return gemm_launch_t<GEMM_W8, EPI_PLAIN>(p, st);
+    return gemm_launch_t<GEMM_BF16, EPI_PLAIN>(p, st);
+}
+
+// Shape checks shared by the grouped GEMM entry points.
+int gemm_check(int mode, int epi, const GemmParams& p) {
+    if (p.E < 1 || p.E > G_MAX_E || p.M < 0 || p.K < G_BK || p.K % G_BK || p.Nw < 1) return FNX_EARG;
+    if (mode != GEMM_BF16 && (p.gs < G_BK || p.gs % G_BK || p.K % p.gs)) return FNX_ESHAPE;
+    if (epi == EPI_PLAIN ? p.Nw % G_BM : (p.Nw % 128)) return FNX_ESHAPE;
+    if (p.ld_act % 8 || !aligned16(p.act) || !aligned16(p.w) || (p.scales && !aligned16(p.scales))) return FNX_EALIGN;
+    if (p.row_index && p.index_div < 1) return FNX_EARG;
+    return FNX_OK;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+// ======================================================================== misc
+FNX_API const char* fnx_b200_version(void) { return "fnx_b200 1.0 (sm_100a; tcgen05 grouped GEMM, W4 decode GEMV)"; }
+
+FNX_API unsigned fnx_device_errors(int clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_fnx_errors, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    if (clear) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_fnx_errors, &z, sizeof(z));
+    }
+    return v;
+}
+
+// ======================================================================== reference-compatible exports
+FNX_API int fnx_weighted_reduce(void* input, void* weights, void* inverse, void* output, int batch, int groups,
+                                int width, int row_stride, int mode, int order, void* stream) {
+    if (batch < 1 || width < 1 || groups < 1 || groups > 64 || mode < 0 || mode > 2 || order != 0 ||
+        row_stride < width)
+        return FNX_EARG;
+    if (mode == 2 && !inverse) return FNX_EARG;
+    return weighted_reduce_launch(input, weights, inverse, output, batch, groups, width, row_stride, mode,
+                                  (cudaStream_t)stream);
+}
+
+FNX_API int fnx_moe_merge_ex(void* e, void* s, void* g, void* y, int batch, int width, void* stream) {
+    if (batch < 1 || width < 1) return FNX_EARG;
+    return moe_merge_launch(e, s, g, y, batch, width, (cudaStream_t)stream);
+}
+
+FNX_API int fnx_moe_merge(void* e, void* s, void* g, void* y, int batch, void* stream) {
+    return fnx_moe_merge_ex(e, s, g, y, batch, 2560, stream);
+}
+
+FNX_API int fnx_moe_epilogue_ex(void* y, void* w, void* shared, void* gate, void* out, int k, int width, void* stream) {
+    if (k < 1 || k > 64 || width < 1) return FNX_EARG;
+    moe_epilogue_kernel<<<(width + 255) / 256, 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)y, (const bf16*)w, (const bf16*)shared, (const bf16*)gate, (bf16*)out, k, width);
+    return launch_rc();
+}
+
+FNX_API int fnx_moe_epilogue(void* y, void* w, void* shared, void* gate, void* out, void* stream) {
+    return fnx_moe_epilogue_ex(y, w, shared, gate, out, 10, 2560, stream);
+}
+
+FNX_API int fnx_gather_pair_ex(void* w, void* s, void* ids, void* ow, void* os, int E, int K, int G, int N,
+                               int nslots, void* stream) {
+    if (K < 1 || G < 1 || N < 8 || N % 8 || nslots < 1 || nslots > 65535) return FNX_EARG;
+    const bool v16 = (N / 2) % 16 == 0 && aligned16(w) && aligned16(s) && aligned16(ow) && aligned16(os);
+    if (!v16 && (N / 2) % 2) return FNX_ESHAPE;
+    const long long units = ((long long)K * N / 2 + (long long)G * N * 2) / (v16 ? 16 : 2);
+    dim3 grid((unsigned)grid_for(units, 256 * 4), (unsigned)nslots);
+    gather_pair_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const uint8_t*)w, (const uint8_t*)s, (const int64_t*)ids,
+                                                                (uint8_t*)ow, (uint8_t*)os, E, K, G, N, nslots);
+    return launch_rc();
+}
+
+FNX_API int fnx_gather_pair(void* w, void* s, void* ids, void* ow, void* os, int K, int G, int N, void* stream) {
+    return fnx_gather_pair_ex(w, s, ids, ow, os, 0, K, G, N, 10, stream);
+}
+
+FNX_API int fnx_moe_combine(void* yd, void* wf, void* inverse, void* sh, void* gate, long long gate_ld, void* out, int T,
+                            int k, int H, void* stream) {
+    if (T < 0 || k < 1 || k > 64 || H < 1 || gate_ld < 1) return FNX_EARG;
+    if (T == 0) return FNX_OK;
+    const bool vec = H % 8 == 0 && aligned16(yd) && aligned16(sh) && aligned16(out);
+    const int grid = grid_for((long long)T * (vec ? H / 8 : H), 256);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (vec)
+        moe_combine_kernel<true><<<grid, 256, 0, st>>>((const bf16*)yd, (const float*)wf, (const int64_t*)inverse,
+                                                        (const bf16*)sh, (const bf16*)gate, gate_ld, (bf16*)out, T, k, H);
+    else
+        moe_combine_kernel<false><<<grid, 256, 0, st>>>((const bf16*)yd, (const float*)wf, (const int64_t*)inverse,
+                                                         (const bf16*)sh, (const bf16*)gate, gate_ld, (bf16*)out, T, k, H);
+    return launch_rc();
+}
+
+// ======================================================================== routing
+FNX_API int fnx_router_topk(void* logits, long long ld, void* bias, void* w_out, void* idx_out, void* wf_out, int T,
+                            int E, int k, void* stream) {
+    if (T < 0 || E < 1 || E > ROUTE_MAX_E || k < 1 || k > ROUTE_MAX_K || k > E || ld < E) return FNX_EARG;
+    if (T == 0) return FNX_OK;
+    const int blocks = (T + 7) / 8;
+    cudaStream_t st = (cudaStream_t)stream;
+#define FNX_TOPK(P) router_topk_kernel<P><<<blocks, 256, 0, st>>>((const bf16*)logits, ld, (const float*)bias, \
+        (bf16*)w_out, (int64_t*)idx_out, nullptr, (float*)wf_out, T, E, k)
+    if (E <= 256) FNX_TOPK(8);
+    else if (E <= 512) FNX_TOPK(16);
+    else if (E <= 1024) FNX_TOPK(32);
+    else FNX_TOPK(64);
+#undef FNX_TOPK
+    return launch_rc();
+}
+
+FNX_API size_t fnx_moe_permute_workspace(int n, int E) {
+    const int chunks = (n + PERM_CHUNK - 1) / PERM_CHUNK;
+    return (size_t)(chunks < 1 ? 1 : chunks) * E * sizeof(int);
+}
+
+FNX_API int fnx_moe_permute(void* idx, void* order, void* inverse, void* ends, void* counts, int n, int E,
+                            void* workspace, size_t ws_bytes, void* stream) {
+    if (n < 0 || E < 1 || E > PERM_MAX_E) return FNX_EARG;
+    if (ws_bytes < fnx_moe_permute_workspace(n, E)) return FNX_EWORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int chunks = (n + PERM_CHUNK - 1) / PERM_CHUNK;
+    int* hist = (int*)workspace;
+    if (chunks == 0) {
+        cudaMemsetAsync(ends, 0, sizeof(int64_t) * E, st);
+        if (counts) cudaMemsetAsync(counts, 0, sizeof(int64_t) * E, st);
+        return launch_rc();
+    }
+    permute_hist_kernel<<<chunks, 256, E * sizeof(int), st>>>((const int64_t*)idx, n, E, hist);
+    permute_scan_kernel<<<1, 1024, 0, st>>>(hist, chunks, E, (int64_t*)ends, (int64_t*)counts);
+    permute_scatter_kernel<<<chunks, 32, (E + PERM_CHUNK) * sizeof(int), st>>>((const int64_t*)idx, n, E, hist, (int64_t*)order,
+                                                               (int64_t*)inverse);
+    return launch_rc();
+}
+
+// ======================================================================== grouped GEMMs
+FNX_API int fnx_moe_grouped_w4(const void* act, long long ld_act, const void* row_index, int index_div, const void* w4,
+                               const void* scales, const void* ends, void* out, long long ld_out, int E, int M, int K,
+                               int Nw, int gs, int epilogue, void* stream) {
+    GemmParams p{};
+    p.act = (const bf16*)act; p.ld_act = ld_act; p.row_index = (const int64_t*)row_index; p.index_div = index_div;
+    p.w = w4; p.scales = (const bf16*)scales; p.ends = (const int64_t*)ends; p.out = (bf16*)out; p.ld_out = ld_out;
+    p.E = E; p.M = M; p.K = K; p.Nw = Nw; p.gs = gs;
+    if (epilogue < 0 || epilogue > 2) return FNX_EARG;
+    p.m_tiles = epilogue == EPI_PLAIN ? Nw / G_BM : (Nw / 2) / 64;
+    const int rc = gemm_check(GEMM_W4, epilogue, p);
+    if (rc) return rc;
+    if (M == 0) return FNX_OK;
+    return gemm_launch(GEMM_W4, epilogue, p, (cudaStream_t)stream);
+}
+
+FNX_API int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G,
+                           void* stream) {
+    GemmParams p{};
+    p.act = (const bf16*)x; p.ld_act = K; p.w = w8t; p.scales = (const bf16*)sc; p.out = (bf16*)y; p.ld_out = N;
+    p.E = 1; p.M = M; p.K = K; p.Nw = N; p.gs = G > 0 ? K / G : 0; p.m_tiles = N / G_BM;
+    if (G < 1 || K % G) return FNX_EARG;
+    const int rc = gemm_check(GEMM_W8, EPI_PLAIN, p);
+    if (rc) return rc;
+    if (N % 8) return FNX_ESHAPE;
+    if (M == 0) return FNX_OK;
+    return gemm_launch(GEMM_W8, EPI_PLAIN, p, (cudaStream_t)stream);
+}
+
+FNX_API int fnx_bf16_gemm_nt(const void* x, long long ld_x, const void* w, void* y, long long ld_y, int M, int K, int N,
+                             void* stream) {
+    GemmParams p{};
+    p.act = (const bf16*)x; p.ld_act = ld_x; p.w = w; p.out = (bf16*)y; p.ld_out = ld_y;
+    p.E = 1; p.M = M; p.K = K; p.Nw = N; p.gs = K; p.m_tiles = N / G_BM;
+    const int rc = gemm_check(GEMM_BF16, EPI_PLAIN, p);
+    if (rc) return rc;
+    if (M == 0) return FNX_OK;
+    return gemm_launch(GEMM_BF16, EPI_PLAIN, p, (cudaStream_t)stream);
+}
+
+// ======================================================================== decode layer
+namespace {
+struct DecodeLayout {
+    size_t logits, wf, idx, part, part2, act, act_sh, yd, sh, counters, total;
+    int ks1, ks2, R;
+};
+
+DecodeLayout decode_layout(int M, int H, int I, int E, int k) {
+    DecodeLayout L{};
+    L.R = E + 1;
+    const int nfb = I / DEC_FB;
+    // K splits sized so each grid holds >= 2 blocks per SM
+    L.ks1 = 1;
+    while (L.ks1 < 64 && M * nfb * L.ks1 < 64 && (H / (L.ks1 * 2)) % 128 == 0) L.ks1 *= 2;
+    L.ks2 = 1;
+    while (L.ks2 < 64 && M * k * nfb * L.ks2 < 2 * num_sms() && (H / (L.ks2 * 2)) % 128 == 0) L.ks2 *= 2;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
+    L.logits = take((size_t)M * L.R * 2);
+    L.wf = take((size_t)M * k * 4);
+    L.idx = take((size_t)M * k * 4);
+    L.part = take((size_t)M * nfb * L.ks1 * 2 * DEC_FB * 4);
+    L.part2 = take((size_t)M * k * nfb * L.ks2 * 2 * DEC_FB * 4);
+    L.act = take((size_t)M * k * I * 2);
+    L.act_sh = take((size_t)M * I * 2);
+    L.yd = take((size_t)M * k * H * 2);
+    L.sh = take((size_t)M * H * 2);
+    L.counters = take((size_t)(1 + M * nfb + M * k * nfb + H / DEC_FB) * 4);
+    L.total = off;
+    return L;
+}
+}  // namespace
+
+FNX_API size_t fnx_moe_decode_workspace(int M, int H, int I, int E, int k) {
+    if (M < 1 || M > DEC_MAX_M || H < 1 || I < 1 || E < 1 || k < 1) return 0;
+    return decode_layout(M, H, I, E, k).total;
+}
+
+// router: bf16 [E+1, H] (rows 0..E-1 router, row E shared-expert gate); all other weights
+// in the int4pack artifact layout.  workspace must be zero-filled before its first use;
+// every completed call leaves its tickets at zero again.
+FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu_w4, const void* gu_s, const void* dn_w4,
+                              const void* dn_s, const void* sh_gu_w4, const void* sh_gu_s, const void* sh_dn_w4,
+                              const void* sh_dn_s, const void* bias, void* out, void* w_out, void* idx_out, int M,
+                              int H, int I, int E, int k, int gs, void* workspace, size_t ws_bytes, void* stream) {
+    if (M < 1 || M > DEC_MAX_M || E < 1 || E > ROUTE_MAX_E || k < 1 || k > 32 || k > E) return FNX_EARG;
+    if (H % 256 || I % DEC_FB || H % DEC_FB || gs < 8 || gs % 8 || H % gs || I % gs) return FNX_ESHAPE;
+    const DecodeLayout L = decode_layout(M, H, I, E, k);
+    if (!workspace || ws_bytes < L.total) return FNX_EWORKSPACE;
+    if (!aligned16(x) || !aligned16(router) || !aligned16(gu_w4) || !aligned16(dn_w4) || !aligned16(gu_s) ||
+        !aligned16(dn_s) || !aligned16(sh_gu_w4) || !aligned16(sh_dn_w4) || !aligned16(sh_gu_s) || !aligned16(sh_dn_s))
+        return FNX_EALIGN;
+    uint8_t* ws = (uint8_t*)workspace;
+    DecodeParams p{};
+    p.x = (const bf16*)x; p.router = (const bf16*)router;
+    p.gu_w4 = (const int32_t*)gu_w4; p.gu_s = (const bf16*)gu_s; p.dn_w4 = (const int32_t*)dn_w4; p.dn_s = (const bf16*)dn_s;
+    p.sh_gu_w4 = (const int32_t*)sh_gu_w4; p.sh_gu_s = (const bf16*)sh_gu_s;
+    p.sh_dn_w4 = (const int32_t*)sh_dn_w4; p.sh_dn_s = (const bf16*)sh_dn_s;
+    p.out = (bf16*)out; p.w_out = (bf16*)w_out; p.idx_out = (int64_t*)idx_out; p.bias = (const float*)bias;
+    p.logits = (bf16*)(ws + L.logits); p.wf = (float*)(ws + L.wf); p.idx = (int32_t*)(ws + L.idx);
+    p.part = (float*)(ws + L.part); p.part2 = (float*)(ws + L.part2);
+    p.act = (bf16*)(ws + L.act); p.act_sh = (bf16*)(ws + L.act_sh); p.yd = (bf16*)(ws + L.yd); p.sh = (bf16*)(ws + L.sh);
+    p.counters = (unsigned*)(ws + L.counters);
+    p.M = M; p.H = H; p.I = I; p.E = E; p.k = k; p.gs = gs; p.R = L.R; p.ks1 = L.ks1; p.ks2 = L.ks2;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int nfb = I / DEC_FB;
+    const int router_blocks = (L.R + 7) / 8;
+    decode_d1_kernel<<<router_blocks + M * nfb * L.ks1, DEC_THREADS, 0, st>>>(p, router_blocks);
+    decode_d2_kernel<<<M * k * nfb * L.ks2, DEC_THREADS, 0, st>>>(p);
+    decode_d3_kernel<<<(M * k + M) * (H / DEC_FB), DEC_THREADS, 0, st>>>(p);
+    return launch_rc();
+}
+
+// ======================================================================== legacy W4 GEMV
+FNX_API int fnx_w4gemv_launch(void* p4, void* s4t, void* xe, void* xo, void* y, void* dbg, void* ids, int N, int K,
+                              int nExp, int nblk, int lay, void* stream) {
+    (void)dbg;
+    (void)nblk;
+    if (N < 1 || K < 128 || K % 128 || nExp < 1 || (lay != 1 && lay != 2)) return FNX_EARG;
+    if (!aligned16(p4)) return FNX_EALIGN;
+    W4GemvLayer L{(const uint8_t*)p4, (const __half*)s4t, (const float*)xe, (const float*)(xo ? xo : xe), (float*)y};
+    const int blocks = (nExp * N + 7) / 8;
+    if (lay == 1) w4gemv_kernel<1><<<blocks, 256, 0, (cudaStream_t)stream>>>(L, (const int32_t*)ids, N, K, nExp);
+    else w4gemv_kernel<2><<<blocks, 256, 0, (cudaStream_t)stream>>>(L, (const int32_t*)ids, N, K, nExp);
+    return launch_rc();
+}
+
+FNX_API int fnx_w4gemv_launch_layers(void** p4, void** s4t, void** x, void** y, int nL, int N, int K, int nExp, int nblk,
+                                     int lay, void* dbg, void* stream) {
+    (void)dbg;
+    (void)nblk;
+    if (nL < 1 || nL > W4GEMV_MAX_LAYERS || N < 1 || K < 128 || K % 128 || nExp < 1 || (lay != 1 && lay != 2))
+        return FNX_EARG;
+    W4GemvLayers Ls{};
+    for (int i = 0; i < nL; ++i) {
+        if (!aligned16(p4[i])) return FNX_EALIGN;
+        Ls.L[i] = W4GemvLayer{(const uint8_t*)p4[i], (const __half*)s4t[i], (const float*)x[i],
+                              (const float*)x[i], (float*)y[i]};
+    }
+    dim3 grid((nExp * N + 7) / 8, nL);
+    if (lay == 1) w4gemv_layers_kernel<1><<<grid, 256, 0, (cudaStream_t)stream>>>(Ls, N, K, nExp);
+    else w4gemv_layers_kernel<2><<<grid, 256, 0, (cudaStream_t)stream>>>(Ls, N, K, nExp);
+    return launch_rc();
+}

@@ -1,0 +1,507 @@
+// Expert-major grouped GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+//   out[row_begin(e) + n, f] = epilogue( sum_k W_e[k, f] * X[src(row_begin(e) + n), k] )
+//
+// for every expert e with rows [ends[e-1], ends[e]).  This is the restated
+// npu_grouped_matmul(group_type=0) of fnx/engine.py:749-753 (prefill gate/up and down)
+// and, with one group, npu_weight_quant_batchmatmul (dense W8A16, router, shared expert).
+//
+// Orientation ("swap-AB"): the weight features are the UMMA M dimension (128 rows of A)
+// and the expert's token rows are N (16..128 in steps of 16), so an expert with ~80
+// tokens pads to 80, not to 128.  D[f, n] accumulates in TMEM (fp32, lane = feature,
+// column = token), double-buffered so the epilogue of one tile overlaps the next.
+//
+// Warp roles (512 threads):
+//   warps 0, 3    B loaders: gather token rows with cp.async into K-major SW128 tiles
+//                 (alternate 16-byte chunks), keeping B_LAG stages in flight
+//   warp 1        TMEM allocator + single-thread MMA issuer (tcgen05.mma kind::f16)
+//   warp 2        TMA producer: W4 -> raw int4 words + scales into an R_STAGES-deep ring;
+//                 BF16 -> the A tiles themselves (128-byte swizzle)
+//   warps 4-7     epilogue warpgroup: tcgen05.ld -> bf16 / SwiGLU -> global
+//   warps 8-15    A producers (W4/W8), two groups of four warps taking alternate k-blocks:
+//                 int4 / int8 -> bf16(q * s) (exactly rounded) -> SW128 smem
+// Every wait is bounded (fnx_common.cuh); a timeout sets an abort flag and all roles
+// unwind to the final barrier, where the allocating warp frees TMEM.
+#pragma once
+#include "fnx_common.cuh"
+
+namespace fnx {
+
+enum GemmMode { GEMM_W4 = 0, GEMM_W8 = 1, GEMM_BF16 = 2 };
+enum GemmEpi { EPI_PLAIN = 0, EPI_SWIGLU_F32 = 1, EPI_SWIGLU_BF16 = 2 };
+
+constexpr int G_BM = 128;          // weight features per tile (UMMA M)
+constexpr int G_BK = 64;           // k per stage (one 128-byte swizzle row of bf16)
+constexpr int G_BN = 128;          // max token rows per tile
+constexpr int G_STAGES = 5;
+constexpr int G_R_STAGES = 8;      // raw int4 ring depth (even: each stage belongs to one producer group)
+constexpr int G_B_LAG = 3;         // cp.async stages the B loader keeps in flight
+constexpr int G_THREADS = 512;
+constexpr int G_A_BYTES = G_BM * G_BK * 2;     // 16 KB
+constexpr int G_B_BYTES = G_BN * G_BK * 2;     // 16 KB
+constexpr int G_RAW_W = 2 * 64 * 8 * 4;        // 4 KB: [half][64 k][8 words]
+constexpr int G_RAW_BYTES = G_RAW_W + 2 * 64 * 2;   // + scales [half][64 features]
+constexpr int G_MAX_E = 1024;
+
+struct GemmParams {
+    CUtensorMap tmap_a;         // W4: int32 words [E*K, Nw/8] box {8, 64};  BF16: bf16 [E*Nw, K] box {64, 128}, SW128
+    CUtensorMap tmap_s;         // W4: bf16 scales [E*G, Nw] box {64, 1}
+    const bf16* act;            // token rows bf16 [*, K], row stride ld_act elements
+    long long ld_act;
+    const int64_t* row_index;   // null: row r of the problem reads act row r; else row_index[r] / index_div
+    int index_div;
+    const void* w;              // W4: int32 [E, K, Nw/8]; W8: int8 [E, K, Nw]; BF16: bf16 [E, Nw, K]
+    const bf16* scales;         // W4/W8: bf16 [E, K/gs, Nw]
+    const int64_t* ends;        // [E] cumulative row counts; null: one group of M rows
+    bf16* out;                  // bf16 [M, ld_out]
+    long long ld_out;
+    int E, M, K, Nw, gs;
+    int m_tiles;                // tiles along the feature dimension
+};
+
+struct GemmSmem {
+    uint64_t a_full[G_STAGES], b_full[G_STAGES], empty[G_STAGES];
+    uint64_t raw_full[G_R_STAGES], raw_empty[G_R_STAGES];
+    uint64_t acc_full[2], acc_empty[2], final_bar;
+    uint32_t tmem_base;
+    volatile int abort;
+    int total_tiles;
+    int tile_start[G_MAX_E + 1];
+};
+
+struct TileInfo {
+    int e, m, row0, nrows;
+};
+
+FNX_DEV bool decode_tile(const GemmSmem& S, const GemmParams& p, int tile, TileInfo& ti) {
+    if (tile >= S.total_tiles) return false;
+    int lo = 0, hi = p.E;              // largest e with tile_start[e] <= tile
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (S.tile_start[mid] <= tile) lo = mid; else hi = mid;
+    }
+    const int e = lo;
+    const int local = tile - S.tile_start[e];
+    const int chunk = local / p.m_tiles;
+    ti.e = e;
+    ti.m = local % p.m_tiles;
+    const long long begin = p.ends ? (e ? p.ends[e - 1] : 0) : 0;
+    const long long end = p.ends ? p.ends[e] : p.M;
+    ti.row0 = (int)begin + chunk * G_BN;
+    ti.nrows = (int)min((long long)G_BN, end - ti.row0);
+    return true;
+}
+
+// First weight feature of half h (64 features) in feature tile m.
+template <int EPI>
+FNX_DEV int half_feature(int h, int m, int Nw) {
+    return EPI == EPI_PLAIN ? m * G_BM + h * 64 : (h ? Nw / 2 : 0) + m * 64;
+}
+// A row holding the feature (half h, word j, nibble pf) of the tile, i.e. feature
+// half_feature(h) + 8j + pf.  Rows are ordered nibble-major (8pf + j) so that a warp's
+// 16-byte stores of one nibble position fall into eight different swizzle chunks
+// (conflict-free); SwiGLU keeps a feature's gate and up on adjacent rows.
+template <int EPI>
+FNX_DEV int a_row(int h, int j, int pf) {
+    const int q = 8 * pf + j;
+    return EPI == EPI_PLAIN ? h * 64 + q : 2 * q + h;
+}
+// Inverse of a_row for the epilogue: the feature offset (within the tile for PLAIN,
+// within the half for SwiGLU) held by accumulator lane r.
+template <int EPI>
+FNX_DEV int lane_feature(int r) {
+    if (EPI == EPI_PLAIN) {
+        const int q = r & 63;
+        return (r & 64) + 8 * (q & 7) + (q >> 3);
+    }
+    const int q = r >> 1;
+    return 8 * (q & 7) + (q >> 3);
+}
+
+// ------------------------------------------------------------------ A producers
+// W4: thread (h, kq, j) of a 128-thread group dequantises the 8x8 block of k rows
+// 8kq .. 8kq+7 of the stage and the 8 features of word column j in half h, reading the
+// raw words and scales the TMA warp staged in shared memory.
+template <int EPI>
+FNX_DEV void produce_a_w4(const uint8_t* raw, uint8_t* a_tile, int t) {
+    const int j = t & 7, kq = (t >> 3) & 7, h = t >> 6;
+    const uint32_t* rw = reinterpret_cast<const uint32_t*>(raw) + h * 512 + kq * 64 + j;
+    uint32_t wv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) wv[i] = rw[i * 8];
+    const uint4 sv = *reinterpret_cast<const uint4*>(raw + G_RAW_W + h * 128 + j * 16);
+    const uint32_t sarr[4] = {sv.x, sv.y, sv.z, sv.w};
+    // spread nibbles: ev[i] holds nibbles 0,2,4,6 (offset binary) in bytes 0..3, ov[i] nibbles 1,3,5,7
+    uint32_t ev[8], ov[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t x = wv[i] ^ 0x88888888u;
+        ev[i] = x & 0x0f0f0f0fu;
+        ov[i] = (x >> 4) & 0x0f0f0f0fu;
+    }
+    const uint32_t k136 = 0x43084308u;
+#pragma unroll
+    for (int pf = 0; pf < 8; ++pf) {
+        const int q = pf >> 1;
+        // selector: byte q of the first operand, zero (sign of a byte < 0x80), byte q of
+        // the second operand, zero -> [k even | k odd] nibbles of feature pf
+        const uint32_t sel = (uint32_t)q | ((8u | q) << 4) | ((4u + q) << 8) | ((8u | (4u + q)) << 12);
+        const uint32_t s16 = (pf & 1) ? (sarr[pf >> 1] >> 16) : (sarr[pf >> 1] & 0xffffu);
+        const uint32_t s2 = s16 | (s16 << 16);
+        uint32_t outv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t a = (pf & 1) ? ov[2 * i] : ev[2 * i];
+            const uint32_t b = (pf & 1) ? ov[2 * i + 1] : ev[2 * i + 1];
+            uint32_t t2;
+            asm("prmt.b32 %0, %1, %2, %3;" : "=r"(t2) : "r"(a), "r"(b), "r"(sel));
+            t2 |= 0x43004300u;
+            uint32_t qv;
+            asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(qv) : "r"(t2), "r"(k136));
+            outv[i] = bmul2(qv, s2);
+        }
+        const int r = a_row<EPI>(h, j, pf);
+        *reinterpret_cast<uint4*>(a_tile + sw128_offset(r, kq)) = make_uint4(outv[0], outv[1], outv[2], outv[3]);
+    }
+}
+
+// W8: same block shape, int8 weights read directly (L2-resident dense projections).
+template <int EPI>
+FNX_DEV void produce_a_w8(const GemmParams& p, const TileInfo& ti, int kb, uint8_t* a_tile, int t) {
+    const int j = t & 7, kq = (t >> 3) & 7, h = t >> 6;
+    const int fbase = half_feature<EPI>(h, ti.m, p.Nw) + j * 8;
+    const int k0 = kb * G_BK + kq * 8;
+    const int8_t* wp = reinterpret_cast<const int8_t*>(p.w) + ((long long)ti.e * p.K + k0) * p.Nw + fbase;
+    uint2 wv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) wv[i] = __ldg(reinterpret_cast<const uint2*>(wp + (long long)i * p.Nw));
+    const int G = p.K / p.gs;
+    const uint4 sv = __ldg(reinterpret_cast<const uint4*>(p.scales + ((long long)ti.e * G + k0 / p.gs) * p.Nw + fbase));
+    const uint32_t sarr[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+    for (int pf = 0; pf < 8; ++pf) {
+        const float s = (pf & 1) ? bf_hi(sarr[pf >> 1]) : bf_lo(sarr[pf >> 1]);
+        uint32_t outv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t w0 = pf < 4 ? wv[2 * i].x : wv[2 * i].y;
+            const uint32_t w1 = pf < 4 ? wv[2 * i + 1].x : wv[2 * i + 1].y;
+            const int sh = (pf & 3) * 8;
+            const float q0 = (float)(int8_t)((w0 >> sh) & 0xffu);
+            const float q1 = (float)(int8_t)((w1 >> sh) & 0xffu);
+            outv[i] = pack_bf2(__fmul_rn(q0, s), __fmul_rn(q1, s));
+        }
+        const int r = a_row<EPI>(h, j, pf);
+        *reinterpret_cast<uint4*>(a_tile + sw128_offset(r, kq)) = make_uint4(outv[0], outv[1], outv[2], outv[3]);
+    }
+}
+
+// ------------------------------------------------------------------ epilogue
+// PERM: A rows follow a_row() (dequantising producers); otherwise rows are in feature
+// order (TMA-loaded bf16 weights).
+template <int EPI, bool PERM>
+FNX_DEV void epilogue_chunk(const GemmParams& p, const TileInfo& ti, int r, int n0, const uint32_t (&v)[16]) {
+    const int lane = threadIdx.x & 31;
+    if (EPI == EPI_PLAIN) {
+        const int f = ti.m * G_BM + (PERM ? lane_feature<EPI>(r) : r);
+        bf16* o = p.out + (long long)(ti.row0 + n0) * p.ld_out + f;
+        const int lim = ti.nrows - n0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            if (i < lim) o[(long long)i * p.ld_out] = f2bf(__uint_as_float(v[i]));
+    } else {
+        // lane pairs (2i, 2i+1) hold gate / up of feature m*64 + r/2 for 16 tokens;
+        // the even lane finishes tokens 0..7, the odd lane tokens 8..15.
+        const bool odd = lane & 1;
+        float g[8], u[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float a0 = round_bf(__uint_as_float(v[i]));          // my value, token i
+            const float a1 = round_bf(__uint_as_float(v[8 + i]));      // my value, token 8+i
+            // send the half the partner finishes, receive the half I finish
+            const float recv = __shfl_xor_sync(0xffffffffu, odd ? a0 : a1, 1);
+            const float mine = odd ? a1 : a0;
+            g[i] = odd ? recv : mine;
+            u[i] = odd ? mine : recv;
+        }
+        const int f = ti.m * 64 + (PERM ? lane_feature<EPI>(r) : (r >> 1));
+        const int nb = n0 + (odd ? 8 : 0);
+        bf16* o = p.out + (long long)(ti.row0 + nb) * p.ld_out + f;
+        const int lim = ti.nrows - nb;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float a;
+            if (EPI == EPI_SWIGLU_F32) a = __fmul_rn(silu_f32(g[i]), u[i]);
+            else a = __fmul_rn(round_bf(silu_f32(g[i])), u[i]);
+            if (i < lim) o[(long long)i * p.ld_out] = f2bf(a);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ the kernel
+template <int MODE, int EPI>
+__global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid_constant__ GemmParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* a_tiles = base;
+    uint8_t* b_tiles = a_tiles + G_STAGES * G_A_BYTES;
+    uint8_t* raw_tiles = b_tiles + G_STAGES * G_B_BYTES;
+    GemmSmem& S = *reinterpret_cast<GemmSmem*>(raw_tiles + (MODE == GEMM_W4 ? G_R_STAGES * G_RAW_BYTES : 0));
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // ---- prologue: barriers, TMEM, per-expert tile offsets
+    if (tid == 0) {
+        for (int s = 0; s < G_STAGES; ++s) {
+            mbar_init(&S.a_full[s], MODE == GEMM_BF16 ? 1 : 4);
+            mbar_init(&S.b_full[s], 2);
+            mbar_init(&S.empty[s], 1);
+        }
+        for (int s = 0; s < G_R_STAGES; ++s) {
+            mbar_init(&S.raw_full[s], 1);
+            mbar_init(&S.raw_empty[s], 4);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&S.acc_full[b], 1);
+            mbar_init(&S.acc_empty[b], 4);
+        }
+        mbar_init(&S.final_bar, 1);
+        S.abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&S.tmem_base, 256);
+        tmem_relinquish();
+    }
+    if (warp == 2 && lane == 0) {
+        tma_prefetch_desc(&p.tmap_a);
+        if (MODE == GEMM_W4) tma_prefetch_desc(&p.tmap_s);
+    }
+    {
+        // tile_start[e] = sum_{e' < e} ceil(count(e') / G_BN) * m_tiles   (block scan)
+        __shared__ int warp_sums[G_THREADS / 32];
+        __shared__ int carry;
+        if (tid == 0) carry = 0;
+        __syncthreads();
+        for (int e0 = 0; e0 < p.E; e0 += G_THREADS) {
+            const int e = e0 + tid;
+            int n = 0;
+            if (e < p.E) {
+                const long long begin = p.ends ? (e ? p.ends[e - 1] : 0) : 0;
+                const long long end = p.ends ? p.ends[e] : p.M;
+                const long long cnt = end > begin ? end - begin : 0;   // malformed ends -> no tiles
+                n = (int)((cnt + G_BN - 1) / G_BN) * p.m_tiles;
+            }
+            int incl = n;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (lane == 31) warp_sums[warp] = incl;
+            __syncthreads();
+            int before = carry;
+            for (int w = 0; w < warp; ++w) before += warp_sums[w];
+            if (e < p.E) S.tile_start[e] = before + incl - n;
+            __syncthreads();
+            if (tid == G_THREADS - 1) carry = before + incl;
+            __syncthreads();
+        }
+        if (tid == 0) {
+            S.tile_start[p.E] = carry;
+            S.total_tiles = carry;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = S.tmem_base;
+    const int KB = p.K / G_BK;
+
+    if (warp == 0 || warp == 3) {
+        // ------------------------------------------------ B loaders (two warps, alternate 16-byte chunks)
+        const int bw = warp == 3 ? 1 : 0;
+        int it = 0, pending = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && !S.abort; tile += gridDim.x) {
+            TileInfo ti;
+            if (!decode_tile(S, p, tile, ti)) break;
+            const bf16* rows[G_BN / 32];
+#pragma unroll
+            for (int i = 0; i < G_BN / 32; ++i) {
+                const int n = lane + 32 * i;
+                long long src = -1;
+                if (n < ti.nrows) {
+                    const long long r = ti.row0 + n;
+                    src = p.row_index ? p.row_index[r] / p.index_div : r;
+                }
+                rows[i] = src >= 0 ? p.act + src * p.ld_act : nullptr;
+            }
+            const int npad = (ti.nrows + 15) & ~15;
+            for (int kb = 0; kb < KB; ++kb, ++it) {
+                const int s = it % G_STAGES;
+                if (!mbar_wait(&S.empty[s], ((it / G_STAGES) & 1) ^ 1)) { S.abort = 1; ok = false; break; }
+                const uint32_t bt = smem_u32(b_tiles + s * G_B_BYTES);
+#pragma unroll
+                for (int i = 0; i < G_BN / 32; ++i) {
+                    const int n = lane + 32 * i;
+                    if (n < npad) {
+                        const bf16* src = rows[i] ? rows[i] + kb * G_BK : p.act;
+#pragma unroll
+                        for (int c = bw; c < 8; c += 2)
+                            cp_async_16_zfill(bt + sw128_offset(n, c), src + c * 8, rows[i] != nullptr);
+                    }
+                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
+                if (++pending > G_B_LAG) {
+                    asm volatile("cp.async.wait_group %0;" ::"n"(G_B_LAG) : "memory");
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S.b_full[(it - G_B_LAG) % G_STAGES]);
+                    --pending;
+                }
+            }
+        }
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0)
+            for (int q = pending; q > 0; --q) mbar_arrive(&S.b_full[(it - q) % G_STAGES]);
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int it = 0, tcount = 0;
+            for (int tile = blockIdx.x; !S.abort; tile += gridDim.x, ++tcount) {
+                TileInfo ti;
+                if (!decode_tile(S, p, tile, ti)) break;
+                const int ab = tcount & 1;
+                if (!mbar_wait(&S.acc_empty[ab], ((tcount >> 1) & 1) ^ 1)) { S.abort = 1; break; }
+                tc_fence_after();
+                const int npad = (ti.nrows + 15) & ~15;
+                const uint32_t idesc = idesc_bf16_f32(G_BM, npad);
+                const uint32_t d = tmem + ab * G_BN;
+                bool ok = true;
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    const int s = it % G_STAGES;
+                    const uint32_t ph = (it / G_STAGES) & 1;
+                    if (!mbar_wait(&S.a_full[s], ph) || !mbar_wait(&S.b_full[s], ph)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(a_tiles + s * G_A_BYTES);
+                    const uint32_t b0 = smem_u32(b_tiles + s * G_B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < G_BK / 16; ++kk)
+                        umma_bf16(d, sdesc_kmajor_sw128(a0 + kk * 32), sdesc_kmajor_sw128(b0 + kk * 32), idesc,
+                                  (kb | kk) ? 1u : 0u);
+                    umma_commit(&S.empty[s]);
+                }
+                if (!ok) { S.abort = 1; break; }
+                umma_commit(&S.acc_full[ab]);
+            }
+            umma_commit(&S.final_bar);
+            mbar_wait(&S.final_bar, 0);
+        }
+        __syncwarp();
+    } else if (warp == 2) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int it = 0;
+            const int G = MODE == GEMM_W4 ? p.K / p.gs : 1;
+            for (int tile = blockIdx.x; !S.abort; tile += gridDim.x) {
+                TileInfo ti;
+                if (!decode_tile(S, p, tile, ti)) break;
+                bool ok = true;
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    if (MODE == GEMM_W4) {
+                        const int rs = it % G_R_STAGES;
+                        if (!mbar_wait(&S.raw_empty[rs], ((it / G_R_STAGES) & 1) ^ 1)) { ok = false; break; }
+                        uint8_t* raw = raw_tiles + rs * G_RAW_BYTES;
+                        mbar_arrive_expect_tx(&S.raw_full[rs], G_RAW_BYTES);
+                        const int row = ti.e * p.K + kb * G_BK;
+                        const int srow = ti.e * G + (kb * G_BK) / p.gs;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int f0 = half_feature<EPI>(h, ti.m, p.Nw);
+                            tma_load_2d(smem_u32(raw + h * 2048), &p.tmap_a, &S.raw_full[rs], f0 / 8, row);
+                            tma_load_2d(smem_u32(raw + G_RAW_W + h * 128), &p.tmap_s, &S.raw_full[rs], f0, srow);
+                        }
+                    } else if (MODE == GEMM_BF16) {
+                        const int s = it % G_STAGES;
+                        if (!mbar_wait(&S.empty[s], ((it / G_STAGES) & 1) ^ 1)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&S.a_full[s], G_A_BYTES);
+                        tma_load_2d(smem_u32(a_tiles + s * G_A_BYTES), &p.tmap_a, &S.a_full[s], kb * G_BK,
+                                    ti.e * p.Nw + ti.m * G_BM);
+                    }
+                }
+                if (!ok) { S.abort = 1; break; }
+            }
+        }
+        __syncwarp();
+    } else if (warp >= 4 && warp < 8) {
+        // ------------------------------------------------ epilogue warpgroup
+        const int e4 = warp - 4;
+        int tcount = 0;
+        for (int tile = blockIdx.x; !S.abort; tile += gridDim.x, ++tcount) {
+            TileInfo ti;
+            if (!decode_tile(S, p, tile, ti)) break;
+            const int ab = tcount & 1;
+            if (!mbar_wait(&S.acc_full[ab], (tcount >> 1) & 1)) { S.abort = 1; break; }
+            tc_fence_after();
+            const int r = e4 * 32 + lane;
+            const int npad = (ti.nrows + 15) & ~15;
+            for (int n0 = 0; n0 < npad; n0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem + ((uint32_t)(e4 * 32) << 16) + ab * G_BN + n0, v);
+                tmem_ld_wait();
+                epilogue_chunk<EPI, MODE != GEMM_BF16>(p, ti, r, n0, v);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.acc_empty[ab]);
+        }
+    } else if (warp >= 8 && MODE != GEMM_BF16) {
+        // ------------------------------------------------ A producers
+        const int grp = (warp - 8) >> 2;
+        const int t = tid - 256 - grp * 128;
+        int it = 0;
+        for (int tile = blockIdx.x; !S.abort; tile += gridDim.x) {
+            TileInfo ti;
+            if (!decode_tile(S, p, tile, ti)) break;
+            bool ok = true;
+            for (int kb = 0; kb < KB; ++kb, ++it) {
+                if ((it & 1) != grp) continue;
+                const int s = it % G_STAGES;
+                uint8_t* at = a_tiles + s * G_A_BYTES;
+                if (MODE == GEMM_W4) {
+                    const int rs = it % G_R_STAGES;
+                    if (!mbar_wait(&S.raw_full[rs], (it / G_R_STAGES) & 1)) { ok = false; break; }
+                    if (!mbar_wait(&S.empty[s], ((it / G_STAGES) & 1) ^ 1)) { ok = false; break; }
+                    produce_a_w4<EPI>(raw_tiles + rs * G_RAW_BYTES, at, t);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&S.raw_empty[rs]);
+                } else {
+                    if (!mbar_wait(&S.empty[s], ((it / G_STAGES) & 1) ^ 1)) { ok = false; break; }
+                    produce_a_w8<EPI>(p, ti, kb, at, t);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.a_full[s]);
+            }
+            if (!ok) { S.abort = 1; break; }
+        }
+    }
+
+    // ---- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
+inline size_t grouped_gemm_smem_bytes(int mode) {
+    return 1024 + (size_t)G_STAGES * (G_A_BYTES + G_B_BYTES) + (mode == GEMM_W4 ? (size_t)G_R_STAGES * G_RAW_BYTES : 0) +
+           sizeof(GemmSmem);
+}
+
+}  // namespace fnx

@@ -1,0 +1,201 @@
+// Router top-k and the expert-major permutation.
+//
+// Routing (fnx/engine.py:1811-1813 in the reference): probs = softmax(fp32(logits));
+// (w, idx) = topk(probs, k); w = bf16(w / sum(w)).  Ties are broken by ascending expert
+// id (descending probability first), so the selection is a pure function of the bf16
+// logits.  Permutation (fnx/engine.py:1817-1840): a stable counting sort of the flattened
+// ids -> order (expert-major, (token*k + slot) order inside an expert), its inverse, and
+// the cumulative per-expert row counts `ends`.
+#pragma once
+#include "fnx_common.cuh"
+
+namespace fnx {
+
+constexpr int ROUTE_MAX_E = 2048;     // experts per token row handled by one warp
+constexpr int ROUTE_MAX_K = 32;       // top-k slots (one lane each)
+
+// Top-k of one row by one warp; PER = experts per lane (E <= 32*PER).  Returns, in lane
+// j < k, slot j's probability (my_p) and expert id (my_i); `tot` is the slot-order sum of
+// the k probabilities (identical in every lane).  CG reads the row through L2 (rows
+// written by other blocks of the same kernel).
+template <int PER, bool CG>
+FNX_DEV void topk_warp(const bf16* row, const float* bias, int E, int k, float& my_p, int& my_i, float& tot) {
+    const int lane = threadIdx.x & 31;
+    float v[PER];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        const int e = i * 32 + lane;
+        float x = -INFINITY;
+        if (e < E) {
+            x = CG ? __uint_as_float((uint32_t)__ldcg(reinterpret_cast<const unsigned short*>(row) + e) << 16)
+                   : bf2f(row[e]);
+            if (bias) x = __fadd_rn(x, bias[e]);
+        }
+        v[i] = x;
+        mx = fmaxf(mx, x);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        const int e = i * 32 + lane;
+        const float p = e < E ? expf(__fsub_rn(v[i], mx)) : 0.f;
+        v[i] = p;
+        sum = __fadd_rn(sum, p);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    const float inv = 1.0f / sum;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) v[i] = (i * 32 + lane) < E ? __fmul_rn(v[i], inv) : -1.f;
+
+    my_p = 0.f;
+    tot = 0.f;
+    my_i = 0;
+    for (int j = 0; j < k; ++j) {
+        // highest probability, lowest id on ties (ascending e within a lane keeps the lowest)
+        float bp = -2.f;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < PER; ++i)
+            if (v[i] > bp) { bp = v[i]; bi = i * 32 + lane; }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (op > bp || (op == bp && oi < bi)) { bp = op; bi = oi; }
+        }
+#pragma unroll
+        for (int i = 0; i < PER; ++i)
+            if (i * 32 + lane == bi) v[i] = -1.f;
+        if (lane == j) { my_p = bp; my_i = bi; }
+        tot = __fadd_rn(tot, bp);
+    }
+}
+
+// One warp per token.  logits: bf16 [T, ld] (first E columns); bias: fp32 [E] or null.
+template <int PER>
+__global__ void __launch_bounds__(256) router_topk_kernel(const bf16* __restrict__ logits, long long ld,
+                                                          const float* __restrict__ bias, bf16* __restrict__ w_out,
+                                                          int64_t* __restrict__ idx_out, int32_t* __restrict__ idx32_out,
+                                                          float* __restrict__ wf_out, int T, int E, int k) {
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= T) return;
+    float my_p, tot;
+    int my_i;
+    topk_warp<PER, false>(logits + (long long)t * ld, bias, E, k, my_p, my_i, tot);
+    if (lane < k) {
+        const bf16 wb = f2bf(my_p / tot);
+        const long long o = (long long)t * k + lane;
+        w_out[o] = wb;
+        if (idx_out) idx_out[o] = my_i;
+        if (idx32_out) idx32_out[o] = my_i;
+        if (wf_out) wf_out[o] = bf2f(wb);
+    }
+}
+
+// ------------------------------------------------------------------ permutation
+// Stable counting sort of n = T*k expert ids (int64) in chunks of PERM_CHUNK entries.
+constexpr int PERM_CHUNK = 1024;
+constexpr int PERM_MAX_E = 4096;
+
+// pass 1: per-chunk histograms hist[chunk][E]
+__global__ void __launch_bounds__(256) permute_hist_kernel(const int64_t* __restrict__ ids, int n, int E,
+                                                           int* __restrict__ hist) {
+    extern __shared__ int sh[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = 0;
+    __syncthreads();
+    const int c0 = blockIdx.x * PERM_CHUNK;
+    for (int i = c0 + threadIdx.x; i < min(n, c0 + PERM_CHUNK); i += blockDim.x) {
+        const long long e = ids[i];
+        if (e >= 0 && e < E) atomicAdd(&sh[e], 1);
+        else fnx_flag_error(FNX_DEVERR_BADID);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(long long)blockIdx.x * E + e] = sh[e];
+}
+
+// pass 2 (one block): ends[e] = inclusive cumsum of counts; hist[c][e] becomes the
+// starting output position of chunk c's entries for expert e.
+__global__ void __launch_bounds__(1024) permute_scan_kernel(int* __restrict__ hist, int nchunks, int E,
+                                                            int64_t* __restrict__ ends, int64_t* __restrict__ counts_out) {
+    __shared__ int part[1024];
+    __shared__ int carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int e0 = 0; e0 < E; e0 += blockDim.x) {
+        const int e = e0 + threadIdx.x;
+        int cnt = 0;
+        if (e < E)
+#pragma unroll 8
+            for (int c = 0; c < nchunks; ++c) cnt += hist[(long long)c * E + e];
+        part[threadIdx.x] = cnt;
+        __syncthreads();
+        // inclusive Hillis-Steele scan over the block
+        for (int o = 1; o < blockDim.x; o <<= 1) {
+            const int add = threadIdx.x >= o ? part[threadIdx.x - o] : 0;
+            __syncthreads();
+            part[threadIdx.x] += add;
+            __syncthreads();
+        }
+        const int incl = part[threadIdx.x] + carry;
+        if (e < E) {
+            ends[e] = incl;
+            if (counts_out) counts_out[e] = cnt;
+            int pos = incl - cnt;
+            for (int c = 0; c < nchunks; ++c) {
+                const long long h = (long long)c * E + e;
+                const int v = hist[h];
+                hist[h] = pos;
+                pos += v;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1) carry = incl;
+        __syncthreads();
+    }
+}
+
+// pass 3: one warp per chunk walks its entries in order; __match_any_sync gives each
+// entry its rank among equal ids in the same 32-entry batch, so positions are stable.
+__global__ void __launch_bounds__(32) permute_scatter_kernel(const int64_t* __restrict__ ids, int n, int E,
+                                                             const int* __restrict__ start,
+                                                             int64_t* __restrict__ order, int64_t* __restrict__ inverse) {
+    extern __shared__ int cursor[];
+    int* sid = cursor + E;                       // this chunk's ids, loaded in one coalesced pass
+    const int lane = threadIdx.x;
+    const int c0 = blockIdx.x * PERM_CHUNK;
+    const int c1 = min(n, c0 + PERM_CHUNK);
+    for (int e = lane; e < E; e += 32) cursor[e] = start[(long long)blockIdx.x * E + e];
+#pragma unroll 8
+    for (int i = c0 + lane; i < c1; i += 32) {
+        const long long e = ids[i];
+        sid[i - c0] = (e >= 0 && e < E) ? (int)e : -1;
+    }
+    __syncwarp();
+    for (int b = c0; b < c1; b += 32) {
+        const int i = b + lane;
+        const bool valid = i < c1;
+        long long e = valid ? sid[i - c0] : -1;
+        const bool good = valid && e >= 0 && e < E;
+        const unsigned act = __ballot_sync(0xffffffffu, good);
+        const int key = good ? (int)e : -1 - lane;       // invalid lanes get unique keys
+        const unsigned peers = __match_any_sync(0xffffffffu, key);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        int base = 0;
+        if (good) base = cursor[e];
+        __syncwarp();
+        if (good && rank == 0) cursor[e] = base + __popc(peers & act);
+        __syncwarp();
+        if (good) {
+            const long long pos = base + rank;
+            order[pos] = i;
+            if (inverse) inverse[i] = pos;
+        }
+    }
+}
+
+}  // namespace fnx

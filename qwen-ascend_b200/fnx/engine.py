@@ -1,0 +1,284 @@
+"""Quantised weight containers and the MoE layer, backed by ``libfnx_b200.so``.
+
+Mirrors the reference's MoE/quant section of ``fnx/engine.py``:
+
+* ``ExpW4``  (reference ``fnx/engine.py:619-753``): int4pack experts + bf16 group scales;
+  ``apply`` / ``apply_diag`` / ``apply_grouped`` run the tcgen05 grouped GEMM.
+* ``DenseW8`` (reference ``fnx/engine.py:297-384``): int8 ``[K, N]`` + bf16 ``[G, N]``
+  scales, N-concatenation by ``merge``; calls run the W8A16 kernels.
+* ``MoELayer`` (reference ``FnLayer._moe``, ``fnx/engine.py:1782-1930``): shared expert,
+  router top-k, expert-major permutation, grouped gate/up + SwiGLU, grouped down,
+  slot-order combine and sigmoid-gated shared merge.  ``T <= 16`` tokens take the fused
+  decode kernels, larger batches the prefill pipeline.
+
+All tensors live on a CUDA device; nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+BF16 = torch.bfloat16
+EPI_PLAIN, EPI_SWIGLU_F32, EPI_SWIGLU_BF16 = 0, 1, 2
+DECODE_MAX_TOKENS = 16
+
+
+def _grouped_w4(act, w4, scales, ends, out, *, E, M, K, Nw, gs, epilogue, row_index=None, index_div=1):
+    rc = _lib.lib().fnx_moe_grouped_w4(act.data_ptr(), act.stride(0), _lib.ptr(row_index), index_div, w4.data_ptr(),
+                                       scales.data_ptr(), _lib.ptr(ends), out.data_ptr(), out.stride(0), E, M, K, Nw,
+                                       gs, epilogue, _lib.stream(act.device))
+    _lib.check(rc, "grouped W4A16 GEMM")
+    return out
+
+
+class ExpW4:
+    """Experts in the W4A16 artifact layout (``tools/repack_w4a16.py``):
+    ``w4`` int32 ``[K, E, N/8]`` (or ``[E, K, N/8]`` with ``expert_major``), ``s8t`` int8
+    ``[G, E, N]`` and ``base`` bf16 ``[E, N]``; the real scale is
+    ``bf16(bf16(s8t) * base)``, cached as ``_scales [E, G, N]`` exactly as
+    ``FNX_W4_SCALE_CACHE=1`` does (``fnx/engine.py:653-659``).  The kernels read the
+    expert-major words, so a K-major artifact is transposed once here (the byte-exact
+    transpose of ``tools/repack_w4_em.py``)."""
+
+    def __init__(self, w4, s8t, base, gs, expert_major=False):
+        _lib.require_cuda(w4)
+        self.expert_major = True
+        self.w4 = (w4 if expert_major else w4.permute(1, 0, 2)).contiguous()
+        self.E, self.K = self.w4.shape[0], self.w4.shape[1]
+        self.N = self.w4.shape[2] * 8
+        self.G = s8t.shape[0]
+        self.gs = gs
+        self._scales = (s8t.permute(1, 0, 2).to(BF16) * base.to(BF16)[:, None, :]).contiguous()
+        self.s8t = self.base = None
+
+    @classmethod
+    def from_scales(cls, w4_em, scales, gs):
+        """Expert-major words ``[E, K, N/8]`` and ready bf16 scales ``[E, G, N]``."""
+        _lib.require_cuda(w4_em, scales)
+        o = cls.__new__(cls)
+        o.expert_major = True
+        o.w4 = w4_em.contiguous()
+        o.E, o.K = o.w4.shape[0], o.w4.shape[1]
+        o.N = o.w4.shape[2] * 8
+        o.G = scales.shape[1]
+        o.gs = gs
+        o._scales = scales.contiguous()
+        o.s8t = o.base = None
+        return o
+
+    def _selected(self, ids):
+        return self.w4.index_select(0, ids).contiguous(), self._scales.index_select(0, ids).contiguous()
+
+    def apply(self, x, ids):
+        """x ``[M, K]`` bf16, ids ``[k]`` -> ``[M, k*N]``: every row times every selected expert."""
+        M, k = x.shape[0], ids.numel()
+        w, s = self._selected(ids)
+        rows = torch.arange(k * M, device=x.device, dtype=torch.int64) % M
+        ends = torch.arange(1, k + 1, device=x.device, dtype=torch.int64) * M
+        out = torch.empty(k * M, self.N, dtype=BF16, device=x.device)
+        _grouped_w4(x.to(BF16).contiguous(), w, s, ends, out, E=k, M=k * M, K=self.K, Nw=self.N, gs=self.gs,
+                    epilogue=EPI_PLAIN, row_index=rows)
+        return out.view(k, M, self.N).transpose(0, 1).reshape(M, k * self.N)
+
+    def apply_diag(self, x, ids):
+        """Row j of x uses expert ids[j] -> ``[k, N]`` (the diagonal of the Cartesian product)."""
+        k = x.shape[0]
+        w, s = self._selected(ids)
+        ends = torch.arange(1, k + 1, device=x.device, dtype=torch.int64)
+        out = torch.empty(k, self.N, dtype=BF16, device=x.device)
+        return _grouped_w4(x.to(BF16).contiguous(), w, s, ends, out, E=k, M=k, K=self.K, Nw=self.N, gs=self.gs,
+                           epilogue=EPI_PLAIN)
+
+    def apply_grouped(self, x, group_ends, host_ends=None):
+        """Rows sorted by expert (cumulative ``group_ends`` over all E experts)."""
+        out = torch.empty(x.shape[0], self.N, dtype=BF16, device=x.device)
+        return _grouped_w4(x.to(BF16).contiguous(), self.w4, self._scales, group_ends.contiguous(), out, E=self.E,
+                           M=x.shape[0], K=self.K, Nw=self.N, gs=self.gs, epilogue=EPI_PLAIN)
+
+
+class DenseW8:
+    """Dense int8 weights, per-group bf16 scales (``fnx/engine.py:297-384``):
+    ``q`` int8 ``[N, K(+pad)]``, ``s`` ``[N, G]`` -> ``w8t [K, N]``, ``sc [G, N]`` bf16."""
+
+    def __init__(self, q, s, K=None):
+        gs = q.shape[-1] // s.shape[-1]
+        kk = q.shape[-1] if K is None else K
+        if kk % gs:
+            raise ValueError(f"DenseW8: K={kk} is not a multiple of gs={gs}")
+        g = kk // gs
+        self.w8t = q[:, :kk].t().contiguous()
+        self.sc = s[:, :g].t().contiguous().to(BF16)
+        self.gs = gs
+        self.K = kk
+        self.N = self.w8t.shape[1]
+        self.chunks = None
+
+    def make_chunks(self, chunk_n):
+        """Kept for interface parity; the B200 kernel has no N limit, so nothing is split."""
+        return None
+
+    def deq_w(self):
+        w = self.w8t.to(BF16) * self.sc.repeat_interleave(self.gs, dim=0)
+        return w.t().contiguous()
+
+    def __call__(self, x):
+        sh = x.shape
+        x2 = (x if x.dtype == BF16 else x.to(BF16)).reshape(-1, sh[-1]).contiguous()
+        _lib.require_cuda(x2, self.w8t)
+        y = torch.empty(x2.shape[0], self.N, dtype=BF16, device=x2.device)
+        rc = _lib.lib().fnx_w8a16_gemm(x2.data_ptr(), self.w8t.data_ptr(), self.sc.data_ptr(), y.data_ptr(),
+                                       x2.shape[0], self.K, self.N, self.sc.shape[0], _lib.stream(x2.device))
+        _lib.check(rc, "W8A16 GEMM")
+        return y if x.dim() <= 2 else y.view(*sh[:-1], self.N)
+
+    @staticmethod
+    def merge(parts):
+        assert parts and all(p is not None for p in parts)
+        gs = parts[0].gs
+        assert all(p.gs == gs and p.K == parts[0].K for p in parts), "group size / K differ, cannot merge"
+        o = DenseW8.__new__(DenseW8)
+        o.w8t = torch.cat([p.w8t for p in parts], dim=1)
+        o.sc = torch.cat([p.sc for p in parts], dim=1)
+        o.gs, o.K, o.N = gs, parts[0].K, o.w8t.shape[1]
+        o.chunks = None
+        return o
+
+
+class MoELayer:
+    """One W4A16 MoE layer: routed experts (expert-major int4pack + bf16 group scales),
+    an always-on W4 shared expert with a sigmoid gate, and a bf16 router.
+
+    ``router_cat`` concatenates the router rows and the shared-expert gate row into one
+    bf16 ``[R, H]`` GEMM operand (the reference's load-time concat,
+    ``fnx/engine.py:1223-1236``), padded to a multiple of 128 rows with zeros."""
+
+    def __init__(self, gu_w4, gu_scales, dn_w4, dn_scales, gate_w, sh_gu_w4, sh_gu_scales, sh_dn_w4, sh_dn_scales,
+                 sh_gate, k, gs, bias=None):
+        _lib.require_cuda(gu_w4, dn_w4, gate_w, sh_gu_w4, sh_dn_w4)
+        self.gu = ExpW4.from_scales(gu_w4, gu_scales, gs)
+        self.dn = ExpW4.from_scales(dn_w4, dn_scales, gs)
+        self.E, self.H = gate_w.shape
+        self.I = self.gu.N // 2
+        self.k, self.gs = k, gs
+        R = self.E + 1
+        self.R = R
+        self.R_pad = (R + 127) // 128 * 128
+        rc = torch.zeros(self.R_pad, self.H, dtype=BF16, device=gate_w.device)
+        rc[:self.E] = gate_w
+        rc[self.E] = sh_gate.reshape(-1)
+        self.router_cat = rc
+        self.sh_gu_w4, self.sh_gu_s = sh_gu_w4.contiguous(), sh_gu_scales.contiguous()
+        self.sh_dn_w4, self.sh_dn_s = sh_dn_w4.contiguous(), sh_dn_scales.contiguous()
+        self.bias = None if bias is None else bias.to(torch.float32).to(gate_w.device).contiguous()
+        self._ws = {}
+
+    @classmethod
+    def from_synth(cls, t, shape, bias=None):
+        return cls(t["gu_w4"], t["gu_scales"], t["dn_w4"], t["dn_scales"], t["gate_w"], t["sh_gu_w4"],
+                   t["sh_gu_scales"], t["sh_dn_w4"], t["sh_dn_scales"], t["sh_gate"], shape.k, shape.gs, bias=bias)
+
+    def weight_bytes(self):
+        return sum(t.numel() * t.element_size() for t in (self.gu.w4, self.gu._scales, self.dn.w4, self.dn._scales,
+                                                           self.router_cat, self.sh_gu_w4, self.sh_gu_s,
+                                                           self.sh_dn_w4, self.sh_dn_s))
+
+    # ---------------------------------------------------------------- routing
+    def logits(self, x):
+        """bf16 ``[T, R_pad]``: router logits in columns ``[0, E)``, shared gate in column E."""
+        T = x.shape[0]
+        out = torch.empty(T, self.R_pad, dtype=BF16, device=x.device)
+        rc = _lib.lib().fnx_bf16_gemm_nt(x.data_ptr(), x.stride(0), self.router_cat.data_ptr(), out.data_ptr(),
+                                         out.stride(0), T, self.H, self.R_pad, _lib.stream(x.device))
+        _lib.check(rc, "router GEMM")
+        return out
+
+    def topk(self, logits, ld=None):
+        T = logits.shape[0]
+        w = torch.empty(T, self.k, dtype=BF16, device=logits.device)
+        idx = torch.empty(T, self.k, dtype=torch.int64, device=logits.device)
+        wf = torch.empty(T, self.k, dtype=torch.float32, device=logits.device)
+        rc = _lib.lib().fnx_router_topk(logits.data_ptr(), ld or logits.stride(0), _lib.ptr(self.bias), w.data_ptr(),
+                                        idx.data_ptr(), wf.data_ptr(), T, self.E, self.k, _lib.stream(logits.device))
+        _lib.check(rc, "router top-k")
+        return w, idx, wf
+
+    def permute(self, idx):
+        n = idx.numel()
+        dev = idx.device
+        order = torch.empty(n, dtype=torch.int64, device=dev)
+        inverse = torch.empty(n, dtype=torch.int64, device=dev)
+        ends = torch.empty(self.E, dtype=torch.int64, device=dev)
+        wsb = _lib.lib().fnx_moe_permute_workspace(n, self.E)
+        ws = torch.empty(max(1, wsb), dtype=torch.uint8, device=dev)
+        rc = _lib.lib().fnx_moe_permute(idx.data_ptr(), order.data_ptr(), inverse.data_ptr(), ends.data_ptr(), None, n,
+                                        self.E, ws.data_ptr(), wsb, _lib.stream(dev))
+        _lib.check(rc, "expert permutation")
+        return order, inverse, ends
+
+    # ---------------------------------------------------------------- paths
+    def forward(self, x):
+        x = x.reshape(-1, self.H)
+        if x.dtype != BF16:
+            x = x.to(BF16)
+        x = x.contiguous()
+        if x.shape[0] <= DECODE_MAX_TOKENS:
+            return self.decode(x)[0]
+        return self.prefill(x)
+
+    __call__ = forward
+
+    def prefill(self, x, details=False):
+        """Grouped path (``fnx/engine.py:1815-1853``) for ``T`` tokens."""
+        T, H, I, k, E = x.shape[0], self.H, self.I, self.k, self.E
+        dev = x.device
+        logits = self.logits(x)
+        w, idx, wf = self.topk(logits)
+        order, inverse, ends = self.permute(idx)
+        act = torch.empty(T * k, I, dtype=BF16, device=dev)
+        _grouped_w4(x, self.gu.w4, self.gu._scales, ends, act, E=E, M=T * k, K=H, Nw=2 * I, gs=self.gs,
+                    epilogue=EPI_SWIGLU_F32, row_index=order, index_div=k)
+        yd = torch.empty(T * k, H, dtype=BF16, device=dev)
+        _grouped_w4(act, self.dn.w4, self.dn._scales, ends, yd, E=E, M=T * k, K=I, Nw=H, gs=self.gs,
+                    epilogue=EPI_PLAIN)
+        sh_act = torch.empty(T, I, dtype=BF16, device=dev)
+        _grouped_w4(x, self.sh_gu_w4, self.sh_gu_s, None, sh_act, E=1, M=T, K=H, Nw=2 * I, gs=self.gs,
+                    epilogue=EPI_SWIGLU_BF16)
+        sh = torch.empty(T, H, dtype=BF16, device=dev)
+        _grouped_w4(sh_act, self.sh_dn_w4, self.sh_dn_s, None, sh, E=1, M=T, K=I, Nw=H, gs=self.gs,
+                    epilogue=EPI_PLAIN)
+        out = torch.empty(T, H, dtype=BF16, device=dev)
+        gate = logits[:, E:E + 1]
+        rc = _lib.lib().fnx_moe_combine(yd.data_ptr(), wf.data_ptr(), inverse.data_ptr(), sh.data_ptr(),
+                                        gate.data_ptr(), logits.stride(0), out.data_ptr(), T, k, H, _lib.stream(dev))
+        _lib.check(rc, "MoE combine")
+        if details:
+            return out, dict(logits=logits[:, :E], gate=gate, w=w, idx=idx, order=order, inverse=inverse, ends=ends,
+                             act=act, yd=yd, sh=sh, sh_act=sh_act)
+        return out
+
+    def decode_workspace(self, M, device):
+        key = (M, str(device))
+        ws = self._ws.get(key)
+        if ws is None:
+            n = _lib.lib().fnx_moe_decode_workspace(M, self.H, self.I, self.E, self.k)
+            ws = torch.zeros(n, dtype=torch.uint8, device=device)      # tickets start at zero
+            self._ws[key] = ws
+        return ws
+
+    def decode(self, x, out=None, w_out=None, idx_out=None):
+        """Fused decode kernels for ``M <= 16`` tokens; returns ``(out, w, idx)``."""
+        M = x.shape[0]
+        dev = x.device
+        out = torch.empty(M, self.H, dtype=BF16, device=dev) if out is None else out
+        w_out = torch.empty(M, self.k, dtype=BF16, device=dev) if w_out is None else w_out
+        idx_out = torch.empty(M, self.k, dtype=torch.int64, device=dev) if idx_out is None else idx_out
+        ws = self.decode_workspace(M, dev)
+        rc = _lib.lib().fnx_moe_decode_w4(
+            x.data_ptr(), self.router_cat.data_ptr(), self.gu.w4.data_ptr(), self.gu._scales.data_ptr(),
+            self.dn.w4.data_ptr(), self.dn._scales.data_ptr(), self.sh_gu_w4.data_ptr(), self.sh_gu_s.data_ptr(),
+            self.sh_dn_w4.data_ptr(), self.sh_dn_s.data_ptr(), _lib.ptr(self.bias), out.data_ptr(), w_out.data_ptr(),
+            idx_out.data_ptr(), M, self.H, self.I, self.E, self.k, self.gs, ws.data_ptr(), ws.numel(),
+            _lib.stream(dev))
+        _lib.check(rc, "MoE decode")
+        return out, w_out, idx_out

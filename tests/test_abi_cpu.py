@@ -1,0 +1,94 @@
+"""CPU checks of the C ABI: the library loads without a GPU, exports every symbol the
+header declares, and rejects bad arguments on the host before any launch."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parents[1]
+HEADER = REPO / "include" / "fnx_b200.h"
+
+
+def header_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(fnx_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import build as fnx_build   # qwen-ascend_b200/build.py
+    fnx_build.build()
+    from fnx import _lib
+    return _lib.lib()
+
+
+def test_header_symbols_exported(lib):
+    syms = header_symbols()
+    assert len(syms) >= 20
+    for s in syms:
+        assert hasattr(lib, s), s
+    from fnx import _lib
+    assert set(syms) == set(_lib.SIGNATURES), "ctypes table and header disagree"
+
+
+def test_version(lib):
+    assert b"sm_100a" in lib.fnx_b200_version()
+
+
+def test_host_side_rejections(lib):
+    # rejected before any CUDA call, so these are safe without a device
+    assert lib.fnx_weighted_reduce(None, None, None, None, 0, 10, 2560, 2560, 1, 0, None) == -1
+    assert lib.fnx_weighted_reduce(None, None, None, None, 1, 10, 2560, 2560, 1, 1, None) == -1   # order != 0
+    assert lib.fnx_weighted_reduce(None, None, None, None, 1, 10, 2560, 2560, 2, 0, None) == -1   # mode 2 w/o inverse
+    assert lib.fnx_weighted_reduce(None, None, None, None, 1, 65, 2560, 2560, 1, 0, None) == -1
+    assert lib.fnx_gather_pair(None, None, None, None, None, 0, 1, 1280, None) == -1
+    assert lib.fnx_gather_pair(None, None, None, None, None, 16, 1, 1281, None) == -1
+    assert lib.fnx_router_topk(None, 512, None, None, None, None, 4, 512, 33, None) == -1
+    assert lib.fnx_router_topk(None, 100, None, None, None, None, 4, 512, 10, None) == -1
+    assert lib.fnx_moe_permute(None, None, None, None, None, 10, 5000, None, 0, None) == -1
+    assert lib.fnx_moe_permute(None, None, None, None, None, 10, 8, None, 0, None) == -5
+    # grouped GEMM shape rules: K % 64, gs % 64, Nw % 128
+    assert lib.fnx_moe_grouped_w4(None, 2048, None, 1, None, None, None, None, 1024, 8, 64, 100, 1024, 128, 0, None) == -1
+    assert lib.fnx_moe_grouped_w4(None, 2048, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1000, 128, 0, None) == -2
+    assert lib.fnx_moe_grouped_w4(None, 2048, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1024, 32, 0, None) == -2
+    assert lib.fnx_moe_grouped_w4(None, 2048, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1024, 128, 3, None) == -1
+    assert lib.fnx_w4gemv_launch(None, None, None, None, None, None, None, 1024, 100, 10, 20, 2, None) == -1
+    assert lib.fnx_w4gemv_launch(None, None, None, None, None, None, None, 1024, 2048, 10, 20, 3, None) == -1
+    assert lib.fnx_moe_decode_w4(*([None] * 14), 17, 2048, 512, 512, 10, 128, None, 0, None) == -1
+    assert lib.fnx_moe_decode_w4(*([None] * 14), 1, 2048, 512, 512, 10, 128, None, 0, None) == -5
+
+
+def test_workspace_sizes(lib):
+    assert lib.fnx_moe_permute_workspace(40960, 512) == 40 * 512 * 4
+    assert lib.fnx_moe_decode_workspace(0, 2048, 512, 512, 10) == 0
+    n1 = lib.fnx_moe_decode_workspace(1, 2048, 512, 512, 10)
+    n16 = lib.fnx_moe_decode_workspace(16, 2048, 512, 512, 10)
+    assert 0 < n1 < n16 < 64 << 20
+
+
+def test_python_wrappers_return_none_for_unsupported():
+    import torch
+    from fnx import expert_gather, moe_epilogue, post_ops, weighted_reduce
+    v = torch.zeros(2, 10, 64, dtype=torch.bfloat16)
+    assert weighted_reduce.reduce(v, torch.zeros(2, 10, dtype=torch.float32)) is None      # weights dtype
+    assert weighted_reduce.reduce(v.view(20, 64), torch.zeros(2, 10, dtype=torch.bfloat16)) is None   # CPU tensors
+    assert weighted_reduce.reduce(v, torch.zeros(2, 3, 64, dtype=torch.bfloat16), mean=True) is None
+    assert post_ops.moe_merge(torch.zeros(1, 8, dtype=torch.bfloat16), torch.zeros(1, 8, dtype=torch.bfloat16),
+                              torch.zeros(1, dtype=torch.bfloat16)) is None
+    assert moe_epilogue.merge(torch.zeros(10, 640, dtype=torch.bfloat16), torch.zeros(1, 10, dtype=torch.bfloat16),
+                              torch.zeros(1, 64, dtype=torch.bfloat16), torch.zeros(1, dtype=torch.bfloat16)) is None
+
+    class P:
+        expert_major = False
+        _scales = None
+    assert expert_gather.gather(P(), torch.zeros(10, dtype=torch.int64)) is None
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    from fnx import _lib
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setenv("FNX_B200_SO", str(tmp_path / "missing.so"))
+    with pytest.raises(OSError):
+        _lib.lib()

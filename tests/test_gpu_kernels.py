@@ -1,0 +1,158 @@
+"""GPU parity of the byte/rounding-exact kernels against the oracle and the reference
+goldens, called through the C ABI (drop-in modules)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+BF16 = torch.bfloat16
+DEV = "cuda"
+
+
+def bits_equal(a, b):
+    return a.shape == b.shape and torch.equal(a.cpu().view(torch.int16), b.cpu().view(torch.int16))
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    from fnx import _lib
+    _lib.lib()
+    _lib.device_errors()
+    yield
+    assert _lib.device_errors() == 0
+
+
+def test_weighted_reduce_goldens(golden):
+    from fnx.weighted_reduce import reduce
+    cases = golden("reduce_cases")
+    c = cases["adversarial"]
+    got = reduce(c["values"].to(DEV).view(-1, c["values"].shape[-1]), c["weights"].to(DEV))
+    assert bits_equal(got, c["expected"])
+    for B in (1, 3, 9):
+        c = cases[f"inverse{B}"]
+        got = reduce(c["values"].to(DEV), c["weights"].to(DEV), inverse=c["inverse"].to(DEV))
+        assert bits_equal(got, c["expected"])
+    c = cases["mean4"]
+    got = reduce(c["values"].to(DEV), c["weights"].to(DEV), mean=True)
+    assert bits_equal(got, c["expected"])
+
+
+@pytest.mark.parametrize("B,k,H", [(1, 10, 2560), (128, 10, 2048), (513, 8, 2048), (4096, 10, 2048), (7, 3, 100)])
+def test_weighted_reduce_random(B, k, H):
+    from fnx.weighted_reduce import reduce
+    g = torch.Generator().manual_seed(B * 131 + k)
+    v = (torch.randn(B * k, H, generator=g) * 10).to(BF16)
+    w = torch.rand(B, k, generator=g).to(BF16)
+    inv = torch.randperm(B * k, generator=g)
+    got = reduce(v.to(DEV), w.to(DEV), inverse=inv.to(DEV))
+    assert bits_equal(got, O.weighted_reduce(v, w, inverse=inv))
+    got1 = reduce(v.to(DEV), w.to(DEV))
+    assert bits_equal(got1, O.weighted_reduce(v, w))
+
+
+def test_epilogue_and_merge(golden):
+    from fnx import moe_epilogue, post_ops
+    c = golden("reduce_cases")["epilogue"]
+    got = moe_epilogue.merge(c["cartesian"].to(DEV), c["weights"].to(DEV), c["shared"].to(DEV), c["gate"].to(DEV))
+    assert bits_equal(got, c["expected"])
+    g = torch.Generator().manual_seed(141)
+    for i in range(16):
+        B, W = (1, 2560) if i % 2 else (5, 2048)
+        e = (torch.randn(B, W, generator=g) * (0.01 if i % 4 else 10)).to(BF16)
+        s = (torch.randn(B, W, generator=g) * 0.1).to(BF16)
+        gt = (torch.randn(B, 1, generator=g) * 8).to(BF16)
+        got = post_ops.moe_merge(e.to(DEV), s.to(DEV), gt.to(DEV))
+        assert bits_equal(got, O.moe_merge(e, s, gt))
+
+
+def test_gather_pair():
+    from fnx import engine, expert_gather
+    from fnx import _lib
+    g = torch.Generator().manual_seed(138)
+    E, K, N, G = 512, 256, 1024, 2
+    w = torch.randint(-2 ** 31, 2 ** 31 - 1, (E, K, N // 8), generator=g, dtype=torch.int64).to(torch.int32)
+    s = (torch.randn(E, G, N, generator=g) * .01).to(BF16)
+    proj = engine.ExpW4.from_scales(w.to(DEV), s.to(DEV), K // G)
+    for step in range(8):
+        ids = torch.randperm(E, generator=g)[:10] if step % 4 else torch.tensor([0, 511, 0, 123, 12, 510, 50, 100, 300, 399])
+        ow, os_ = expert_gather.gather(proj, ids.to(DEV))
+        rw, rs = O.gather_pair(w, s, ids)
+        assert torch.equal(ow.cpu(), rw) and bits_equal(os_, rs)
+    # the reference-signature export (10 slots, no range check)
+    ids = torch.tensor([3, 17, 61, 200, 255, 256, 400, 401, 510, 511], device=DEV)
+    ow = torch.empty(K, 10 * N // 8, dtype=torch.int32, device=DEV)
+    os_ = torch.empty(G, 10 * N, dtype=BF16, device=DEV)
+    rc = _lib.lib().fnx_gather_pair(proj.w4.data_ptr(), proj._scales.data_ptr(), ids.data_ptr(), ow.data_ptr(),
+                                    os_.data_ptr(), K, G, N, _lib.stream(ow.device))
+    assert rc == 0
+    rw, rs = O.gather_pair(w, s, ids.cpu())
+    assert torch.equal(ow.cpu(), rw) and bits_equal(os_, rs)
+
+
+@pytest.mark.parametrize("T,E,k", [(64, 64, 8), (4096, 512, 10), (3, 16, 4), (100, 1000, 32)])
+def test_router_topk_and_permute(T, E, k):
+    from fnx import _lib
+    g = torch.Generator().manual_seed(T + E)
+    logits = torch.randn(T, E, generator=g).to(BF16)
+    dl = logits.to(DEV)
+    w = torch.empty(T, k, dtype=BF16, device=DEV)
+    idx = torch.empty(T, k, dtype=torch.int64, device=DEV)
+    wf = torch.empty(T, k, dtype=torch.float32, device=DEV)
+    rc = _lib.lib().fnx_router_topk(dl.data_ptr(), E, None, w.data_ptr(), idx.data_ptr(), wf.data_ptr(), T, E, k,
+                                    _lib.stream(dl.device))
+    assert rc == 0
+    rw, ridx, probs = O.route(logits, k)
+    assert torch.equal(idx.cpu(), ridx), "routing ids must be bit-exact given the logits"
+    ulp = O.bf16_ulp_diff(w.cpu(), rw)
+    assert int(ulp.max()) <= 1 and float((ulp == 0).float().mean()) > 0.99
+    assert torch.equal(wf.cpu(), w.cpu().float())
+    # permutation
+    from fnx.engine import MoELayer
+    lay = MoELayer.__new__(MoELayer)
+    lay.E = E
+    order, inverse, ends = lay.permute(idx)
+    ro, _, rends, rinv = O.permute(idx.cpu(), E)
+    assert torch.equal(order.cpu(), ro) and torch.equal(ends.cpu(), rends) and torch.equal(inverse.cpu(), rinv)
+    assert O.is_within_group_permutation(order.cpu(), torch.argsort(idx.cpu().reshape(-1).float()), idx.cpu().reshape(-1))
+
+
+def test_permute_edge_cases():
+    from fnx.engine import MoELayer
+    lay = MoELayer.__new__(MoELayer)
+    for E, ids in ((8, torch.zeros(37, dtype=torch.int64)), (8, torch.full((5,), 7, dtype=torch.int64)),
+                   (512, torch.arange(2048 + 17) % 512), (4, torch.tensor([3, 0, 3, 0, 1]))):
+        lay.E = E
+        order, inverse, ends = lay.permute(ids.to(DEV))
+        ro, _, rends, rinv = O.permute(ids, E)
+        assert torch.equal(order.cpu(), ro) and torch.equal(ends.cpu(), rends) and torch.equal(inverse.cpu(), rinv)
+
+
+def test_w4gemv_goldens(golden):
+    from fnx.w4gemv_op import W4GemvOp
+    gd = golden("w4gemv")
+    op = W4GemvOp()
+    p4, N, K = gd["p4"].numpy(), gd["N"], gd["K"]
+    s4t = op.prepare_layer(gd["s4"].numpy())
+    x = gd["x"].numpy()
+    for lay, p in ((1, p4), (2, op.to_v2_layout(p4, N, K))):
+        pd = torch.from_numpy(np.ascontiguousarray(p)).to(DEV)
+        y = op.run(pd, s4t, x, x.shape[0], N, K, expert_ids=gd["perm"].numpy(), lay=lay).cpu().numpy()
+        assert np.abs(y - gd["y_perm"].numpy()).max() < 1e-4
+    assert np.array_equal(op.to_v2_layout(p4, N, K), gd["v2"].numpy())
+    # moe_forward and run_layers
+    ids = np.array([2, 0, 1], dtype=np.int32)
+    wts = np.array([0.5, 0.25, 0.125], dtype=np.float32)
+    pd = torch.from_numpy(np.ascontiguousarray(p4)).to(DEV)
+    got = op.moe_forward(pd, s4t, x[0], ids, wts, N, K).cpu().numpy()
+    ref = (O.w4gemv(p4, np.ascontiguousarray(np.transpose(gd["s4"].numpy(), (0, 2, 1))), np.repeat(x[:1], 3, 0),
+                    ids, N, K, 1) * wts[:, None]).sum(0)
+    assert np.abs(got - ref).max() < 1e-4
+    v2 = torch.from_numpy(op.to_v2_layout(p4, N, K)).to(DEV)
+    xs = [torch.from_numpy(x).to(DEV) for _ in range(2)]
+    ys = [torch.empty(3, N, device=DEV) for _ in range(2)]
+    op.run_layers([v2, v2], [s4t, s4t], xs, ys, N, K, 3, lay=2)
+    ref = O.w4gemv(gd["v2"].numpy(), np.ascontiguousarray(np.transpose(gd["s4"].numpy(), (0, 2, 1))), x,
+                   np.arange(3), N, K, 2)
+    assert np.abs(ys[1].cpu().numpy() - ref).max() < 1e-4

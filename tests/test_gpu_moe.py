@@ -1,0 +1,185 @@
+"""GPU parity of the tensor-core grouped GEMM, the decode kernels and the whole MoE layer
+against the CPU oracle (which is pinned to the reference's own code)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from fnx import synth
+
+pytestmark = pytest.mark.gpu
+BF16 = torch.bfloat16
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _errors():
+    from fnx import _lib
+    _lib.lib()
+    _lib.device_errors()
+    yield
+    assert _lib.device_errors() == 0
+
+
+def _w4(E, K, N, gs, seed):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    w = torch.from_numpy(rng.integers(0, 2 ** 32, size=(E, K, N // 8), dtype=np.uint32).view(np.int32))
+    s = torch.from_numpy(np.abs(rng.standard_normal((E, K // gs, N), dtype=np.float32)) * 0.02).to(BF16)
+    return w, s
+
+
+@pytest.mark.parametrize("E,counts,K,N,gs,epi", [
+    (1, [16], 64, 128, 64, 0),
+    (1, [1], 128, 128, 64, 0),
+    (3, [5, 0, 37], 256, 256, 128, 0),
+    (4, [129, 1, 0, 300], 512, 128, 64, 0),
+    (6, [7, 80, 0, 200, 16, 1], 256, 256, 128, 1),
+    (2, [33, 90], 256, 256, 128, 2),
+])
+def test_grouped_w4(E, counts, K, N, gs, epi):
+    from fnx.engine import _grouped_w4
+    w, s = _w4(E, K, N, gs, seed=E * 7 + K)
+    M = sum(counts)
+    g = torch.Generator().manual_seed(M)
+    src = torch.randn(M + 5, K, generator=g).to(BF16)
+    perm = torch.randperm(M, generator=g)
+    ends = torch.tensor(np.cumsum(counts), dtype=torch.int64)
+    nout = N if epi == 0 else N // 2
+    out = torch.full((M, nout), float("nan"), dtype=BF16, device=DEV)
+    _grouped_w4(src.to(DEV), w.to(DEV), s.to(DEV), ends.to(DEV), out, E=E, M=M, K=K, Nw=N, gs=gs, epilogue=epi,
+                row_index=(perm * 2).to(DEV), index_div=2)
+    rows = src[perm]
+    ref = O.grouped_matmul(rows, ends, lambda e: O.deq_w4(O.unpack_int4pack(w[e]), s[e], gs))
+    if epi == 1:
+        ref = O.swiglu_fp32(ref, N // 2)
+    elif epi == 2:
+        ref = O.swiglu_shared(ref, N // 2)
+    rep = O.tolerance_report(out.cpu(), ref)
+    assert O.within_tolerance(out.cpu(), ref), rep
+    assert rep["exact_fraction"] > 0.9, rep
+
+
+def test_bf16_and_w8_gemm(golden):
+    from fnx import _lib
+    from fnx.engine import DenseW8
+    g = torch.Generator().manual_seed(5)
+    M, K, N = 77, 256, 384
+    x = torch.randn(M, K, generator=g).to(BF16)
+    wt = (torch.randn(N, K, generator=g) * 0.05).to(BF16)
+    y = torch.empty(M, N, dtype=BF16, device=DEV)
+    xd, wd = x.to(DEV), wt.to(DEV)
+    rc = _lib.lib().fnx_bf16_gemm_nt(xd.data_ptr(), K, wd.data_ptr(), y.data_ptr(), N, M, K, N, _lib.stream(y.device))
+    assert rc == 0
+    ref = O.w4a16_matmul(x, wt.t())
+    assert O.within_tolerance(y.cpu(), ref), O.tolerance_report(y.cpu(), ref)
+    # DenseW8 on the reference's merged qkv+z layout (golden from QW's torch dequant path)
+    gd = golden("dense_w8")
+    rng = np.random.Generator(np.random.PCG64(gd["seed"]))
+    parts = []
+    for n in gd["Ns"]:
+        q = torch.from_numpy(rng.integers(-127, 128, size=(n, gd["K"]), dtype=np.int8))
+        sc = torch.from_numpy(np.abs(rng.standard_normal((n, 1), dtype=np.float32)) * 0.01).to(BF16)
+        parts.append(DenseW8(q.to(DEV), sc.to(DEV)))
+    merged = DenseW8.merge(parts)
+    for m in (1, 16):
+        got = merged(gd["x"][:m].to(DEV)).cpu()
+        rep = O.tolerance_report(got, gd["qw_out"][:m])
+        assert O.within_tolerance(got, gd["qw_out"][:m]), rep
+
+
+def _layer(shape, seed):
+    from fnx.engine import MoELayer
+    t = synth.make_layer(shape, seed=seed)
+    return t, O.Layer(t, shape.gs), MoELayer.from_synth({k: v.to(DEV) for k, v in t.items()}, shape)
+
+
+def _check_layer(x, L, shape, out, w, idx, logits=None):
+    sh, gate, rlogits = O.shared_and_logits(x, L)
+    if logits is not None:
+        rep = O.tolerance_report(logits.float().cpu(), rlogits.float())
+        assert rep["rel_l2"] < 5e-3, rep
+        # routing given the GPU logits is bit-exact
+        rw, ridx, _ = O.route(logits.cpu(), shape.k)
+        assert torch.equal(ridx, idx.cpu())
+        assert int(O.bf16_ulp_diff(rw, w.cpu()).max()) <= 1
+    ref = O.moe_forward(x, L, shape.k, routing=(w.cpu(), idx.cpu()))
+    rep = O.tolerance_report(out.cpu(), ref)
+    assert O.within_tolerance(out.cpu(), ref), rep
+    return rep
+
+
+PIN = synth.MoEShape(H=256, I=128, E=16, k=4, gs=128)
+
+
+@pytest.mark.parametrize("shape,T,seed", [(PIN, 48, 11), (synth.CFG1, 64, 0), (synth.CFG2, 256, 2),
+                                          (synth.MoEShape(H=512, I=256, E=64, k=6, gs=64), 333, 4)])
+def test_prefill_layer(shape, T, seed):
+    t, L, layer = _layer(shape, seed)
+    x = synth.make_tokens(T, shape.H, seed=seed + 1)
+    out, d = layer.prefill(x.to(DEV), details=True)
+    _check_layer(x, L, shape, out, d["w"], d["idx"], d["logits"])
+    # the intermediate contract: act / yd rows in expert-major order
+    ref_out, rd = O.moe_forward(x, L, shape.k, routing=(d["w"].cpu(), d["idx"].cpu()), details=True)
+    assert torch.equal(d["order"].cpu(), rd["order"]) and torch.equal(d["ends"].cpu(), rd["ends"])
+    assert O.within_tolerance(d["act"].cpu(), rd["act"]), O.tolerance_report(d["act"].cpu(), rd["act"])
+    assert O.within_tolerance(d["yd"].cpu(), rd["yd"]), O.tolerance_report(d["yd"].cpu(), rd["yd"])
+
+
+@pytest.mark.parametrize("shape,M,seed", [(PIN, 1, 11), (synth.CFG2, 1, 2), (synth.CFG2, 4, 3), (synth.CFG2, 16, 5),
+                                          (synth.MoEShape(H=512, I=256, E=64, k=6, gs=64), 3, 4)])
+def test_decode_layer(shape, M, seed):
+    t, L, layer = _layer(shape, seed)
+    x = synth.make_tokens(M, shape.H, seed=seed + 7)
+    xd = x.to(DEV)
+    out, w, idx = layer.decode(xd)
+    logits = layer.logits(xd)[:, :shape.E]
+    _check_layer(x, L, shape, out, w, idx, logits)
+    # repeated calls reuse the workspace: identical bits
+    out2, _, _ = layer.decode(xd)
+    assert torch.equal(out.view(torch.int16), out2.view(torch.int16))
+
+
+def test_decode_matches_reference_golden(golden):
+    """The production decode branch golden at cfg-2 shapes (reference routing)."""
+    g = golden("cfg2_decode")
+    H, I, E, k, gs = g["shape"]
+    shape = synth.MoEShape(H, I, E, k, gs)
+    t, L, layer = _layer(shape, g["seed"])
+    x = synth.make_tokens(1, H, seed=g["xseed"])
+    out, w, idx = layer.decode(x.to(DEV))
+    wr = (g["probs_topk"] / g["probs_topk"].sum(-1, keepdim=True)).to(BF16)
+    probs = torch.softmax(g["logits"].float(), -1)
+    assert bool(O.same_topk(idx.cpu(), w.cpu(), g["idx"], wr, probs, k).all())
+    if sorted(idx[0].tolist()) == sorted(g["idx"][0].tolist()):
+        ref = g["out"]
+    else:
+        # a tie at the k-th probability: the reference's topk picked another tied expert,
+        # so the output is checked against the reference formulation with this routing
+        assert bool(O.boundary_tie(probs, k)[0])
+        ref = O.moe_forward(x, L, k, routing=(w.cpu(), idx.cpu()))
+    rep = O.tolerance_report(out.cpu(), ref)
+    assert O.within_tolerance(out.cpu(), ref), rep
+
+
+def test_expw4_apply_paths():
+    from fnx.engine import ExpW4
+    E, K, N, gs = 32, 256, 256, 128
+    w, s = _w4(E, K, N, gs, seed=3)
+    ex = ExpW4.from_scales(w.to(DEV), s.to(DEV), gs)
+    ids = torch.tensor([3, 17, 3, 31, 0], dtype=torch.int64)
+    x = torch.randn(1, K).to(BF16)
+    y = ex.apply(x.to(DEV), ids.to(DEV)).cpu()
+    ref = torch.cat([O.w4a16_matmul(x, O.deq_w4(O.unpack_int4pack(w[e]), s[e], gs)) for e in ids.tolist()], 1)
+    assert O.within_tolerance(y, ref)
+    xa = torch.randn(5, K).to(BF16)
+    yd = ex.apply_diag(xa.to(DEV), ids.to(DEV)).cpu()
+    refd = torch.cat([O.w4a16_matmul(xa[j:j + 1], O.deq_w4(O.unpack_int4pack(w[e]), s[e], gs))
+                      for j, e in enumerate(ids.tolist())], 0)
+    assert O.within_tolerance(yd, refd)
+    # K-major artifact constructor (s8t/base): real scale = bf16(bf16(s8t) * base)
+    g = torch.Generator().manual_seed(9)
+    s8t = torch.randint(-127, 128, (K // gs, E, N), generator=g, dtype=torch.int8)
+    base = (torch.rand(E, N, generator=g) * 1e-3).to(BF16)
+    ex2 = ExpW4(w.permute(1, 0, 2).contiguous().to(DEV), s8t.to(DEV), base.to(DEV), gs, expert_major=False)
+    assert torch.equal(ex2.w4.cpu(), w)
+    assert torch.equal(ex2._scales.cpu().view(torch.int16), O.cached_scales(s8t, base).view(torch.int16))
