@@ -117,6 +117,18 @@ int fnx_moe_decode_w4(const void* x, const void* router, const void* gu_w4, cons
                       const void* sh_dn_s, const void* bias, void* out, void* w_out, void* idx_out, int M, int H, int I,
                       int E, int k, int gs, void* workspace, size_t ws_bytes, void* stream);
 
+/* fnx_moe_decode_w4 for callers that cannot allocate device memory (no counterpart in the
+ * reference): a plugin host or FFI binding that hands over only input and output buffers,
+ * or a serving process that forbids device allocation after start-up.  The scratch is a
+ * 4 MiB array compiled into the library (held by every GPU that loads it until exit); shapes
+ * needing more than that (see fnx_moe_decode_workspace) return -5.  The first call on a
+ * device looks the array's address up, so make it before any stream capture.  Every call on
+ * a device shares the array, so calls that overlap on the GPU race.  Allocates nothing. */
+int fnx_moe_decode_w4_noalloc(const void* x, const void* router, const void* gu_w4, const void* gu_s,
+                              const void* dn_w4, const void* dn_s, const void* sh_gu_w4, const void* sh_gu_s,
+                              const void* sh_dn_w4, const void* sh_dn_s, const void* bias, void* out, void* w_out,
+                              void* idx_out, int M, int H, int I, int E, int k, int gs, void* stream);
+
 /* ---- library ---- */
 const char* fnx_b200_version(void);
 /* device error bits since the last clear: 1 bounded wait expired, 2 expert id out of range,

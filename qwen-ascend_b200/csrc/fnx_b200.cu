@@ -446,3 +446,62 @@ FNX_API int fnx_w4gemv_launch_layers(void** p4, void** s4t, void** x, void** y, 
     else w4gemv_layers_kernel<2><<<grid, 256, 0, (cudaStream_t)stream>>>(Ls, N, K, nExp);
     return launch_rc();
 }
+
+// ======================================================================== decode layer, no allocation
+// Some callers cannot allocate device memory: a plugin host or FFI binding that hands the
+// library only its input and output buffers (all device memory belongs to the host's own
+// pool and no allocator is exposed), or a serving process that forbids device allocation
+// once it has started.  For them the decode layer runs on a fixed scratch area compiled
+// into the library: FNX_NOALLOC_SCRATCH_BYTES of device memory that every GPU which loads
+// the library keeps until the process exits.
+#define FNX_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+static __device__ __align__(256) unsigned char g_fnx_noalloc_scratch[FNX_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+// Device address of the scratch array for the current device.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per device (with
+// that device current) and cached.
+void* noalloc_scratch(int* rc) {
+    static void* addr[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        *rc = FNX_ELAUNCH;
+        return nullptr;
+    }
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_fnx_noalloc_scratch) != cudaSuccess || p == nullptr) {
+            *rc = FNX_ELAUNCH;
+            return nullptr;
+        }
+        addr[dev] = p;
+    }
+    return addr[dev];
+}
+}  // namespace
+
+// fnx_moe_decode_w4 without a caller-provided workspace: the scratch is the library's
+// static array.  The first call on each device looks its address up, so make that first
+// call before any stream capture.  Shapes whose workspace (fnx_moe_decode_workspace)
+// exceeds FNX_NOALLOC_SCRATCH_BYTES are rejected with FNX_EWORKSPACE.  The array is shared
+// by every call on a device and keeps the last call's contents; the tickets that must start
+// at zero are cleared at the start of each call.  Calls that overlap on the GPU (other
+// streams, other threads) race on the array.
+FNX_API int fnx_moe_decode_w4_noalloc(const void* x, const void* router, const void* gu_w4, const void* gu_s,
+                                      const void* dn_w4, const void* dn_s, const void* sh_gu_w4, const void* sh_gu_s,
+                                      const void* sh_dn_w4, const void* sh_dn_s, const void* bias, void* out,
+                                      void* w_out, void* idx_out, int M, int H, int I, int E, int k, int gs,
+                                      void* stream) {
+    if (M < 1 || M > DEC_MAX_M || E < 1 || E > ROUTE_MAX_E || k < 1 || k > 32 || k > E) return FNX_EARG;
+    if (H % 256 || I % DEC_FB || H % DEC_FB || gs < 8 || gs % 8 || H % gs || I % gs) return FNX_ESHAPE;
+    const DecodeLayout L = decode_layout(M, H, I, E, k);
+    if (L.total > FNX_NOALLOC_SCRATCH_BYTES) return FNX_EWORKSPACE;
+    int rc = FNX_OK;
+    uint8_t* ws = (uint8_t*)noalloc_scratch(&rc);
+    if (!ws) return rc;
+    if (cudaMemsetAsync(ws + L.counters, 0, L.total - L.counters, (cudaStream_t)stream) != cudaSuccess)
+        return FNX_ELAUNCH;
+    return fnx_moe_decode_w4(x, router, gu_w4, gu_s, dn_w4, dn_s, sh_gu_w4, sh_gu_s, sh_dn_w4, sh_dn_s, bias, out,
+                             w_out, idx_out, M, H, I, E, k, gs, ws, FNX_NOALLOC_SCRATCH_BYTES, stream);
+}
