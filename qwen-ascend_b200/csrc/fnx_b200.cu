@@ -146,13 +146,7 @@ int gemm_launch_t(GemmParams& p, cudaStream_t st) {
         configured = true;
     }
     int rc = FNX_OK;
-    if (MODE == GEMM_W4) {
-        rc = make_map_2d(&p.tmap_a, p.w, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, (unsigned long long)p.Nw / 8,
-                         (unsigned long long)p.E * p.K, 8, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (!rc)
-            rc = make_map_2d(&p.tmap_s, p.scales, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (unsigned long long)p.Nw,
-                             (unsigned long long)p.E * (p.K / p.gs), 64, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
-    } else if (MODE == GEMM_BF16) {
+    if (MODE == GEMM_BF16) {
         rc = make_map_2d(&p.tmap_a, p.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (unsigned long long)p.K,
                          (unsigned long long)p.E * p.Nw, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     }
@@ -303,11 +297,13 @@ FNX_API int fnx_moe_permute(void* idx, void* order, void* inverse, void* ends, v
 }
 
 // ======================================================================== grouped GEMMs
-FNX_API int fnx_moe_grouped_w4(const void* act, long long ld_act, const void* row_index, int index_div, const void* w4,
-                               const void* scales, const void* ends, void* out, long long ld_out, int E, int M, int K,
-                               int Nw, int gs, int epilogue, void* stream) {
+FNX_API int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_rows, const void* row_index,
+                               int index_div, const void* w4, const void* scales, const void* ends, void* out,
+                               long long ld_out, int E, int M, int K, int Nw, int gs, int epilogue, void* stream) {
     GemmParams p{};
     p.act = (const bf16*)act; p.ld_act = ld_act; p.row_index = (const int64_t*)row_index; p.index_div = index_div;
+    p.act_rows = act_rows;
+    if (act_rows < 0 || (!row_index && act_rows < M)) return FNX_EARG;
     p.w = w4; p.scales = (const bf16*)scales; p.ends = (const int64_t*)ends; p.out = (bf16*)out; p.ld_out = ld_out;
     p.E = E; p.M = M; p.K = K; p.Nw = Nw; p.gs = gs;
     if (epilogue < 0 || epilogue > 2) return FNX_EARG;
@@ -322,6 +318,7 @@ FNX_API int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void*
                            void* stream) {
     GemmParams p{};
     p.act = (const bf16*)x; p.ld_act = K; p.w = w8t; p.scales = (const bf16*)sc; p.out = (bf16*)y; p.ld_out = N;
+    p.act_rows = M;
     p.E = 1; p.M = M; p.K = K; p.Nw = N; p.gs = G > 0 ? K / G : 0; p.m_tiles = N / G_BM;
     if (G < 1 || K % G) return FNX_EARG;
     const int rc = gemm_check(GEMM_W8, EPI_PLAIN, p);
@@ -335,11 +332,26 @@ FNX_API int fnx_bf16_gemm_nt(const void* x, long long ld_x, const void* w, void*
                              void* stream) {
     GemmParams p{};
     p.act = (const bf16*)x; p.ld_act = ld_x; p.w = w; p.out = (bf16*)y; p.ld_out = ld_y;
+    p.act_rows = M;
     p.E = 1; p.M = M; p.K = K; p.Nw = N; p.gs = K; p.m_tiles = N / G_BM;
     const int rc = gemm_check(GEMM_BF16, EPI_PLAIN, p);
     if (rc) return rc;
     if (M == 0) return FNX_OK;
     return gemm_launch(GEMM_BF16, EPI_PLAIN, p, (cudaStream_t)stream);
+}
+
+// ======================================================================== load-time repack
+FNX_API int fnx_repack_w4_tiles(const void* w4, const void* scales, void* tw, void* ts, int E, int K, int Nw, int gs,
+                                int swiglu, void* stream) {
+    if (E < 1 || K < 64 || K % 64 || Nw < 128 || Nw % 128 || gs < 64 || gs % 64 || K % gs || (swiglu != 0 && swiglu != 1))
+        return FNX_EARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    const long long words = (long long)E * K * (Nw / 8);
+    repack_w4_tiles_kernel<<<grid_for(words, 256), 256, 0, st>>>((const uint32_t*)w4, (uint32_t*)tw, E, K, Nw, swiglu);
+    const long long sc = (long long)E * (K / gs) * Nw;
+    repack_scales_tiles_kernel<<<grid_for(sc, 256), 256, 0, st>>>((const bf16*)scales, (bf16*)ts, E, K / gs, Nw,
+                                                                  swiglu);
+    return launch_rc();
 }
 
 // ======================================================================== decode layer
@@ -352,24 +364,26 @@ struct DecodeLayout {
 DecodeLayout decode_layout(int M, int H, int I, int E, int k) {
     DecodeLayout L{};
     L.R = E + 1;
-    const int nfb = I / DEC_FB;
-    // K splits sized so each grid holds >= 2 blocks per SM
+    const int mt = I / 64, kb = H / 64;
+    // K splits (divisors of the k-block count, >= 2 k-blocks each) sized so the shared
+    // gate/up grid has >= 64 blocks and the routed one >= 2 blocks per SM
     L.ks1 = 1;
-    while (L.ks1 < 64 && M * nfb * L.ks1 < 64 && (H / (L.ks1 * 2)) % 128 == 0) L.ks1 *= 2;
+    while (L.ks1 < 64 && M * mt * L.ks1 < 64 && kb % (L.ks1 * 2) == 0 && kb / (L.ks1 * 2) >= 2) L.ks1 *= 2;
     L.ks2 = 1;
-    while (L.ks2 < 64 && M * k * nfb * L.ks2 < 2 * num_sms() && (H / (L.ks2 * 2)) % 128 == 0) L.ks2 *= 2;
+    while (L.ks2 < 64 && M * k * mt * L.ks2 < 2 * num_sms() && kb % (L.ks2 * 2) == 0 && kb / (L.ks2 * 2) >= 2)
+        L.ks2 *= 2;
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
     L.logits = take((size_t)M * L.R * 2);
     L.wf = take((size_t)M * k * 4);
     L.idx = take((size_t)M * k * 4);
-    L.part = take((size_t)M * nfb * L.ks1 * 2 * DEC_FB * 4);
-    L.part2 = take((size_t)M * k * nfb * L.ks2 * 2 * DEC_FB * 4);
+    L.part = take((size_t)M * mt * L.ks1 * 128 * 4);
+    L.part2 = take((size_t)M * k * mt * L.ks2 * 128 * 4);
     L.act = take((size_t)M * k * I * 2);
     L.act_sh = take((size_t)M * I * 2);
     L.yd = take((size_t)M * k * H * 2);
     L.sh = take((size_t)M * H * 2);
-    L.counters = take((size_t)(1 + M * nfb + M * k * nfb + H / DEC_FB) * 4);
+    L.counters = take((size_t)(1 + M * mt + M * k * mt + H / 128) * 4);
     L.total = off;
     return L;
 }
@@ -380,15 +394,17 @@ FNX_API size_t fnx_moe_decode_workspace(int M, int H, int I, int E, int k) {
     return decode_layout(M, H, I, E, k).total;
 }
 
-// router: bf16 [E+1, H] (rows 0..E-1 router, row E shared-expert gate); all other weights
-// in the int4pack artifact layout.  workspace must be zero-filled before its first use;
-// every completed call leaves its tickets at zero again.
+// router: bf16 [E+1, H] (rows 0..E-1 router, row E shared-expert gate); expert weights in
+// the tile-major layout of fnx_repack_w4_tiles (gate/up in SwiGLU row order, down plain).
+// workspace must be zero-filled before its first use; every completed call leaves its
+// tickets at zero again.
 FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu_w4, const void* gu_s, const void* dn_w4,
                               const void* dn_s, const void* sh_gu_w4, const void* sh_gu_s, const void* sh_dn_w4,
                               const void* sh_dn_s, const void* bias, void* out, void* w_out, void* idx_out, int M,
                               int H, int I, int E, int k, int gs, void* workspace, size_t ws_bytes, void* stream) {
     if (M < 1 || M > DEC_MAX_M || E < 1 || E > ROUTE_MAX_E || k < 1 || k > 32 || k > E) return FNX_EARG;
-    if (H % 256 || I % DEC_FB || H % DEC_FB || gs < 8 || gs % 8 || H % gs || I % gs) return FNX_ESHAPE;
+    if (H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K || gs < 64 || gs % 64 || H % gs || I % gs)
+        return FNX_ESHAPE;
     const DecodeLayout L = decode_layout(M, H, I, E, k);
     if (!workspace || ws_bytes < L.total) return FNX_EWORKSPACE;
     if (!aligned16(x) || !aligned16(router) || !aligned16(gu_w4) || !aligned16(dn_w4) || !aligned16(gu_s) ||
@@ -397,9 +413,9 @@ FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu_
     uint8_t* ws = (uint8_t*)workspace;
     DecodeParams p{};
     p.x = (const bf16*)x; p.router = (const bf16*)router;
-    p.gu_w4 = (const int32_t*)gu_w4; p.gu_s = (const bf16*)gu_s; p.dn_w4 = (const int32_t*)dn_w4; p.dn_s = (const bf16*)dn_s;
-    p.sh_gu_w4 = (const int32_t*)sh_gu_w4; p.sh_gu_s = (const bf16*)sh_gu_s;
-    p.sh_dn_w4 = (const int32_t*)sh_dn_w4; p.sh_dn_s = (const bf16*)sh_dn_s;
+    p.gu_tw = (const uint32_t*)gu_w4; p.gu_ts = (const bf16*)gu_s; p.dn_tw = (const uint32_t*)dn_w4; p.dn_ts = (const bf16*)dn_s;
+    p.sh_gu_tw = (const uint32_t*)sh_gu_w4; p.sh_gu_ts = (const bf16*)sh_gu_s;
+    p.sh_dn_tw = (const uint32_t*)sh_dn_w4; p.sh_dn_ts = (const bf16*)sh_dn_s;
     p.out = (bf16*)out; p.w_out = (bf16*)w_out; p.idx_out = (int64_t*)idx_out; p.bias = (const float*)bias;
     p.logits = (bf16*)(ws + L.logits); p.wf = (float*)(ws + L.wf); p.idx = (int32_t*)(ws + L.idx);
     p.part = (float*)(ws + L.part); p.part2 = (float*)(ws + L.part2);
@@ -407,11 +423,11 @@ FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu_
     p.counters = (unsigned*)(ws + L.counters);
     p.M = M; p.H = H; p.I = I; p.E = E; p.k = k; p.gs = gs; p.R = L.R; p.ks1 = L.ks1; p.ks2 = L.ks2;
     cudaStream_t st = (cudaStream_t)stream;
-    const int nfb = I / DEC_FB;
+    const int mt = I / 64;
     const int router_blocks = (L.R + 7) / 8;
-    decode_d1_kernel<<<router_blocks + M * nfb * L.ks1, DEC_THREADS, 0, st>>>(p, router_blocks);
-    decode_d2_kernel<<<M * k * nfb * L.ks2, DEC_THREADS, 0, st>>>(p);
-    decode_d3_kernel<<<(M * k + M) * (H / DEC_FB), DEC_THREADS, 0, st>>>(p);
+    decode_d1_kernel<<<router_blocks + M * mt * L.ks1, DEC_THREADS, 0, st>>>(p, router_blocks);
+    decode_d2_kernel<<<M * k * mt * L.ks2, DEC_THREADS, 0, st>>>(p);
+    decode_d3_kernel<<<(M * k + M) * (H / 128), DEC_THREADS, 0, st>>>(p);
     return launch_rc();
 }
 
@@ -494,7 +510,10 @@ FNX_API int fnx_moe_decode_w4_noalloc(const void* x, const void* router, const v
                                       void* w_out, void* idx_out, int M, int H, int I, int E, int k, int gs,
                                       void* stream) {
     if (M < 1 || M > DEC_MAX_M || E < 1 || E > ROUTE_MAX_E || k < 1 || k > 32 || k > E) return FNX_EARG;
-    if (H % 256 || I % DEC_FB || H % DEC_FB || gs < 8 || gs % 8 || H % gs || I % gs) return FNX_ESHAPE;
+    if (H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K || gs < 64 || gs % 64 || H % gs || I % gs) {
+        const DecodeLayout L0 = decode_layout(M, H, I, E, k);
+        return L0.total > FNX_NOALLOC_SCRATCH_BYTES ? FNX_EWORKSPACE : FNX_ESHAPE;
+    }
     const DecodeLayout L = decode_layout(M, H, I, E, k);
     if (L.total > FNX_NOALLOC_SCRATCH_BYTES) return FNX_EWORKSPACE;
     int rc = FNX_OK;

@@ -180,6 +180,35 @@ FNX_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, in
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
         ::"r"(dst), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y) : "memory");
 }
+// L2 cache policies: stream-once data (weights) should not evict data that is re-read
+// (gathered activations).
+FNX_DEV uint64_t l2_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+FNX_DEV uint64_t l2_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// Linear bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16),
+// completion counted on an mbarrier's transaction bytes.
+FNX_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(dst), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy) : "memory");
+}
+// Prefetch a global range (16-byte aligned, size a multiple of 16) into L2.
+FNX_DEV void l2_prefetch(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+// 16-byte cp.async with zero fill (src_size 0) and an L2 policy.
+FNX_DEV void cp_async_16_hint(uint32_t dst, const void* src, bool valid, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;"
+                 ::"r"(dst), "l"(src), "r"(valid ? 16 : 0), "l"(policy) : "memory");
+}
 FNX_DEV void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }

@@ -30,6 +30,10 @@ __global__ void __launch_bounds__(256) weighted_reduce_kernel(const bf16* __rest
         for (int g = 0; g < groups; ++g) {
             const long long slot = (long long)t * groups + g;
             const long long row = MODE == 2 ? inverse[slot] : slot;
+            if (MODE == 2 && (row < 0 || row >= (long long)batch * groups)) {   // not a permutation entry
+                fnx_flag_error(FNX_DEVERR_BADID);
+                continue;
+            }
             const bf16* src = in + row * row_stride + c;
             if (VEC) {
                 uint4 v = ld_nc_v4(src);
@@ -125,6 +129,10 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const bf16* __restrict
         for (int j = 0; j < k; ++j) {
             const long long slot = (long long)t * k + j;
             const long long row = inverse ? inverse[slot] : slot;
+            if (row < 0 || row >= (long long)T * k) {      // an id outside [0, E) left no row
+                fnx_flag_error(FNX_DEVERR_BADID);
+                continue;
+            }
             const float s = w[slot];
             if (VEC) {
                 const uint4 v = ld_nc_v4(yd + row * H + c);

@@ -13,10 +13,11 @@
 //
 // Warp roles (512 threads):
 //   warps 0, 3    B loaders: gather token rows with cp.async into K-major SW128 tiles
-//                 (alternate 16-byte chunks), keeping B_LAG stages in flight
+//                 (alternate 16-byte chunks); a stage is full when every loader
+//                 thread's copies have landed (cp.async.mbarrier.arrive)
 //   warp 1        TMEM allocator + single-thread MMA issuer (tcgen05.mma kind::f16)
-//   warp 2        TMA producer: W4 -> raw int4 words + scales into an R_STAGES-deep ring;
-//                 BF16 -> the A tiles themselves (128-byte swizzle)
+//   warp 2        TMA producer: W4 -> 4 KB tile-major weight blocks + scales (bulk copies)
+//                 into an R_STAGES-deep ring; BF16 -> the A tiles themselves (128B swizzle)
 //   warps 4-7     epilogue warpgroup: tcgen05.ld -> bf16 / SwiGLU -> global
 //   warps 8-15    A producers (W4/W8), two groups of four warps taking alternate k-blocks:
 //                 int4 / int8 -> bf16(q * s) (exactly rounded) -> SW128 smem
@@ -24,6 +25,7 @@
 // unwind to the final barrier, where the allocating warp frees TMEM.
 #pragma once
 #include "fnx_common.cuh"
+#include "kernels_repack.cuh"
 
 namespace fnx {
 
@@ -33,25 +35,26 @@ enum GemmEpi { EPI_PLAIN = 0, EPI_SWIGLU_F32 = 1, EPI_SWIGLU_BF16 = 2 };
 constexpr int G_BM = 128;          // weight features per tile (UMMA M)
 constexpr int G_BK = 64;           // k per stage (one 128-byte swizzle row of bf16)
 constexpr int G_BN = 128;          // max token rows per tile
-constexpr int G_STAGES = 5;
-constexpr int G_R_STAGES = 8;      // raw int4 ring depth (even: each stage belongs to one producer group)
-constexpr int G_B_LAG = 3;         // cp.async stages the B loader keeps in flight
+constexpr int G_STAGES = 4;
+constexpr int G_R_STAGES = 16;     // raw int4 ring depth (even: each stage belongs to one producer group)
+constexpr int G_PF_AHEAD = 32;     // weight blocks prefetched into L2 ahead of the raw ring
 constexpr int G_THREADS = 512;
 constexpr int G_A_BYTES = G_BM * G_BK * 2;     // 16 KB
 constexpr int G_B_BYTES = G_BN * G_BK * 2;     // 16 KB
-constexpr int G_RAW_W = 2 * 64 * 8 * 4;        // 4 KB: [half][64 k][8 words]
-constexpr int G_RAW_BYTES = G_RAW_W + 2 * 64 * 2;   // + scales [half][64 features]
+constexpr int G_RAW_W = 8 * 128 * 4;           // 4 KB: one tile-major block [8 chunks][128 rows] of words
+constexpr int G_RAW_BYTES = G_RAW_W + 128 * 2;      // + the rows' scales for the block's k group
 constexpr int G_MAX_E = 1024;
 
 struct GemmParams {
-    CUtensorMap tmap_a;         // W4: int32 words [E*K, Nw/8] box {8, 64};  BF16: bf16 [E*Nw, K] box {64, 128}, SW128
-    CUtensorMap tmap_s;         // W4: bf16 scales [E*G, Nw] box {64, 1}
-    const bf16* act;            // token rows bf16 [*, K], row stride ld_act elements
+    CUtensorMap tmap_a;         // BF16: bf16 weights [E*Nw, K], box {64, 128}, 128-byte swizzle
+    const bf16* act;            // token rows bf16 [act_rows, K], row stride ld_act elements
     long long ld_act;
+    long long act_rows;         // gathered row indices outside [0, act_rows) read zeros (and are flagged)
     const int64_t* row_index;   // null: row r of the problem reads act row r; else row_index[r] / index_div
     int index_div;
-    const void* w;              // W4: int32 [E, K, Nw/8]; W8: int8 [E, K, Nw]; BF16: bf16 [E, Nw, K]
-    const bf16* scales;         // W4/W8: bf16 [E, K/gs, Nw]
+    const void* w;              // W4: tile-major int32 [E, MT, K/64, 8, 128] (kernels_repack.cuh);
+                                // W8: int8 [E, K, Nw]; BF16: bf16 [E, Nw, K]
+    const bf16* scales;         // W4: tile-major bf16 [E, MT, K/gs, 128]; W8: bf16 [E, K/gs, Nw]
     const int64_t* ends;        // [E] cumulative row counts; null: one group of M rows
     bf16* out;                  // bf16 [M, ld_out]
     long long ld_out;
@@ -85,8 +88,8 @@ FNX_DEV bool decode_tile(const GemmSmem& S, const GemmParams& p, int tile, TileI
     const int chunk = local / p.m_tiles;
     ti.e = e;
     ti.m = local % p.m_tiles;
-    const long long begin = p.ends ? (e ? p.ends[e - 1] : 0) : 0;
-    const long long end = p.ends ? p.ends[e] : p.M;
+    const long long begin = min((long long)p.M, (long long)(p.ends ? (e ? p.ends[e - 1] : 0) : 0));
+    const long long end = min((long long)p.M, (long long)(p.ends ? p.ends[e] : p.M));
     ti.row0 = (int)begin + chunk * G_BN;
     ti.nrows = (int)min((long long)G_BN, end - ti.row0);
     return true;
@@ -119,49 +122,23 @@ FNX_DEV int lane_feature(int r) {
 }
 
 // ------------------------------------------------------------------ A producers
-// W4: thread (h, kq, j) of a 128-thread group dequantises the 8x8 block of k rows
-// 8kq .. 8kq+7 of the stage and the 8 features of word column j in half h, reading the
-// raw words and scales the TMA warp staged in shared memory.
-template <int EPI>
-FNX_DEV void produce_a_w4(const uint8_t* raw, uint8_t* a_tile, int t) {
-    const int j = t & 7, kq = (t >> 3) & 7, h = t >> 6;
-    const uint32_t* rw = reinterpret_cast<const uint32_t*>(raw) + h * 512 + kq * 64 + j;
+// W4: thread r of a 128-thread group dequantises tile row r of the stage: eight words
+// (8 consecutive k each) from the tile-major block the TMA warp copied, scaled by the
+// row's group scale, into the eight 16-byte chunks of A row r.  Reads are consecutive
+// words across the warp and the swizzled stores hit eight distinct chunks per 8 rows:
+// both conflict-free.
+FNX_DEV void produce_a_w4(const uint8_t* raw, uint8_t* a_tile, int r) {
+    const uint32_t* rw = reinterpret_cast<const uint32_t*>(raw);
+    const uint32_t s16 = reinterpret_cast<const uint16_t*>(raw + G_RAW_W)[r];
+    const uint32_t s2 = s16 | (s16 << 16);
     uint32_t wv[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) wv[i] = rw[i * 8];
-    const uint4 sv = *reinterpret_cast<const uint4*>(raw + G_RAW_W + h * 128 + j * 16);
-    const uint32_t sarr[4] = {sv.x, sv.y, sv.z, sv.w};
-    // spread nibbles: ev[i] holds nibbles 0,2,4,6 (offset binary) in bytes 0..3, ov[i] nibbles 1,3,5,7
-    uint32_t ev[8], ov[8];
+    for (int c = 0; c < 8; ++c) wv[c] = rw[c * 128 + r];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const uint32_t x = wv[i] ^ 0x88888888u;
-        ev[i] = x & 0x0f0f0f0fu;
-        ov[i] = (x >> 4) & 0x0f0f0f0fu;
-    }
-    const uint32_t k136 = 0x43084308u;
-#pragma unroll
-    for (int pf = 0; pf < 8; ++pf) {
-        const int q = pf >> 1;
-        // selector: byte q of the first operand, zero (sign of a byte < 0x80), byte q of
-        // the second operand, zero -> [k even | k odd] nibbles of feature pf
-        const uint32_t sel = (uint32_t)q | ((8u | q) << 4) | ((4u + q) << 8) | ((8u | (4u + q)) << 12);
-        const uint32_t s16 = (pf & 1) ? (sarr[pf >> 1] >> 16) : (sarr[pf >> 1] & 0xffffu);
-        const uint32_t s2 = s16 | (s16 << 16);
-        uint32_t outv[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t a = (pf & 1) ? ov[2 * i] : ev[2 * i];
-            const uint32_t b = (pf & 1) ? ov[2 * i + 1] : ev[2 * i + 1];
-            uint32_t t2;
-            asm("prmt.b32 %0, %1, %2, %3;" : "=r"(t2) : "r"(a), "r"(b), "r"(sel));
-            t2 |= 0x43004300u;
-            uint32_t qv;
-            asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(qv) : "r"(t2), "r"(k136));
-            outv[i] = bmul2(qv, s2);
-        }
-        const int r = a_row<EPI>(h, j, pf);
-        *reinterpret_cast<uint4*>(a_tile + sw128_offset(r, kq)) = make_uint4(outv[0], outv[1], outv[2], outv[3]);
+    for (int c = 0; c < 8; ++c) {
+        const uint32_t o0 = tile_pair(wv[c], 0, s2), o1 = tile_pair(wv[c], 1, s2);
+        const uint32_t o2 = tile_pair(wv[c], 2, s2), o3 = tile_pair(wv[c], 3, s2);
+        *reinterpret_cast<uint4*>(a_tile + sw128_offset(r, c)) = make_uint4(o0, o1, o2, o3);
     }
 }
 
@@ -197,8 +174,8 @@ FNX_DEV void produce_a_w8(const GemmParams& p, const TileInfo& ti, int kb, uint8
 }
 
 // ------------------------------------------------------------------ epilogue
-// PERM: A rows follow a_row() (dequantising producers); otherwise rows are in feature
-// order (TMA-loaded bf16 weights).
+// PERM: A rows follow a_row() (the W8 producers); otherwise rows are in tile order:
+// feature 128m + r, or for SwiGLU gate / up of feature 64m + r/2 on even / odd rows.
 template <int EPI, bool PERM>
 FNX_DEV void epilogue_chunk(const GemmParams& p, const TileInfo& ti, int r, int n0, const uint32_t (&v)[16]) {
     const int lane = threadIdx.x & 31;
@@ -254,7 +231,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
     if (tid == 0) {
         for (int s = 0; s < G_STAGES; ++s) {
             mbar_init(&S.a_full[s], MODE == GEMM_BF16 ? 1 : 4);
-            mbar_init(&S.b_full[s], 2);
+            mbar_init(&S.b_full[s], 64);   // one cp.async-completion arrival per loader thread
             mbar_init(&S.empty[s], 1);
         }
         for (int s = 0; s < G_R_STAGES; ++s) {
@@ -273,10 +250,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
         tmem_alloc(&S.tmem_base, 256);
         tmem_relinquish();
     }
-    if (warp == 2 && lane == 0) {
-        tma_prefetch_desc(&p.tmap_a);
-        if (MODE == GEMM_W4) tma_prefetch_desc(&p.tmap_s);
-    }
+    if (MODE == GEMM_BF16 && warp == 2 && lane == 0) tma_prefetch_desc(&p.tmap_a);
     {
         // tile_start[e] = sum_{e' < e} ceil(count(e') / G_BN) * m_tiles   (block scan)
         __shared__ int warp_sums[G_THREADS / 32];
@@ -287,8 +261,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
             const int e = e0 + tid;
             int n = 0;
             if (e < p.E) {
-                const long long begin = p.ends ? (e ? p.ends[e - 1] : 0) : 0;
-                const long long end = p.ends ? p.ends[e] : p.M;
+                const long long begin = min((long long)p.M, (long long)(p.ends ? (e ? p.ends[e - 1] : 0) : 0));
+                const long long end = min((long long)p.M, (long long)(p.ends ? p.ends[e] : p.M));
                 const long long cnt = end > begin ? end - begin : 0;   // malformed ends -> no tiles
                 n = (int)((cnt + G_BN - 1) / G_BN) * p.m_tiles;
             }
@@ -321,7 +295,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
     if (warp == 0 || warp == 3) {
         // ------------------------------------------------ B loaders (two warps, alternate 16-byte chunks)
         const int bw = warp == 3 ? 1 : 0;
-        int it = 0, pending = 0;
+        const uint64_t keep = l2_evict_last();      // token rows are re-read by every feature tile
+        int it = 0;
         bool ok = true;
         for (int tile = blockIdx.x; ok && !S.abort; tile += gridDim.x) {
             TileInfo ti;
@@ -334,6 +309,10 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                 if (n < ti.nrows) {
                     const long long r = ti.row0 + n;
                     src = p.row_index ? p.row_index[r] / p.index_div : r;
+                    if (src < 0 || src >= p.act_rows) {
+                        fnx_flag_error(FNX_DEVERR_BADID);
+                        src = -1;                 // gathered as zeros
+                    }
                 }
                 rows[i] = src >= 0 ? p.act + src * p.ld_act : nullptr;
             }
@@ -349,24 +328,14 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                         const bf16* src = rows[i] ? rows[i] + kb * G_BK : p.act;
 #pragma unroll
                         for (int c = bw; c < 8; c += 2)
-                            cp_async_16_zfill(bt + sw128_offset(n, c), src + c * 8, rows[i] != nullptr);
+                            cp_async_16_hint(bt + sw128_offset(n, c), src + c * 8, rows[i] != nullptr, keep);
                     }
                 }
-                asm volatile("cp.async.commit_group;" ::: "memory");
-                if (++pending > G_B_LAG) {
-                    asm volatile("cp.async.wait_group %0;" ::"n"(G_B_LAG) : "memory");
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&S.b_full[(it - G_B_LAG) % G_STAGES]);
-                    --pending;
-                }
+                // every loader thread arrives once its own copies of this stage have landed
+                cp_async_mbar_arrive(&S.b_full[s]);
             }
         }
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0)
-            for (int q = pending; q > 0; --q) mbar_arrive(&S.b_full[(it - q) % G_STAGES]);
+        asm volatile("cp.async.wait_all;" ::: "memory");
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
@@ -406,24 +375,39 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
         if (lane == 0) {
             int it = 0;
             const int G = MODE == GEMM_W4 ? p.K / p.gs : 1;
+            const uint64_t stream_once = l2_evict_first();   // each weight block is read once
+            // L2 prefetch cursor G_PF_AHEAD blocks ahead of the bulk copies: keeps enough
+            // weight bytes in flight to cover HBM latency without more shared memory
+            int pf_tile = blockIdx.x, pf_kb = 0;
+            TileInfo pti;
+            bool pf_ok = MODE == GEMM_W4 && decode_tile(S, p, pf_tile, pti);
+            auto prefetch_next = [&]() {
+                if (!pf_ok) return;
+                const long long t = (long long)pti.e * p.m_tiles + pti.m;
+                l2_prefetch(reinterpret_cast<const uint32_t*>(p.w) + (t * KB + pf_kb) * 1024, G_RAW_W);
+                if (++pf_kb == KB) {
+                    pf_kb = 0;
+                    pf_tile += gridDim.x;
+                    pf_ok = decode_tile(S, p, pf_tile, pti);
+                }
+            };
+            for (int i = 0; i < G_PF_AHEAD; ++i) prefetch_next();
             for (int tile = blockIdx.x; !S.abort; tile += gridDim.x) {
                 TileInfo ti;
                 if (!decode_tile(S, p, tile, ti)) break;
                 bool ok = true;
                 for (int kb = 0; kb < KB; ++kb, ++it) {
                     if (MODE == GEMM_W4) {
+                        prefetch_next();
                         const int rs = it % G_R_STAGES;
                         if (!mbar_wait(&S.raw_empty[rs], ((it / G_R_STAGES) & 1) ^ 1)) { ok = false; break; }
                         uint8_t* raw = raw_tiles + rs * G_RAW_BYTES;
                         mbar_arrive_expect_tx(&S.raw_full[rs], G_RAW_BYTES);
-                        const int row = ti.e * p.K + kb * G_BK;
-                        const int srow = ti.e * G + (kb * G_BK) / p.gs;
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int f0 = half_feature<EPI>(h, ti.m, p.Nw);
-                            tma_load_2d(smem_u32(raw + h * 2048), &p.tmap_a, &S.raw_full[rs], f0 / 8, row);
-                            tma_load_2d(smem_u32(raw + G_RAW_W + h * 128), &p.tmap_s, &S.raw_full[rs], f0, srow);
-                        }
+                        const long long tile = (long long)ti.e * p.m_tiles + ti.m;
+                        const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(p.w) + (tile * KB + kb) * 1024;
+                        const bf16* ssrc = p.scales + (tile * G + (kb * G_BK) / p.gs) * 128;
+                        bulk_load(smem_u32(raw), wsrc, G_RAW_W, &S.raw_full[rs], stream_once);
+                        bulk_load(smem_u32(raw + G_RAW_W), ssrc, 256, &S.raw_full[rs], stream_once);
                     } else if (MODE == GEMM_BF16) {
                         const int s = it % G_STAGES;
                         if (!mbar_wait(&S.empty[s], ((it / G_STAGES) & 1) ^ 1)) { ok = false; break; }
@@ -452,7 +436,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                 uint32_t v[16];
                 tmem_ld16(tmem + ((uint32_t)(e4 * 32) << 16) + ab * G_BN + n0, v);
                 tmem_ld_wait();
-                epilogue_chunk<EPI, MODE != GEMM_BF16>(p, ti, r, n0, v);
+                epilogue_chunk<EPI, MODE == GEMM_W8>(p, ti, r, n0, v);
             }
             tc_fence_before();
             __syncwarp();
@@ -475,7 +459,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                     const int rs = it % G_R_STAGES;
                     if (!mbar_wait(&S.raw_full[rs], (it / G_R_STAGES) & 1)) { ok = false; break; }
                     if (!mbar_wait(&S.empty[s], ((it / G_STAGES) & 1) ^ 1)) { ok = false; break; }
-                    produce_a_w4<EPI>(raw_tiles + rs * G_RAW_BYTES, at, t);
+                    produce_a_w4(raw_tiles + rs * G_RAW_BYTES, at, t);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&S.raw_empty[rs]);
                 } else {

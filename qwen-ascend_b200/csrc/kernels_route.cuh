@@ -48,8 +48,13 @@ FNX_DEV void topk_warp(const bf16* row, const float* bias, int E, int k, float& 
 #pragma unroll
     for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
     const float inv = 1.0f / sum;
+    // probabilities; a NaN (from NaN logits) counts as 0 so that k valid, distinct ids are
+    // always selected (garbage logits must never turn into an out-of-range expert id)
 #pragma unroll
-    for (int i = 0; i < PER; ++i) v[i] = (i * 32 + lane) < E ? __fmul_rn(v[i], inv) : -1.f;
+    for (int i = 0; i < PER; ++i) {
+        const float pr = __fmul_rn(v[i], inv);
+        v[i] = (i * 32 + lane) < E ? (pr >= 0.f ? pr : 0.f) : -1.f;
+    }
 
     my_p = 0.f;
     tot = 0.f;
@@ -194,6 +199,8 @@ __global__ void __launch_bounds__(32) permute_scatter_kernel(const int64_t* __re
             const long long pos = base + rank;
             order[pos] = i;
             if (inverse) inverse[i] = pos;
+        } else if (valid && inverse) {
+            inverse[i] = -1;          // an id outside [0, E): no row (flagged by the histogram pass)
         }
     }
 }

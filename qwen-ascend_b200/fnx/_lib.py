@@ -32,7 +32,8 @@ SIGNATURES = {
     "fnx_router_topk": ([P, LL, P, P, P, P, I, I, I, P], I),
     "fnx_moe_permute_workspace": ([I, I], SZ),
     "fnx_moe_permute": ([P] * 5 + [I, I, P, SZ, P], I),
-    "fnx_moe_grouped_w4": ([P, LL, P, I, P, P, P, P, LL] + [I] * 6 + [P], I),
+    "fnx_moe_grouped_w4": ([P, LL, LL, P, I, P, P, P, P, LL] + [I] * 6 + [P], I),
+    "fnx_repack_w4_tiles": ([P] * 4 + [I] * 5 + [P], I),
     "fnx_w8a16_gemm": ([P] * 4 + [I] * 4 + [P], I),
     "fnx_bf16_gemm_nt": ([P, LL, P, P, LL, I, I, I, P], I),
     "fnx_moe_decode_workspace": ([I] * 5, SZ),

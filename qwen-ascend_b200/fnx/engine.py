@@ -24,8 +24,28 @@ EPI_PLAIN, EPI_SWIGLU_F32, EPI_SWIGLU_BF16 = 0, 1, 2
 DECODE_MAX_TOKENS = 16
 
 
+def repack_w4(w4, scales, swiglu):
+    """Expert-major int4pack ``[E, K, N/8]`` + bf16 scales ``[E, K/gs, N]`` -> the tile-major
+    layout the kernels stream (``fnx_repack_w4_tiles``): words ``[E, N/128, K/64, 8, 128]``
+    and scales ``[E, N/128, K/gs, 128]``.  ``swiglu`` orders the rows of a tile as gate/up
+    pairs (for the fused SwiGLU epilogue); otherwise rows are consecutive features.  Runs
+    once at load; the artifact layout itself is read unchanged."""
+    _lib.require_cuda(w4, scales)
+    E, K, n8 = w4.shape
+    N, G = n8 * 8, scales.shape[1]
+    tw = torch.empty(E, N // 128, K // 64, 8, 128, dtype=torch.int32, device=w4.device)
+    ts = torch.empty(E, N // 128, G, 128, dtype=BF16, device=w4.device)
+    rc = _lib.lib().fnx_repack_w4_tiles(w4.contiguous().data_ptr(), scales.contiguous().data_ptr(), tw.data_ptr(),
+                                        ts.data_ptr(), E, K, N, K // G, 1 if swiglu else 0, _lib.stream(w4.device))
+    _lib.check(rc, "W4 tile repack")
+    return tw, ts
+
+
 def _grouped_w4(act, w4, scales, ends, out, *, E, M, K, Nw, gs, epilogue, row_index=None, index_div=1):
-    rc = _lib.lib().fnx_moe_grouped_w4(act.data_ptr(), act.stride(0), _lib.ptr(row_index), index_div, w4.data_ptr(),
+    """Grouped GEMM over tile-major weights ``w4``/``scales`` (see ``repack_w4``; the SwiGLU
+    epilogues need the SwiGLU row order)."""
+    rc = _lib.lib().fnx_moe_grouped_w4(act.data_ptr(), act.stride(0), act.shape[0], _lib.ptr(row_index), index_div,
+                                       w4.data_ptr(),
                                        scales.data_ptr(), _lib.ptr(ends), out.data_ptr(), out.stride(0), E, M, K, Nw,
                                        gs, epilogue, _lib.stream(act.device))
     _lib.check(rc, "grouped W4A16 GEMM")
@@ -67,8 +87,17 @@ class ExpW4:
         o.s8t = o.base = None
         return o
 
+    def tiles(self):
+        """The tile-major copy the GEMM reads (built once, then cached)."""
+        t = getattr(self, "_tiles", None)
+        if t is None:
+            t = repack_w4(self.w4, self._scales, swiglu=False)
+            self._tiles = t
+        return t
+
     def _selected(self, ids):
-        return self.w4.index_select(0, ids).contiguous(), self._scales.index_select(0, ids).contiguous()
+        tw, ts = self.tiles()
+        return tw.index_select(0, ids).contiguous(), ts.index_select(0, ids).contiguous()
 
     def apply(self, x, ids):
         """x ``[M, K]`` bf16, ids ``[k]`` -> ``[M, k*N]``: every row times every selected expert."""
@@ -93,7 +122,8 @@ class ExpW4:
     def apply_grouped(self, x, group_ends, host_ends=None):
         """Rows sorted by expert (cumulative ``group_ends`` over all E experts)."""
         out = torch.empty(x.shape[0], self.N, dtype=BF16, device=x.device)
-        return _grouped_w4(x.to(BF16).contiguous(), self.w4, self._scales, group_ends.contiguous(), out, E=self.E,
+        tw, ts = self.tiles()
+        return _grouped_w4(x.to(BF16).contiguous(), tw, ts, group_ends.contiguous(), out, E=self.E,
                            M=x.shape[0], K=self.K, Nw=self.N, gs=self.gs, epilogue=EPI_PLAIN)
 
 
@@ -146,8 +176,9 @@ class DenseW8:
 
 
 class MoELayer:
-    """One W4A16 MoE layer: routed experts (expert-major int4pack + bf16 group scales),
-    an always-on W4 shared expert with a sigmoid gate, and a bf16 router.
+    """One W4A16 MoE layer: routed experts (expert-major int4pack + bf16 group scales, kept
+    as the tile-major copies of ``repack_w4``), an always-on W4 shared expert with a sigmoid
+    gate, and a bf16 router.
 
     ``router_cat`` concatenates the router rows and the shared-expert gate row into one
     bf16 ``[R, H]`` GEMM operand (the reference's load-time concat,
@@ -156,10 +187,13 @@ class MoELayer:
     def __init__(self, gu_w4, gu_scales, dn_w4, dn_scales, gate_w, sh_gu_w4, sh_gu_scales, sh_dn_w4, sh_dn_scales,
                  sh_gate, k, gs, bias=None):
         _lib.require_cuda(gu_w4, dn_w4, gate_w, sh_gu_w4, sh_dn_w4)
-        self.gu = ExpW4.from_scales(gu_w4, gu_scales, gs)
-        self.dn = ExpW4.from_scales(dn_w4, dn_scales, gs)
         self.E, self.H = gate_w.shape
-        self.I = self.gu.N // 2
+        self.I = gu_w4.shape[2] * 8 // 2
+        # tile-major copies (the artifact tensors are not kept)
+        self.gu_tw, self.gu_ts = repack_w4(gu_w4, gu_scales, swiglu=True)
+        self.dn_tw, self.dn_ts = repack_w4(dn_w4, dn_scales, swiglu=False)
+        self.sh_gu_tw, self.sh_gu_ts = repack_w4(sh_gu_w4[None], sh_gu_scales[None], swiglu=True)
+        self.sh_dn_tw, self.sh_dn_ts = repack_w4(sh_dn_w4[None], sh_dn_scales[None], swiglu=False)
         self.k, self.gs = k, gs
         R = self.E + 1
         self.R = R
@@ -168,8 +202,6 @@ class MoELayer:
         rc[:self.E] = gate_w
         rc[self.E] = sh_gate.reshape(-1)
         self.router_cat = rc
-        self.sh_gu_w4, self.sh_gu_s = sh_gu_w4.contiguous(), sh_gu_scales.contiguous()
-        self.sh_dn_w4, self.sh_dn_s = sh_dn_w4.contiguous(), sh_dn_scales.contiguous()
         self.bias = None if bias is None else bias.to(torch.float32).to(gate_w.device).contiguous()
         self._ws = {}
 
@@ -179,9 +211,9 @@ class MoELayer:
                    t["sh_gu_scales"], t["sh_dn_w4"], t["sh_dn_scales"], t["sh_gate"], shape.k, shape.gs, bias=bias)
 
     def weight_bytes(self):
-        return sum(t.numel() * t.element_size() for t in (self.gu.w4, self.gu._scales, self.dn.w4, self.dn._scales,
-                                                           self.router_cat, self.sh_gu_w4, self.sh_gu_s,
-                                                           self.sh_dn_w4, self.sh_dn_s))
+        return sum(t.numel() * t.element_size() for t in (self.gu_tw, self.gu_ts, self.dn_tw, self.dn_ts,
+                                                           self.router_cat, self.sh_gu_tw, self.sh_gu_ts,
+                                                           self.sh_dn_tw, self.sh_dn_ts))
 
     # ---------------------------------------------------------------- routing
     def logits(self, x):
@@ -236,16 +268,16 @@ class MoELayer:
         w, idx, wf = self.topk(logits)
         order, inverse, ends = self.permute(idx)
         act = torch.empty(T * k, I, dtype=BF16, device=dev)
-        _grouped_w4(x, self.gu.w4, self.gu._scales, ends, act, E=E, M=T * k, K=H, Nw=2 * I, gs=self.gs,
+        _grouped_w4(x, self.gu_tw, self.gu_ts, ends, act, E=E, M=T * k, K=H, Nw=2 * I, gs=self.gs,
                     epilogue=EPI_SWIGLU_F32, row_index=order, index_div=k)
         yd = torch.empty(T * k, H, dtype=BF16, device=dev)
-        _grouped_w4(act, self.dn.w4, self.dn._scales, ends, yd, E=E, M=T * k, K=I, Nw=H, gs=self.gs,
+        _grouped_w4(act, self.dn_tw, self.dn_ts, ends, yd, E=E, M=T * k, K=I, Nw=H, gs=self.gs,
                     epilogue=EPI_PLAIN)
         sh_act = torch.empty(T, I, dtype=BF16, device=dev)
-        _grouped_w4(x, self.sh_gu_w4, self.sh_gu_s, None, sh_act, E=1, M=T, K=H, Nw=2 * I, gs=self.gs,
+        _grouped_w4(x, self.sh_gu_tw, self.sh_gu_ts, None, sh_act, E=1, M=T, K=H, Nw=2 * I, gs=self.gs,
                     epilogue=EPI_SWIGLU_BF16)
         sh = torch.empty(T, H, dtype=BF16, device=dev)
-        _grouped_w4(sh_act, self.sh_dn_w4, self.sh_dn_s, None, sh, E=1, M=T, K=I, Nw=H, gs=self.gs,
+        _grouped_w4(sh_act, self.sh_dn_tw, self.sh_dn_ts, None, sh, E=1, M=T, K=I, Nw=H, gs=self.gs,
                     epilogue=EPI_PLAIN)
         out = torch.empty(T, H, dtype=BF16, device=dev)
         gate = logits[:, E:E + 1]
@@ -275,9 +307,9 @@ class MoELayer:
         idx_out = torch.empty(M, self.k, dtype=torch.int64, device=dev) if idx_out is None else idx_out
         ws = self.decode_workspace(M, dev)
         rc = _lib.lib().fnx_moe_decode_w4(
-            x.data_ptr(), self.router_cat.data_ptr(), self.gu.w4.data_ptr(), self.gu._scales.data_ptr(),
-            self.dn.w4.data_ptr(), self.dn._scales.data_ptr(), self.sh_gu_w4.data_ptr(), self.sh_gu_s.data_ptr(),
-            self.sh_dn_w4.data_ptr(), self.sh_dn_s.data_ptr(), _lib.ptr(self.bias), out.data_ptr(), w_out.data_ptr(),
+            x.data_ptr(), self.router_cat.data_ptr(), self.gu_tw.data_ptr(), self.gu_ts.data_ptr(),
+            self.dn_tw.data_ptr(), self.dn_ts.data_ptr(), self.sh_gu_tw.data_ptr(), self.sh_gu_ts.data_ptr(),
+            self.sh_dn_tw.data_ptr(), self.sh_dn_ts.data_ptr(), _lib.ptr(self.bias), out.data_ptr(), w_out.data_ptr(),
             idx_out.data_ptr(), M, self.H, self.I, self.E, self.k, self.gs, ws.data_ptr(), ws.numel(),
             _lib.stream(dev))
         _lib.check(rc, "MoE decode")

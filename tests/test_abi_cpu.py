@@ -50,10 +50,12 @@ def test_host_side_rejections(lib):
     assert lib.fnx_moe_permute(None, None, None, None, None, 10, 5000, None, 0, None) == -1
     assert lib.fnx_moe_permute(None, None, None, None, None, 10, 8, None, 0, None) == -5
     # grouped GEMM shape rules: K % 64, gs % 64, Nw % 128
-    assert lib.fnx_moe_grouped_w4(None, 2048, None, 1, None, None, None, None, 1024, 8, 64, 100, 1024, 128, 0, None) == -1
-    assert lib.fnx_moe_grouped_w4(None, 2048, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1000, 128, 0, None) == -2
-    assert lib.fnx_moe_grouped_w4(None, 2048, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1024, 32, 0, None) == -2
-    assert lib.fnx_moe_grouped_w4(None, 2048, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1024, 128, 3, None) == -1
+    g = lib.fnx_moe_grouped_w4
+    assert g(None, 2048, 64, None, 1, None, None, None, None, 1024, 8, 64, 100, 1024, 128, 0, None) == -1
+    assert g(None, 2048, 64, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1000, 128, 0, None) == -2
+    assert g(None, 2048, 64, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1024, 32, 0, None) == -2
+    assert g(None, 2048, 64, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1024, 128, 3, None) == -1
+    assert g(None, 2048, 10, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1024, 128, 0, None) == -1  # rows < M
     assert lib.fnx_w4gemv_launch(None, None, None, None, None, None, None, 1024, 100, 10, 20, 2, None) == -1
     assert lib.fnx_w4gemv_launch(None, None, None, None, None, None, None, 1024, 2048, 10, 20, 3, None) == -1
     assert lib.fnx_moe_decode_w4(*([None] * 14), 17, 2048, 512, 512, 10, 128, None, 0, None) == -1

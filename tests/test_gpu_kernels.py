@@ -118,6 +118,44 @@ def test_router_topk_and_permute(T, E, k):
     assert O.is_within_group_permutation(order.cpu(), torch.argsort(idx.cpu().reshape(-1).float()), idx.cpu().reshape(-1))
 
 
+def test_invalid_routing_is_contained():
+    """NaN logits still give k valid distinct ids; ids outside [0, E) are flagged and leave
+    no row (inverse = -1) that a later gather could follow out of bounds."""
+    from fnx import _lib
+    from fnx.engine import MoELayer
+    T, E, k = 6, 64, 8
+    logits = torch.full((T, E), float("nan"), dtype=BF16, device=DEV)
+    logits[1, 5] = 1.0
+    w = torch.empty(T, k, dtype=BF16, device=DEV)
+    idx = torch.empty(T, k, dtype=torch.int64, device=DEV)
+    rc = _lib.lib().fnx_router_topk(logits.data_ptr(), E, None, w.data_ptr(), idx.data_ptr(), None, T, E, k,
+                                    _lib.stream(logits.device))
+    assert rc == 0
+    ids = idx.cpu()
+    assert int(ids.min()) >= 0 and int(ids.max()) < E
+    assert all(len(set(r.tolist())) == k for r in ids)
+    lay = MoELayer.__new__(MoELayer)
+    lay.E = 8
+    bad = torch.tensor([3, 9, 1, -2, 3, 7], dtype=torch.int64)
+    order, inverse, ends = lay.permute(bad.to(DEV))
+    torch.cuda.synchronize()
+    assert _lib.device_errors() & 2
+    assert int(ends[-1]) == 4 and inverse.cpu()[[1, 3]].tolist() == [-1, -1]
+    # the combine skips the missing rows instead of following them
+    H = 64
+    yd = torch.randn(6, H, device=DEV).to(BF16)
+    wf = torch.ones(2, 3, device=DEV)
+    sh = torch.zeros(2, H, dtype=BF16, device=DEV)
+    gate = torch.zeros(2, 1, dtype=BF16, device=DEV)
+    out = torch.empty(2, H, dtype=BF16, device=DEV)
+    rc = _lib.lib().fnx_moe_combine(yd.data_ptr(), wf.data_ptr(), inverse.data_ptr(), sh.data_ptr(), gate.data_ptr(), 1,
+                                    out.data_ptr(), 2, 3, H, _lib.stream(yd.device))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert _lib.device_errors() & 2
+    assert bool(torch.isfinite(out.float()).all())
+
+
 def test_permute_edge_cases():
     from fnx.engine import MoELayer
     lay = MoELayer.__new__(MoELayer)

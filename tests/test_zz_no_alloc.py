@@ -29,9 +29,9 @@ def test_decode_noalloc_matches_workspace_entry_point():
         w = torch.empty_like(ref_w)
         idx = torch.empty_like(ref_idx)
         rc = lib.fnx_moe_decode_w4_noalloc(
-            x.data_ptr(), layer.router_cat.data_ptr(), layer.gu.w4.data_ptr(), layer.gu._scales.data_ptr(),
-            layer.dn.w4.data_ptr(), layer.dn._scales.data_ptr(), layer.sh_gu_w4.data_ptr(), layer.sh_gu_s.data_ptr(),
-            layer.sh_dn_w4.data_ptr(), layer.sh_dn_s.data_ptr(), None, out.data_ptr(), w.data_ptr(), idx.data_ptr(),
+            x.data_ptr(), layer.router_cat.data_ptr(), layer.gu_tw.data_ptr(), layer.gu_ts.data_ptr(),
+            layer.dn_tw.data_ptr(), layer.dn_ts.data_ptr(), layer.sh_gu_tw.data_ptr(), layer.sh_gu_ts.data_ptr(),
+            layer.sh_dn_tw.data_ptr(), layer.sh_dn_ts.data_ptr(), None, out.data_ptr(), w.data_ptr(), idx.data_ptr(),
             M, shape.H, shape.I, shape.E, shape.k, shape.gs, _lib.stream(dev))
         assert rc == 0
         torch.cuda.synchronize()
