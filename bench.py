@@ -205,8 +205,8 @@ def bench_prefill(args, world, rank, dev):
     act = torch.empty(T_PREFILL * K_TOP, I, dtype=torch.bfloat16, device=dev)
 
     def gu():
-        _grouped_w4(xs[0], lay.gu_tw, lay.gu_ts, d["ends"], act, E=E, M=T_PREFILL * K_TOP, K=H, Nw=2 * I,
-                    gs=GS, epilogue=EPI_SWIGLU_F32, row_index=d["order"], index_div=K_TOP)
+        _grouped_w4(xs[0], lay.gu_t, d["ends"], act, E=E, M=T_PREFILL * K_TOP, K=H, Nw=2 * I,
+                    epilogue=EPI_SWIGLU_F32, row_index=d["order"], index_div=K_TOP)
     for _ in range(3):
         gu()
     gu_ms = time_events(gu, 10, stream)

@@ -80,28 +80,30 @@ int fnx_moe_permute(void* idx, void* order, void* inverse, void* ends, void* cou
                     size_t ws_bytes, void* stream);
 
 /* Load-time repack of the int4pack artifact (w4 int32 [E,K,Nw/8] expert-major, scales bf16
- * [E,K/gs,Nw]; tools/repack_w4a16.py, tools/repack_w4_em.py) into the tile-major layout the
- * B200 kernels stream: tw int32 [E, Nw/128, K/64, 8, 128] -- word (c, r) of k-block kb holds the
- * 8 weights k = 64kb+8c..+7 of tile row r as offset-binary nibbles in the order 0,2,4,6,1,3,5,7
- * -- and ts bf16 [E, Nw/128, K/gs, 128].  swiglu=1 orders tile rows as gate/up pairs
- * (row 2i: gate feature 64m+i, row 2i+1: up feature Nw/2+64m+i); swiglu=0: row r = 128m+r.
- * K % 64 == 0, Nw % 128 == 0, gs % 64 == 0.  (The reference's equivalent step is the
- * load-time scale cache of fnx/engine.py:653-659 and W4GemvOp.prepare_layer.) */
-int fnx_repack_w4_tiles(const void* w4, const void* scales, void* tw, void* ts, int E, int K, int Nw, int gs,
-                        int swiglu, void* stream);
+ * [E,K/gs,Nw]; tools/repack_w4a16.py, tools/repack_w4_em.py) into the tile blocks the B200
+ * kernels stream: tiles int32 [E, Nw/128, K/64, 1088], one 4352-byte block per (expert,
+ * feature tile m, k-block kb), contiguous along kb.  Word c*128 + r (c < 8) holds the 8 weights
+ * k = 64kb+8c..+7 of tile row r as offset-binary nibbles in the order 0,2,4,6,1,3,5,7; bf16
+ * 2048 + r (words 1024..1087) is row r's scale for the group holding kb (repeated in each
+ * k-block of a group).  swiglu=1 orders tile rows as gate/up pairs (row 2i: gate feature
+ * 64m+i, row 2i+1: up feature Nw/2+64m+i); swiglu=0: row r = 128m+r.
+ * K % 64 == 0, Nw % 128 == 0, gs % 64 == 0, K % gs == 0.  (The reference's equivalent step is
+ * the load-time scale cache of fnx/engine.py:653-659 and W4GemvOp.prepare_layer.) */
+size_t fnx_w4_tiles_bytes(int E, int K, int Nw);
+int fnx_repack_w4_tiles(const void* w4, const void* scales, void* tiles, int E, int K, int Nw, int gs, int swiglu,
+                        void* stream);
 
 /* Expert-major grouped W4A16 GEMM on tcgen05 (restated npu_grouped_matmul,
  * fnx/engine.py:723-753): rows [ends[e-1], ends[e]) use expert e.  Row r reads act row
  * row_index[r] / index_div (row_index NULL: act row r); a row index outside [0, act_rows)
- * reads zeros and sets device error 2.  w4 / scales are the tile-major
- * copies of fnx_repack_w4_tiles (swiglu=1 for epilogues 1 and 2); ends NULL means one group
- * of M rows.
+ * reads zeros and sets device error 2.  tiles are the blocks of fnx_repack_w4_tiles
+ * (swiglu=1 for epilogues 1 and 2); ends NULL means one group of M rows.
  * epilogue 0: out bf16 [M, Nw];  1: SwiGLU of gate = features [0,Nw/2), up = [Nw/2,Nw)
  * in fp32 on bf16-rounded inputs -> out [M, Nw/2];  2: the shared expert's SwiGLU
- * bf16(bf16(silu(g)) * u).  K % 64 == 0, gs % 64 == 0, Nw % 128 == 0. */
+ * bf16(bf16(silu(g)) * u).  K % 64 == 0, Nw % 128 == 0. */
 int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_rows, const void* row_index, int index_div,
-                       const void* w4, const void* scales, const void* ends, void* out, long long ld_out, int E, int M,
-                       int K, int Nw, int gs, int epilogue, void* stream);
+                       const void* tiles, const void* ends, void* out, long long ld_out, int E, int M, int K, int Nw,
+                       int epilogue, void* stream);
 
 /* DenseW8.__call__ (fnx/engine.py:350-365): y bf16 [M,N] = x bf16 [M,K] . bf16(w8t int8 [K,N]
  * * sc bf16 [G,N]) with fp32 accumulation.  K % 64 == 0, N % 128 == 0. */
@@ -120,17 +122,16 @@ int fnx_moe_combine(void* yd, void* wf, void* inverse, void* sh, void* gate, lon
 
 /* Whole decode MoE layer for M <= 16 tokens (fnx/engine.py:1786-1889 decode branch):
  * router bf16 [E+1, H] (row E = shared-expert gate), routed and shared experts as the
- * tile-major copies of fnx_repack_w4_tiles (gate/up with swiglu=1, down with swiglu=0);
+ * tile blocks of fnx_repack_w4_tiles (gate/up with swiglu=1, down with swiglu=0);
  * out bf16 [M,H], w_out bf16 [M,k], idx_out int64 [M,k] (may be NULL).
- * H % 256 == 0, I % 128 == 0, H, I <= 4096, gs % 64 == 0.
+ * H % 256 == 0, I % 128 == 0, H, I <= 4096.
  * workspace: fnx_moe_decode_workspace(M,H,I,E,k) bytes, zero-filled before first use;
  * each completed call leaves it ready for the next.  Calls sharing a workspace must not
  * overlap on the GPU. */
 size_t fnx_moe_decode_workspace(int M, int H, int I, int E, int k);
-int fnx_moe_decode_w4(const void* x, const void* router, const void* gu_w4, const void* gu_s, const void* dn_w4,
-                      const void* dn_s, const void* sh_gu_w4, const void* sh_gu_s, const void* sh_dn_w4,
-                      const void* sh_dn_s, const void* bias, void* out, void* w_out, void* idx_out, int M, int H, int I,
-                      int E, int k, int gs, void* workspace, size_t ws_bytes, void* stream);
+int fnx_moe_decode_w4(const void* x, const void* router, const void* gu, const void* dn, const void* sh_gu,
+                      const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H, int I,
+                      int E, int k, void* workspace, size_t ws_bytes, void* stream);
 
 /* fnx_moe_decode_w4 for callers that cannot allocate device memory (no counterpart in the
  * reference): a plugin host or FFI binding that hands over only input and output buffers,
@@ -139,10 +140,9 @@ int fnx_moe_decode_w4(const void* x, const void* router, const void* gu_w4, cons
  * needing more than that (see fnx_moe_decode_workspace) return -5.  The first call on a
  * device looks the array's address up, so make it before any stream capture.  Every call on
  * a device shares the array, so calls that overlap on the GPU race.  Allocates nothing. */
-int fnx_moe_decode_w4_noalloc(const void* x, const void* router, const void* gu_w4, const void* gu_s,
-                              const void* dn_w4, const void* dn_s, const void* sh_gu_w4, const void* sh_gu_s,
-                              const void* sh_dn_w4, const void* sh_dn_s, const void* bias, void* out, void* w_out,
-                              void* idx_out, int M, int H, int I, int E, int k, int gs, void* stream);
+int fnx_moe_decode_w4_noalloc(const void* x, const void* router, const void* gu, const void* dn, const void* sh_gu,
+                              const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H,
+                              int I, int E, int k, void* stream);
 
 /* ---- library ---- */
 const char* fnx_b200_version(void);

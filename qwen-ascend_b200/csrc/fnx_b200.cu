@@ -168,7 +168,7 @@ int gemm_launch(int mode, int epi, GemmParams& p, cudaStream_t st) {
 // Shape checks shared by the grouped GEMM entry points.
 int gemm_check(int mode, int epi, const GemmParams& p) {
     if (p.E < 1 || p.E > G_MAX_E || p.M < 0 || p.K < G_BK || p.K % G_BK || p.Nw < 1) return FNX_EARG;
-    if (mode != GEMM_BF16 && (p.gs < G_BK || p.gs % G_BK || p.K % p.gs)) return FNX_ESHAPE;
+    if (mode == GEMM_W8 && (p.gs < G_BK || p.gs % G_BK || p.K % p.gs)) return FNX_ESHAPE;
     if (epi == EPI_PLAIN ? p.Nw % G_BM : (p.Nw % 128)) return FNX_ESHAPE;
     if (p.ld_act % 8 || !aligned16(p.act) || !aligned16(p.w) || (p.scales && !aligned16(p.scales))) return FNX_EALIGN;
     if (p.row_index && p.index_div < 1) return FNX_EARG;
@@ -298,14 +298,14 @@ FNX_API int fnx_moe_permute(void* idx, void* order, void* inverse, void* ends, v
 
 // ======================================================================== grouped GEMMs
 FNX_API int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_rows, const void* row_index,
-                               int index_div, const void* w4, const void* scales, const void* ends, void* out,
-                               long long ld_out, int E, int M, int K, int Nw, int gs, int epilogue, void* stream) {
+                               int index_div, const void* tiles, const void* ends, void* out, long long ld_out, int E,
+                               int M, int K, int Nw, int epilogue, void* stream) {
     GemmParams p{};
     p.act = (const bf16*)act; p.ld_act = ld_act; p.row_index = (const int64_t*)row_index; p.index_div = index_div;
     p.act_rows = act_rows;
-    if (act_rows < 0 || (!row_index && act_rows < M)) return FNX_EARG;
-    p.w = w4; p.scales = (const bf16*)scales; p.ends = (const int64_t*)ends; p.out = (bf16*)out; p.ld_out = ld_out;
-    p.E = E; p.M = M; p.K = K; p.Nw = Nw; p.gs = gs;
+    if (act_rows < 0 || act_rows > 0x7fffffffLL || (!row_index && act_rows < M)) return FNX_EARG;
+    p.w = tiles; p.ends = (const int64_t*)ends; p.out = (bf16*)out; p.ld_out = ld_out;
+    p.E = E; p.M = M; p.K = K; p.Nw = Nw; p.gs = 0;
     if (epilogue < 0 || epilogue > 2) return FNX_EARG;
     p.m_tiles = epilogue == EPI_PLAIN ? Nw / G_BM : (Nw / 2) / 64;
     const int rc = gemm_check(GEMM_W4, epilogue, p);
@@ -341,16 +341,19 @@ FNX_API int fnx_bf16_gemm_nt(const void* x, long long ld_x, const void* w, void*
 }
 
 // ======================================================================== load-time repack
-FNX_API int fnx_repack_w4_tiles(const void* w4, const void* scales, void* tw, void* ts, int E, int K, int Nw, int gs,
+FNX_API size_t fnx_w4_tiles_bytes(int E, int K, int Nw) {
+    if (E < 1 || K < 64 || K % 64 || Nw < 128 || Nw % 128) return 0;
+    return (size_t)E * (Nw / 128) * (K / 64) * TILE_BLOCK_BYTES;
+}
+
+FNX_API int fnx_repack_w4_tiles(const void* w4, const void* scales, void* tiles, int E, int K, int Nw, int gs,
                                 int swiglu, void* stream) {
     if (E < 1 || K < 64 || K % 64 || Nw < 128 || Nw % 128 || gs < 64 || gs % 64 || K % gs || (swiglu != 0 && swiglu != 1))
         return FNX_EARG;
-    cudaStream_t st = (cudaStream_t)stream;
-    const long long words = (long long)E * K * (Nw / 8);
-    repack_w4_tiles_kernel<<<grid_for(words, 256), 256, 0, st>>>((const uint32_t*)w4, (uint32_t*)tw, E, K, Nw, swiglu);
-    const long long sc = (long long)E * (K / gs) * Nw;
-    repack_scales_tiles_kernel<<<grid_for(sc, 256), 256, 0, st>>>((const bf16*)scales, (bf16*)ts, E, K / gs, Nw,
-                                                                  swiglu);
+    if (!aligned16(tiles)) return FNX_EALIGN;
+    const long long words = (long long)fnx_w4_tiles_bytes(E, K, Nw) / 4;
+    repack_w4_tiles_kernel<<<grid_for(words, 256), 256, 0, (cudaStream_t)stream>>>(
+        (const uint32_t*)w4, (const bf16*)scales, (uint32_t*)tiles, E, K, Nw, gs, swiglu);
     return launch_rc();
 }
 
@@ -394,34 +397,31 @@ FNX_API size_t fnx_moe_decode_workspace(int M, int H, int I, int E, int k) {
     return decode_layout(M, H, I, E, k).total;
 }
 
-// router: bf16 [E+1, H] (rows 0..E-1 router, row E shared-expert gate); expert weights in
-// the tile-major layout of fnx_repack_w4_tiles (gate/up in SwiGLU row order, down plain).
+// router: bf16 [E+1, H] (rows 0..E-1 router, row E shared-expert gate); expert weights as
+// the tile blocks of fnx_repack_w4_tiles (gate/up in SwiGLU row order, down plain).
 // workspace must be zero-filled before its first use; every completed call leaves its
 // tickets at zero again.
-FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu_w4, const void* gu_s, const void* dn_w4,
-                              const void* dn_s, const void* sh_gu_w4, const void* sh_gu_s, const void* sh_dn_w4,
-                              const void* sh_dn_s, const void* bias, void* out, void* w_out, void* idx_out, int M,
-                              int H, int I, int E, int k, int gs, void* workspace, size_t ws_bytes, void* stream) {
+FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu, const void* dn, const void* sh_gu,
+                              const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H,
+                              int I, int E, int k, void* workspace, size_t ws_bytes, void* stream) {
     if (M < 1 || M > DEC_MAX_M || E < 1 || E > ROUTE_MAX_E || k < 1 || k > 32 || k > E) return FNX_EARG;
-    if (H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K || gs < 64 || gs % 64 || H % gs || I % gs)
-        return FNX_ESHAPE;
+    if (H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K) return FNX_ESHAPE;
     const DecodeLayout L = decode_layout(M, H, I, E, k);
     if (!workspace || ws_bytes < L.total) return FNX_EWORKSPACE;
-    if (!aligned16(x) || !aligned16(router) || !aligned16(gu_w4) || !aligned16(dn_w4) || !aligned16(gu_s) ||
-        !aligned16(dn_s) || !aligned16(sh_gu_w4) || !aligned16(sh_dn_w4) || !aligned16(sh_gu_s) || !aligned16(sh_dn_s))
+    if (!aligned16(x) || !aligned16(router) || !aligned16(gu) || !aligned16(dn) || !aligned16(sh_gu) ||
+        !aligned16(sh_dn))
         return FNX_EALIGN;
     uint8_t* ws = (uint8_t*)workspace;
     DecodeParams p{};
     p.x = (const bf16*)x; p.router = (const bf16*)router;
-    p.gu_tw = (const uint32_t*)gu_w4; p.gu_ts = (const bf16*)gu_s; p.dn_tw = (const uint32_t*)dn_w4; p.dn_ts = (const bf16*)dn_s;
-    p.sh_gu_tw = (const uint32_t*)sh_gu_w4; p.sh_gu_ts = (const bf16*)sh_gu_s;
-    p.sh_dn_tw = (const uint32_t*)sh_dn_w4; p.sh_dn_ts = (const bf16*)sh_dn_s;
+    p.gu_tw = (const uint32_t*)gu; p.dn_tw = (const uint32_t*)dn;
+    p.sh_gu_tw = (const uint32_t*)sh_gu; p.sh_dn_tw = (const uint32_t*)sh_dn;
     p.out = (bf16*)out; p.w_out = (bf16*)w_out; p.idx_out = (int64_t*)idx_out; p.bias = (const float*)bias;
     p.logits = (bf16*)(ws + L.logits); p.wf = (float*)(ws + L.wf); p.idx = (int32_t*)(ws + L.idx);
     p.part = (float*)(ws + L.part); p.part2 = (float*)(ws + L.part2);
     p.act = (bf16*)(ws + L.act); p.act_sh = (bf16*)(ws + L.act_sh); p.yd = (bf16*)(ws + L.yd); p.sh = (bf16*)(ws + L.sh);
     p.counters = (unsigned*)(ws + L.counters);
-    p.M = M; p.H = H; p.I = I; p.E = E; p.k = k; p.gs = gs; p.R = L.R; p.ks1 = L.ks1; p.ks2 = L.ks2;
+    p.M = M; p.H = H; p.I = I; p.E = E; p.k = k; p.R = L.R; p.ks1 = L.ks1; p.ks2 = L.ks2;
     cudaStream_t st = (cudaStream_t)stream;
     const int mt = I / 64;
     const int router_blocks = (L.R + 7) / 8;
@@ -504,13 +504,11 @@ void* noalloc_scratch(int* rc) {
 // by every call on a device and keeps the last call's contents; the tickets that must start
 // at zero are cleared at the start of each call.  Calls that overlap on the GPU (other
 // streams, other threads) race on the array.
-FNX_API int fnx_moe_decode_w4_noalloc(const void* x, const void* router, const void* gu_w4, const void* gu_s,
-                                      const void* dn_w4, const void* dn_s, const void* sh_gu_w4, const void* sh_gu_s,
-                                      const void* sh_dn_w4, const void* sh_dn_s, const void* bias, void* out,
-                                      void* w_out, void* idx_out, int M, int H, int I, int E, int k, int gs,
-                                      void* stream) {
+FNX_API int fnx_moe_decode_w4_noalloc(const void* x, const void* router, const void* gu, const void* dn,
+                                      const void* sh_gu, const void* sh_dn, const void* bias, void* out, void* w_out,
+                                      void* idx_out, int M, int H, int I, int E, int k, void* stream) {
     if (M < 1 || M > DEC_MAX_M || E < 1 || E > ROUTE_MAX_E || k < 1 || k > 32 || k > E) return FNX_EARG;
-    if (H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K || gs < 64 || gs % 64 || H % gs || I % gs) {
+    if (H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K) {
         const DecodeLayout L0 = decode_layout(M, H, I, E, k);
         return L0.total > FNX_NOALLOC_SCRATCH_BYTES ? FNX_EWORKSPACE : FNX_ESHAPE;
     }
@@ -521,6 +519,6 @@ FNX_API int fnx_moe_decode_w4_noalloc(const void* x, const void* router, const v
     if (!ws) return rc;
     if (cudaMemsetAsync(ws + L.counters, 0, L.total - L.counters, (cudaStream_t)stream) != cudaSuccess)
         return FNX_ELAUNCH;
-    return fnx_moe_decode_w4(x, router, gu_w4, gu_s, dn_w4, dn_s, sh_gu_w4, sh_gu_s, sh_dn_w4, sh_dn_s, bias, out,
-                             w_out, idx_out, M, H, I, E, k, gs, ws, FNX_NOALLOC_SCRATCH_BYTES, stream);
+    return fnx_moe_decode_w4(x, router, gu, dn, sh_gu, sh_dn, bias, out, w_out, idx_out, M, H, I, E, k, ws,
+                             FNX_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -12,8 +12,9 @@
 // kernels/moe_epilogue) computed without the Cartesian product and without copying the
 // selected experts.  Weights are read in the tile-major layout (kernels_repack.cuh): one
 // thread owns one tile row (one output feature), so each k-block of a tile is a
-// contiguous 4 KB stream read as consecutive 4-byte words across the block, and a dot
-// product never crosses threads.  K-splits write fp32 partials; the last block of a group
+// contiguous 4 KB stream (plus its inline scales) read as consecutive 4-byte words across
+// the block, and a dot product never crosses threads.  K-splits write fp32 partials; the
+// last block of a group
 // (atomic ticket, no waiting) sums them in a fixed order, so results are deterministic.
 #pragma once
 #include "fnx_common.cuh"
@@ -29,14 +30,10 @@ constexpr int DEC_MAX_K = 4096;          // largest K (H or I) a block stages in
 struct DecodeParams {
     const bf16* x;                   // [M, H]
     const bf16* router;              // [R, H] router rows 0..E-1, shared gate row E
-    const uint32_t* gu_tw;           // routed gate/up, tile-major SwiGLU order [E, I/64, H/64, 8, 128]
-    const bf16* gu_ts;               // [E, I/64, H/gs, 128]
-    const uint32_t* dn_tw;           // routed down, tile-major [E, H/128, I/64, 8, 128]
-    const bf16* dn_ts;               // [E, H/128, I/gs, 128]
+    const uint32_t* gu_tw;           // routed gate/up tile blocks, SwiGLU order [E, I/64, H/64, TILE_BLOCK_WORDS]
+    const uint32_t* dn_tw;           // routed down tile blocks [E, H/128, I/64, TILE_BLOCK_WORDS]
     const uint32_t* sh_gu_tw;        // shared expert, same layouts with E = 1
-    const bf16* sh_gu_ts;
     const uint32_t* sh_dn_tw;
-    const bf16* sh_dn_ts;
     bf16* out;                       // [M, H]
     bf16* w_out;                     // [M, k] bf16 routing weights (optional)
     int64_t* idx_out;                // [M, k] expert ids (optional)
@@ -52,7 +49,7 @@ struct DecodeParams {
     bf16* yd;                        // [M*k, H]
     bf16* sh;                        // [M, H]
     unsigned* counters;              // zero-initialised tickets
-    int M, H, I, E, k, gs, R;
+    int M, H, I, E, k, R;
     int ks1, ks2;                    // K splits of the shared and routed gate/up GEMVs
 };
 
@@ -89,8 +86,7 @@ FNX_DEV void stage_x(uint32_t* xs2, const bf16* x, int K) {
 // Dot products of the 128 rows of one weight tile with x over k-blocks [kb0, kb1):
 // thread (half, r) takes the k-blocks kb0 + half, kb0 + half + 2, ...; the two halves are
 // added in a fixed order.  Result in red[r] (shared memory, 128 floats).
-FNX_DEV void tile_dot(const uint32_t* __restrict__ tw, const bf16* __restrict__ ts, const uint32_t* xs2, int gs,
-                      int kb0, int kb1, float* red) {
+FNX_DEV void tile_dot(const uint32_t* __restrict__ tw, const uint32_t* xs2, int kb0, int kb1, float* red) {
     const int r = threadIdx.x & 127, half = threadIdx.x >> 7;
     float a0 = 0.f, a1 = 0.f;
     for (int kb = kb0 + half; kb < kb1; kb += 4) {
@@ -103,10 +99,10 @@ FNX_DEV void tile_dot(const uint32_t* __restrict__ tw, const bf16* __restrict__ 
                 for (int c = 0; c < 8; ++c) {
                     uint32_t v;
                     asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v)
-                                 : "l"(tw + ((long long)kbu * 8 + c) * 128 + r));
+                                 : "l"(tw + (long long)kbu * TILE_BLOCK_WORDS + c * 128 + r));
                     wv[u][c] = v;
                 }
-                const uint32_t s16 = __ldg(reinterpret_cast<const unsigned short*>(ts) + (long long)(kbu * 64 / gs) * 128 + r);
+                const uint32_t s16 = __ldg(reinterpret_cast<const unsigned short*>(tw + (long long)kbu * TILE_BLOCK_WORDS + 1024) + r);
                 s2[u] = s16 | (s16 << 16);
             } else {
 #pragma unroll
@@ -152,7 +148,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_d1_kernel(const DecodePara
     __shared__ __align__(16) uint32_t xs2[DEC_MAX_K / 2];
     __shared__ float red[128];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int MT = gu_tiles(p), KB = p.H / 64, G = p.H / p.gs;
+    const int MT = gu_tiles(p), KB = p.H / 64;
     if ((int)blockIdx.x < router_blocks) {
         // ---- router + shared gate row: one warp per row, all tokens
         const int e = blockIdx.x * (DEC_THREADS / 32) + warp;
@@ -193,7 +189,7 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_d1_kernel(const DecodePara
         const int ks = b % p.ks1, m = (b / p.ks1) % MT, t = b / (p.ks1 * MT);
         const int nkb = KB / p.ks1;
         stage_x(xs2, p.x + (long long)t * p.H, p.H);
-        tile_dot(p.sh_gu_tw + (long long)m * KB * 1024, p.sh_gu_ts + (long long)m * G * 128, xs2, p.gs, ks * nkb,
+        tile_dot(p.sh_gu_tw + (long long)m * KB * TILE_BLOCK_WORDS, xs2, ks * nkb,
                  (ks + 1) * nkb, red);
         float* part = p.part + (((long long)t * MT + m) * p.ks1 + ks) * 128;
         if (tid < 128) part[tid] = red[tid];
@@ -236,14 +232,14 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_d2_kernel(const DecodePara
     __shared__ __align__(16) uint32_t xs2[DEC_MAX_K / 2];
     __shared__ float red[128];
     const int tid = threadIdx.x;
-    const int MT = gu_tiles(p), KB = p.H / 64, G = p.H / p.gs;
+    const int MT = gu_tiles(p), KB = p.H / 64;
     const int b = blockIdx.x;
     const int ks = b % p.ks2, m = (b / p.ks2) % MT, row = b / (p.ks2 * MT);
     const int ex = __ldcg(p.idx + row), t = row / p.k;
     const int nkb = KB / p.ks2;
     stage_x(xs2, p.x + (long long)t * p.H, p.H);
     const long long tile = (long long)ex * MT + m;
-    tile_dot(p.gu_tw + tile * KB * 1024, p.gu_ts + tile * G * 128, xs2, p.gs, ks * nkb, (ks + 1) * nkb, red);
+    tile_dot(p.gu_tw + tile * KB * TILE_BLOCK_WORDS, xs2, ks * nkb, (ks + 1) * nkb, red);
     float* part = p.part2 + (((long long)row * MT + m) * p.ks2 + ks) * 128;
     if (tid < 128) part[tid] = red[tid];
     if (last_block(ctr_gu(p) + row * MT + m, p.ks2)) {
@@ -264,19 +260,19 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_d3_kernel(const DecodePara
     __shared__ __align__(16) uint32_t xs2[DEC_MAX_K / 2];
     __shared__ float red[128];
     const int tid = threadIdx.x;
-    const int MT = dn_tiles(p), KB = p.I / 64, G = p.I / p.gs;
+    const int MT = dn_tiles(p), KB = p.I / 64;
     const int m = blockIdx.x % MT, row = blockIdx.x / MT;
     const int nrows = p.M * p.k;
     if (row < nrows) {
         const int ex = __ldcg(p.idx + row);
         stage_x(xs2, p.act + (long long)row * p.I, p.I);
         const long long tile = (long long)ex * MT + m;
-        tile_dot(p.dn_tw + tile * KB * 1024, p.dn_ts + tile * G * 128, xs2, p.gs, 0, KB, red);
+        tile_dot(p.dn_tw + tile * KB * TILE_BLOCK_WORDS, xs2, 0, KB, red);
         if (tid < 128) p.yd[(long long)row * p.H + m * 128 + tid] = f2bf(red[tid]);
     } else {
         const int t = row - nrows;
         stage_x(xs2, p.act_sh + (long long)t * p.I, p.I);
-        tile_dot(p.sh_dn_tw + (long long)m * KB * 1024, p.sh_dn_ts + (long long)m * G * 128, xs2, p.gs, 0, KB, red);
+        tile_dot(p.sh_dn_tw + (long long)m * KB * TILE_BLOCK_WORDS, xs2, 0, KB, red);
         if (tid < 128) p.sh[(long long)t * p.H + m * 128 + tid] = f2bf(red[tid]);
     }
     if (last_block(ctr_dn(p) + m, nrows + p.M)) {

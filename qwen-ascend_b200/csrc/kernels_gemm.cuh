@@ -10,19 +10,28 @@
 // and the expert's token rows are N (16..128 in steps of 16), so an expert with ~80
 // tokens pads to 80, not to 128.  D[f, n] accumulates in TMEM (fp32, lane = feature,
 // column = token), double-buffered so the epilogue of one tile overlaps the next.
+// W4: the dequantised A stages live in TMEM too (columns 256..511, tcgen05.st from the
+// producers, read by the MMA as its A operand), so shared memory carries only the
+// token tiles and the raw int4 blocks.
 //
-// Warp roles (512 threads):
-//   warps 0, 3    B loaders: gather token rows with cp.async into K-major SW128 tiles
-//                 (alternate 16-byte chunks); a stage is full when every loader
-//                 thread's copies have landed (cp.async.mbarrier.arrive)
-//   warp 1        TMEM allocator + single-thread MMA issuer (tcgen05.mma kind::f16)
-//   warp 2        TMA producer: W4 -> 4 KB tile-major weight blocks + scales (bulk copies)
-//                 into an R_STAGES-deep ring; BF16 -> the A tiles themselves (128B swizzle)
+// Warp roles (608 threads):
+//   warps 0,16-18 B loaders: gather token rows with cp.async into K-major SW128 tiles; a
+//                 stage is full when every lane's copies have landed (cp.async.mbarrier.arrive)
+//   warp 1        TMEM allocator + MMA issuer.  It touches no shared memory while MMAs are
+//                 in flight (a shared-memory access there waits for the queued MMAs and
+//                 halves the issue rate): stages are handed to it by warp 3 through named
+//                 barriers, tile sizes come from registers filled once per 256 tiles.
+//   warp 2        copy producer: W4 -> tile blocks (4 KB of int4 + their scales) in bulk
+//                 copies of four k-blocks; BF16 -> the A tiles by TMA (128-byte swizzle)
+//   warp 3        waiter: waits on the stage mbarriers and releases the MMA warp
 //   warps 4-7     epilogue warpgroup: tcgen05.ld -> bf16 / SwiGLU -> global
 //   warps 8-15    A producers (W4/W8), two groups of four warps taking alternate k-blocks:
-//                 int4 / int8 -> bf16(q * s) (exactly rounded) -> SW128 smem
-// Every wait is bounded (fnx_common.cuh); a timeout sets an abort flag and all roles
-// unwind to the final barrier, where the allocating warp frees TMEM.
+//                 int4 / int8 -> bf16(q * s) (exactly rounded) -> TMEM (W4) / SW128 smem (W8)
+// Every mbarrier wait is bounded (fnx_common.cuh); a timeout sets an abort flag and the
+// roles unwind to the final barrier, where the allocating warp frees TMEM.  The waiter and
+// the MMA warp always run their full, identical stage count (the waiter stops waiting
+// after an abort but keeps handing over), so the named barriers between them never
+// strand a warp.
 #pragma once
 #include "fnx_common.cuh"
 #include "kernels_repack.cuh"
@@ -35,15 +44,31 @@ enum GemmEpi { EPI_PLAIN = 0, EPI_SWIGLU_F32 = 1, EPI_SWIGLU_BF16 = 2 };
 constexpr int G_BM = 128;          // weight features per tile (UMMA M)
 constexpr int G_BK = 64;           // k per stage (one 128-byte swizzle row of bf16)
 constexpr int G_BN = 128;          // max token rows per tile
-constexpr int G_STAGES = 4;
-constexpr int G_R_STAGES = 16;     // raw int4 ring depth (even: each stage belongs to one producer group)
-constexpr int G_PF_AHEAD = 32;     // weight blocks prefetched into L2 ahead of the raw ring
-constexpr int G_THREADS = 512;
+constexpr int G_MAX_STAGES = 8;
+// Raw int4 ring: G_R_OPS slots of G_OPK tile blocks.  One bulk copy fills a slot with up to
+// G_OPK consecutive k-blocks of a tile (17 KB): a bulk copy costs the copy engine a few
+// hundred cycles however small it is, so 4 KB copies cap the stream near 4.5 TB/s.
+constexpr int G_OPK = 4;
+constexpr int G_R_OPS = 4;
+constexpr int G_THREADS = 608;    // 19 warps
+constexpr int G_LOADERS = 4;       // B loader warps: 0, 16, 17, 18
+constexpr int G_BAR_FULL = 1;      // named barrier: waiter -> MMA warp, "stage j is full"
+constexpr int G_BAR_TAKEN = 2;     // named barrier: MMA warp -> waiter, "stage j was issued"
 constexpr int G_A_BYTES = G_BM * G_BK * 2;     // 16 KB
 constexpr int G_B_BYTES = G_BN * G_BK * 2;     // 16 KB
-constexpr int G_RAW_W = 8 * 128 * 4;           // 4 KB: one tile-major block [8 chunks][128 rows] of words
-constexpr int G_RAW_BYTES = G_RAW_W + 128 * 2;      // + the rows' scales for the block's k group
+constexpr int G_RAW_W = 8 * 128 * 4;           // 4 KB: the words [8 chunks][128 rows] of a tile block
+constexpr int G_RAW_BYTES = TILE_BLOCK_BYTES;  // + the rows' scales for the block's k group
 constexpr int G_MAX_E = 1024;
+
+template <int MODE>
+struct GemmCfg {
+    static constexpr bool A_TMEM = MODE == 0;                 // GEMM_W4: A stages in tensor memory
+    static constexpr int STAGES = A_TMEM ? 8 : 6;
+    static constexpr int R_SLOTS = MODE == 0 ? G_R_OPS * G_OPK : 0;   // raw tile blocks in the ring
+    static constexpr uint32_t TMEM_COLS = A_TMEM ? 512 : 256;
+    static constexpr uint32_t A_COL0 = 2 * G_BN;              // A stages follow the two accumulators
+    static_assert(STAGES <= G_MAX_STAGES && (!A_TMEM || A_COL0 + STAGES * 32 <= TMEM_COLS), "tmem budget");
+};
 
 struct GemmParams {
     CUtensorMap tmap_a;         // BF16: bf16 weights [E*Nw, K], box {64, 128}, 128-byte swizzle
@@ -52,9 +77,9 @@ struct GemmParams {
     long long act_rows;         // gathered row indices outside [0, act_rows) read zeros (and are flagged)
     const int64_t* row_index;   // null: row r of the problem reads act row r; else row_index[r] / index_div
     int index_div;
-    const void* w;              // W4: tile-major int32 [E, MT, K/64, 8, 128] (kernels_repack.cuh);
-                                // W8: int8 [E, K, Nw]; BF16: bf16 [E, Nw, K]
-    const bf16* scales;         // W4: tile-major bf16 [E, MT, K/gs, 128]; W8: bf16 [E, K/gs, Nw]
+    const void* w;              // W4: tile blocks int32 [E, MT, K/64, TILE_BLOCK_WORDS] with their
+                                // scales inline (kernels_repack.cuh); W8: int8 [E, K, Nw]; BF16: bf16 [E, Nw, K]
+    const bf16* scales;         // W8: bf16 [E, K/gs, Nw] (unused otherwise)
     const int64_t* ends;        // [E] cumulative row counts; null: one group of M rows
     bf16* out;                  // bf16 [M, ld_out]
     long long ld_out;
@@ -63,8 +88,8 @@ struct GemmParams {
 };
 
 struct GemmSmem {
-    uint64_t a_full[G_STAGES], b_full[G_STAGES], empty[G_STAGES];
-    uint64_t raw_full[G_R_STAGES], raw_empty[G_R_STAGES];
+    uint64_t a_full[G_MAX_STAGES], b_full[G_MAX_STAGES], empty[G_MAX_STAGES];
+    uint64_t raw_full[G_R_OPS], raw_empty[G_R_OPS];
     uint64_t acc_full[2], acc_empty[2], final_bar;
     uint32_t tmem_base;
     volatile int abort;
@@ -124,10 +149,10 @@ FNX_DEV int lane_feature(int r) {
 // ------------------------------------------------------------------ A producers
 // W4: thread r of a 128-thread group dequantises tile row r of the stage: eight words
 // (8 consecutive k each) from the tile-major block the TMA warp copied, scaled by the
-// row's group scale, into the eight 16-byte chunks of A row r.  Reads are consecutive
-// words across the warp and the swizzled stores hit eight distinct chunks per 8 rows:
-// both conflict-free.
-FNX_DEV void produce_a_w4(const uint8_t* raw, uint8_t* a_tile, int r) {
+// row's group scale, into 32 registers = the row's 64 bf16 as tensor-memory columns
+// (column 4c + i holds k = 8c + 2i in its low half, 8c + 2i + 1 in its high half).
+// The reads are consecutive words across the warp: conflict-free.
+FNX_DEV void produce_a_w4(const uint8_t* raw, int r, uint32_t (&a)[32]) {
     const uint32_t* rw = reinterpret_cast<const uint32_t*>(raw);
     const uint32_t s16 = reinterpret_cast<const uint16_t*>(raw + G_RAW_W)[r];
     const uint32_t s2 = s16 | (s16 << 16);
@@ -135,11 +160,9 @@ FNX_DEV void produce_a_w4(const uint8_t* raw, uint8_t* a_tile, int r) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) wv[c] = rw[c * 128 + r];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const uint32_t o0 = tile_pair(wv[c], 0, s2), o1 = tile_pair(wv[c], 1, s2);
-        const uint32_t o2 = tile_pair(wv[c], 2, s2), o3 = tile_pair(wv[c], 3, s2);
-        *reinterpret_cast<uint4*>(a_tile + sw128_offset(r, c)) = make_uint4(o0, o1, o2, o3);
-    }
+    for (int c = 0; c < 8; ++c)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[4 * c + i] = tile_pair(wv[c], i, s2);
 }
 
 // W8: same block shape, int8 weights read directly (L2-resident dense projections).
@@ -218,26 +241,28 @@ FNX_DEV void epilogue_chunk(const GemmParams& p, const TileInfo& ti, int r, int 
 // ------------------------------------------------------------------ the kernel
 template <int MODE, int EPI>
 __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid_constant__ GemmParams p) {
+    using C = GemmCfg<MODE>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* a_tiles = base;
-    uint8_t* b_tiles = a_tiles + G_STAGES * G_A_BYTES;
-    uint8_t* raw_tiles = b_tiles + G_STAGES * G_B_BYTES;
-    GemmSmem& S = *reinterpret_cast<GemmSmem*>(raw_tiles + (MODE == GEMM_W4 ? G_R_STAGES * G_RAW_BYTES : 0));
+    uint8_t* b_tiles = base;
+    uint8_t* a_tiles = b_tiles + C::STAGES * G_B_BYTES;          // shared-memory A (W8, BF16)
+    uint8_t* raw_tiles = a_tiles + (C::A_TMEM ? 0 : C::STAGES * G_A_BYTES);
+    GemmSmem& S = *reinterpret_cast<GemmSmem*>(raw_tiles + C::R_SLOTS * G_RAW_BYTES);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     // ---- prologue: barriers, TMEM, per-expert tile offsets
     if (tid == 0) {
-        for (int s = 0; s < G_STAGES; ++s) {
+        for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(&S.a_full[s], MODE == GEMM_BF16 ? 1 : 4);
-            mbar_init(&S.b_full[s], 64);   // one cp.async-completion arrival per loader thread
+            mbar_init(&S.b_full[s], 32 * G_LOADERS);   // one cp.async-completion arrival per loader lane
             mbar_init(&S.empty[s], 1);
         }
-        for (int s = 0; s < G_R_STAGES; ++s) {
-            mbar_init(&S.raw_full[s], 1);
-            mbar_init(&S.raw_empty[s], 4);
-        }
+        if (MODE == GEMM_W4)
+            for (int s = 0; s < G_R_OPS; ++s) {
+                mbar_init(&S.raw_full[s], 1);
+                mbar_init(&S.raw_empty[s], 8);     // every producer warp releases every op
+            }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&S.acc_full[b], 1);
             mbar_init(&S.acc_empty[b], 4);
@@ -247,7 +272,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(&S.tmem_base, 256);
+        tmem_alloc(&S.tmem_base, C::TMEM_COLS);
         tmem_relinquish();
     }
     if (MODE == GEMM_BF16 && warp == 2 && lane == 0) tma_prefetch_desc(&p.tmap_a);
@@ -292,16 +317,17 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
     const uint32_t tmem = S.tmem_base;
     const int KB = p.K / G_BK;
 
-    if (warp == 0 || warp == 3) {
-        // ------------------------------------------------ B loaders (two warps, alternate 16-byte chunks)
-        const int bw = warp == 3 ? 1 : 0;
+    if (warp == 0 || warp >= 16) {
+        // ------------------------------------------------ B loaders
+        const int lw = warp == 0 ? 0 : warp - 15;
         const uint64_t keep = l2_evict_last();      // token rows are re-read by every feature tile
         int it = 0;
         bool ok = true;
         for (int tile = blockIdx.x; ok && !S.abort; tile += gridDim.x) {
             TileInfo ti;
             if (!decode_tile(S, p, tile, ti)) break;
-            const bf16* rows[G_BN / 32];
+            // lane L resolves the source rows of tile rows L, L+32, L+64, L+96 (-1: zeros) ...
+            int src_row[G_BN / 32];
 #pragma unroll
             for (int i = 0; i < G_BN / 32; ++i) {
                 const int n = lane + 32 * i;
@@ -314,103 +340,113 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                         src = -1;                 // gathered as zeros
                     }
                 }
-                rows[i] = src >= 0 ? p.act + src * p.ld_act : nullptr;
+                src_row[i] = (int)src;
+            }
+            // ... and then holds those of the rows it copies: instruction i = lw + 4u copies tile
+            // rows 4i .. 4i+3, lane L row 4i + L/8 (once per tile: the per-stage loop below is
+            // address arithmetic and copies only)
+            int rix[G_BN / 4 / G_LOADERS];
+#pragma unroll
+            for (int u = 0; u < G_BN / 4 / G_LOADERS; ++u) {
+                const int i = lw + G_LOADERS * u;
+                rix[u] = __shfl_sync(0xffffffffu, src_row[u / 2], (4 * i + (lane >> 3)) & 31);
             }
             const int npad = (ti.nrows + 15) & ~15;
+            const int c = lane & 7;               // 16-byte chunk of the 128-byte row slice
             for (int kb = 0; kb < KB; ++kb, ++it) {
-                const int s = it % G_STAGES;
-                if (!mbar_wait(&S.empty[s], ((it / G_STAGES) & 1) ^ 1)) { S.abort = 1; ok = false; break; }
+                const int s = it % C::STAGES;
+                if (!mbar_wait(&S.empty[s], ((it / C::STAGES) & 1) ^ 1)) { S.abort = 1; ok = false; break; }
                 const uint32_t bt = smem_u32(b_tiles + s * G_B_BYTES);
+                const bf16* kbase = p.act + kb * G_BK + c * 8;
+                // one instruction copies 4 whole 128-byte row slices (8 lanes per row), so each
+                // touches 4 cache lines instead of 32
 #pragma unroll
-                for (int i = 0; i < G_BN / 32; ++i) {
-                    const int n = lane + 32 * i;
-                    if (n < npad) {
-                        const bf16* src = rows[i] ? rows[i] + kb * G_BK : p.act;
-#pragma unroll
-                        for (int c = bw; c < 8; c += 2)
-                            cp_async_16_hint(bt + sw128_offset(n, c), src + c * 8, rows[i] != nullptr, keep);
+                for (int u = 0; u < G_BN / 4 / G_LOADERS; ++u) {
+                    const int i = lw + G_LOADERS * u;
+                    if (4 * i < npad) {
+                        const int n = 4 * i + (lane >> 3);
+                        const int r = rix[u];
+                        cp_async_16_hint(bt + sw128_offset(n, c), r >= 0 ? kbase + (long long)r * p.ld_act : p.act,
+                                         r >= 0, keep);
                     }
                 }
-                // every loader thread arrives once its own copies of this stage have landed
+                // every lane arrives once its own copies of this stage have landed
                 cp_async_mbar_arrive(&S.b_full[s]);
             }
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
     } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            int it = 0, tcount = 0;
-            for (int tile = blockIdx.x; !S.abort; tile += gridDim.x, ++tcount) {
-                TileInfo ti;
-                if (!decode_tile(S, p, tile, ti)) break;
-                const int ab = tcount & 1;
-                if (!mbar_wait(&S.acc_empty[ab], ((tcount >> 1) & 1) ^ 1)) { S.abort = 1; break; }
+        // ------------------------------------------------ MMA issuer (whole warp, one elected lane issues)
+        const int my_tiles = S.total_tiles > (int)blockIdx.x ? (S.total_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const int total_stages = my_tiles * KB;
+        int j = 0;
+        uint32_t pack = 0;          // lane L: (token rows / 16 - 1) of tiles 8L .. 8L+7 of the epoch
+        for (int i = 0; i < my_tiles; ++i) {
+            if ((i & 255) == 0) {
+                // once per 256 tiles: the only shared-memory reads of this warp in the loop
+                pack = 0;
+#pragma unroll 1
+                for (int q = 0; q < 8; ++q) {
+                    const int t = i + 8 * lane + q;
+                    TileInfo ti;
+                    if (t < my_tiles && decode_tile(S, p, (int)blockIdx.x + t * (int)gridDim.x, ti))
+                        pack |= (uint32_t)(((ti.nrows + 15) >> 4) - 1) << (4 * q);
+                }
+            }
+            const int loc = i & 255;
+            const uint32_t n16 = ((__shfl_sync(0xffffffffu, pack, loc >> 3) >> (4 * (loc & 7))) & 15u) + 1u;
+            const int ab = i & 1;
+            const uint32_t idesc = idesc_bf16_f32(G_BM, (int)n16 * 16);
+            const uint32_t d = tmem + ab * G_BN;
+            for (int kb = 0; kb < KB; ++kb, ++j) {
+                const int s = j % C::STAGES;
+                named_bar_sync(G_BAR_FULL, 64);
                 tc_fence_after();
-                const int npad = (ti.nrows + 15) & ~15;
-                const uint32_t idesc = idesc_bf16_f32(G_BM, npad);
-                const uint32_t d = tmem + ab * G_BN;
-                bool ok = true;
-                for (int kb = 0; kb < KB; ++kb, ++it) {
-                    const int s = it % G_STAGES;
-                    const uint32_t ph = (it / G_STAGES) & 1;
-                    if (!mbar_wait(&S.a_full[s], ph) || !mbar_wait(&S.b_full[s], ph)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t a0 = smem_u32(a_tiles + s * G_A_BYTES);
+                if (elect_one()) {
                     const uint32_t b0 = smem_u32(b_tiles + s * G_B_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < G_BK / 16; ++kk)
-                        umma_bf16(d, sdesc_kmajor_sw128(a0 + kk * 32), sdesc_kmajor_sw128(b0 + kk * 32), idesc,
-                                  (kb | kk) ? 1u : 0u);
+                    for (int kk = 0; kk < G_BK / 16; ++kk) {
+                        if (C::A_TMEM)
+                            umma_bf16_ts(d, tmem + C::A_COL0 + s * 32 + kk * 8, sdesc_kmajor_sw128(b0 + kk * 32),
+                                         idesc, (kb | kk) ? 1u : 0u);
+                        else
+                            umma_bf16(d, sdesc_kmajor_sw128(smem_u32(a_tiles + s * G_A_BYTES) + kk * 32),
+                                      sdesc_kmajor_sw128(b0 + kk * 32), idesc, (kb | kk) ? 1u : 0u);
+                    }
                     umma_commit(&S.empty[s]);
+                    if (kb == KB - 1) umma_commit(&S.acc_full[ab]);
                 }
-                if (!ok) { S.abort = 1; break; }
-                umma_commit(&S.acc_full[ab]);
+                __syncwarp();
+                if (j + 1 < total_stages) named_bar_arrive(G_BAR_TAKEN, 64);
             }
-            umma_commit(&S.final_bar);
-            mbar_wait(&S.final_bar, 0);
         }
+        if (elect_one()) umma_commit(&S.final_bar);
         __syncwarp();
+        mbar_wait(&S.final_bar, 0);
     } else if (warp == 2) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            int it = 0;
-            const int G = MODE == GEMM_W4 ? p.K / p.gs : 1;
+            int it = 0, op = 0;
             const uint64_t stream_once = l2_evict_first();   // each weight block is read once
-            // L2 prefetch cursor G_PF_AHEAD blocks ahead of the bulk copies: keeps enough
-            // weight bytes in flight to cover HBM latency without more shared memory
-            int pf_tile = blockIdx.x, pf_kb = 0;
-            TileInfo pti;
-            bool pf_ok = MODE == GEMM_W4 && decode_tile(S, p, pf_tile, pti);
-            auto prefetch_next = [&]() {
-                if (!pf_ok) return;
-                const long long t = (long long)pti.e * p.m_tiles + pti.m;
-                l2_prefetch(reinterpret_cast<const uint32_t*>(p.w) + (t * KB + pf_kb) * 1024, G_RAW_W);
-                if (++pf_kb == KB) {
-                    pf_kb = 0;
-                    pf_tile += gridDim.x;
-                    pf_ok = decode_tile(S, p, pf_tile, pti);
-                }
-            };
-            for (int i = 0; i < G_PF_AHEAD; ++i) prefetch_next();
             for (int tile = blockIdx.x; !S.abort; tile += gridDim.x) {
                 TileInfo ti;
                 if (!decode_tile(S, p, tile, ti)) break;
                 bool ok = true;
-                for (int kb = 0; kb < KB; ++kb, ++it) {
-                    if (MODE == GEMM_W4) {
-                        prefetch_next();
-                        const int rs = it % G_R_STAGES;
-                        if (!mbar_wait(&S.raw_empty[rs], ((it / G_R_STAGES) & 1) ^ 1)) { ok = false; break; }
-                        uint8_t* raw = raw_tiles + rs * G_RAW_BYTES;
-                        mbar_arrive_expect_tx(&S.raw_full[rs], G_RAW_BYTES);
-                        const long long tile = (long long)ti.e * p.m_tiles + ti.m;
-                        const uint32_t* wsrc = reinterpret_cast<const uint32_t*>(p.w) + (tile * KB + kb) * 1024;
-                        const bf16* ssrc = p.scales + (tile * G + (kb * G_BK) / p.gs) * 128;
-                        bulk_load(smem_u32(raw), wsrc, G_RAW_W, &S.raw_full[rs], stream_once);
-                        bulk_load(smem_u32(raw + G_RAW_W), ssrc, 256, &S.raw_full[rs], stream_once);
-                    } else if (MODE == GEMM_BF16) {
-                        const int s = it % G_STAGES;
-                        if (!mbar_wait(&S.empty[s], ((it / G_STAGES) & 1) ^ 1)) { ok = false; break; }
+                if (MODE == GEMM_W4) {
+                    const uint8_t* tsrc = reinterpret_cast<const uint8_t*>(p.w) +
+                                          ((long long)ti.e * p.m_tiles + ti.m) * KB * (long long)G_RAW_BYTES;
+                    for (int kb0 = 0; kb0 < KB; kb0 += G_OPK, ++op) {
+                        const int os = op % G_R_OPS;
+                        if (!mbar_wait(&S.raw_empty[os], ((op / G_R_OPS) & 1) ^ 1)) { ok = false; break; }
+                        const uint32_t bytes = (uint32_t)min(G_OPK, KB - kb0) * G_RAW_BYTES;
+                        mbar_arrive_expect_tx(&S.raw_full[os], bytes);
+                        bulk_load(smem_u32(raw_tiles + os * G_OPK * G_RAW_BYTES), tsrc + (long long)kb0 * G_RAW_BYTES,
+                                  bytes, &S.raw_full[os], stream_once);
+                    }
+                } else if (MODE == GEMM_BF16) {
+                    for (int kb = 0; kb < KB; ++kb, ++it) {
+                        const int s = it % C::STAGES;
+                        if (!mbar_wait(&S.empty[s], ((it / C::STAGES) & 1) ^ 1)) { ok = false; break; }
                         mbar_arrive_expect_tx(&S.a_full[s], G_A_BYTES);
                         tma_load_2d(smem_u32(a_tiles + s * G_A_BYTES), &p.tmap_a, &S.a_full[s], kb * G_BK,
                                     ti.e * p.Nw + ti.m * G_BM);
@@ -420,6 +456,32 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
             }
         }
         __syncwarp();
+    } else if (warp == 3) {
+        // ------------------------------------------------ waiter: mbarriers -> named barriers
+        // Runs exactly the MMA warp's stage count.  After an abort it stops waiting (the
+        // data may never come) but keeps handing stages over, so the MMA warp never blocks
+        // on a named barrier for good; the MMAs then read stale tiles of a failed launch.
+        bool dead = false;
+        int j = 0, i = 0;
+        for (int tile = blockIdx.x; tile < S.total_tiles; tile += gridDim.x, ++i) {
+            const int ab = i & 1;
+            dead = __any_sync(0xffffffffu, dead || S.abort);
+            if (!dead) {
+                const bool ok = mbar_wait(&S.acc_empty[ab], ((i >> 1) & 1) ^ 1);
+                if (!__all_sync(0xffffffffu, ok)) { dead = true; S.abort = 1; }
+            }
+            for (int kb = 0; kb < KB; ++kb, ++j) {
+                const int s = j % C::STAGES;
+                const uint32_t ph = (j / C::STAGES) & 1;
+                dead = __any_sync(0xffffffffu, dead || S.abort);
+                if (!dead) {
+                    const bool ok = mbar_wait(&S.a_full[s], ph) && mbar_wait(&S.b_full[s], ph);
+                    if (!__all_sync(0xffffffffu, ok)) { dead = true; S.abort = 1; }
+                }
+                if (j > 0) named_bar_sync(G_BAR_TAKEN, 64);
+                named_bar_arrive(G_BAR_FULL, 64);
+            }
+        }
     } else if (warp >= 4 && warp < 8) {
         // ------------------------------------------------ epilogue warpgroup
         const int e4 = warp - 4;
@@ -445,33 +507,49 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
     } else if (warp >= 8 && MODE != GEMM_BF16) {
         // ------------------------------------------------ A producers
         const int grp = (warp - 8) >> 2;
-        const int t = tid - 256 - grp * 128;
-        int it = 0;
-        for (int tile = blockIdx.x; !S.abort; tile += gridDim.x) {
+        const int q = warp & 3;                 // TMEM lane quarter this warp may access
+        const int t = q * 32 + lane;            // tile row
+        int it = 0, op = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && !S.abort; tile += gridDim.x) {
             TileInfo ti;
             if (!decode_tile(S, p, tile, ti)) break;
-            bool ok = true;
             for (int kb = 0; kb < KB; ++kb, ++it) {
-                if ((it & 1) != grp) continue;
-                const int s = it % G_STAGES;
-                uint8_t* at = a_tiles + s * G_A_BYTES;
+                const int s = it % C::STAGES;
                 if (MODE == GEMM_W4) {
-                    const int rs = it % G_R_STAGES;
-                    if (!mbar_wait(&S.raw_full[rs], (it / G_R_STAGES) & 1)) { ok = false; break; }
-                    if (!mbar_wait(&S.empty[s], ((it / G_STAGES) & 1) ^ 1)) { ok = false; break; }
-                    produce_a_w4(raw_tiles + rs * G_RAW_BYTES, at, t);
+                    const int os = op % G_R_OPS;
+                    const uint32_t rph = (op / G_R_OPS) & 1;
+                    if ((it & 1) == grp) {
+                        const bool got = mbar_wait(&S.raw_full[os], rph) &&
+                                         mbar_wait(&S.empty[s], ((it / C::STAGES) & 1) ^ 1);
+                        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+                        uint32_t a[32];
+                        produce_a_w4(raw_tiles + (os * G_OPK + kb % G_OPK) * G_RAW_BYTES, t, a);
+                        tmem_st32(tmem + ((uint32_t)(q * 32) << 16) + C::A_COL0 + s * 32, a);
+                        tmem_st_wait();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&S.a_full[s]);
+                    }
+                    if (kb % G_OPK == G_OPK - 1 || kb == KB - 1) {
+                        // end of a copy: release the slot.  A warp that owned no block of it
+                        // first waits for it to have landed, so its release always counts
+                        // toward this copy's phase.
+                        if (!__all_sync(0xffffffffu, mbar_wait(&S.raw_full[os], rph))) { ok = false; break; }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&S.raw_empty[os]);
+                        ++op;
+                    }
+                } else if ((it & 1) == grp) {
+                    if (!mbar_wait(&S.empty[s], ((it / C::STAGES) & 1) ^ 1)) { ok = false; break; }
+                    produce_a_w8<EPI>(p, ti, kb, a_tiles + s * G_A_BYTES, t);
+                    fence_proxy_async_smem();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&S.raw_empty[rs]);
-                } else {
-                    if (!mbar_wait(&S.empty[s], ((it / G_STAGES) & 1) ^ 1)) { ok = false; break; }
-                    produce_a_w8<EPI>(p, ti, kb, at, t);
+                    if (lane == 0) mbar_arrive(&S.a_full[s]);
                 }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&S.a_full[s]);
             }
-            if (!ok) { S.abort = 1; break; }
         }
+        if (!ok) S.abort = 1;
     }
 
     // ---- teardown
@@ -479,13 +557,19 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 256);
+        tmem_dealloc(tmem, C::TMEM_COLS);
     }
 }
 
-inline size_t grouped_gemm_smem_bytes(int mode) {
-    return 1024 + (size_t)G_STAGES * (G_A_BYTES + G_B_BYTES) + (mode == GEMM_W4 ? (size_t)G_R_STAGES * G_RAW_BYTES : 0) +
+template <int MODE>
+inline size_t grouped_gemm_smem_bytes_t() {
+    using C = GemmCfg<MODE>;
+    return 1024 + (size_t)C::STAGES * (G_B_BYTES + (C::A_TMEM ? 0 : G_A_BYTES)) + (size_t)C::R_SLOTS * G_RAW_BYTES +
            sizeof(GemmSmem);
+}
+inline size_t grouped_gemm_smem_bytes(int mode) {
+    return mode == GEMM_W4 ? grouped_gemm_smem_bytes_t<GEMM_W4>()
+                           : mode == GEMM_W8 ? grouped_gemm_smem_bytes_t<GEMM_W8>() : grouped_gemm_smem_bytes_t<GEMM_BF16>();
 }
 
 }  // namespace fnx

@@ -4,11 +4,14 @@
 //
 // Input  w  int32 [E, K, Nw/8]  nibble t of word j = W[k, 8j+t], two's complement
 //        s  bf16  [E, K/gs, Nw]
-// Output tw int32 [E, MT, K/64, 8, 128]: for expert e, feature tile m and k-block kb, word
-//        (c, r) holds the 8 weights W[kb*64 + 8c + i, f(m, r)] of tile row r, as offset-binary
-//        nibbles (q + 8) in the order i = 0,2,4,6,1,3,5,7, so that
-//        ((word >> 4i) & 0x000f000f) yields the pair (k = 8c+2i, 8c+2i+1).
-//        ts bf16  [E, MT, K/gs, 128]: the scale of row r for every k group.
+// Output t  int32 [E, MT, K/64, TILE_BLOCK_WORDS]: one 4352-byte block per (expert e,
+//        feature tile m, k-block kb), contiguous along kb, so a tile's whole K range is one
+//        linear stream and consecutive k-blocks can be fetched by one bulk copy:
+//          word c*128 + r (c < 8, r < 128): the 8 weights W[kb*64 + 8c + i, f(m, r)] of tile
+//            row r as offset-binary nibbles (q + 8) in the order i = 0,2,4,6,1,3,5,7, so
+//            that ((word >> 4i) & 0x000f000f) yields the pair (k = 8c+2i, 8c+2i+1);
+//          half-word 2048 + r: the scale of tile row r for the group holding k-block kb
+//            (repeated in every k-block of a group when gs > 64).
 // Tile rows: PLAIN  f(m, r) = 128m + r                                 (MT = Nw / 128)
 //            SWIGLU f(m, r) = (r odd ? Nw/2 : 0) + 64m + r/2  (gate/up of a feature on
 //                             adjacent rows, so a SwiGLU epilogue pairs lanes 2i, 2i+1)
@@ -18,53 +21,48 @@
 
 namespace fnx {
 
+constexpr int TILE_BLOCK_WORDS = 1024 + 64;                 // 4096 B of weights + 256 B of scales
+constexpr int TILE_BLOCK_BYTES = TILE_BLOCK_WORDS * 4;      // 4352
+
 FNX_DEV int tile_feature(int m, int r, int Nw, bool swiglu) {
     return swiglu ? ((r & 1) ? Nw / 2 : 0) + 64 * m + (r >> 1) : 128 * m + r;
 }
 
-__global__ void __launch_bounds__(256) repack_w4_tiles_kernel(const uint32_t* __restrict__ w,
-                                                              uint32_t* __restrict__ tw, int E, int K, int Nw,
+__global__ void __launch_bounds__(256) repack_w4_tiles_kernel(const uint32_t* __restrict__ w, const bf16* __restrict__ s,
+                                                              uint32_t* __restrict__ t, int E, int K, int Nw, int gs,
                                                               int swiglu) {
-    const int MT = Nw / 128, KB = K / 64;
-    const long long total = (long long)E * MT * KB * 8 * 128;
+    const int MT = Nw / 128, KB = K / 64, G = K / gs;
+    const long long total = (long long)E * MT * KB * TILE_BLOCK_WORDS;
     const int nw8 = Nw / 8;
     for (long long o = blockIdx.x * (long long)blockDim.x + threadIdx.x; o < total;
          o += (long long)gridDim.x * blockDim.x) {
-        const int r = (int)(o & 127);
-        const int c = (int)((o >> 7) & 7);
-        long long rest = o >> 10;
+        const int wd = (int)(o % TILE_BLOCK_WORDS);
+        long long rest = o / TILE_BLOCK_WORDS;
         const int kb = (int)(rest % KB);
         rest /= KB;
         const int m = (int)(rest % MT);
         const int e = (int)(rest / MT);
-        const int f = tile_feature(m, r, Nw, swiglu != 0);
-        const int k0 = kb * 64 + 8 * c;
-        const uint32_t* src = w + ((long long)e * K + k0) * nw8 + (f >> 3);
-        const int sh = 4 * (f & 7);
         uint32_t out = 0;
+        if (wd < 1024) {
+            const int r = wd & 127, c = wd >> 7;
+            const int f = tile_feature(m, r, Nw, swiglu != 0);
+            const int k0 = kb * 64 + 8 * c;
+            const uint32_t* src = w + ((long long)e * K + k0) * nw8 + (f >> 3);
+            const int sh = 4 * (f & 7);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t nib = ((src[(long long)i * nw8] >> sh) & 15u) ^ 8u;     // offset binary
-            const int pos = (i & 1) ? 4 + (i >> 1) : (i >> 1);                    // 0,2,4,6 -> 0..3; 1,3,5,7 -> 4..7
-            out |= nib << (4 * pos);
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t nib = ((src[(long long)i * nw8] >> sh) & 15u) ^ 8u;     // offset binary
+                const int pos = (i & 1) ? 4 + (i >> 1) : (i >> 1);                    // 0,2,4,6 -> 0..3; 1,3,5,7 -> 4..7
+                out |= nib << (4 * pos);
+            }
+        } else {
+            const int r = 2 * (wd - 1024);
+            const bf16* srow = s + ((long long)e * G + (kb * 64) / gs) * Nw;
+            const uint32_t lo = bf16_bits(srow[tile_feature(m, r, Nw, swiglu != 0)]);
+            const uint32_t hi = bf16_bits(srow[tile_feature(m, r + 1, Nw, swiglu != 0)]);
+            out = lo | (hi << 16);
         }
-        tw[o] = out;
-    }
-}
-
-__global__ void __launch_bounds__(256) repack_scales_tiles_kernel(const bf16* __restrict__ s, bf16* __restrict__ ts,
-                                                                  int E, int G, int Nw, int swiglu) {
-    const int MT = Nw / 128;
-    const long long total = (long long)E * MT * G * 128;
-    for (long long o = blockIdx.x * (long long)blockDim.x + threadIdx.x; o < total;
-         o += (long long)gridDim.x * blockDim.x) {
-        const int r = (int)(o & 127);
-        long long rest = o >> 7;
-        const int g = (int)(rest % G);
-        rest /= G;
-        const int m = (int)(rest % MT);
-        const int e = (int)(rest / MT);
-        ts[o] = s[((long long)e * G + g) * Nw + tile_feature(m, r, Nw, swiglu != 0)];
+        t[o] = out;
     }
 }
 

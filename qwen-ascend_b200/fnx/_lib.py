@@ -32,13 +32,14 @@ SIGNATURES = {
     "fnx_router_topk": ([P, LL, P, P, P, P, I, I, I, P], I),
     "fnx_moe_permute_workspace": ([I, I], SZ),
     "fnx_moe_permute": ([P] * 5 + [I, I, P, SZ, P], I),
-    "fnx_moe_grouped_w4": ([P, LL, LL, P, I, P, P, P, P, LL] + [I] * 6 + [P], I),
-    "fnx_repack_w4_tiles": ([P] * 4 + [I] * 5 + [P], I),
+    "fnx_moe_grouped_w4": ([P, LL, LL, P, I, P, P, P, LL] + [I] * 5 + [P], I),
+    "fnx_w4_tiles_bytes": ([I] * 3, SZ),
+    "fnx_repack_w4_tiles": ([P] * 3 + [I] * 5 + [P], I),
     "fnx_w8a16_gemm": ([P] * 4 + [I] * 4 + [P], I),
     "fnx_bf16_gemm_nt": ([P, LL, P, P, LL, I, I, I, P], I),
     "fnx_moe_decode_workspace": ([I] * 5, SZ),
-    "fnx_moe_decode_w4": ([P] * 14 + [I] * 6 + [P, SZ, P], I),
-    "fnx_moe_decode_w4_noalloc": ([P] * 14 + [I] * 6 + [P], I),
+    "fnx_moe_decode_w4": ([P] * 10 + [I] * 5 + [P, SZ, P], I),
+    "fnx_moe_decode_w4_noalloc": ([P] * 10 + [I] * 5 + [P], I),
     "fnx_w4gemv_launch": ([P] * 7 + [I] * 5 + [P], I),
     "fnx_w4gemv_launch_layers": ([ctypes.POINTER(P)] * 4 + [I] * 6 + [P, P], I),
 }

@@ -24,30 +24,32 @@ EPI_PLAIN, EPI_SWIGLU_F32, EPI_SWIGLU_BF16 = 0, 1, 2
 DECODE_MAX_TOKENS = 16
 
 
+TILE_BLOCK_WORDS = 1088          # 1024 words of int4 + 128 bf16 scales per (tile, k-block)
+
+
 def repack_w4(w4, scales, swiglu):
-    """Expert-major int4pack ``[E, K, N/8]`` + bf16 scales ``[E, K/gs, N]`` -> the tile-major
-    layout the kernels stream (``fnx_repack_w4_tiles``): words ``[E, N/128, K/64, 8, 128]``
-    and scales ``[E, N/128, K/gs, 128]``.  ``swiglu`` orders the rows of a tile as gate/up
-    pairs (for the fused SwiGLU epilogue); otherwise rows are consecutive features.  Runs
-    once at load; the artifact layout itself is read unchanged."""
+    """Expert-major int4pack ``[E, K, N/8]`` + bf16 scales ``[E, K/gs, N]`` -> the tile blocks
+    the kernels stream (``fnx_repack_w4_tiles``): int32 ``[E, N/128, K/64, 1088]``, each block
+    the 8x128 words of one (feature tile, k-block) followed by the 128 rows' scales.
+    ``swiglu`` orders the rows of a tile as gate/up pairs (for the fused SwiGLU epilogue);
+    otherwise rows are consecutive features.  Runs once at load; the artifact layout itself
+    is read unchanged."""
     _lib.require_cuda(w4, scales)
     E, K, n8 = w4.shape
     N, G = n8 * 8, scales.shape[1]
-    tw = torch.empty(E, N // 128, K // 64, 8, 128, dtype=torch.int32, device=w4.device)
-    ts = torch.empty(E, N // 128, G, 128, dtype=BF16, device=w4.device)
-    rc = _lib.lib().fnx_repack_w4_tiles(w4.contiguous().data_ptr(), scales.contiguous().data_ptr(), tw.data_ptr(),
-                                        ts.data_ptr(), E, K, N, K // G, 1 if swiglu else 0, _lib.stream(w4.device))
+    t = torch.empty(E, N // 128, K // 64, TILE_BLOCK_WORDS, dtype=torch.int32, device=w4.device)
+    rc = _lib.lib().fnx_repack_w4_tiles(w4.contiguous().data_ptr(), scales.contiguous().data_ptr(), t.data_ptr(),
+                                        E, K, N, K // G, 1 if swiglu else 0, _lib.stream(w4.device))
     _lib.check(rc, "W4 tile repack")
-    return tw, ts
+    return t
 
 
-def _grouped_w4(act, w4, scales, ends, out, *, E, M, K, Nw, gs, epilogue, row_index=None, index_div=1):
-    """Grouped GEMM over tile-major weights ``w4``/``scales`` (see ``repack_w4``; the SwiGLU
-    epilogues need the SwiGLU row order)."""
+def _grouped_w4(act, tiles, ends, out, *, E, M, K, Nw, epilogue, row_index=None, index_div=1):
+    """Grouped GEMM over the tile blocks of ``repack_w4`` (the SwiGLU epilogues need the
+    SwiGLU row order)."""
     rc = _lib.lib().fnx_moe_grouped_w4(act.data_ptr(), act.stride(0), act.shape[0], _lib.ptr(row_index), index_div,
-                                       w4.data_ptr(),
-                                       scales.data_ptr(), _lib.ptr(ends), out.data_ptr(), out.stride(0), E, M, K, Nw,
-                                       gs, epilogue, _lib.stream(act.device))
+                                       tiles.data_ptr(), _lib.ptr(ends), out.data_ptr(), out.stride(0), E, M, K, Nw,
+                                       epilogue, _lib.stream(act.device))
     _lib.check(rc, "grouped W4A16 GEMM")
     return out
 
@@ -88,7 +90,7 @@ class ExpW4:
         return o
 
     def tiles(self):
-        """The tile-major copy the GEMM reads (built once, then cached)."""
+        """The tile blocks the GEMM reads (built once, then cached)."""
         t = getattr(self, "_tiles", None)
         if t is None:
             t = repack_w4(self.w4, self._scales, swiglu=False)
@@ -96,35 +98,32 @@ class ExpW4:
         return t
 
     def _selected(self, ids):
-        tw, ts = self.tiles()
-        return tw.index_select(0, ids).contiguous(), ts.index_select(0, ids).contiguous()
+        return self.tiles().index_select(0, ids).contiguous()
 
     def apply(self, x, ids):
         """x ``[M, K]`` bf16, ids ``[k]`` -> ``[M, k*N]``: every row times every selected expert."""
         M, k = x.shape[0], ids.numel()
-        w, s = self._selected(ids)
+        w = self._selected(ids)
         rows = torch.arange(k * M, device=x.device, dtype=torch.int64) % M
         ends = torch.arange(1, k + 1, device=x.device, dtype=torch.int64) * M
         out = torch.empty(k * M, self.N, dtype=BF16, device=x.device)
-        _grouped_w4(x.to(BF16).contiguous(), w, s, ends, out, E=k, M=k * M, K=self.K, Nw=self.N, gs=self.gs,
+        _grouped_w4(x.to(BF16).contiguous(), w, ends, out, E=k, M=k * M, K=self.K, Nw=self.N,
                     epilogue=EPI_PLAIN, row_index=rows)
         return out.view(k, M, self.N).transpose(0, 1).reshape(M, k * self.N)
 
     def apply_diag(self, x, ids):
         """Row j of x uses expert ids[j] -> ``[k, N]`` (the diagonal of the Cartesian product)."""
         k = x.shape[0]
-        w, s = self._selected(ids)
+        w = self._selected(ids)
         ends = torch.arange(1, k + 1, device=x.device, dtype=torch.int64)
         out = torch.empty(k, self.N, dtype=BF16, device=x.device)
-        return _grouped_w4(x.to(BF16).contiguous(), w, s, ends, out, E=k, M=k, K=self.K, Nw=self.N, gs=self.gs,
-                           epilogue=EPI_PLAIN)
+        return _grouped_w4(x.to(BF16).contiguous(), w, ends, out, E=k, M=k, K=self.K, Nw=self.N, epilogue=EPI_PLAIN)
 
     def apply_grouped(self, x, group_ends, host_ends=None):
         """Rows sorted by expert (cumulative ``group_ends`` over all E experts)."""
         out = torch.empty(x.shape[0], self.N, dtype=BF16, device=x.device)
-        tw, ts = self.tiles()
-        return _grouped_w4(x.to(BF16).contiguous(), tw, ts, group_ends.contiguous(), out, E=self.E,
-                           M=x.shape[0], K=self.K, Nw=self.N, gs=self.gs, epilogue=EPI_PLAIN)
+        return _grouped_w4(x.to(BF16).contiguous(), self.tiles(), group_ends.contiguous(), out, E=self.E,
+                           M=x.shape[0], K=self.K, Nw=self.N, epilogue=EPI_PLAIN)
 
 
 class DenseW8:
@@ -177,7 +176,7 @@ class DenseW8:
 
 class MoELayer:
     """One W4A16 MoE layer: routed experts (expert-major int4pack + bf16 group scales, kept
-    as the tile-major copies of ``repack_w4``), an always-on W4 shared expert with a sigmoid
+    as the tile blocks of ``repack_w4``), an always-on W4 shared expert with a sigmoid
     gate, and a bf16 router.
 
     ``router_cat`` concatenates the router rows and the shared-expert gate row into one
@@ -189,11 +188,11 @@ class MoELayer:
         _lib.require_cuda(gu_w4, dn_w4, gate_w, sh_gu_w4, sh_dn_w4)
         self.E, self.H = gate_w.shape
         self.I = gu_w4.shape[2] * 8 // 2
-        # tile-major copies (the artifact tensors are not kept)
-        self.gu_tw, self.gu_ts = repack_w4(gu_w4, gu_scales, swiglu=True)
-        self.dn_tw, self.dn_ts = repack_w4(dn_w4, dn_scales, swiglu=False)
-        self.sh_gu_tw, self.sh_gu_ts = repack_w4(sh_gu_w4[None], sh_gu_scales[None], swiglu=True)
-        self.sh_dn_tw, self.sh_dn_ts = repack_w4(sh_dn_w4[None], sh_dn_scales[None], swiglu=False)
+        # tile blocks (the artifact tensors are not kept)
+        self.gu_t = repack_w4(gu_w4, gu_scales, swiglu=True)
+        self.dn_t = repack_w4(dn_w4, dn_scales, swiglu=False)
+        self.sh_gu_t = repack_w4(sh_gu_w4[None], sh_gu_scales[None], swiglu=True)
+        self.sh_dn_t = repack_w4(sh_dn_w4[None], sh_dn_scales[None], swiglu=False)
         self.k, self.gs = k, gs
         R = self.E + 1
         self.R = R
@@ -211,9 +210,8 @@ class MoELayer:
                    t["sh_gu_scales"], t["sh_dn_w4"], t["sh_dn_scales"], t["sh_gate"], shape.k, shape.gs, bias=bias)
 
     def weight_bytes(self):
-        return sum(t.numel() * t.element_size() for t in (self.gu_tw, self.gu_ts, self.dn_tw, self.dn_ts,
-                                                           self.router_cat, self.sh_gu_tw, self.sh_gu_ts,
-                                                           self.sh_dn_tw, self.sh_dn_ts))
+        return sum(t.numel() * t.element_size()
+                   for t in (self.gu_t, self.dn_t, self.router_cat, self.sh_gu_t, self.sh_dn_t))
 
     # ---------------------------------------------------------------- routing
     def logits(self, x):
@@ -268,17 +266,14 @@ class MoELayer:
         w, idx, wf = self.topk(logits)
         order, inverse, ends = self.permute(idx)
         act = torch.empty(T * k, I, dtype=BF16, device=dev)
-        _grouped_w4(x, self.gu_tw, self.gu_ts, ends, act, E=E, M=T * k, K=H, Nw=2 * I, gs=self.gs,
-                    epilogue=EPI_SWIGLU_F32, row_index=order, index_div=k)
+        _grouped_w4(x, self.gu_t, ends, act, E=E, M=T * k, K=H, Nw=2 * I, epilogue=EPI_SWIGLU_F32,
+                    row_index=order, index_div=k)
         yd = torch.empty(T * k, H, dtype=BF16, device=dev)
-        _grouped_w4(act, self.dn_tw, self.dn_ts, ends, yd, E=E, M=T * k, K=I, Nw=H, gs=self.gs,
-                    epilogue=EPI_PLAIN)
+        _grouped_w4(act, self.dn_t, ends, yd, E=E, M=T * k, K=I, Nw=H, epilogue=EPI_PLAIN)
         sh_act = torch.empty(T, I, dtype=BF16, device=dev)
-        _grouped_w4(x, self.sh_gu_tw, self.sh_gu_ts, None, sh_act, E=1, M=T, K=H, Nw=2 * I, gs=self.gs,
-                    epilogue=EPI_SWIGLU_BF16)
+        _grouped_w4(x, self.sh_gu_t, None, sh_act, E=1, M=T, K=H, Nw=2 * I, epilogue=EPI_SWIGLU_BF16)
         sh = torch.empty(T, H, dtype=BF16, device=dev)
-        _grouped_w4(sh_act, self.sh_dn_tw, self.sh_dn_ts, None, sh, E=1, M=T, K=I, Nw=H, gs=self.gs,
-                    epilogue=EPI_PLAIN)
+        _grouped_w4(sh_act, self.sh_dn_t, None, sh, E=1, M=T, K=I, Nw=H, epilogue=EPI_PLAIN)
         out = torch.empty(T, H, dtype=BF16, device=dev)
         gate = logits[:, E:E + 1]
         rc = _lib.lib().fnx_moe_combine(yd.data_ptr(), wf.data_ptr(), inverse.data_ptr(), sh.data_ptr(),
@@ -307,10 +302,8 @@ class MoELayer:
         idx_out = torch.empty(M, self.k, dtype=torch.int64, device=dev) if idx_out is None else idx_out
         ws = self.decode_workspace(M, dev)
         rc = _lib.lib().fnx_moe_decode_w4(
-            x.data_ptr(), self.router_cat.data_ptr(), self.gu_tw.data_ptr(), self.gu_ts.data_ptr(),
-            self.dn_tw.data_ptr(), self.dn_ts.data_ptr(), self.sh_gu_tw.data_ptr(), self.sh_gu_ts.data_ptr(),
-            self.sh_dn_tw.data_ptr(), self.sh_dn_ts.data_ptr(), _lib.ptr(self.bias), out.data_ptr(), w_out.data_ptr(),
-            idx_out.data_ptr(), M, self.H, self.I, self.E, self.k, self.gs, ws.data_ptr(), ws.numel(),
-            _lib.stream(dev))
+            x.data_ptr(), self.router_cat.data_ptr(), self.gu_t.data_ptr(), self.dn_t.data_ptr(),
+            self.sh_gu_t.data_ptr(), self.sh_dn_t.data_ptr(), _lib.ptr(self.bias), out.data_ptr(), w_out.data_ptr(),
+            idx_out.data_ptr(), M, self.H, self.I, self.E, self.k, ws.data_ptr(), ws.numel(), _lib.stream(dev))
         _lib.check(rc, "MoE decode")
         return out, w_out, idx_out

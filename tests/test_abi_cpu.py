@@ -49,17 +49,19 @@ def test_host_side_rejections(lib):
     assert lib.fnx_router_topk(None, 100, None, None, None, None, 4, 512, 10, None) == -1
     assert lib.fnx_moe_permute(None, None, None, None, None, 10, 5000, None, 0, None) == -1
     assert lib.fnx_moe_permute(None, None, None, None, None, 10, 8, None, 0, None) == -5
-    # grouped GEMM shape rules: K % 64, gs % 64, Nw % 128
+    # grouped GEMM shape rules: K % 64, Nw % 128, epilogue in 0..2, act rows >= M without an index
     g = lib.fnx_moe_grouped_w4
-    assert g(None, 2048, 64, None, 1, None, None, None, None, 1024, 8, 64, 100, 1024, 128, 0, None) == -1
-    assert g(None, 2048, 64, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1000, 128, 0, None) == -2
-    assert g(None, 2048, 64, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1024, 32, 0, None) == -2
-    assert g(None, 2048, 64, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1024, 128, 3, None) == -1
-    assert g(None, 2048, 10, None, 1, None, None, None, None, 1024, 8, 64, 2048, 1024, 128, 0, None) == -1  # rows < M
+    assert g(None, 2048, 64, None, 1, None, None, None, 1024, 8, 64, 100, 1024, 0, None) == -1
+    assert g(None, 2048, 64, None, 1, None, None, None, 1024, 8, 64, 2048, 1000, 0, None) == -2
+    assert g(None, 2048, 64, None, 1, None, None, None, 1024, 8, 64, 2048, 1024, 3, None) == -1
+    assert g(None, 2048, 10, None, 1, None, None, None, 1024, 8, 64, 2048, 1024, 0, None) == -1  # rows < M
+    assert lib.fnx_repack_w4_tiles(None, None, None, 8, 2048, 1024, 96, 0, None) == -1          # gs % 64
+    assert lib.fnx_w4_tiles_bytes(512, 2048, 1024) == 512 * 8 * 32 * 4352
+    assert lib.fnx_w4_tiles_bytes(512, 2048, 1000) == 0
     assert lib.fnx_w4gemv_launch(None, None, None, None, None, None, None, 1024, 100, 10, 20, 2, None) == -1
     assert lib.fnx_w4gemv_launch(None, None, None, None, None, None, None, 1024, 2048, 10, 20, 3, None) == -1
-    assert lib.fnx_moe_decode_w4(*([None] * 14), 17, 2048, 512, 512, 10, 128, None, 0, None) == -1
-    assert lib.fnx_moe_decode_w4(*([None] * 14), 1, 2048, 512, 512, 10, 128, None, 0, None) == -5
+    assert lib.fnx_moe_decode_w4(*([None] * 10), 17, 2048, 512, 512, 10, None, 0, None) == -1
+    assert lib.fnx_moe_decode_w4(*([None] * 10), 1, 2048, 512, 512, 10, None, 0, None) == -5
 
 
 def test_workspace_sizes(lib):

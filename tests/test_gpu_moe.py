@@ -5,7 +5,7 @@ import pytest
 import torch
 
 import oracle as O
-from fnx import synth
+from fnx import _lib, synth
 
 pytestmark = pytest.mark.gpu
 BF16 = torch.bfloat16
@@ -39,7 +39,7 @@ def _w4(E, K, N, gs, seed):
 def test_grouped_w4(E, counts, K, N, gs, epi):
     from fnx.engine import _grouped_w4, repack_w4
     w, s = _w4(E, K, N, gs, seed=E * 7 + K)
-    tw, ts = repack_w4(w.to(DEV), s.to(DEV), swiglu=epi != 0)
+    t = repack_w4(w.to(DEV), s.to(DEV), swiglu=epi != 0)
     M = sum(counts)
     g = torch.Generator().manual_seed(M)
     src = torch.randn(M + 5, K, generator=g).to(BF16)
@@ -47,7 +47,7 @@ def test_grouped_w4(E, counts, K, N, gs, epi):
     ends = torch.tensor(np.cumsum(counts), dtype=torch.int64)
     nout = N if epi == 0 else N // 2
     out = torch.full((M, nout), float("nan"), dtype=BF16, device=DEV)
-    _grouped_w4(src.to(DEV), tw, ts, ends.to(DEV), out, E=E, M=M, K=K, Nw=N, gs=gs, epilogue=epi,
+    _grouped_w4(src.to(DEV), t, ends.to(DEV), out, E=E, M=M, K=K, Nw=N, epilogue=epi,
                 row_index=(perm * 2).to(DEV), index_div=2)
     rows = src[perm]
     ref = O.grouped_matmul(rows, ends, lambda e: O.deq_w4(O.unpack_int4pack(w[e]), s[e], gs))
@@ -60,11 +60,18 @@ def test_grouped_w4(E, counts, K, N, gs, epi):
     assert rep["exact_fraction"] > 0.9, rep
 
 
-def tile_unpack(tw, ts, K, N, swiglu):
-    """CPU decode of the tile-major layout back to int8 q [E, K, N] and bf16 scales [E, G, N]."""
-    E, MT, KB = tw.shape[:3]
-    G = ts.shape[2]
-    words = tw.to(torch.int64) & 0xFFFFFFFF                          # [E, MT, KB, 8, 128]
+def tile_unpack(t, K, N, gs, swiglu):
+    """CPU decode of the tile blocks back to int8 q [E, K, N] and bf16 scales [E, G, N]; also
+    checks that every k-block of a scale group carries the group's scales."""
+    E, MT, KB = t.shape[:3]
+    G = K // gs
+    words = (t[..., :1024].to(torch.int64) & 0xFFFFFFFF).reshape(E, MT, KB, 8, 128)
+    bs = t[..., 1024:].contiguous().view(torch.int16).view(BF16)     # [E, MT, KB, 128]
+    per = gs // 64
+    for g in range(G):
+        for j in range(1, per):
+            assert torch.equal(bs[:, :, g * per + j].view(torch.int16), bs[:, :, g * per].view(torch.int16))
+    ts = bs[:, :, ::per]                                             # [E, MT, G, 128]
     pos = torch.tensor([0, 4, 1, 5, 2, 6, 3, 7])                     # nibble position of k-offset i
     nib = torch.stack([(words >> (4 * int(pos[i]))) & 15 for i in range(8)], -1) - 8   # [E,MT,KB,8c,128r,8i]
     q_tile = nib.permute(0, 1, 4, 2, 3, 5).reshape(E, MT, 128, K)    # [E, MT, r, k]
@@ -81,12 +88,13 @@ def tile_unpack(tw, ts, K, N, swiglu):
 @pytest.mark.parametrize("swiglu", [False, True])
 def test_repack_layout(swiglu):
     from fnx.engine import repack_w4
-    E, K, N, gs = 3, 256, 384, 64
-    w, s = _w4(E, K, N, gs, seed=77)
-    tw, ts = repack_w4(w.to(DEV), s.to(DEV), swiglu=swiglu)
-    q, sc = tile_unpack(tw.cpu(), ts.cpu(), K, N, swiglu)
-    assert torch.equal(q, O.unpack_int4pack(w))
-    assert torch.equal(sc.view(torch.int16), s.view(torch.int16))
+    for E, K, N, gs in ((3, 256, 384, 64), (2, 512, 256, 128)):
+        w, s = _w4(E, K, N, gs, seed=77)
+        t = repack_w4(w.to(DEV), s.to(DEV), swiglu=swiglu)
+        assert t.numel() * 4 == _lib.lib().fnx_w4_tiles_bytes(E, K, N)
+        q, sc = tile_unpack(t.cpu(), K, N, gs, swiglu)
+        assert torch.equal(q, O.unpack_int4pack(w))
+        assert torch.equal(sc.view(torch.int16), s.view(torch.int16))
 
 
 def test_bf16_and_w8_gemm(golden):

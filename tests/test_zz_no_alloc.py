@@ -29,10 +29,9 @@ def test_decode_noalloc_matches_workspace_entry_point():
         w = torch.empty_like(ref_w)
         idx = torch.empty_like(ref_idx)
         rc = lib.fnx_moe_decode_w4_noalloc(
-            x.data_ptr(), layer.router_cat.data_ptr(), layer.gu_tw.data_ptr(), layer.gu_ts.data_ptr(),
-            layer.dn_tw.data_ptr(), layer.dn_ts.data_ptr(), layer.sh_gu_tw.data_ptr(), layer.sh_gu_ts.data_ptr(),
-            layer.sh_dn_tw.data_ptr(), layer.sh_dn_ts.data_ptr(), None, out.data_ptr(), w.data_ptr(), idx.data_ptr(),
-            M, shape.H, shape.I, shape.E, shape.k, shape.gs, _lib.stream(dev))
+            x.data_ptr(), layer.router_cat.data_ptr(), layer.gu_t.data_ptr(), layer.dn_t.data_ptr(),
+            layer.sh_gu_t.data_ptr(), layer.sh_dn_t.data_ptr(), None, out.data_ptr(), w.data_ptr(), idx.data_ptr(),
+            M, shape.H, shape.I, shape.E, shape.k, _lib.stream(dev))
         assert rc == 0
         torch.cuda.synchronize()
         assert torch.equal(idx, ref_idx)
@@ -42,5 +41,5 @@ def test_decode_noalloc_matches_workspace_entry_point():
     # a shape whose scratch exceeds the static array is rejected before any launch
     big = lib.fnx_moe_decode_workspace(16, 8192, 4096, 2048, 32)
     assert big > 4 << 20
-    rc = lib.fnx_moe_decode_w4_noalloc(*([None] * 14), 16, 8192, 4096, 2048, 32, 128, None)
+    rc = lib.fnx_moe_decode_w4_noalloc(*([None] * 10), 16, 8192, 4096, 2048, 32, None)
     assert rc == -5
