@@ -6,12 +6,14 @@
 // negative FNX_E* code when an argument is rejected before launch.  Declarations and
 // the reference interface each one replaces are in include/fnx_b200.h.
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "fnx_common.cuh"
 #include "kernels_combine.cuh"
 #include "kernels_decode.cuh"
 #include "kernels_gemm.cuh"
+#include "kernels_gemm_pair.cuh"
 #include "kernels_route.cuh"
 #include "kernels_w4gemv.cuh"
 
@@ -155,7 +157,54 @@ int gemm_launch_t(GemmParams& p, cudaStream_t st) {
     return launch_rc();
 }
 
+// CTA-pair W4 kernel: clusters of two CTAs, as many clusters as fit at once (the tile
+// schedule is persistent and static, so every launched cluster must be resident).
+template <int EPI>
+int gemm_pair_launch_t(GemmParams& p, cudaStream_t st) {
+    const size_t smem = grouped_gemm_pair_smem_bytes();
+    static int clusters = 0;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(G_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (!clusters) {
+        if (cudaFuncSetAttribute(grouped_gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem) != cudaSuccess)
+            return FNX_ELAUNCH;
+        cfg.gridDim = dim3(2 * (num_sms() / 2));
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, grouped_gemm_pair_kernel<EPI>, &cfg) != cudaSuccess || n < 1)
+            return FNX_ELAUNCH;
+        clusters = n < num_sms() / 2 ? n : num_sms() / 2;
+    }
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.stream = st;
+    if (cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel<EPI>, p) != cudaSuccess) return FNX_ELAUNCH;
+    return launch_rc();
+}
+
+// FNX_GEMM_PAIR=0 selects the single-CTA W4 kernel (for comparisons).
+bool pair_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("FNX_GEMM_PAIR");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
+}
+
 int gemm_launch(int mode, int epi, GemmParams& p, cudaStream_t st) {
+    if (mode == GEMM_W4 && p.m_tiles % 2 == 0 && p.K % (G_BK * P_KS) == 0 && pair_enabled()) {
+        if (epi == EPI_PLAIN) return gemm_pair_launch_t<EPI_PLAIN>(p, st);
+        if (epi == EPI_SWIGLU_F32) return gemm_pair_launch_t<EPI_SWIGLU_F32>(p, st);
+        return gemm_pair_launch_t<EPI_SWIGLU_BF16>(p, st);
+    }
     if (mode == GEMM_W4) {
         if (epi == EPI_PLAIN) return gemm_launch_t<GEMM_W4, EPI_PLAIN>(p, st);
         if (epi == EPI_SWIGLU_F32) return gemm_launch_t<GEMM_W4, EPI_SWIGLU_F32>(p, st);

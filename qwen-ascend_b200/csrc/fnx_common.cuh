@@ -150,13 +150,23 @@ FNX_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait on an mbarrier phase.  Returns false (and flags the error) on timeout.
+// Failed polls back off for FNX_WAIT_SLEEP_NS: a barrier poll is a shared-memory
+// operation, and warps polling without pause queue ahead of the MMA warp's commits.
+#ifndef FNX_WAIT_SLEEP_NS
+#define FNX_WAIT_SLEEP_NS 64
+#endif
+FNX_DEV void wait_backoff() {
+    if (FNX_WAIT_SLEEP_NS > 0) __nanosleep(FNX_WAIT_SLEEP_NS);
+}
 FNX_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = fnx_globaltimer();
     while (true) {
 #pragma unroll 1
-        for (int i = 0; i < 32; ++i)
+        for (int i = 0; i < 32; ++i) {
+            wait_backoff();
             if (mbar_try_wait(bar, parity)) return true;
+        }
         if (fnx_globaltimer() - t0 > FNX_WAIT_NS) {
             fnx_flag_error(FNX_DEVERR_TIMEOUT);
             return false;
@@ -223,6 +233,18 @@ FNX_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.c
 FNX_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
+// CTA-pair (cta_group::2) forms: one warp in each CTA of the pair allocates the same
+// columns in both CTAs' tensor memory; MMAs issued by the pair's rank-0 CTA use both.
+FNX_DEV void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+}
+FNX_DEV void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+FNX_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
 FNX_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 FNX_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -251,6 +273,89 @@ FNX_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
         : "memory");
 }
 FNX_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D (+)= A * B^T over a CTA pair (M = 256: A rows 0..127 from this CTA's tensor memory,
+// 128..255 from the peer's at the same address; each CTA holds N/2 rows of B at the same
+// shared-memory address; D lands in both CTAs' tensor memory).  Issued by rank 0 only.
+FNX_DEV void umma_bf16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                               uint32_t accumulate) {
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}"
+                 ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// Arrive on the mbarrier at this shared-memory offset in every CTA of cta_mask once the
+// pair MMAs issued so far complete.
+FNX_DEV void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(smem_u32(bar)), "h"(cta_mask) : "memory");
+}
+
+// ------------------------------------------------------------------ clusters
+FNX_DEV uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+FNX_DEV uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+FNX_DEV uint32_t num_clusters_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// All threads of every CTA in the cluster (release / acquire).
+FNX_DEV void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared-memory address of `p` in CTA `rank` of this cluster.
+FNX_DEV uint32_t mapa_rank(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+FNX_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Remote arrival without the cluster-scope release.  For announcing data this thread did
+// not write and that is already complete in shared / tensor memory (observed through a
+// local mbarrier): the release would only wait for this thread's own outstanding memory
+// operations, which costs ~860 cycles per call on the relay path.
+FNX_DEV void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+FNX_DEV bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+                 " selp.u32 %0, 1, 0, p;\n}" : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+FNX_DEV bool mbar_test_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+                 " selp.u32 %0, 1, 0, p;\n}" : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait on a phase completed by arrivals from another SM (remote arrives, pair
+// MMA commits).  Polls with the non-suspending test_wait: a thread suspended in try_wait
+// is woken late when the completing arrival comes from another SM.
+FNX_DEV bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+    if (mbar_test_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = fnx_globaltimer();
+    while (true) {
+#pragma unroll 1
+        for (int i = 0; i < 64; ++i) {
+            wait_backoff();
+            if (mbar_test_wait_cluster(bar, parity)) return true;
+        }
+        if (fnx_globaltimer() - t0 > FNX_WAIT_NS) {
+            fnx_flag_error(FNX_DEVERR_TIMEOUT);
+            return false;
+        }
+    }
+}
 
 // Named CTA barriers (ids 1..15; 0 is __syncthreads).  Executed by whole warps.
 FNX_DEV void named_bar_sync(int id, int threads) {

@@ -50,6 +50,7 @@ constexpr int G_MAX_STAGES = 8;
 // hundred cycles however small it is, so 4 KB copies cap the stream near 4.5 TB/s.
 constexpr int G_OPK = 4;
 constexpr int G_R_OPS = 4;
+constexpr int G_MAX_R_OPS = 8;
 constexpr int G_THREADS = 608;    // 19 warps
 constexpr int G_LOADERS = 4;       // B loader warps: 0, 16, 17, 18
 constexpr int G_BAR_FULL = 1;      // named barrier: waiter -> MMA warp, "stage j is full"
@@ -89,7 +90,8 @@ struct GemmParams {
 
 struct GemmSmem {
     uint64_t a_full[G_MAX_STAGES], b_full[G_MAX_STAGES], empty[G_MAX_STAGES];
-    uint64_t raw_full[G_R_OPS], raw_empty[G_R_OPS];
+    uint64_t raw_full[G_MAX_R_OPS], raw_empty[G_MAX_R_OPS];
+    uint64_t peer_full[G_MAX_STAGES];   // CTA-pair kernel: the peer's stage is full (on rank 0)
     uint64_t acc_full[2], acc_empty[2], final_bar;
     uint32_t tmem_base;
     volatile int abort;
