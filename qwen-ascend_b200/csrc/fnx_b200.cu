@@ -200,7 +200,8 @@ bool pair_enabled() {
 }
 
 int gemm_launch(int mode, int epi, GemmParams& p, cudaStream_t st) {
-    if (mode == GEMM_W4 && p.m_tiles % 2 == 0 && p.K % (G_BK * P_KS) == 0 && pair_enabled()) {
+    if (mode == GEMM_W4 && p.m_tiles % 2 == 0 && p.K % (G_BK * P_KS) == 0 && p.ld_out % 8 == 0 && aligned16(p.out) &&
+        pair_enabled()) {
         if (epi == EPI_PLAIN) return gemm_pair_launch_t<EPI_PLAIN>(p, st);
         if (epi == EPI_SWIGLU_F32) return gemm_pair_launch_t<EPI_SWIGLU_F32>(p, st);
         return gemm_pair_launch_t<EPI_SWIGLU_BF16>(p, st);

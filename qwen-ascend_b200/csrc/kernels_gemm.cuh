@@ -240,6 +240,58 @@ FNX_DEV void epilogue_chunk(const GemmParams& p, const TileInfo& ti, int r, int 
     }
 }
 
+// Staged form for tile-ordered rows (the W4 kernels): the warp's 32 accumulator lanes x 16
+// tokens go through a 1 KB shared buffer so that global stores are 16-byte vectors along
+// the feature dimension (one token row segment per 4 or 2 lanes) instead of 2-byte
+// stores strided by the output row.  Needs ld_out % 8 == 0 and a 16-byte aligned out.
+template <int EPI>
+FNX_DEV void epilogue_chunk_staged(const GemmParams& p, const TileInfo& ti, int w4, int n0, const uint32_t (&v)[16],
+                                   uint16_t* stage) {
+    const int lane = threadIdx.x & 31;
+    if (EPI == EPI_PLAIN) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) stage[i * 32 + lane] = (uint16_t)bf16_bits(f2bf(__uint_as_float(v[i])));
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int c = q * 32 + lane, tok = c >> 2, part = c & 3;
+            if (n0 + tok < ti.nrows) {
+                const uint4 val = *reinterpret_cast<const uint4*>(stage + tok * 32 + part * 8);
+                *reinterpret_cast<uint4*>(p.out + (long long)(ti.row0 + n0 + tok) * p.ld_out + ti.m * G_BM + w4 * 32 +
+                                          part * 8) = val;
+            }
+        }
+    } else {
+        const bool odd = lane & 1;
+        float g[8], u[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float a0 = round_bf(__uint_as_float(v[i]));
+            const float a1 = round_bf(__uint_as_float(v[8 + i]));
+            const float recv = __shfl_xor_sync(0xffffffffu, odd ? a0 : a1, 1);
+            const float mine = odd ? a1 : a0;
+            g[i] = odd ? recv : mine;
+            u[i] = odd ? mine : recv;
+        }
+        const int nb = odd ? 8 : 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float a;
+            if (EPI == EPI_SWIGLU_F32) a = __fmul_rn(silu_f32(g[i]), u[i]);
+            else a = __fmul_rn(round_bf(silu_f32(g[i])), u[i]);
+            stage[(nb + i) * 16 + (lane >> 1)] = (uint16_t)bf16_bits(f2bf(a));
+        }
+        __syncwarp();
+        const int tok = lane >> 1, part = lane & 1;
+        if (n0 + tok < ti.nrows) {
+            const uint4 val = *reinterpret_cast<const uint4*>(stage + tok * 16 + part * 8);
+            *reinterpret_cast<uint4*>(p.out + (long long)(ti.row0 + n0 + tok) * p.ld_out + ti.m * 64 + w4 * 16 +
+                                      part * 8) = val;
+        }
+    }
+    __syncwarp();
+}
+
 // ------------------------------------------------------------------ the kernel
 template <int MODE, int EPI>
 __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid_constant__ GemmParams p) {

@@ -66,6 +66,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
     uint8_t* b_tiles = base;
     uint8_t* raw_tiles = b_tiles + P_STAGES * P_B_BYTES;
     GemmSmem& S = *reinterpret_cast<GemmSmem*>(raw_tiles + P_R_OPS * G_OPK * G_RAW_BYTES);
+    uint16_t* epi_stage = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(&S) + ((sizeof(GemmSmem) + 15) & ~15));
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t rank = cluster_rank();
@@ -316,19 +317,19 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
             const int ab = tcount & 1;
             if (!mbar_wait_cluster(&S.acc_full[ab], (tcount >> 1) & 1)) { S.abort = 1; break; }
             tc_fence_after();
-            const int r = e4 * 32 + lane;
             const int npad = (ti.nrows + 15) & ~15;
             for (int n0 = 0; n0 < npad; n0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem + ((uint32_t)(e4 * 32) << 16) + ab * G_BN + n0, v);
                 tmem_ld_wait();
-                epilogue_chunk<EPI, false>(p, ti, r, n0, v);
+                epilogue_chunk_staged<EPI>(p, ti, e4, n0, v, epi_stage + e4 * 512);
             }
             tc_fence_before();
             __syncwarp();
+            // the accumulator reads completed (tcgen05.wait::ld): a relaxed arrival suffices
             if (lane == 0) {
                 if (rank == 0) mbar_arrive(&S.acc_empty[ab]);
-                else mbar_arrive_remote(mapa_rank(&S.acc_empty[ab], 0));
+                else mbar_arrive_remote_relaxed(mapa_rank(&S.acc_empty[ab], 0));
             }
         }
     } else if (warp >= 8) {
@@ -384,7 +385,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
 }
 
 inline size_t grouped_gemm_pair_smem_bytes() {
-    return 1024 + (size_t)P_STAGES * P_B_BYTES + (size_t)P_R_OPS * G_OPK * G_RAW_BYTES + sizeof(GemmSmem);
+    return 1024 + (size_t)P_STAGES * P_B_BYTES + (size_t)P_R_OPS * G_OPK * G_RAW_BYTES +
+           ((sizeof(GemmSmem) + 15) & ~(size_t)15) + 4 * 512 * sizeof(uint16_t);
 }
 
 }  // namespace fnx
