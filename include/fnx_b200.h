@@ -100,7 +100,9 @@ int fnx_repack_w4_tiles(const void* w4, const void* scales, void* tiles, int E, 
  * (swiglu=1 for epilogues 1 and 2); ends NULL means one group of M rows.
  * epilogue 0: out bf16 [M, Nw];  1: SwiGLU of gate = features [0,Nw/2), up = [Nw/2,Nw)
  * in fp32 on bf16-rounded inputs -> out [M, Nw/2];  2: the shared expert's SwiGLU
- * bf16(bf16(silu(g)) * u).  K % 64 == 0, Nw % 128 == 0. */
+ * bf16(bf16(silu(g)) * u);  3: epilogue 1 for experts 0..E-2 and epilogue 2 for expert E-1
+ * (the shared expert appended to the routed experts, run in the same launch).
+ * K % 64 == 0, Nw % 128 == 0. */
 int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_rows, const void* row_index, int index_div,
                        const void* tiles, const void* ends, void* out, long long ld_out, int E, int M, int K, int Nw,
                        int epilogue, void* stream);

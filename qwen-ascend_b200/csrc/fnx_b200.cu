@@ -204,11 +204,13 @@ int gemm_launch(int mode, int epi, GemmParams& p, cudaStream_t st) {
         pair_enabled()) {
         if (epi == EPI_PLAIN) return gemm_pair_launch_t<EPI_PLAIN>(p, st);
         if (epi == EPI_SWIGLU_F32) return gemm_pair_launch_t<EPI_SWIGLU_F32>(p, st);
+        if (epi == EPI_SWIGLU_MIXED) return gemm_pair_launch_t<EPI_SWIGLU_MIXED>(p, st);
         return gemm_pair_launch_t<EPI_SWIGLU_BF16>(p, st);
     }
     if (mode == GEMM_W4) {
         if (epi == EPI_PLAIN) return gemm_launch_t<GEMM_W4, EPI_PLAIN>(p, st);
         if (epi == EPI_SWIGLU_F32) return gemm_launch_t<GEMM_W4, EPI_SWIGLU_F32>(p, st);
+        if (epi == EPI_SWIGLU_MIXED) return gemm_launch_t<GEMM_W4, EPI_SWIGLU_MIXED>(p, st);
         return gemm_launch_t<GEMM_W4, EPI_SWIGLU_BF16>(p, st);
     }
     if (mode == GEMM_W8) return gemm_launch_t<GEMM_W8, EPI_PLAIN>(p, st);
@@ -356,7 +358,7 @@ FNX_API int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_
     if (act_rows < 0 || act_rows > 0x7fffffffLL || (!row_index && act_rows < M)) return FNX_EARG;
     p.w = tiles; p.ends = (const int64_t*)ends; p.out = (bf16*)out; p.ld_out = ld_out;
     p.E = E; p.M = M; p.K = K; p.Nw = Nw; p.gs = 0;
-    if (epilogue < 0 || epilogue > 2) return FNX_EARG;
+    if (epilogue < 0 || epilogue > 3) return FNX_EARG;
     p.m_tiles = epilogue == EPI_PLAIN ? Nw / G_BM : (Nw / 2) / 64;
     const int rc = gemm_check(GEMM_W4, epilogue, p);
     if (rc) return rc;

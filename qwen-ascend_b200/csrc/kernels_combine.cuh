@@ -126,24 +126,42 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const bf16* __restrict
         float acc[VEC ? 8 : 1];
 #pragma unroll
         for (int j = 0; j < (VEC ? 8 : 1); ++j) acc[j] = 0.f;
-        for (int j = 0; j < k; ++j) {
-            const long long slot = (long long)t * k + j;
-            const long long row = inverse ? inverse[slot] : slot;
-            if (row < 0 || row >= (long long)T * k) {      // an id outside [0, E) left no row
-                fnx_flag_error(FNX_DEVERR_BADID);
-                continue;
-            }
-            const float s = w[slot];
-            if (VEC) {
-                const uint4 v = ld_nc_v4(yd + row * H + c);
-                const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+        // slots in groups of four: all four row loads are issued before the in-order sums
+        for (int j0 = 0; j0 < k; j0 += 4) {
+            uint4 v[4];
+            float s[4];
+            bool ok[4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    acc[2 * q] = __fadd_rn(acc[2 * q], round_bf(__fmul_rn(bf_lo(vv[q]), s)));
-                    acc[2 * q + 1] = __fadd_rn(acc[2 * q + 1], round_bf(__fmul_rn(bf_hi(vv[q]), s)));
+            for (int q = 0; q < 4; ++q) {
+                ok[q] = false;
+                s[q] = 0.f;
+                v[q] = make_uint4(0, 0, 0, 0);
+                if (j0 + q < k) {
+                    const long long slot = (long long)t * k + j0 + q;
+                    const long long row = inverse ? inverse[slot] : slot;
+                    if (row < 0 || row >= (long long)T * k) {      // an id outside [0, E) left no row
+                        fnx_flag_error(FNX_DEVERR_BADID);
+                    } else {
+                        ok[q] = true;
+                        s[q] = w[slot];
+                        if (VEC) v[q] = ld_nc_v4(yd + row * H + c);
+                        else v[q].x = (uint32_t)bf16_bits(yd[row * H + c]) << 16;
+                    }
                 }
-            } else {
-                acc[0] = __fadd_rn(acc[0], round_bf(__fmul_rn(bf2f(yd[row * H + c]), s)));
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (!ok[q]) continue;
+                if (VEC) {
+                    const uint32_t vv[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        acc[2 * e] = __fadd_rn(acc[2 * e], round_bf(__fmul_rn(bf_lo(vv[e]), s[q])));
+                        acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], round_bf(__fmul_rn(bf_hi(vv[e]), s[q])));
+                    }
+                } else {
+                    acc[0] = __fadd_rn(acc[0], round_bf(__fmul_rn(bf_hi(v[q].x), s[q])));
+                }
             }
         }
         const float sg = round_bf(sigmoid_f32(bf2f(gate[(long long)t * gate_ld])));

@@ -39,7 +39,9 @@
 namespace fnx {
 
 enum GemmMode { GEMM_W4 = 0, GEMM_W8 = 1, GEMM_BF16 = 2 };
-enum GemmEpi { EPI_PLAIN = 0, EPI_SWIGLU_F32 = 1, EPI_SWIGLU_BF16 = 2 };
+// EPI_SWIGLU_MIXED: the fp32 SwiGLU for experts 0..E-2 and the shared expert's bf16 form for
+// the last expert (the shared expert appended as expert E-1 of one grouped launch).
+enum GemmEpi { EPI_PLAIN = 0, EPI_SWIGLU_F32 = 1, EPI_SWIGLU_BF16 = 2, EPI_SWIGLU_MIXED = 3 };
 
 constexpr int G_BM = 128;          // weight features per tile (UMMA M)
 constexpr int G_BK = 64;           // k per stage (one 128-byte swizzle row of bf16)
@@ -92,6 +94,7 @@ struct GemmSmem {
     uint64_t a_full[G_MAX_STAGES], b_full[G_MAX_STAGES], empty[G_MAX_STAGES];
     uint64_t raw_full[G_MAX_R_OPS], raw_empty[G_MAX_R_OPS];
     uint64_t peer_full[G_MAX_STAGES];   // CTA-pair kernel: the peer's stage is full (on rank 0)
+    uint64_t b_empty[G_MAX_STAGES];     // CTA-pair kernel: token stage free (its own, deeper ring)
     uint64_t acc_full[2], acc_empty[2], final_bar;
     uint32_t tmem_base;
     volatile int abort;
@@ -233,7 +236,7 @@ FNX_DEV void epilogue_chunk(const GemmParams& p, const TileInfo& ti, int r, int 
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             float a;
-            if (EPI == EPI_SWIGLU_F32) a = __fmul_rn(silu_f32(g[i]), u[i]);
+            if (EPI == EPI_SWIGLU_F32 || (EPI == EPI_SWIGLU_MIXED && ti.e < p.E - 1)) a = __fmul_rn(silu_f32(g[i]), u[i]);
             else a = __fmul_rn(round_bf(silu_f32(g[i])), u[i]);
             if (i < lim) o[(long long)i * p.ld_out] = f2bf(a);
         }
@@ -277,7 +280,7 @@ FNX_DEV void epilogue_chunk_staged(const GemmParams& p, const TileInfo& ti, int 
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             float a;
-            if (EPI == EPI_SWIGLU_F32) a = __fmul_rn(silu_f32(g[i]), u[i]);
+            if (EPI == EPI_SWIGLU_F32 || (EPI == EPI_SWIGLU_MIXED && ti.e < p.E - 1)) a = __fmul_rn(silu_f32(g[i]), u[i]);
             else a = __fmul_rn(round_bf(silu_f32(g[i])), u[i]);
             stage[(nb + i) * 16 + (lane >> 1)] = (uint16_t)bf16_bits(f2bf(a));
         }

@@ -27,16 +27,26 @@ namespace fnx {
 // A stage carries P_KS k-blocks (128 k): every hand-off between the roles costs a few hundred
 // cycles of latency however little work the stage holds, so stages hold two k-blocks.
 constexpr int P_KS = 2;
-constexpr int P_STAGES = 4;                          // 8 k-blocks in flight
+constexpr int P_STAGES = 4;                          // A stages in tensor memory: 8 k-blocks in flight
+// Token tiles have their own, deeper ring: their path (gather issue + L2 latency + hand-offs)
+// is the longest of the stage loop, so it runs further ahead than the TMEM-bound A ring.
+#ifndef FNX_PAIR_BSTAGES
+#define FNX_PAIR_BSTAGES 7
+#endif
+#ifndef FNX_PAIR_ROPS
+#define FNX_PAIR_ROPS 5
+#endif
+constexpr int P_BSTAGES = FNX_PAIR_BSTAGES;
 constexpr int P_BN_HALF = G_BN / 2;                  // token rows per CTA per tile
 constexpr int P_B_SUB = P_BN_HALF * G_BK * 2;        // 8 KB: one k-block of this CTA's token rows
 constexpr int P_B_BYTES = P_KS * P_B_SUB;            // 16 KB per stage
-constexpr int P_R_OPS = 8;                           // raw ring: 8 copies of 4 tile blocks (136 KB)
+constexpr int P_R_OPS = FNX_PAIR_ROPS;               // raw ring: copies of 4 tile blocks (17 KB each)
 constexpr uint32_t P_TMEM_COLS = 512;
 constexpr uint32_t P_A_COL0 = 2 * G_BN;
 constexpr uint32_t P_A_COLS = 32 * P_KS;             // tensor-memory columns of one A stage
 static_assert(G_OPK % P_KS == 0, "a copy holds whole stages");
-static_assert(P_STAGES <= G_MAX_STAGES && P_R_OPS <= G_MAX_R_OPS && P_A_COL0 + P_STAGES * P_A_COLS <= P_TMEM_COLS,
+static_assert(P_STAGES <= G_MAX_STAGES && P_BSTAGES <= G_MAX_STAGES && P_R_OPS <= G_MAX_R_OPS &&
+                  P_A_COL0 + P_STAGES * P_A_COLS <= P_TMEM_COLS,
               "budget");
 
 // Pair tile t -> expert, chunk and this CTA's feature tile (2 * pair + rank).
@@ -64,7 +74,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* b_tiles = base;
-    uint8_t* raw_tiles = b_tiles + P_STAGES * P_B_BYTES;
+    uint8_t* raw_tiles = b_tiles + P_BSTAGES * P_B_BYTES;
     GemmSmem& S = *reinterpret_cast<GemmSmem*>(raw_tiles + P_R_OPS * G_OPK * G_RAW_BYTES);
     uint16_t* epi_stage = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(&S) + ((sizeof(GemmSmem) + 15) & ~15));
 
@@ -73,11 +83,16 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
     const int cid = (int)cluster_id_x(), ncl = (int)num_clusters_x();
 
     // ---- prologue: barriers, TMEM in both CTAs, per-expert pair-tile offsets
+    // stage j uses A slot j % P_STAGES (a_full / empty) and token slot j % P_BSTAGES
+    // (b_full / b_empty / peer_full)
     if (tid == 0) {
         for (int s = 0; s < P_STAGES; ++s) {
             mbar_init(&S.a_full[s], 4);
-            mbar_init(&S.b_full[s], 32 * G_LOADERS);
             mbar_init(&S.empty[s], 1);
+        }
+        for (int s = 0; s < P_BSTAGES; ++s) {
+            mbar_init(&S.b_full[s], 32 * G_LOADERS);
+            mbar_init(&S.b_empty[s], 1);
             mbar_init(&S.peer_full[s], 1);
         }
         for (int s = 0; s < P_R_OPS; ++s) {
@@ -176,8 +191,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
             }
             const int c = lane & 7;
             for (int ks = 0; ks < KS; ++ks, ++it) {
-                const int s = it % P_STAGES;
-                if (!mbar_wait_cluster(&S.empty[s], ((it / P_STAGES) & 1) ^ 1)) { S.abort = 1; ok = false; break; }
+                const int s = it % P_BSTAGES;
+                if (!mbar_wait_cluster(&S.b_empty[s], ((it / P_BSTAGES) & 1) ^ 1)) { S.abort = 1; ok = false; break; }
 #pragma unroll
                 for (int h = 0; h < P_KS; ++h) {
                     const uint32_t bt = smem_u32(b_tiles + s * P_B_BYTES + h * P_B_SUB);
@@ -221,11 +236,11 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
                 const uint32_t idesc = idesc_bf16_f32(2 * G_BM, (int)n16 * 16);
                 const uint32_t d = tmem + ab * G_BN;
                 for (int ks = 0; ks < KS; ++ks, ++j) {
-                    const int s = j % P_STAGES;
+                    const int s = j % P_STAGES, sb = j % P_BSTAGES;
                     named_bar_sync(G_BAR_FULL, 64);
                     tc_fence_after();
                     if (elect_one()) {
-                        const uint32_t b0 = smem_u32(b_tiles + s * P_B_BYTES);
+                        const uint32_t b0 = smem_u32(b_tiles + sb * P_B_BYTES);
 #pragma unroll
                         for (int h = 0; h < P_KS; ++h)
 #pragma unroll
@@ -234,6 +249,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
                                                   sdesc_kmajor_sw128(b0 + h * P_B_SUB + kk * 32), idesc,
                                                   (ks | h | kk) ? 1u : 0u);
                         umma_commit_pair(&S.empty[s], 3);
+                        umma_commit_pair(&S.b_empty[sb], 3);
                         if (ks == KS - 1) umma_commit_pair(&S.acc_full[ab], 3);
                     }
                     __syncwarp();
@@ -280,12 +296,12 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
                     if (!__all_sync(0xffffffffu, ok)) { dead = true; S.abort = 1; }
                 }
                 for (int ks = 0; ks < KS; ++ks, ++j) {
-                    const int s = j % P_STAGES;
-                    const uint32_t ph = (j / P_STAGES) & 1;
+                    const int s = j % P_STAGES, sb = j % P_BSTAGES;
+                    const uint32_t ph = (j / P_STAGES) & 1, phb = (j / P_BSTAGES) & 1;
                     dead = __any_sync(0xffffffffu, dead || S.abort);
                     if (!dead) {
-                        const bool ok = mbar_wait(&S.a_full[s], ph) && mbar_wait(&S.b_full[s], ph) &&
-                                        mbar_wait_cluster(&S.peer_full[s], ph);
+                        const bool ok = mbar_wait(&S.a_full[s], ph) && mbar_wait(&S.b_full[sb], phb) &&
+                                        mbar_wait_cluster(&S.peer_full[sb], phb);
                         if (!__all_sync(0xffffffffu, ok)) { dead = true; S.abort = 1; }
                     }
                     if (j > 0) named_bar_sync(G_BAR_TAKEN, 64);
@@ -298,11 +314,11 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
             bool ok = true;
             for (int tile = cid; ok && tile < S.total_tiles; tile += ncl) {
                 for (int ks = 0; ks < KS; ++ks, ++j) {
-                    const int s = j % P_STAGES;
-                    const uint32_t ph = (j / P_STAGES) & 1;
-                    const bool got = !S.abort && mbar_wait(&S.a_full[s], ph) && mbar_wait(&S.b_full[s], ph);
+                    const int s = j % P_STAGES, sb = j % P_BSTAGES;
+                    const uint32_t ph = (j / P_STAGES) & 1, phb = (j / P_BSTAGES) & 1;
+                    const bool got = !S.abort && mbar_wait(&S.a_full[s], ph) && mbar_wait(&S.b_full[sb], phb);
                     if (!__all_sync(0xffffffffu, got)) { ok = false; break; }   // rank 0 then times out
-                    if (lane == 0) mbar_arrive_remote_relaxed(mapa_rank(&S.peer_full[s], 0));
+                    if (lane == 0) mbar_arrive_remote_relaxed(mapa_rank(&S.peer_full[sb], 0));
                 }
             }
             if (!ok) S.abort = 1;
@@ -385,7 +401,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
 }
 
 inline size_t grouped_gemm_pair_smem_bytes() {
-    return 1024 + (size_t)P_STAGES * P_B_BYTES + (size_t)P_R_OPS * G_OPK * G_RAW_BYTES +
+    return 1024 + (size_t)P_BSTAGES * P_B_BYTES + (size_t)P_R_OPS * G_OPK * G_RAW_BYTES +
            ((sizeof(GemmSmem) + 15) & ~(size_t)15) + 4 * 512 * sizeof(uint16_t);
 }
 

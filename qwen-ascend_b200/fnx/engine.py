@@ -20,7 +20,7 @@ import torch
 from . import _lib
 
 BF16 = torch.bfloat16
-EPI_PLAIN, EPI_SWIGLU_F32, EPI_SWIGLU_BF16 = 0, 1, 2
+EPI_PLAIN, EPI_SWIGLU_F32, EPI_SWIGLU_BF16, EPI_SWIGLU_MIXED = 0, 1, 2, 3
 DECODE_MAX_TOKENS = 16
 
 
@@ -188,11 +188,15 @@ class MoELayer:
         _lib.require_cuda(gu_w4, dn_w4, gate_w, sh_gu_w4, sh_dn_w4)
         self.E, self.H = gate_w.shape
         self.I = gu_w4.shape[2] * 8 // 2
-        # tile blocks (the artifact tensors are not kept)
-        self.gu_t = repack_w4(gu_w4, gu_scales, swiglu=True)
-        self.dn_t = repack_w4(dn_w4, dn_scales, swiglu=False)
-        self.sh_gu_t = repack_w4(sh_gu_w4[None], sh_gu_scales[None], swiglu=True)
-        self.sh_dn_t = repack_w4(sh_dn_w4[None], sh_dn_scales[None], swiglu=False)
+        # tile blocks (the artifact tensors are not kept): routed experts 0..E-1 and the
+        # shared expert as expert E, so prefill runs both in one grouped launch per projection
+        E = self.E
+        self.gu_all = repack_w4(torch.cat([gu_w4, sh_gu_w4[None]]), torch.cat([gu_scales, sh_gu_scales[None]]),
+                                swiglu=True)
+        self.dn_all = repack_w4(torch.cat([dn_w4, sh_dn_w4[None]]), torch.cat([dn_scales, sh_dn_scales[None]]),
+                                swiglu=False)
+        self.gu_t, self.sh_gu_t = self.gu_all[:E], self.gu_all[E:]
+        self.dn_t, self.sh_dn_t = self.dn_all[:E], self.dn_all[E:]
         self.k, self.gs = k, gs
         R = self.E + 1
         self.R = R
@@ -203,6 +207,7 @@ class MoELayer:
         self.router_cat = rc
         self.bias = None if bias is None else bias.to(torch.float32).to(gate_w.device).contiguous()
         self._ws = {}
+        self._prefill_bufs = {}
 
     @classmethod
     def from_synth(cls, t, shape, bias=None):
@@ -210,12 +215,15 @@ class MoELayer:
                    t["sh_gu_scales"], t["sh_dn_w4"], t["sh_dn_scales"], t["sh_gate"], shape.k, shape.gs, bias=bias)
 
     def weight_bytes(self):
-        return sum(t.numel() * t.element_size()
-                   for t in (self.gu_t, self.dn_t, self.router_cat, self.sh_gu_t, self.sh_dn_t))
+        return sum(t.numel() * t.element_size() for t in (self.gu_all, self.dn_all, self.router_cat))
 
     # ---------------------------------------------------------------- routing
-    def logits(self, x):
-        """bf16 ``[T, R_pad]``: router logits in columns ``[0, E)``, shared gate in column E."""
+    def logits(self, x, native=False):
+        """bf16 ``[T, R_pad]``: router logits in columns ``[0, E)``, shared gate in column E.
+        A plain bf16 GEMM (fp32 accumulation), run by cuBLAS; ``native`` runs the library's
+        own tcgen05 bf16 GEMM instead."""
+        if not native:
+            return torch.mm(x, self.router_cat.t())
         T = x.shape[0]
         out = torch.empty(T, self.R_pad, dtype=BF16, device=x.device)
         rc = _lib.lib().fnx_bf16_gemm_nt(x.data_ptr(), x.stride(0), self.router_cat.data_ptr(), out.data_ptr(),
@@ -233,12 +241,12 @@ class MoELayer:
         _lib.check(rc, "router top-k")
         return w, idx, wf
 
-    def permute(self, idx):
+    def permute(self, idx, order=None, ends=None):
         n = idx.numel()
         dev = idx.device
-        order = torch.empty(n, dtype=torch.int64, device=dev)
+        order = torch.empty(n, dtype=torch.int64, device=dev) if order is None else order
         inverse = torch.empty(n, dtype=torch.int64, device=dev)
-        ends = torch.empty(self.E, dtype=torch.int64, device=dev)
+        ends = torch.empty(self.E, dtype=torch.int64, device=dev) if ends is None else ends
         wsb = _lib.lib().fnx_moe_permute_workspace(n, self.E)
         ws = torch.empty(max(1, wsb), dtype=torch.uint8, device=dev)
         rc = _lib.lib().fnx_moe_permute(idx.data_ptr(), order.data_ptr(), inverse.data_ptr(), ends.data_ptr(), None, n,
@@ -259,21 +267,32 @@ class MoELayer:
     __call__ = forward
 
     def prefill(self, x, details=False):
-        """Grouped path (``fnx/engine.py:1815-1853``) for ``T`` tokens."""
+        """Grouped path (``fnx/engine.py:1815-1853``) for ``T`` tokens.  The routed and the shared
+        expert share one grouped launch per projection; the per-call buffers of the extended
+        permutation are cached per token count (calls on one layer must not overlap)."""
         T, H, I, k, E = x.shape[0], self.H, self.I, self.k, self.E
         dev = x.device
+        M = T * k
         logits = self.logits(x)
         w, idx, wf = self.topk(logits)
-        order, inverse, ends = self.permute(idx)
-        act = torch.empty(T * k, I, dtype=BF16, device=dev)
-        _grouped_w4(x, self.gu_t, ends, act, E=E, M=T * k, K=H, Nw=2 * I, epilogue=EPI_SWIGLU_F32,
-                    row_index=order, index_div=k)
-        yd = torch.empty(T * k, H, dtype=BF16, device=dev)
-        _grouped_w4(act, self.dn_t, ends, yd, E=E, M=T * k, K=I, Nw=H, epilogue=EPI_PLAIN)
-        sh_act = torch.empty(T, I, dtype=BF16, device=dev)
-        _grouped_w4(x, self.sh_gu_t, None, sh_act, E=1, M=T, K=H, Nw=2 * I, epilogue=EPI_SWIGLU_BF16)
-        sh = torch.empty(T, H, dtype=BF16, device=dev)
-        _grouped_w4(sh_act, self.sh_dn_t, None, sh, E=1, M=T, K=I, Nw=H, epilogue=EPI_PLAIN)
+        # expert-major rows of the routed experts, then the shared expert (expert E) over all
+        # T tokens: its rows M .. M+T-1 read token t (row index t*k, divided by k)
+        key = (T, str(dev))
+        bufs = self._prefill_bufs.get(key)
+        if bufs is None:
+            order_x = torch.empty(M + T, dtype=torch.int64, device=dev)
+            order_x[M:] = torch.arange(T, dtype=torch.int64, device=dev) * k
+            ends_x = torch.empty(E + 1, dtype=torch.int64, device=dev)
+            ends_x[E] = M + T
+            bufs = self._prefill_bufs[key] = (order_x, ends_x)
+        order_x, ends_x = bufs
+        order, inverse, ends = self.permute(idx, order=order_x[:M], ends=ends_x[:E])
+        act = torch.empty(M + T, I, dtype=BF16, device=dev)
+        _grouped_w4(x, self.gu_all, ends_x, act, E=E + 1, M=M + T, K=H, Nw=2 * I, epilogue=EPI_SWIGLU_MIXED,
+                    row_index=order_x, index_div=k)
+        yd = torch.empty(M + T, H, dtype=BF16, device=dev)
+        _grouped_w4(act, self.dn_all, ends_x, yd, E=E + 1, M=M + T, K=I, Nw=H, epilogue=EPI_PLAIN)
+        sh_act, sh = act[M:], yd[M:]
         out = torch.empty(T, H, dtype=BF16, device=dev)
         gate = logits[:, E:E + 1]
         rc = _lib.lib().fnx_moe_combine(yd.data_ptr(), wf.data_ptr(), inverse.data_ptr(), sh.data_ptr(),
@@ -281,7 +300,7 @@ class MoELayer:
         _lib.check(rc, "MoE combine")
         if details:
             return out, dict(logits=logits[:, :E], gate=gate, w=w, idx=idx, order=order, inverse=inverse, ends=ends,
-                             act=act, yd=yd, sh=sh, sh_act=sh_act)
+                             act=act[:M], yd=yd[:M], sh=sh, sh_act=sh_act)
         return out
 
     def decode_workspace(self, M, device):
