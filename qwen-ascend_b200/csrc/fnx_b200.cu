@@ -420,12 +420,17 @@ DecodeLayout decode_layout(int M, int H, int I, int E, int k) {
     DecodeLayout L{};
     L.R = E + 1;
     const int mt = I / 64, kb = H / 64;
-    // K splits (divisors of the k-block count, >= 2 k-blocks each) sized so the shared
-    // gate/up grid has >= 64 blocks and the routed one >= 2 blocks per SM
+    // K splits (powers of two dividing the k-block count).  An item fetches its k-range
+    // with one bulk copy of at most DEC_CH tile blocks, so splits start there and grow
+    // (>= 2 k-blocks each) until the phase has about one item per resident block: the
+    // shared gate/up shares phase 1 with the router rows, the routed gate/up has phase 2.
+    const int slots = 2 * num_sms();
     L.ks1 = 1;
-    while (L.ks1 < 64 && M * mt * L.ks1 < 64 && kb % (L.ks1 * 2) == 0 && kb / (L.ks1 * 2) >= 2) L.ks1 *= 2;
+    while (kb / L.ks1 > DEC_CH && kb % (L.ks1 * 2) == 0) L.ks1 *= 2;
+    while (L.ks1 < 64 && M * mt * L.ks1 < slots / 2 && kb % (L.ks1 * 2) == 0 && kb / (L.ks1 * 2) >= 2) L.ks1 *= 2;
     L.ks2 = 1;
-    while (L.ks2 < 64 && M * k * mt * L.ks2 < 2 * num_sms() && kb % (L.ks2 * 2) == 0 && kb / (L.ks2 * 2) >= 2)
+    while (kb / L.ks2 > DEC_CH && kb % (L.ks2 * 2) == 0) L.ks2 *= 2;
+    while (L.ks2 < 64 && M * k * mt * L.ks2 < slots && kb % (L.ks2 * 2) == 0 && kb / (L.ks2 * 2) >= 2)
         L.ks2 *= 2;
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
@@ -438,7 +443,7 @@ DecodeLayout decode_layout(int M, int H, int I, int E, int k) {
     L.act_sh = take((size_t)M * I * 2);
     L.yd = take((size_t)M * k * H * 2);
     L.sh = take((size_t)M * H * 2);
-    L.counters = take((size_t)(1 + M * mt + M * k * mt + H / 128) * 4);
+    L.counters = take((size_t)(1 + M * mt + M * k * mt + H / 128 + 2) * 4);   // + barrier 2, exit ticket
     L.total = off;
     return L;
 }
@@ -474,12 +479,29 @@ FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu,
     p.act = (bf16*)(ws + L.act); p.act_sh = (bf16*)(ws + L.act_sh); p.yd = (bf16*)(ws + L.yd); p.sh = (bf16*)(ws + L.sh);
     p.counters = (unsigned*)(ws + L.counters);
     p.M = M; p.H = H; p.I = I; p.E = E; p.k = k; p.R = L.R; p.ks1 = L.ks1; p.ks2 = L.ks2;
-    cudaStream_t st = (cudaStream_t)stream;
-    const int mt = I / 64;
-    const int router_blocks = (L.R + 7) / 8;
-    decode_d1_kernel<<<router_blocks + M * mt * L.ks1, DEC_THREADS, 0, st>>>(p, router_blocks);
-    decode_d2_kernel<<<M * k * mt * L.ks2, DEC_THREADS, 0, st>>>(p);
-    decode_d3_kernel<<<(M * k + M) * (H / 128), DEC_THREADS, 0, st>>>(p);
+    // one cooperative launch of every block that fits at once (the phases meet at grid
+    // barriers, so all blocks must be resident)
+    static int grid = 0;
+    if (!grid) {
+        if (cudaFuncSetAttribute(decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM))
+            return FNX_ELAUNCH;
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_kernel, DEC_THREADS, DEC_SMEM) ||
+            per_sm < 1)
+            return FNX_ELAUNCH;
+        grid = per_sm * num_sms();
+    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(DEC_THREADS);
+    cfg.dynamicSmemBytes = DEC_SMEM;
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, decode_fused_kernel, p) != cudaSuccess) return FNX_ELAUNCH;
     return launch_rc();
 }
 

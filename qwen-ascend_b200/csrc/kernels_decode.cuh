@@ -1,11 +1,6 @@
-// Decode (M <= 16 tokens) W4A16 MoE layer as three HBM-bound GEMV kernels.
-//
-//   D1  router logits (bf16 GEMV over [E+1, H]: E router rows + the shared-expert gate
-//       row) and the shared expert's gate/up; the last block to finish runs top-k and
-//       publishes the routing.
-//   D2  routed gate/up for every (token, slot) row + fp32 SwiGLU -> act [M*k, I]
-//   D3  routed down for every row + shared down; the last block of each 128-column tile
-//       does the slot-order weighted reduce and the sigmoid-gated shared merge.
+// Decode (M <= 16 tokens) W4A16 MoE layer as one cooperative, HBM-bound GEMV kernel with
+// three phases (router + shared gate/up; routed gate/up + shared down; routed down +
+// combine), described above decode_fused_kernel below.
 //
 // This is the reference's decode branch (fnx/engine.py:1786-1889: concatenated shared
 // GEMM, softmax/top-k, gather + W4A16 gate/up, fp32 swiglu, Cartesian down,
@@ -26,6 +21,10 @@ namespace fnx {
 constexpr int DEC_THREADS = 256;
 constexpr int DEC_MAX_M = 16;
 constexpr int DEC_MAX_K = 4096;          // largest K (H or I) a block stages in shared memory
+constexpr int DEC_CH = 16;               // k-blocks per bulk copy (69.6 KB of shared memory)
+// dynamic shared memory of the decode kernels: one chunk of tile blocks, or D1's eight
+// router rows of H <= DEC_MAX_K bf16
+constexpr int DEC_SMEM = DEC_CH * TILE_BLOCK_BYTES > 8 * DEC_MAX_K * 2 ? DEC_CH * TILE_BLOCK_BYTES : 8 * DEC_MAX_K * 2;
 
 struct DecodeParams {
     const bf16* x;                   // [M, H]
@@ -76,63 +75,65 @@ FNX_DEV bool last_block(unsigned* ctr, unsigned n) {
     return last;
 }
 
-// Stage x (bf16 [K]) as bf16 pairs in shared memory.
-FNX_DEV void stage_x(uint32_t* xs2, const bf16* x, int K) {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(x);
-    for (int i = threadIdx.x; i < K / 2; i += blockDim.x) xs2[i] = src[i];
-    __syncthreads();
-}
-
-// Dot products of the 128 rows of one weight tile with x over k-blocks [kb0, kb1):
-// thread (half, r) takes the k-blocks kb0 + half, kb0 + half + 2, ...; the two halves are
-// added in a fixed order.  Result in red[r] (shared memory, 128 floats).
-FNX_DEV void tile_dot(const uint32_t* __restrict__ tw, const uint32_t* xs2, int kb0, int kb1, float* red) {
+// Dot products of the 128 rows of one weight tile with x (bf16 [K], staged into xs2 while
+// the first copy is in flight; x_cg reads it through L2) over k-blocks [kb0, kb1).  The
+// tile blocks of a chunk of <= DEC_CH k-blocks are contiguous in HBM and arrive in shared
+// memory (wbuf) by one bulk copy issued by thread 0, so a block keeps its whole chunk in
+// flight at once; thread (half, r) then takes the chunk's k-blocks half, half + 2, ... of
+// tile row r (conflict-free: consecutive rows are consecutive words) and the two halves are
+// added in a fixed order.  Result in red[r] (shared memory, 128 floats).  `phase` tracks
+// the block's mbarrier across calls.
+FNX_DEV void tile_dot(const uint32_t* __restrict__ tw, const bf16* x, int K, bool x_cg, uint32_t* xs2, int kb0,
+                      int kb1, uint32_t* wbuf, uint64_t* bar, uint32_t& phase, float* red) {
     const int r = threadIdx.x & 127, half = threadIdx.x >> 7;
     float a0 = 0.f, a1 = 0.f;
-    for (int kb = kb0 + half; kb < kb1; kb += 4) {
-        uint32_t wv[2][8], s2[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int kbu = kb + 2 * u;
-            if (kbu < kb1) {
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t v;
-                    asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v)
-                                 : "l"(tw + (long long)kbu * TILE_BLOCK_WORDS + c * 128 + r));
-                    wv[u][c] = v;
-                }
-                const uint32_t s16 = __ldg(reinterpret_cast<const unsigned short*>(tw + (long long)kbu * TILE_BLOCK_WORDS + 1024) + r);
-                s2[u] = s16 | (s16 << 16);
-            } else {
-#pragma unroll
-                for (int c = 0; c < 8; ++c) wv[u][c] = 0x88888888u;      // q = 0
-                s2[u] = 0;
-            }
+    for (int c0 = kb0; c0 < kb1; c0 += DEC_CH) {
+        const int n = min(DEC_CH, kb1 - c0);
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(bar, (uint32_t)n * TILE_BLOCK_BYTES);
+            bulk_load(smem_u32(wbuf), tw + (long long)c0 * TILE_BLOCK_WORDS, (uint32_t)n * TILE_BLOCK_BYTES, bar,
+                      l2_evict_first());
         }
+        if (c0 == kb0) {                  // the input row, while the weights are in flight
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(x);
+            for (int i = threadIdx.x; i < K / 2; i += blockDim.x) xs2[i] = x_cg ? __ldcg(src + i) : src[i];
+            __syncthreads();
+        }
+        mbar_wait(bar, phase);            // a timeout is flagged; the block finishes with stale data
+        phase ^= 1u;
+        for (int j = half; j < n; j += 2) {
+            const uint32_t* blk = wbuf + j * TILE_BLOCK_WORDS;
+            const uint32_t s16 = reinterpret_cast<const unsigned short*>(blk + 1024)[r];
+            const uint32_t s2 = s16 | (s16 << 16);
+            const uint4* xq = reinterpret_cast<const uint4*>(xs2 + (c0 + j) * 32);
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int kbu = kb + 2 * u;
-            if (kbu < kb1) {
-                const uint4* xq = reinterpret_cast<const uint4*>(xs2 + kbu * 32);
+            for (int c = 0; c < 8; ++c) {
+                const uint32_t w = blk[c * 128 + r];
+                const uint4 xv = xq[c];
+                const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint4 xv = xq[c];
-                    const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint32_t w2 = tile_pair(wv[u][c], i, s2[u]);
-                        fma_bf_lo(a0, w2, xx[i]);
-                        fma_bf_hi(a1, w2, xx[i]);
-                    }
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t w2 = tile_pair(w, i, s2);
+                    fma_bf_lo(a0, w2, xx[i]);
+                    fma_bf_hi(a1, w2, xx[i]);
                 }
             }
         }
+        __syncthreads();                  // wbuf is refilled by the next chunk
     }
     __shared__ float halves[2][128];
     halves[half][r] = __fadd_rn(a0, a1);
     __syncthreads();
     if (threadIdx.x < 128) red[r] = __fadd_rn(halves[0][r], halves[1][r]);
+    __syncthreads();
+}
+
+// The block's bulk-copy mbarrier (initialised once per launch).
+FNX_DEV void init_block_bar(uint64_t* bar) {
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
     __syncthreads();
 }
 
@@ -143,54 +144,164 @@ FNX_DEV float sum_parts(const float* base, int ks, int r) {
     return a;
 }
 
-// ------------------------------------------------------------------ D1
-__global__ void __launch_bounds__(DEC_THREADS) decode_d1_kernel(const DecodeParams p, int router_blocks) {
-    __shared__ __align__(16) uint32_t xs2[DEC_MAX_K / 2];
-    __shared__ float red[128];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int MT = gu_tiles(p), KB = p.H / 64;
-    if ((int)blockIdx.x < router_blocks) {
-        // ---- router + shared gate row: one warp per row, all tokens
-        const int e = blockIdx.x * (DEC_THREADS / 32) + warp;
-        if (e < p.R) {
-            float acc[DEC_MAX_M];
-#pragma unroll
-            for (int t = 0; t < DEC_MAX_M; ++t) acc[t] = 0.f;
-            const bf16* wr = p.router + (long long)e * p.H;
-            for (int c = lane * 8; c < p.H; c += 256) {
-                const uint4 wv = ld_nc_v4(wr + c);
-                const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-                for (int t = 0; t < DEC_MAX_M; ++t) {
-                    if (t < p.M) {
-                        const uint4 xv = *reinterpret_cast<const uint4*>(p.x + (long long)t * p.H + c);
-                        const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            fma_bf_lo(acc[t], ww[i], xx[i]);
-                            fma_bf_hi(acc[t], ww[i], xx[i]);
-                        }
-                    }
-                }
+// ------------------------------------------------------------------ the fused decode kernel
+// One cooperative launch: three phases separated by two grid barriers.
+//   phase 1  router + shared-gate logits (eight rows per item) and the shared expert's
+//            gate/up (items (t, m, ks); the last item of a (t, m) group applies its SwiGLU)
+//   barrier  then every block routes the tokens from the logits itself (the same
+//            deterministic top-k, so all blocks agree; block 0 publishes the routing)
+//   phase 2  routed gate/up (items (row, m, ks); the last of a group: fp32 SwiGLU -> act)
+//            and the shared expert's down projection (items (t, m) -> sh)
+//   barrier
+//   phase 3  routed down (items (row, m) -> yd); the last item of output tile m reduces the
+//            k slots of every token in order and merges the gated shared output
+// A block walks the items of a phase with stride gridDim.x, so any resident grid works.
+
+struct DecodeRouting {
+    int idx[DEC_MAX_M * ROUTE_MAX_K];
+    float wf[DEC_MAX_M * ROUTE_MAX_K];
+};
+
+FNX_DEV unsigned* ctr_bar1(const DecodeParams& p) { return ctr_d1(p); }
+FNX_DEV unsigned* ctr_bar2(const DecodeParams& p) { return ctr_dn(p) + dn_tiles(p); }
+FNX_DEV unsigned* ctr_exit(const DecodeParams& p) { return ctr_bar2(p) + 1; }
+
+FNX_DEV unsigned ld_acquire_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// All blocks of the grid (co-resident by the cooperative launch); bounded.
+FNX_DEV void grid_barrier(unsigned* ctr, unsigned n) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(ctr, 1u);
+        const uint64_t t0 = fnx_globaltimer();
+        while (ld_acquire_u32(ctr) < n) {
+            __nanosleep(64);
+            if (fnx_globaltimer() - t0 > FNX_WAIT_NS) {
+                fnx_flag_error(FNX_DEVERR_TIMEOUT);
+                break;
             }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+}
+
+// DEC_ROWS consecutive router rows (rows >= E: the shared-expert gate) and, when it fits,
+// the M token rows arrive by bulk copies; two warps per router row take half of H each and
+// their fp32 partials are added in a fixed order.
+constexpr int DEC_ROWS = 4;
+FNX_DEV void router_rows(const DecodeParams& p, int item, uint32_t* wbuf, uint64_t* bar, uint32_t& phase) {
+    __shared__ float partial[DEC_ROWS][2][DEC_MAX_M];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e0 = item * DEC_ROWS;
+    const int nr = min(DEC_ROWS, p.R - e0);
+    const uint32_t rbytes = (uint32_t)nr * p.H * 2, xbytes = (uint32_t)p.M * p.H * 2;
+    const bool x_in_smem = DEC_ROWS * p.H * 2 + (int)xbytes <= DEC_SMEM;
+    const bf16* xs = x_in_smem ? reinterpret_cast<const bf16*>(wbuf) + DEC_ROWS * p.H : p.x;
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(bar, rbytes + (x_in_smem ? xbytes : 0u));
+        bulk_load(smem_u32(wbuf), p.router + (long long)e0 * p.H, rbytes, bar, l2_evict_first());
+        if (x_in_smem) bulk_load(smem_u32(xs), p.x, xbytes, bar, l2_evict_last());
+    }
+    mbar_wait(bar, phase);
+    phase ^= 1u;
+    const int row = warp >> 1, hh = warp & 1;
+    if (row < nr) {
+        float acc[DEC_MAX_M];
+#pragma unroll
+        for (int t = 0; t < DEC_MAX_M; ++t) acc[t] = 0.f;
+        const bf16* wr = reinterpret_cast<const bf16*>(wbuf) + (long long)row * p.H;
+        for (int c = hh * (p.H / 2) + lane * 8; c < (hh + 1) * (p.H / 2); c += 256) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(wr + c);
+            const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
             for (int t = 0; t < DEC_MAX_M; ++t) {
                 if (t < p.M) {
-                    float v = acc[t];
+                    const uint4 xv = *reinterpret_cast<const uint4*>(xs + (long long)t * p.H + c);
+                    const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-                    for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-                    if (lane == 0) p.logits[(long long)t * p.R + e] = f2bf(v);
+                    for (int i = 0; i < 4; ++i) {
+                        fma_bf_lo(acc[t], ww[i], xx[i]);
+                        fma_bf_hi(acc[t], ww[i], xx[i]);
+                    }
                 }
             }
         }
-    } else {
-        // ---- shared expert gate/up: block (t, m, ks)
-        const int b = blockIdx.x - router_blocks;
+#pragma unroll
+        for (int t = 0; t < DEC_MAX_M; ++t) {
+            if (t < p.M) {
+                float v = acc[t];
+#pragma unroll
+                for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+                if (lane == 0) partial[row][hh][t] = v;
+            }
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nr * p.M; i += blockDim.x) {
+        const int rr = i / p.M, t = i % p.M;
+        p.logits[(long long)t * p.R + e0 + rr] = f2bf(__fadd_rn(partial[rr][0][t], partial[rr][1][t]));
+    }
+    __syncthreads();                       // wbuf and partial are reused by the next item
+}
+
+// Top-k of every token (the router kernel's rule) into shared memory; block 0 publishes.
+FNX_DEV void route_tokens(const DecodeParams& p, DecodeRouting& R) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int t = warp; t < p.M; t += DEC_THREADS / 32) {
+        const bf16* row = p.logits + (long long)t * p.R;
+        float my_p, tot;
+        int my_i;
+        if (p.E <= 256) topk_warp<8, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
+        else if (p.E <= 512) topk_warp<16, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
+        else if (p.E <= 1024) topk_warp<32, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
+        else topk_warp<64, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
+        if (lane < p.k) {
+            const bf16 wb = f2bf(my_p / tot);
+            const int o = t * p.k + lane;
+            R.idx[o] = my_i;
+            R.wf[o] = bf2f(wb);
+            if (blockIdx.x == 0) {
+                p.wf[o] = bf2f(wb);
+                p.idx[o] = my_i;
+                if (p.w_out) p.w_out[o] = wb;
+                if (p.idx_out) p.idx_out[o] = my_i;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(DEC_THREADS) decode_fused_kernel(const DecodeParams p) {
+    extern __shared__ __align__(16) uint32_t wbuf[];
+    __shared__ __align__(16) uint32_t xs2[DEC_MAX_K / 2];
+    __shared__ float red[128];
+    __shared__ uint64_t bar;
+    __shared__ DecodeRouting R;
+    uint32_t phase = 0;
+    const int tid = threadIdx.x;
+    const int MT = gu_tiles(p), KB = p.H / 64;          // gate/up: I/64 feature tiles over K = H
+    const int MTd = dn_tiles(p), KBd = p.I / 64;        // down: H/128 feature tiles over K = I
+    const int RB = (p.R + DEC_ROWS - 1) / DEC_ROWS;
+    init_block_bar(&bar);
+
+    // ---- phase 1: logits, shared gate/up
+    const int n1 = RB + p.M * MT * p.ks1;
+    for (int it = blockIdx.x; it < n1; it += gridDim.x) {
+        if (it < RB) {
+            router_rows(p, it, wbuf, &bar, phase);
+            continue;
+        }
+        const int b = it - RB;
         const int ks = b % p.ks1, m = (b / p.ks1) % MT, t = b / (p.ks1 * MT);
         const int nkb = KB / p.ks1;
-        stage_x(xs2, p.x + (long long)t * p.H, p.H);
-        tile_dot(p.sh_gu_tw + (long long)m * KB * TILE_BLOCK_WORDS, xs2, ks * nkb,
-                 (ks + 1) * nkb, red);
+        tile_dot(p.sh_gu_tw + (long long)m * KB * TILE_BLOCK_WORDS, p.x + (long long)t * p.H, p.H, false, xs2,
+                 ks * nkb, (ks + 1) * nkb, wbuf, &bar, phase, red);
         float* part = p.part + (((long long)t * MT + m) * p.ks1 + ks) * 128;
         if (tid < 128) part[tid] = red[tid];
         if (last_block(ctr_sh(p) + t * MT + m, p.ks1)) {
@@ -203,94 +314,72 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_d1_kernel(const DecodePara
             }
         }
     }
-    // ---- the last block of D1 routes every token
-    if (last_block(ctr_d1(p), gridDim.x)) {
-        for (int t = warp; t < p.M; t += DEC_THREADS / 32) {
-            // the router kernel's top-k rule, logits read through L2 (written by other blocks)
-            const bf16* row = p.logits + (long long)t * p.R;
-            float my_p, tot;
-            int my_i;
-            if (p.E <= 256) topk_warp<8, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
-            else if (p.E <= 512) topk_warp<16, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
-            else if (p.E <= 1024) topk_warp<32, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
-            else topk_warp<64, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
-            if (lane < p.k) {
-                const bf16 wb = f2bf(my_p / tot);
-                const int o = t * p.k + lane;
-                p.wf[o] = bf2f(wb);
-                p.idx[o] = my_i;
-                if (p.w_out) p.w_out[o] = wb;
-                if (p.idx_out) p.idx_out[o] = my_i;
+    grid_barrier(ctr_bar1(p), gridDim.x);
+    route_tokens(p, R);
+
+    // ---- phase 2: routed gate/up, shared down
+    const int n2a = p.M * p.k * MT * p.ks2;
+    const int n2 = n2a + p.M * MTd;
+    for (int it = blockIdx.x; it < n2; it += gridDim.x) {
+        if (it < n2a) {
+            const int ks = it % p.ks2, m = (it / p.ks2) % MT, row = it / (p.ks2 * MT);
+            const int ex = R.idx[row], t = row / p.k;
+            const int nkb = KB / p.ks2;
+            tile_dot(p.gu_tw + ((long long)ex * MT + m) * KB * TILE_BLOCK_WORDS, p.x + (long long)t * p.H, p.H, false,
+                     xs2, ks * nkb, (ks + 1) * nkb, wbuf, &bar, phase, red);
+            float* part = p.part2 + (((long long)row * MT + m) * p.ks2 + ks) * 128;
+            if (tid < 128) part[tid] = red[tid];
+            if (last_block(ctr_gu(p) + row * MT + m, p.ks2)) {
+                const float* base = p.part2 + ((long long)row * MT + m) * p.ks2 * 128;
+                if (tid < 64) {
+                    // routed expert: bf16(silu(g) * u) in fp32 on bf16-rounded gate/up
+                    const float g = round_bf(sum_parts(base, p.ks2, 2 * tid));
+                    const float u = round_bf(sum_parts(base, p.ks2, 2 * tid + 1));
+                    p.act[(long long)row * p.I + m * 64 + tid] = f2bf(__fmul_rn(silu_f32(g), u));
+                }
             }
+        } else {
+            const int b = it - n2a, m = b % MTd, t = b / MTd;
+            tile_dot(p.sh_dn_tw + (long long)m * KBd * TILE_BLOCK_WORDS, p.act_sh + (long long)t * p.I, p.I, true, xs2,
+                     0, KBd, wbuf, &bar, phase, red);
+            if (tid < 128) p.sh[(long long)t * p.H + m * 128 + tid] = f2bf(red[tid]);
         }
     }
-}
+    grid_barrier(ctr_bar2(p), gridDim.x);
 
-// ------------------------------------------------------------------ D2
-// block (row, m, ks): routed gate/up tile m over H/ks2 of K for one (token, slot) row.
-__global__ void __launch_bounds__(DEC_THREADS) decode_d2_kernel(const DecodeParams p) {
-    __shared__ __align__(16) uint32_t xs2[DEC_MAX_K / 2];
-    __shared__ float red[128];
-    const int tid = threadIdx.x;
-    const int MT = gu_tiles(p), KB = p.H / 64;
-    const int b = blockIdx.x;
-    const int ks = b % p.ks2, m = (b / p.ks2) % MT, row = b / (p.ks2 * MT);
-    const int ex = __ldcg(p.idx + row), t = row / p.k;
-    const int nkb = KB / p.ks2;
-    stage_x(xs2, p.x + (long long)t * p.H, p.H);
-    const long long tile = (long long)ex * MT + m;
-    tile_dot(p.gu_tw + tile * KB * TILE_BLOCK_WORDS, xs2, ks * nkb, (ks + 1) * nkb, red);
-    float* part = p.part2 + (((long long)row * MT + m) * p.ks2 + ks) * 128;
-    if (tid < 128) part[tid] = red[tid];
-    if (last_block(ctr_gu(p) + row * MT + m, p.ks2)) {
-        const float* base = p.part2 + ((long long)row * MT + m) * p.ks2 * 128;
-        if (tid < 64) {
-            // routed expert: bf16(silu(g) * u) in fp32 on bf16-rounded gate/up
-            const float g = round_bf(sum_parts(base, p.ks2, 2 * tid));
-            const float u = round_bf(sum_parts(base, p.ks2, 2 * tid + 1));
-            p.act[(long long)row * p.I + m * 64 + tid] = f2bf(__fmul_rn(silu_f32(g), u));
-        }
-    }
-}
-
-// ------------------------------------------------------------------ D3
-// block (row, m): rows 0..M*k-1 are routed (token, slot) rows, rows M*k.. the shared
-// expert of each token; output tile m = columns [128m, 128m+128), all of K = I.
-__global__ void __launch_bounds__(DEC_THREADS) decode_d3_kernel(const DecodeParams p) {
-    __shared__ __align__(16) uint32_t xs2[DEC_MAX_K / 2];
-    __shared__ float red[128];
-    const int tid = threadIdx.x;
-    const int MT = dn_tiles(p), KB = p.I / 64;
-    const int m = blockIdx.x % MT, row = blockIdx.x / MT;
+    // ---- phase 3: routed down; the last item of each output tile combines it
     const int nrows = p.M * p.k;
-    if (row < nrows) {
-        const int ex = __ldcg(p.idx + row);
-        stage_x(xs2, p.act + (long long)row * p.I, p.I);
-        const long long tile = (long long)ex * MT + m;
-        tile_dot(p.dn_tw + tile * KB * TILE_BLOCK_WORDS, xs2, 0, KB, red);
+    const int n3 = nrows * MTd;
+    for (int it = blockIdx.x; it < n3; it += gridDim.x) {
+        const int m = it % MTd, row = it / MTd;
+        const int ex = R.idx[row];
+        tile_dot(p.dn_tw + ((long long)ex * MTd + m) * KBd * TILE_BLOCK_WORDS, p.act + (long long)row * p.I, p.I, true,
+                 xs2, 0, KBd, wbuf, &bar, phase, red);
         if (tid < 128) p.yd[(long long)row * p.H + m * 128 + tid] = f2bf(red[tid]);
-    } else {
-        const int t = row - nrows;
-        stage_x(xs2, p.act_sh + (long long)t * p.I, p.I);
-        tile_dot(p.sh_dn_tw + (long long)m * KB * TILE_BLOCK_WORDS, xs2, 0, KB, red);
-        if (tid < 128) p.sh[(long long)t * p.H + m * 128 + tid] = f2bf(red[tid]);
-    }
-    if (last_block(ctr_dn(p) + m, nrows + p.M)) {
-        const unsigned short* yd = reinterpret_cast<const unsigned short*>(p.yd);
-        const unsigned short* sh = reinterpret_cast<const unsigned short*>(p.sh);
-        for (int i = tid; i < p.M * 128; i += DEC_THREADS) {
-            const int t = i / 128, c = m * 128 + i % 128;
-            float acc = 0.f;
-            for (int j = 0; j < p.k; ++j) {
-                const float y = __uint_as_float((uint32_t)__ldcg(yd + (long long)(t * p.k + j) * p.H + c) << 16);
-                acc = __fadd_rn(acc, round_bf(__fmul_rn(y, ld_cg_f32(p.wf + t * p.k + j))));
+        if (last_block(ctr_dn(p) + m, nrows)) {
+            const unsigned short* yd = reinterpret_cast<const unsigned short*>(p.yd);
+            const unsigned short* sh = reinterpret_cast<const unsigned short*>(p.sh);
+            const unsigned short* lg = reinterpret_cast<const unsigned short*>(p.logits);
+            for (int i = tid; i < p.M * 128; i += DEC_THREADS) {
+                const int t = i / 128, c = m * 128 + i % 128;
+                float acc = 0.f;
+                for (int j = 0; j < p.k; ++j) {
+                    const float y = __uint_as_float((uint32_t)__ldcg(yd + (long long)(t * p.k + j) * p.H + c) << 16);
+                    acc = __fadd_rn(acc, round_bf(__fmul_rn(y, R.wf[t * p.k + j])));
+                }
+                const float a = round_bf(acc);
+                const float g = __uint_as_float((uint32_t)__ldcg(lg + (long long)t * p.R + p.E) << 16);
+                const float sg = round_bf(sigmoid_f32(g));
+                const float s = __uint_as_float((uint32_t)__ldcg(sh + (long long)t * p.H + c) << 16);
+                p.out[(long long)t * p.H + c] = f2bf(__fadd_rn(a, round_bf(__fmul_rn(s, sg))));
             }
-            const float a = round_bf(acc);
-            const float g = bf2f(p.logits[(long long)t * p.R + p.E]);
-            const float sg = round_bf(sigmoid_f32(g));
-            const float s = __uint_as_float((uint32_t)__ldcg(sh + (long long)t * p.H + c) << 16);
-            p.out[(long long)t * p.H + c] = f2bf(__fadd_rn(a, round_bf(__fmul_rn(s, sg))));
         }
+    }
+
+    // ---- the last block to leave re-arms the grid barriers for the next call
+    if (last_block(ctr_exit(p), gridDim.x) && tid == 0) {
+        *ctr_bar1(p) = 0;
+        *ctr_bar2(p) = 0;
     }
 }
 

@@ -48,33 +48,36 @@ FNX_DEV void topk_warp(const bf16* row, const float* bias, int E, int k, float& 
 #pragma unroll
     for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
     const float inv = 1.0f / sum;
-    // probabilities; a NaN (from NaN logits) counts as 0 so that k valid, distinct ids are
-    // always selected (garbage logits must never turn into an out-of-range expert id)
+    // probabilities as ordered keys: key = bits(p) + 1 for a non-negative probability (so
+    // integer order is probability order), 0 for a selected or absent expert.  A NaN (from
+    // NaN logits) counts as probability 0 so that k valid, distinct ids are always selected
+    // (garbage logits must never turn into an out-of-range expert id).
+    uint32_t key[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
         const float pr = __fmul_rn(v[i], inv);
-        v[i] = (i * 32 + lane) < E ? (pr >= 0.f ? pr : 0.f) : -1.f;
+        key[i] = (i * 32 + lane) < E ? __float_as_uint(pr > 0.f ? pr : 0.f) + 1u : 0u;
     }
 
     my_p = 0.f;
     tot = 0.f;
     my_i = 0;
     for (int j = 0; j < k; ++j) {
-        // highest probability, lowest id on ties (ascending e within a lane keeps the lowest)
-        float bp = -2.f;
-        int bi = 0x7fffffff;
+        // highest probability, lowest id on ties: a warp max over the keys, then a warp min
+        // over the ids of the lanes holding that key (each lane offers its lowest such id)
+        uint32_t lm = 0;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) lm = max(lm, key[i]);
+        const uint32_t gm = __reduce_max_sync(0xffffffffu, lm);
+        uint32_t cand = 0xffffffffu;
+#pragma unroll
+        for (int i = PER - 1; i >= 0; --i)
+            if (key[i] == gm) cand = (uint32_t)(i * 32 + lane);
+        const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
 #pragma unroll
         for (int i = 0; i < PER; ++i)
-            if (v[i] > bp) { bp = v[i]; bi = i * 32 + lane; }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (op > bp || (op == bp && oi < bi)) { bp = op; bi = oi; }
-        }
-#pragma unroll
-        for (int i = 0; i < PER; ++i)
-            if (i * 32 + lane == bi) v[i] = -1.f;
+            if (i * 32 + lane == bi) key[i] = 0u;
+        const float bp = __uint_as_float(gm - 1u);
         if (lane == j) { my_p = bp; my_i = bi; }
         tot = __fadd_rn(tot, bp);
     }
