@@ -216,7 +216,9 @@ def bench_prefill(args, world, rank, dev):
     roofline = {"kernel": "grouped_gemm_pair_kernel<SwiGLU> (routed gate/up)", "bound": "tensor",
                 "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(achieved / pk["bf16_tflops"], 4), "peak_source": f"{src} bf16 burst",
-                "traffic": None, "ms_per_launch": round(gu_ms, 4),
+                # dram__bytes_read.sum + dram__bytes_write.sum of this launch (587.6 + 8.1 MB),
+                # ncu capture of `bench.py --profile-case gu`, profiles/grouped_gemm_pair_gate_up_T4096.md
+                "traffic": 595.7e6, "traffic_unit": "B", "ms_per_launch": round(gu_ms, 4),
                 "algorithmic_flops_per_launch": gu_flops}
     layer_tflops = prefill_flops(T_PREFILL) / (ms * 1e-3) / 1e12
 
@@ -234,7 +236,9 @@ def bench_prefill(args, world, rank, dev):
         e2e()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(time_events(e2e, args.steps, stream), world)
-    launches_per_step = 10
+    # this library's kernels per layer: top-k, permute (hist, scan, scatter), gate/up, down,
+    # combine; the router logits run on cuBLAS and are not counted
+    launches_per_step = 7
     return dict(value=value, ms=ms, clocks=clk.summary(), roofline=roofline, layer_tflops=layer_tflops,
                 e2e={"value": world * T_PREFILL / (e2e_ms * 1e-3), "unit": "tokens/s",
                      "h2d_bytes_per_step": T_PREFILL * H * 2, "d2h_bytes_per_step": T_PREFILL * H * 2,
