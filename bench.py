@@ -9,9 +9,9 @@ each layer's weights (0.83 GB) exceed the 126 MB L2, and steps rotate over disti
 layers.  ``decode`` reports the decode configuration (M=1 and M=4 tokens, microseconds
 per layer) over a CUDA-graphed rotation of 16 distinct layers (13 GB of weights).
 
-With ``--gpus N`` under torchrun each rank runs the same per-GPU workload (weak scaling):
-the experts are sharded expert-parallel and tokens are exchanged with NCCL all-to-all
-when ``fnx.ep`` is available, otherwise each rank runs an independent replica.
+With ``--gpus N`` under torchrun each rank brings its own T=4096 tokens (weak scaling); the
+experts are sharded expert-parallel (E/N per GPU, ``fnx.ep``) and token rows go to their
+experts' owners and back with NCCL all-to-all-v.  Decode is reported at N=1 only.
 
 ``--impl reference`` times the reference's algorithm on the host CPU (the oracle port of
 ``FnLayer._moe``; the reference itself is Python + torch_npu and cannot run here) on a
@@ -177,7 +177,16 @@ def bench_prefill(args, world, rank, dev):
     from fnx import _lib
     from fnx.engine import EPI_SWIGLU_F32, _grouped_w4
     nl = 2
-    layers = make_layers(nl, dev)
+    full = make_layers(nl, dev)
+    if world > 1:
+        # expert parallel: rank r keeps experts [r*E/N, (r+1)*E/N) of every layer (the same
+        # seeded layers on every rank) and exchanges token rows with NCCL all-to-all
+        from fnx.ep import ExpertParallelMoE
+        layers = [ExpertParallelMoE.from_layer(lay, rank, world) for lay in full]
+        full = full[:1]
+        torch.cuda.empty_cache()
+    else:
+        layers = full
     xs = [synth.make_tokens(T_PREFILL, H, seed=1000 + rank * 10 + i, device=dev) for i in range(nl)]
     stream = torch.cuda.current_stream(dev)
     step = [0]
@@ -185,7 +194,7 @@ def bench_prefill(args, world, rank, dev):
     def run():
         i = step[0] % nl
         step[0] += 1
-        return layers[i].prefill(xs[i])
+        return layers[i](xs[i]) if world > 1 else layers[i].prefill(xs[i])
 
     for _ in range(args.warmup):
         run()
@@ -199,8 +208,20 @@ def bench_prefill(args, world, rank, dev):
     ms = max_over_ranks(ms, world)
     value = world * T_PREFILL / (ms * 1e-3)
 
-    # dominant kernel: routed gate/up grouped GEMM + fused SwiGLU, timed alone
-    lay = layers[0]
+    ep = None
+    if world > 1:
+        sc, rc = layers[(step[0] - 1) % nl].last_counts
+        t = torch.tensor([sum(rc), sum(sc) - sc[rank]], dtype=torch.float64, device=dev)
+        tmax, tsum = t.clone(), t.clone()
+        torch.distributed.all_reduce(tmax, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(tsum)
+        row = H * 2
+        ep = {"experts_per_gpu": E // world, "exchange": "per-slot rows, NCCL all-to-all-v (dispatch + combine)",
+              "recv_rows_max_over_mean": round(float(tmax[0] / (tsum[0] / world)), 4),
+              "a2a_bytes_per_step_per_gpu_max": int(2 * tmax[1] * row)}
+
+    # dominant kernel: routed gate/up grouped GEMM + fused SwiGLU (one-GPU form), timed alone
+    lay = full[0]
     _, d = lay.prefill(xs[0], details=True)
     act = torch.empty(T_PREFILL * K_TOP, I, dtype=torch.bfloat16, device=dev)
 
@@ -237,9 +258,11 @@ def bench_prefill(args, world, rank, dev):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(time_events(e2e, args.steps, stream), world)
     # this library's kernels per layer: top-k, permute (hist, scan, scatter), gate/up, down,
-    # combine; the router logits run on cuBLAS and are not counted
-    launches_per_step = 7
-    return dict(value=value, ms=ms, clocks=clk.summary(), roofline=roofline, layer_tflops=layer_tflops,
+    # combine; the router logits run on cuBLAS and are not counted.  Expert parallel adds the
+    # dispatch layout (3), the dispatch and return row gathers (2) and the owner's permutation (3)
+    # in place of the one-GPU permutation.
+    launches_per_step = 12 if world > 1 else 7
+    return dict(value=value, ms=ms, clocks=clk.summary(), roofline=roofline, layer_tflops=layer_tflops, ep=ep,
                 e2e={"value": world * T_PREFILL / (e2e_ms * 1e-3), "unit": "tokens/s",
                      "h2d_bytes_per_step": T_PREFILL * H * 2, "d2h_bytes_per_step": T_PREFILL * H * 2,
                      "ms_per_step": round(e2e_ms, 4)},
@@ -352,14 +375,15 @@ def main():
         return
 
     r = bench_prefill(args, world, rank, dev)
-    dec = None if args.no_decode else bench_decode(dev)
+    dec = None if (args.no_decode or world > 1) else bench_decode(dev)
     cpu = cpu_baseline(args.cpu_sample) if (rank == 0 and world == 1) else None
     if rank == 0:
         line = {"metric": METRIC, "value": round(r["value"], 1), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded; shapes/distributions of the workload definition)",
-                "config": dict(config, parallelism="replicas" if world > 1 else "single GPU"),
+                "config": dict(config, parallelism=f"ep{world}" if world > 1 else "single GPU",
+                               **({"expert_parallel": r["ep"]} if r["ep"] else {})),
                 "clocks": r["clocks"], "e2e": r["e2e"], "gpu_launches": r["gpu_launches"],
                 "roofline": r["roofline"], "layer_tflops": round(r["layer_tflops"], 1), "decode": dec,
                 "cpu_baseline": cpu}

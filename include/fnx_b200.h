@@ -79,6 +79,30 @@ size_t fnx_moe_permute_workspace(int n, int E);
 int fnx_moe_permute(void* idx, void* order, void* inverse, void* ends, void* counts, int n, int E, void* workspace,
                     size_t ws_bytes, void* stream);
 
+/* Expert-parallel dispatch layout (no counterpart in the reference, whose MoE runs on one
+ * device; the exchange it serves is the NCCL all-to-all of the expert-parallel layer):
+ * experts are owned in contiguous blocks of E/G by G ranks.  A stable counting sort of the
+ * n = T*k slot ids by owner rank id / (E/G): order int64 [n] lists the slots owner-major
+ * ((token*k + slot) order inside an owner), inverse int64 [n] is its inverse permutation
+ * (the row of slot q in the owner-major buffer), counts int64 [G] the slots per owner.
+ * E % G == 0; ids outside [0, E) set device error 2 and get no row.
+ * workspace: fnx_ep_layout_workspace(n, G) bytes. */
+size_t fnx_ep_layout_workspace(int n, int G);
+int fnx_ep_dispatch_layout(const void* idx, int n, int E, int G, void* order, void* inverse, void* counts,
+                           void* workspace, size_t ws_bytes, void* stream);
+
+/* Row gather of the expert-parallel exchange: dst[p] = src[index[p] / index_div] for p < n,
+ * bf16 rows of H elements with leading dimensions ld_src / ld_dst (index NULL: row p).
+ * With ids_out (int64 [n]), also ids_out[p] = ids[index[p]] % ids_mod, the owner-local
+ * expert id of a dispatched slot.  A source row outside [0, src_rows) writes zeros, sets
+ * ids_out[p] = -1 and device error 2.  Dispatch: src = tokens, index = the owner-major
+ * order of fnx_ep_dispatch_layout, index_div = k, ids = the routed ids, ids_mod = E/G.
+ * Return: src = the owner's expert-major down output, index = the inverse of its local
+ * expert permutation, index_div = 1. */
+int fnx_ep_gather_rows(const void* src, long long ld_src, long long src_rows, const void* index, int index_div,
+                       const void* ids, int ids_mod, void* dst, long long ld_dst, void* ids_out, long long n, int H,
+                       void* stream);
+
 /* Load-time repack of the int4pack artifact (w4 int32 [E,K,Nw/8] expert-major, scales bf16
  * [E,K/gs,Nw]; tools/repack_w4a16.py, tools/repack_w4_em.py) into the tile blocks the B200
  * kernels stream: tiles int32 [E, Nw/128, K/64, 1088], one 4352-byte block per (expert,

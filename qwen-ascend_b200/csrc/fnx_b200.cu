@@ -12,6 +12,7 @@
 #include "fnx_common.cuh"
 #include "kernels_combine.cuh"
 #include "kernels_decode.cuh"
+#include "kernels_ep.cuh"
 #include "kernels_gemm.cuh"
 #include "kernels_gemm_pair.cuh"
 #include "kernels_route.cuh"
@@ -329,11 +330,10 @@ FNX_API size_t fnx_moe_permute_workspace(int n, int E) {
     return (size_t)(chunks < 1 ? 1 : chunks) * E * sizeof(int);
 }
 
-FNX_API int fnx_moe_permute(void* idx, void* order, void* inverse, void* ends, void* counts, int n, int E,
-                            void* workspace, size_t ws_bytes, void* stream) {
-    if (n < 0 || E < 1 || E > PERM_MAX_E) return FNX_EARG;
-    if (ws_bytes < fnx_moe_permute_workspace(n, E)) return FNX_EWORKSPACE;
-    cudaStream_t st = (cudaStream_t)stream;
+namespace {
+// stable counting sort of n ids into E buckets of `div` consecutive ids each
+int permute_launch(const void* idx, void* order, void* inverse, void* ends, void* counts, int n, int E, int div,
+                   void* workspace, cudaStream_t st) {
     const int chunks = (n + PERM_CHUNK - 1) / PERM_CHUNK;
     int* hist = (int*)workspace;
     if (chunks == 0) {
@@ -341,10 +341,54 @@ FNX_API int fnx_moe_permute(void* idx, void* order, void* inverse, void* ends, v
         if (counts) cudaMemsetAsync(counts, 0, sizeof(int64_t) * E, st);
         return launch_rc();
     }
-    permute_hist_kernel<<<chunks, 256, E * sizeof(int), st>>>((const int64_t*)idx, n, E, hist);
+    permute_hist_kernel<<<chunks, 256, E * sizeof(int), st>>>((const int64_t*)idx, n, E, div, hist);
     permute_scan_kernel<<<1, 1024, 0, st>>>(hist, chunks, E, (int64_t*)ends, (int64_t*)counts);
-    permute_scatter_kernel<<<chunks, 32, (E + PERM_CHUNK) * sizeof(int), st>>>((const int64_t*)idx, n, E, hist, (int64_t*)order,
-                                                               (int64_t*)inverse);
+    permute_scatter_kernel<<<chunks, 32, (E + PERM_CHUNK) * sizeof(int), st>>>((const int64_t*)idx, n, E, div, hist,
+                                                                                (int64_t*)order, (int64_t*)inverse);
+    return launch_rc();
+}
+}  // namespace
+
+FNX_API int fnx_moe_permute(void* idx, void* order, void* inverse, void* ends, void* counts, int n, int E,
+                            void* workspace, size_t ws_bytes, void* stream) {
+    if (n < 0 || E < 1 || E > PERM_MAX_E) return FNX_EARG;
+    if (ws_bytes < fnx_moe_permute_workspace(n, E)) return FNX_EWORKSPACE;
+    return permute_launch(idx, order, inverse, ends, counts, n, E, 1, workspace, (cudaStream_t)stream);
+}
+
+// ======================================================================== expert parallel
+FNX_API size_t fnx_ep_layout_workspace(int n, int G) {
+    return (fnx_moe_permute_workspace(n, G) + 15) / 16 * 16 + sizeof(int64_t) * (size_t)(G < 1 ? 1 : G);
+}
+
+FNX_API int fnx_ep_dispatch_layout(const void* idx, int n, int E, int G, void* order, void* inverse, void* counts,
+                                   void* workspace, size_t ws_bytes, void* stream) {
+    if (n < 0 || G < 1 || G > PERM_MAX_E || E < G || E % G != 0 || !counts) return FNX_EARG;
+    if (ws_bytes < fnx_ep_layout_workspace(n, G)) return FNX_EWORKSPACE;
+    void* ends = (char*)workspace + (fnx_moe_permute_workspace(n, G) + 15) / 16 * 16;
+    return permute_launch(idx, order, inverse, ends, counts, n, G, E / G, workspace, (cudaStream_t)stream);
+}
+
+FNX_API int fnx_ep_gather_rows(const void* src, long long ld_src, long long src_rows, const void* index, int index_div,
+                               const void* ids, int ids_mod, void* dst, long long ld_dst, void* ids_out, long long n,
+                               int H, void* stream) {
+    if (n < 0 || H < 1 || ld_src < H || ld_dst < H || src_rows < 0 || index_div < 1) return FNX_EARG;
+    if (ids_out && (!ids || !index || ids_mod < 1)) return FNX_EARG;
+    if (n == 0) return FNX_OK;
+    const bool vec = H % 8 == 0 && ld_src % 8 == 0 && ld_dst % 8 == 0 && aligned16(src) && aligned16(dst);
+    const long long warps_needed = n;
+    long long blocks = (warps_needed + 7) / 8;
+    const long long cap = (long long)num_sms() * 8;
+    if (blocks > cap) blocks = cap;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (vec)
+        ep_gather_rows_kernel<true><<<(int)blocks, 256, 0, st>>>((const bf16*)src, ld_src, src_rows, (const int64_t*)index,
+                                                                 index_div, (const int64_t*)ids, ids_mod, (bf16*)dst,
+                                                                 ld_dst, (int64_t*)ids_out, n, H);
+    else
+        ep_gather_rows_kernel<false><<<(int)blocks, 256, 0, st>>>((const bf16*)src, ld_src, src_rows,
+                                                                  (const int64_t*)index, index_div, (const int64_t*)ids,
+                                                                  ids_mod, (bf16*)dst, ld_dst, (int64_t*)ids_out, n, H);
     return launch_rc();
 }
 

@@ -111,15 +111,18 @@ constexpr int PERM_CHUNK = 1024;
 constexpr int PERM_MAX_E = 4096;
 
 // pass 1: per-chunk histograms hist[chunk][E]
-__global__ void __launch_bounds__(256) permute_hist_kernel(const int64_t* __restrict__ ids, int n, int E,
+// Buckets: id / div for ids in [0, E*div) (div = 1: the expert itself; div = E/G: the rank
+// owning a contiguous block of experts, the expert-parallel dispatch).
+__global__ void __launch_bounds__(256) permute_hist_kernel(const int64_t* __restrict__ ids, int n, int E, int div,
                                                            int* __restrict__ hist) {
     extern __shared__ int sh[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = 0;
     __syncthreads();
     const int c0 = blockIdx.x * PERM_CHUNK;
+    const long long lim = (long long)E * div;
     for (int i = c0 + threadIdx.x; i < min(n, c0 + PERM_CHUNK); i += blockDim.x) {
         const long long e = ids[i];
-        if (e >= 0 && e < E) atomicAdd(&sh[e], 1);
+        if (e >= 0 && e < lim) atomicAdd(&sh[div == 1 ? e : e / div], 1);
         else fnx_flag_error(FNX_DEVERR_BADID);
     }
     __syncthreads();
@@ -169,7 +172,7 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int* __restrict__ hi
 
 // pass 3: one warp per chunk walks its entries in order; __match_any_sync gives each
 // entry its rank among equal ids in the same 32-entry batch, so positions are stable.
-__global__ void __launch_bounds__(32) permute_scatter_kernel(const int64_t* __restrict__ ids, int n, int E,
+__global__ void __launch_bounds__(32) permute_scatter_kernel(const int64_t* __restrict__ ids, int n, int E, int div,
                                                              const int* __restrict__ start,
                                                              int64_t* __restrict__ order, int64_t* __restrict__ inverse) {
     extern __shared__ int cursor[];
@@ -181,7 +184,7 @@ __global__ void __launch_bounds__(32) permute_scatter_kernel(const int64_t* __re
 #pragma unroll 8
     for (int i = c0 + lane; i < c1; i += 32) {
         const long long e = ids[i];
-        sid[i - c0] = (e >= 0 && e < E) ? (int)e : -1;
+        sid[i - c0] = (e >= 0 && e < (long long)E * div) ? (int)(div == 1 ? e : e / div) : -1;
     }
     __syncwarp();
     for (int b = c0; b < c1; b += 32) {

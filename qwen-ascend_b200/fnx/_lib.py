@@ -32,6 +32,9 @@ SIGNATURES = {
     "fnx_router_topk": ([P, LL, P, P, P, P, I, I, I, P], I),
     "fnx_moe_permute_workspace": ([I, I], SZ),
     "fnx_moe_permute": ([P] * 5 + [I, I, P, SZ, P], I),
+    "fnx_ep_layout_workspace": ([I, I], SZ),
+    "fnx_ep_dispatch_layout": ([P, I, I, I, P, P, P, P, SZ, P], I),
+    "fnx_ep_gather_rows": ([P, LL, LL, P, I, P, I, P, LL, P, LL, I, P], I),
     "fnx_moe_grouped_w4": ([P, LL, LL, P, I, P, P, P, LL] + [I] * 5 + [P], I),
     "fnx_w4_tiles_bytes": ([I] * 3, SZ),
     "fnx_repack_w4_tiles": ([P] * 3 + [I] * 5 + [P], I),

@@ -197,6 +197,10 @@ class MoELayer:
                                 swiglu=False)
         self.gu_t, self.sh_gu_t = self.gu_all[:E], self.gu_all[E:]
         self.dn_t, self.sh_dn_t = self.dn_all[:E], self.dn_all[E:]
+        self._init_router(gate_w, sh_gate, k, gs, bias)
+
+    def _init_router(self, gate_w, sh_gate, k, gs, bias):
+        self.E, self.H = gate_w.shape
         self.k, self.gs = k, gs
         R = self.E + 1
         self.R = R

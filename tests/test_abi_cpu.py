@@ -62,10 +62,21 @@ def test_host_side_rejections(lib):
     assert lib.fnx_w4gemv_launch(None, None, None, None, None, None, None, 1024, 2048, 10, 20, 3, None) == -1
     assert lib.fnx_moe_decode_w4(*([None] * 10), 17, 2048, 512, 512, 10, None, 0, None) == -1
     assert lib.fnx_moe_decode_w4(*([None] * 10), 1, 2048, 512, 512, 10, None, 0, None) == -5
+    # expert-parallel dispatch layout and row gather
+    d = lib.fnx_ep_dispatch_layout
+    assert d(None, 40960, 512, 3, None, None, None, None, 0, None) == -1          # E % G
+    assert d(None, 40960, 4, 8, None, None, None, None, 0, None) == -1            # G > E
+    assert d(None, 40960, 512, 8, None, None, None, None, 0, None) == -1          # no counts
+    assert d(None, 40960, 512, 8, None, None, 8, None, 0, None) == -5             # workspace
+    gr = lib.fnx_ep_gather_rows
+    assert gr(None, 2048, 10, None, 0, None, 1, None, 2048, None, 5, 2048, None) == -1      # index_div 0
+    assert gr(None, 1000, 10, None, 1, None, 1, None, 2048, None, 5, 2048, None) == -1      # ld_src < H
+    assert gr(None, 2048, 10, None, 1, None, 1, None, 2048, 8, 5, 2048, None) == -1         # ids_out w/o ids
 
 
 def test_workspace_sizes(lib):
     assert lib.fnx_moe_permute_workspace(40960, 512) == 40 * 512 * 4
+    assert lib.fnx_ep_layout_workspace(40960, 8) == 40 * 8 * 4 + 8 * 8
     assert lib.fnx_moe_decode_workspace(0, 2048, 512, 512, 10) == 0
     n1 = lib.fnx_moe_decode_workspace(1, 2048, 512, 512, 10)
     n16 = lib.fnx_moe_decode_workspace(16, 2048, 512, 512, 10)
