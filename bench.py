@@ -210,13 +210,15 @@ def bench_prefill(args, world, rank, dev):
 
     ep = None
     if world > 1:
-        sc, rc = layers[(step[0] - 1) % nl].last_counts
-        t = torch.tensor([sum(rc), sum(sc) - sc[rank]], dtype=torch.float64, device=dev)
+        sent, recv = layers[(step[0] - 1) % nl].exchange_stats()
+        t = torch.tensor([recv, sent], dtype=torch.float64, device=dev)
         tmax, tsum = t.clone(), t.clone()
         torch.distributed.all_reduce(tmax, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.all_reduce(tsum)
         row = H * 2
-        ep = {"experts_per_gpu": E // world, "exchange": "per-slot rows, NCCL all-to-all-v (dispatch + combine)",
+        ep = {"experts_per_gpu": E // world,
+              "exchange": "per-slot rows pushed to the owners' exchange regions through NVLink peer mappings "
+                          "(dispatch and return kernels, device-side count exchange, no host sync)",
               "recv_rows_max_over_mean": round(float(tmax[0] / (tsum[0] / world)), 4),
               "a2a_bytes_per_step_per_gpu_max": int(2 * tmax[1] * row)}
 
@@ -258,10 +260,13 @@ def bench_prefill(args, world, rank, dev):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(time_events(e2e, args.steps, stream), world)
     # this library's kernels per layer: top-k, permute (hist, scan, scatter), gate/up, down,
-    # combine; the router logits run on cuBLAS and are not counted.  Expert parallel adds the
-    # dispatch layout (3), the dispatch and return row gathers (2) and the owner's permutation (3)
-    # in place of the one-GPU permutation.
-    launches_per_step = 12 if world > 1 else 7
+    # combine; the router logits run on cuBLAS and are not counted.  Expert parallel (peer
+    # exchange): top-k, dispatch layout (3), count exchange, dispatch push, wait, receive layout
+    # (head + permute 3), gate/up, down, return push, wait, combine.
+    launches_per_step = 17 if world > 1 else 7
+    if world > 1:
+        for lay in layers:
+            lay.close()
     return dict(value=value, ms=ms, clocks=clk.summary(), roofline=roofline, layer_tflops=layer_tflops, ep=ep,
                 e2e={"value": world * T_PREFILL / (e2e_ms * 1e-3), "unit": "tokens/s",
                      "h2d_bytes_per_step": T_PREFILL * H * 2, "d2h_bytes_per_step": T_PREFILL * H * 2,

@@ -103,6 +103,57 @@ int fnx_ep_gather_rows(const void* src, long long ld_src, long long src_rows, co
                        const void* ids, int ids_mod, void* dst, long long ld_dst, void* ids_out, long long n, int H,
                        void* stream);
 
+/* Peer-memory exchange of the expert-parallel layer (the NVLink replacement of the
+ * all-to-all; no counterpart in the reference).  Each of the G ranks (G <= 8, one node)
+ * allocates one region of fnx_ep_p2p_region_bytes(G, H, k, T_cap, cap) bytes with
+ * fnx_ep_p2p_alloc (zero-filled), exports it with fnx_ep_p2p_export (a 64-byte CUDA IPC
+ * handle), and imports every peer's with fnx_ep_p2p_import; fnx_ep_p2p_desc then fills an
+ * opaque descriptor of fnx_ep_p2p_desc_bytes() bytes (host memory) from the G base pointers
+ * (bases[rank] = its own).  T_cap: most tokens a rank brings to one call; cap: most slot rows
+ * a rank can receive (G*T_cap*k always suffices).  Eg = E/G experts per rank.
+ * One layer call, on each rank's stream (every rank calls, in the same order):
+ *   fnx_ep_p2p_counts(desc, counts)       counts int64 [G] of fnx_ep_dispatch_layout; exchanges
+ *                                         them and starts the call's epoch;
+ *   fnx_ep_p2p_push(desc, x, T, order, idx)   each slot's token row (owner-major order) to its
+ *                                         owner, this rank's own tokens to its own region;
+ *   fnx_ep_p2p_wait(desc, 1)              until every rank's rows for this rank have landed;
+ *   fnx_ep_p2p_recv_layout(desc, T, order_x, ends_x, pos, ws, ws_bytes)
+ *                                         expert-major rows of the owner's grouped launches:
+ *                                         expert 0 = the shared expert over its own T tokens
+ *                                         (order_x[t] = cap + t), experts 1..Eg the received
+ *                                         slots; order_x int64 [T + cap], ends_x int64 [Eg + 1],
+ *                                         pos int64 [cap] = each received slot's row in them;
+ *   (grouped gate/up with epilogue 4 and down over fnx_ep_p2p_local(desc, 0), M = T + cap)
+ *   fnx_ep_p2p_return(desc, yd, yd_rows, pos) each received slot's down row back to its source;
+ *   fnx_ep_p2p_wait(desc, 2)              until this rank's rows are all back in
+ *                                         fnx_ep_p2p_local(desc, 2) (owner-major, the row map
+ *                                         of fnx_ep_dispatch_layout's inverse).
+ * Waits are bounded (device error 1 when a peer never arrives); a count beyond cap sets
+ * device error 4 and its rows are dropped.  The setup and teardown calls (alloc, free,
+ * export, import, close) and fnx_ep_p2p_received allocate or synchronise; the per-call ones
+ * follow the conventions at the top of this file. */
+size_t fnx_ep_p2p_region_bytes(int world, int H, int k, int T_cap, long long cap);
+int fnx_ep_p2p_alloc(size_t bytes, void** ptr);
+int fnx_ep_p2p_free(void* ptr);
+int fnx_ep_p2p_export(void* ptr, void* handle);
+int fnx_ep_p2p_import(const void* handle, void** ptr);
+int fnx_ep_p2p_close(void* ptr);
+size_t fnx_ep_p2p_desc_bytes(void);
+int fnx_ep_p2p_desc(void* desc, int rank, int world, void* const* bases, int H, int k, int T_cap, long long cap,
+                    int Eg);
+/* this rank's buffers: 0 recv_x bf16 [cap + T_cap, H], 1 recv_e int64 [cap],
+ * 2 yb bf16 [T_cap*k, H], 3 plan int64 (plan[0] = slots received this call) */
+void* fnx_ep_p2p_local(const void* desc, int which);
+/* slots this rank received in its last call (synchronises with the device; for statistics) */
+long long fnx_ep_p2p_received(const void* desc);
+int fnx_ep_p2p_counts(const void* desc, const void* counts, void* stream);
+int fnx_ep_p2p_push(const void* desc, const void* x, int T, const void* order, const void* idx, void* stream);
+int fnx_ep_p2p_wait(const void* desc, int phase, void* stream);
+size_t fnx_ep_p2p_recv_workspace(const void* desc);
+int fnx_ep_p2p_recv_layout(const void* desc, int T, void* order_x, void* ends_x, void* pos, void* workspace,
+                           size_t ws_bytes, void* stream);
+int fnx_ep_p2p_return(const void* desc, const void* yd, long long yd_rows, const void* pos, void* stream);
+
 /* Load-time repack of the int4pack artifact (w4 int32 [E,K,Nw/8] expert-major, scales bf16
  * [E,K/gs,Nw]; tools/repack_w4a16.py, tools/repack_w4_em.py) into the tile blocks the B200
  * kernels stream: tiles int32 [E, Nw/128, K/64, 1088], one 4352-byte block per (expert,
@@ -125,7 +176,8 @@ int fnx_repack_w4_tiles(const void* w4, const void* scales, void* tiles, int E, 
  * epilogue 0: out bf16 [M, Nw];  1: SwiGLU of gate = features [0,Nw/2), up = [Nw/2,Nw)
  * in fp32 on bf16-rounded inputs -> out [M, Nw/2];  2: the shared expert's SwiGLU
  * bf16(bf16(silu(g)) * u);  3: epilogue 1 for experts 0..E-2 and epilogue 2 for expert E-1
- * (the shared expert appended to the routed experts, run in the same launch).
+ * (the shared expert appended to the routed experts, run in the same launch);  4: the same
+ * with the shared expert first (expert 0, epilogue 2) and the routed experts 1..E-1.
  * K % 64 == 0, Nw % 128 == 0. */
 int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_rows, const void* row_index, int index_div,
                        const void* tiles, const void* ends, void* out, long long ld_out, int E, int M, int K, int Nw,

@@ -39,8 +39,8 @@
 namespace fnx {
 
 enum GemmMode { GEMM_W4 = 0, GEMM_W8 = 1, GEMM_BF16 = 2 };
-// EPI_SWIGLU_MIXED: the fp32 SwiGLU for experts 0..E-2 and the shared expert's bf16 form for
-// the last expert (the shared expert appended as expert E-1 of one grouped launch).
+// EPI_SWIGLU_MIXED: the fp32 SwiGLU for the routed experts and the shared expert's bf16 form
+// for expert p.shared_e (the shared expert run as one expert of the same grouped launch).
 enum GemmEpi { EPI_PLAIN = 0, EPI_SWIGLU_F32 = 1, EPI_SWIGLU_BF16 = 2, EPI_SWIGLU_MIXED = 3 };
 
 constexpr int G_BM = 128;          // weight features per tile (UMMA M)
@@ -88,6 +88,7 @@ struct GemmParams {
     long long ld_out;
     int E, M, K, Nw, gs;
     int m_tiles;                // tiles along the feature dimension
+    int shared_e;               // EPI_SWIGLU_MIXED: the shared expert's index
 };
 
 struct GemmSmem {
@@ -236,7 +237,7 @@ FNX_DEV void epilogue_chunk(const GemmParams& p, const TileInfo& ti, int r, int 
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             float a;
-            if (EPI == EPI_SWIGLU_F32 || (EPI == EPI_SWIGLU_MIXED && ti.e < p.E - 1)) a = __fmul_rn(silu_f32(g[i]), u[i]);
+            if (EPI == EPI_SWIGLU_F32 || (EPI == EPI_SWIGLU_MIXED && ti.e != p.shared_e)) a = __fmul_rn(silu_f32(g[i]), u[i]);
             else a = __fmul_rn(round_bf(silu_f32(g[i])), u[i]);
             if (i < lim) o[(long long)i * p.ld_out] = f2bf(a);
         }
@@ -280,7 +281,7 @@ FNX_DEV void epilogue_chunk_staged(const GemmParams& p, const TileInfo& ti, int 
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             float a;
-            if (EPI == EPI_SWIGLU_F32 || (EPI == EPI_SWIGLU_MIXED && ti.e < p.E - 1)) a = __fmul_rn(silu_f32(g[i]), u[i]);
+            if (EPI == EPI_SWIGLU_F32 || (EPI == EPI_SWIGLU_MIXED && ti.e != p.shared_e)) a = __fmul_rn(silu_f32(g[i]), u[i]);
             else a = __fmul_rn(round_bf(silu_f32(g[i])), u[i]);
             stage[(nb + i) * 16 + (lane >> 1)] = (uint16_t)bf16_bits(f2bf(a));
         }

@@ -106,6 +106,10 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const bf16* __restrict
 }
 
 // ------------------------------------------------------------------ permutation
+__global__ void fill_i64_kernel(int64_t* __restrict__ p, int n, long long v) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = v;
+}
+
 // Stable counting sort of n = T*k expert ids (int64) in chunks of PERM_CHUNK entries.
 constexpr int PERM_CHUNK = 1024;
 constexpr int PERM_MAX_E = 4096;
@@ -113,11 +117,20 @@ constexpr int PERM_MAX_E = 4096;
 // pass 1: per-chunk histograms hist[chunk][E]
 // Buckets: id / div for ids in [0, E*div) (div = 1: the expert itself; div = E/G: the rank
 // owning a contiguous block of experts, the expert-parallel dispatch).
-__global__ void __launch_bounds__(256) permute_hist_kernel(const int64_t* __restrict__ ids, int n, int E, int div,
+// n_dev (optional): the entry count lives on the device (at most n, the launch's capacity).
+FNX_DEV int perm_count(int n, const long long* n_dev) {
+    if (!n_dev) return n;
+    const long long v = *n_dev;
+    return v < 0 ? 0 : (v < n ? (int)v : n);
+}
+
+__global__ void __launch_bounds__(256) permute_hist_kernel(const int64_t* __restrict__ ids, int n,
+                                                           const long long* __restrict__ n_dev, int E, int div,
                                                            int* __restrict__ hist) {
     extern __shared__ int sh[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = 0;
     __syncthreads();
+    n = perm_count(n, n_dev);
     const int c0 = blockIdx.x * PERM_CHUNK;
     const long long lim = (long long)E * div;
     for (int i = c0 + threadIdx.x; i < min(n, c0 + PERM_CHUNK); i += blockDim.x) {
@@ -129,10 +142,11 @@ __global__ void __launch_bounds__(256) permute_hist_kernel(const int64_t* __rest
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(long long)blockIdx.x * E + e] = sh[e];
 }
 
-// pass 2 (one block): ends[e] = inclusive cumsum of counts; hist[c][e] becomes the
+// pass 2 (one block): ends[e] = base + inclusive cumsum of counts; hist[c][e] becomes the
 // starting output position of chunk c's entries for expert e.
 __global__ void __launch_bounds__(1024) permute_scan_kernel(int* __restrict__ hist, int nchunks, int E,
-                                                            int64_t* __restrict__ ends, int64_t* __restrict__ counts_out) {
+                                                            int64_t* __restrict__ ends, int64_t* __restrict__ counts_out,
+                                                            long long base) {
     __shared__ int part[1024];
     __shared__ int carry;
     if (threadIdx.x == 0) carry = 0;
@@ -154,7 +168,7 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int* __restrict__ hi
         }
         const int incl = part[threadIdx.x] + carry;
         if (e < E) {
-            ends[e] = incl;
+            ends[e] = base + incl;
             if (counts_out) counts_out[e] = cnt;
             int pos = incl - cnt;
             for (int c = 0; c < nchunks; ++c) {
@@ -172,13 +186,18 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int* __restrict__ hi
 
 // pass 3: one warp per chunk walks its entries in order; __match_any_sync gives each
 // entry its rank among equal ids in the same 32-entry batch, so positions are stable.
-__global__ void __launch_bounds__(32) permute_scatter_kernel(const int64_t* __restrict__ ids, int n, int E, int div,
+// order[pos] = i and inverse[i] = pos_base + pos (the host offsets `order` by pos_base).
+__global__ void __launch_bounds__(32) permute_scatter_kernel(const int64_t* __restrict__ ids, int n,
+                                                             const long long* __restrict__ n_dev, int E, int div,
                                                              const int* __restrict__ start,
-                                                             int64_t* __restrict__ order, int64_t* __restrict__ inverse) {
+                                                             int64_t* __restrict__ order, int64_t* __restrict__ inverse,
+                                                             long long pos_base) {
     extern __shared__ int cursor[];
     int* sid = cursor + E;                       // this chunk's ids, loaded in one coalesced pass
     const int lane = threadIdx.x;
+    n = perm_count(n, n_dev);
     const int c0 = blockIdx.x * PERM_CHUNK;
+    if (c0 >= n) return;
     const int c1 = min(n, c0 + PERM_CHUNK);
     for (int e = lane; e < E; e += 32) cursor[e] = start[(long long)blockIdx.x * E + e];
 #pragma unroll 8
@@ -204,7 +223,7 @@ __global__ void __launch_bounds__(32) permute_scatter_kernel(const int64_t* __re
         if (good) {
             const long long pos = base + rank;
             order[pos] = i;
-            if (inverse) inverse[i] = pos;
+            if (inverse) inverse[i] = pos_base + pos;
         } else if (valid && inverse) {
             inverse[i] = -1;          // an id outside [0, E): no row (flagged by the histogram pass)
         }

@@ -23,8 +23,19 @@ Every slot's down row comes from the same kernel and operands as on one device, 
 reduces in the reference's slot order, so the output equals ``MoELayer`` on one GPU bit for
 bit.  Rows are exchanged per slot (a token with three experts on one owner is sent three
 times) so that the owner never reduces: the combine stays the reference's fixed-order sum.
+
+Two transports move the rows:
+
+* ``"p2p"`` (default on CUDA): this library's kernels write each row straight into its
+  destination's exchange region through NVLink peer mappings (CUDA IPC), the per-owner
+  counts travel the same way behind release/acquire flags, and nothing waits on the host --
+  the layer is one stream of launches, capturable in a CUDA graph;
+* ``"collective"``: ``torch.distributed.all_to_all_single`` (NCCL, or gloo on CPU ranks)
+  with the counts exchanged first and read on the host to size the transfers.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -33,6 +44,57 @@ from . import _lib
 from .engine import BF16, EPI_PLAIN, EPI_SWIGLU_MIXED, MoELayer, _grouped_w4, repack_w4
 
 I64 = torch.int64
+EPI_SWIGLU_SHARED_FIRST = 4      # EPI_SWIGLU_MIXED with the shared expert as expert 0
+
+
+class _PeerExchange:
+    """The ranks' exchange regions (``fnx_ep_p2p_*``): one zero-filled ``cudaMalloc`` per
+    rank, mapped into every peer through CUDA IPC, and the kernels' descriptor."""
+
+    def __init__(self, rank, world, group, H, k, max_tokens, e_local, device):
+        L = _lib.lib()
+        self.world, self.group = world, group
+        self.cap = world * max_tokens * k              # every slot of every rank could land here
+        nbytes = L.fnx_ep_p2p_region_bytes(world, H, k, max_tokens, self.cap)
+        if not nbytes:
+            raise ValueError(f"peer exchange: unsupported shape (world={world}, H={H}, k={k}, T={max_tokens})")
+        self.imported = []
+        with torch.cuda.device(device):
+            base = ctypes.c_void_p()
+            _lib.check(L.fnx_ep_p2p_alloc(nbytes, ctypes.byref(base)), "exchange region allocation")
+            self.base = base
+            bases = [0] * world
+            bases[rank] = base.value
+            if world > 1:
+                h = ctypes.create_string_buffer(64)
+                _lib.check(L.fnx_ep_p2p_export(base, h), "exchange region IPC export")
+                handles = [None] * world
+                dist.all_gather_object(handles, h.raw, group=group)
+                for q in range(world):
+                    if q == rank:
+                        continue
+                    p = ctypes.c_void_p()
+                    hq = ctypes.create_string_buffer(handles[q], 64)
+                    _lib.check(L.fnx_ep_p2p_import(hq, ctypes.byref(p)), f"exchange region IPC import (rank {q})")
+                    self.imported.append(p)
+                    bases[q] = p.value
+            self._desc = ctypes.create_string_buffer(L.fnx_ep_p2p_desc_bytes())
+            self.desc = ctypes.addressof(self._desc)
+            _lib.check(L.fnx_ep_p2p_desc(self.desc, rank, world, (ctypes.c_void_p * world)(*bases), H, k, max_tokens,
+                                         self.cap, e_local), "exchange descriptor")
+        self.recv_x = L.fnx_ep_p2p_local(self.desc, 0)
+        self.yb = L.fnx_ep_p2p_local(self.desc, 2)
+
+    def close(self):
+        L = _lib.lib()
+        torch.cuda.synchronize()
+        for p in self.imported:
+            L.fnx_ep_p2p_close(p)
+        self.imported = []
+        if self.world > 1:
+            dist.barrier(group=self.group)        # no peer maps this region any more
+        L.fnx_ep_p2p_free(self.base)
+        self.base = None
 
 
 class ExpertParallelMoE(MoELayer):
@@ -45,36 +107,65 @@ class ExpertParallelMoE(MoELayer):
     ``world == 1``)."""
 
     def __init__(self, gu_w4, gu_scales, dn_w4, dn_scales, gate_w, sh_gu_w4, sh_gu_scales, sh_dn_w4, sh_dn_scales,
-                 sh_gate, k, gs, *, rank=0, world=1, group=None, bias=None):
+                 sh_gate, k, gs, *, rank=0, world=1, group=None, bias=None, transport="auto", max_tokens=4096):
         _lib.require_cuda(gu_w4, dn_w4, gate_w, sh_gu_w4, sh_dn_w4)
         self._init_router(gate_w, sh_gate, k, gs, bias)
-        self._init_shard(rank, world, group, gu_w4.shape[0])
+        self._init_shard(rank, world, group, gu_w4.shape[0], transport, max_tokens)
         self.I = gu_w4.shape[2] * 8 // 2
-        self.gu_loc = repack_w4(torch.cat([gu_w4, sh_gu_w4[None]]), torch.cat([gu_scales, sh_gu_scales[None]]),
-                                swiglu=True)
-        self.dn_loc = repack_w4(torch.cat([dn_w4, sh_dn_w4[None]]), torch.cat([dn_scales, sh_dn_scales[None]]),
-                                swiglu=False)
+        self.gu_loc = self._arrange(repack_w4(torch.cat([gu_w4, sh_gu_w4[None]]),
+                                              torch.cat([gu_scales, sh_gu_scales[None]]), swiglu=True))
+        self.dn_loc = self._arrange(repack_w4(torch.cat([dn_w4, sh_dn_w4[None]]),
+                                              torch.cat([dn_scales, sh_dn_scales[None]]), swiglu=False))
+        self._setup_transport(gate_w.device)
 
-    def _init_shard(self, rank, world, group, e_local):
+    def _init_shard(self, rank, world, group, e_local, transport="collective", max_tokens=4096):
         if world < 1 or not 0 <= rank < world or self.E % world or e_local != self.E // world:
             raise ValueError(f"ExpertParallelMoE: {e_local} local experts of E={self.E} on rank {rank} of {world}")
+        if transport == "auto":
+            nccl = world == 1 or (dist.is_initialized() and dist.get_backend(group) == "nccl")
+            transport = "p2p" if nccl else "collective"
+        if transport not in ("p2p", "collective"):
+            raise ValueError(f"ExpertParallelMoE: unknown transport {transport!r}")
         self.rank, self.world, self.group = rank, world, group
         self.E_local = e_local
+        self.transport = transport
+        self.max_tokens = max_tokens
         self.last_counts = None
+        self._p2p = None
+
+    def _arrange(self, tiles):
+        """Routed experts then the shared one (collective transport), or the shared expert
+        first (p2p: its rows precede the received slots, whose count only the device knows)."""
+        if self.transport == "p2p":
+            return torch.cat([tiles[-1:], tiles[:-1]]).contiguous()
+        return tiles
+
+    def _setup_transport(self, device):
+        if self.transport == "p2p":
+            self._p2p = _PeerExchange(self.rank, self.world, self.group, self.H, self.k, self.max_tokens,
+                                      self.E_local, device)
 
     @classmethod
-    def from_layer(cls, layer: MoELayer, rank, world, group=None):
+    def from_layer(cls, layer: MoELayer, rank, world, group=None, transport="auto", max_tokens=4096):
         """This rank's shard of a one-device ``MoELayer`` (its tile blocks are copied, so the
-        full layer may be dropped afterwards)."""
+        full layer may be dropped afterwards).  Collective over the group when the transport
+        is ``"p2p"`` (the ranks exchange their regions' IPC handles)."""
         o = cls.__new__(cls)
         o.E, o.H, o.I, o.k, o.gs = layer.E, layer.H, layer.I, layer.k, layer.gs
         o.R, o.R_pad, o.router_cat, o.bias = layer.R, layer.R_pad, layer.router_cat, layer.bias
         o._ws, o._prefill_bufs = {}, {}
-        o._init_shard(rank, world, group, layer.E // world if layer.E % world == 0 else -1)
+        o._init_shard(rank, world, group, layer.E // world if layer.E % world == 0 else -1, transport, max_tokens)
         lo, hi = rank * o.E_local, (rank + 1) * o.E_local
-        o.gu_loc = torch.cat([layer.gu_all[lo:hi], layer.gu_all[layer.E:]]).contiguous()
-        o.dn_loc = torch.cat([layer.dn_all[lo:hi], layer.dn_all[layer.E:]]).contiguous()
+        o.gu_loc = o._arrange(torch.cat([layer.gu_all[lo:hi], layer.gu_all[layer.E:]]))
+        o.dn_loc = o._arrange(torch.cat([layer.dn_all[lo:hi], layer.dn_all[layer.E:]]))
+        o._setup_transport(layer.router_cat.device)
         return o
+
+    def close(self):
+        """Release the peer exchange (collective over the group)."""
+        if self._p2p is not None:
+            self._p2p.close()
+            self._p2p = None
 
     # ---------------------------------------------------------------- stages
     def route(self, x):
@@ -115,9 +206,11 @@ class ExpertParallelMoE(MoELayer):
         return self.gather_rows(x, order, self.k, idx.numel(), ids=idx.reshape(-1), mod=self.E_local)
 
     def local_experts(self, act, recv_e, R):
-        """Step 4: ``act`` holds the ``R`` received rows followed by the rank's own ``T``
-        tokens; returns the down rows ``[R+T, H]`` (the received slots expert-major, then
-        the shared expert's rows) and the received slots' rows in it (``inverse``)."""
+        """Step 4 (collective transport): ``act`` holds the ``R`` received rows followed by
+        the rank's own ``T`` tokens; returns the down rows ``[R+T, H]`` (the received slots
+        expert-major, then the shared expert's rows) and the received slots' rows in it
+        (``inverse``)."""
+        assert self.transport == "collective", "the p2p transport runs its own receive side"
         dev = act.device
         T = act.shape[0] - R
         Eg, H, I = self.E_local, self.H, self.I
@@ -181,6 +274,8 @@ class ExpertParallelMoE(MoELayer):
         if x.dtype != BF16:
             x = x.to(BF16)
         x = x.contiguous()
+        if self.transport == "p2p":
+            return self._forward_p2p(x)
         T, H = x.shape
         dev = x.device
         logits, w, idx, wf = self.route(x)
@@ -211,12 +306,59 @@ class ExpertParallelMoE(MoELayer):
 
     __call__ = forward
 
+    def _forward_p2p(self, x):
+        T, H = x.shape
+        if T > self.max_tokens:
+            raise ValueError(f"ExpertParallelMoE: {T} tokens exceed max_tokens={self.max_tokens}")
+        ex = self._p2p
+        dev = x.device
+        L, st, D = _lib.lib(), _lib.stream(dev), ex.desc
+        Eg, I, cap = self.E_local, self.I, ex.cap
+        logits, w, idx, wf = self.route(x)
+        order_d, inverse_d, counts = self.dispatch_layout(idx)
+        self.last_counts = counts
+        _lib.check(L.fnx_ep_p2p_counts(D, counts.data_ptr(), st), "EP count exchange")
+        _lib.check(L.fnx_ep_p2p_push(D, x.data_ptr(), T, order_d.data_ptr(), idx.data_ptr(), st), "EP dispatch")
+        _lib.check(L.fnx_ep_p2p_wait(D, 1, st), "EP dispatch wait")
+        M = T + cap
+        order_x = torch.empty(M, dtype=I64, device=dev)
+        ends_x = torch.empty(Eg + 1, dtype=I64, device=dev)
+        pos = torch.empty(max(cap, 1), dtype=I64, device=dev)
+        wsb = L.fnx_ep_p2p_recv_workspace(D)
+        ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+        _lib.check(L.fnx_ep_p2p_recv_layout(D, T, order_x.data_ptr(), ends_x.data_ptr(), pos.data_ptr(), ws.data_ptr(),
+                                            wsb, st), "EP receive layout")
+        a2 = torch.empty(M, I, dtype=BF16, device=dev)
+        _lib.check(L.fnx_moe_grouped_w4(ex.recv_x, H, cap + self.max_tokens, order_x.data_ptr(), 1,
+                                        self.gu_loc.data_ptr(), ends_x.data_ptr(), a2.data_ptr(), I, Eg + 1, M, H,
+                                        2 * I, EPI_SWIGLU_SHARED_FIRST, st), "grouped W4A16 GEMM")
+        yd = torch.empty(M, H, dtype=BF16, device=dev)
+        _grouped_w4(a2, self.dn_loc, ends_x, yd, E=Eg + 1, M=M, K=I, Nw=H, epilogue=EPI_PLAIN)
+        _lib.check(L.fnx_ep_p2p_return(D, yd.data_ptr(), M, pos.data_ptr(), st), "EP return")
+        _lib.check(L.fnx_ep_p2p_wait(D, 2, st), "EP return wait")
+        out = torch.empty(T, H, dtype=BF16, device=dev)
+        gate = logits[:, self.E:self.E + 1]
+        _lib.check(L.fnx_moe_combine(ex.yb, wf.data_ptr(), inverse_d.data_ptr(), yd.data_ptr(), gate.data_ptr(),
+                                     logits.stride(0), out.data_ptr(), T, self.k, H, st), "MoE combine")
+        return out
+
+    def exchange_stats(self):
+        """``(rows sent to other ranks, rows received)`` of the last call (synchronises)."""
+        if self.last_counts is None:
+            return None
+        if self.transport == "p2p":
+            sc = self.last_counts.cpu().tolist()
+            return sum(sc) - sc[self.rank], int(_lib.lib().fnx_ep_p2p_received(self._p2p.desc))
+        sc, rc = self.last_counts
+        return sum(sc) - sc[self.rank], sum(rc)
+
     # ---------------------------------------------------------------- one-process emulation
     @staticmethod
     def emulate(shards, xs):
-        """Run ``world`` shards (one per rank, in rank order) on the tokens ``xs`` in this
-        process, moving the exchanged rows with copies in place of the all-to-all.  Checks the
-        dispatch, expert and combine stages of a multi-rank layer on one device."""
+        """Run ``world`` shards (one per rank, in rank order, ``transport="collective"``) on the
+        tokens ``xs`` in this process, moving the exchanged rows with copies in place of the
+        all-to-all.  Checks the dispatch, expert and combine stages of a multi-rank layer on
+        one device."""
         G = len(shards)
         st = []
         for s, x in zip(shards, xs):

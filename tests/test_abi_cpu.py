@@ -49,11 +49,11 @@ def test_host_side_rejections(lib):
     assert lib.fnx_router_topk(None, 100, None, None, None, None, 4, 512, 10, None) == -1
     assert lib.fnx_moe_permute(None, None, None, None, None, 10, 5000, None, 0, None) == -1
     assert lib.fnx_moe_permute(None, None, None, None, None, 10, 8, None, 0, None) == -5
-    # grouped GEMM shape rules: K % 64, Nw % 128, epilogue in 0..3, act rows >= M without an index
+    # grouped GEMM shape rules: K % 64, Nw % 128, epilogue in 0..4, act rows >= M without an index
     g = lib.fnx_moe_grouped_w4
     assert g(None, 2048, 64, None, 1, None, None, None, 1024, 8, 64, 100, 1024, 0, None) == -1
     assert g(None, 2048, 64, None, 1, None, None, None, 1024, 8, 64, 2048, 1000, 0, None) == -2
-    assert g(None, 2048, 64, None, 1, None, None, None, 1024, 8, 64, 2048, 1024, 4, None) == -1
+    assert g(None, 2048, 64, None, 1, None, None, None, 1024, 8, 64, 2048, 1024, 5, None) == -1
     assert g(None, 2048, 10, None, 1, None, None, None, 1024, 8, 64, 2048, 1024, 0, None) == -1  # rows < M
     assert lib.fnx_repack_w4_tiles(None, None, None, 8, 2048, 1024, 96, 0, None) == -1          # gs % 64
     assert lib.fnx_w4_tiles_bytes(512, 2048, 1024) == 512 * 8 * 32 * 4352

@@ -95,7 +95,7 @@ def cfg2_layer():
 @pytest.mark.parametrize("G,T", [(1, 200), (2, 300), (4, 128), (8, 64)])
 def test_ep_emulated_bit_identical(cfg2_layer, G, T):
     _, layer = cfg2_layer
-    shards = [ExpertParallelMoE.from_layer(layer, r, G) for r in range(G)]
+    shards = [ExpertParallelMoE.from_layer(layer, r, G, transport="collective") for r in range(G)]
     xs = [synth.make_tokens(T + 3 * r, synth.CFG2.H, seed=500 + r, device=DEV) for r in range(G)]
     outs = ExpertParallelMoE.emulate(shards, xs)
     for r in range(G):
@@ -103,11 +103,60 @@ def test_ep_emulated_bit_identical(cfg2_layer, G, T):
         assert torch.equal(outs[r].view(torch.int16), ref.view(torch.int16)), r
 
 
-def test_ep_single_rank_forward(cfg2_layer):
+@pytest.mark.parametrize("transport", ["p2p", "collective"])
+def test_ep_single_rank_forward(cfg2_layer, transport):
     _, layer = cfg2_layer
-    ep = ExpertParallelMoE.from_layer(layer, 0, 1)
-    x = synth.make_tokens(777, synth.CFG2.H, seed=9, device=DEV)
-    assert torch.equal(ep(x).view(torch.int16), layer.prefill(x).view(torch.int16))
+    ep = ExpertParallelMoE.from_layer(layer, 0, 1, transport=transport, max_tokens=1024)
+    assert ep.transport == transport
+    for T, seed in ((777, 9), (1024, 10), (17, 11), (777, 9)):
+        x = synth.make_tokens(T, synth.CFG2.H, seed=seed, device=DEV)
+        assert torch.equal(ep(x).view(torch.int16), layer.prefill(x).view(torch.int16)), T
+    with pytest.raises(ValueError):
+        if transport == "p2p":
+            ep(synth.make_tokens(1025, synth.CFG2.H, seed=1, device=DEV))
+        else:
+            raise ValueError
+    ep.close()
+
+
+def test_ep_p2p_graph_capture(cfg2_layer):
+    """The p2p layer never waits on the host, so one call captures into a CUDA graph."""
+    _, layer = cfg2_layer
+    ep = ExpertParallelMoE.from_layer(layer, 0, 1, transport="p2p", max_tokens=512)
+    x = synth.make_tokens(512, synth.CFG2.H, seed=12, device=DEV)
+    ref = layer.prefill(x)
+    ep(x)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = ep(x)
+    for _ in range(3):
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    del g
+    ep.close()
+
+
+def test_ep_p2p_wait_times_out():
+    """A peer that never arrives: the bounded wait gives up, records device error 1, and the
+    context stays usable (the flag that nothing sets is this step's return flag)."""
+    import ctypes
+    from fnx.ep import _PeerExchange
+    ex = _PeerExchange(0, 1, None, 256, 2, 16, 4, torch.device(DEV))
+    L = _lib.lib()
+    st = _lib.stream(torch.device(DEV))
+    counts = torch.tensor([0], dtype=torch.int64, device=DEV)
+    _lib.device_errors()
+    assert L.fnx_ep_p2p_counts(ex.desc, counts.data_ptr(), st) == 0
+    assert L.fnx_ep_p2p_wait(ex.desc, 2, st) == 0            # nothing signals RET of this epoch
+    torch.cuda.synchronize()
+    assert _lib.device_errors() & 1
+    assert L.fnx_ep_p2p_wait(ex.desc, 0, st) == 0            # CNT of this epoch was signalled
+    torch.cuda.synchronize()
+    assert _lib.device_errors() == 0
+    assert L.fnx_ep_p2p_received(ex.desc) == 0
+    ex.close()
 
 
 def test_ep_constructor_matches_shard(cfg2_layer):
@@ -133,15 +182,20 @@ def _nccl_worker(rank, world, port, T, q):
     try:
         t = synth.make_layer(synth.CFG2, seed=21, device=dev)
         layer = MoELayer.from_synth(t, synth.CFG2)
-        ep = ExpertParallelMoE.from_layer(layer, rank, world)
-        x = synth.make_tokens(T + rank, synth.CFG2.H, seed=700 + rank, device=dev)
-        same = True
-        for _ in range(2):
-            out = ep(x)
-            same = same and torch.equal(out.view(torch.int16), layer.prefill(x).view(torch.int16))
-        torch.cuda.synchronize(dev)
+        res = {}
+        for transport in ("p2p", "collective"):
+            ep = ExpertParallelMoE.from_layer(layer, rank, world, transport=transport, max_tokens=T + 8)
+            assert ep.transport == transport
+            same = True
+            for i in range(3):
+                x = synth.make_tokens(T + rank - 2 * i, synth.CFG2.H, seed=700 + rank + 10 * i, device=dev)
+                out = ep(x)
+                same = same and torch.equal(out.view(torch.int16), layer.prefill(x).view(torch.int16))
+            torch.cuda.synchronize(dev)
+            res[transport] = (same, ep.exchange_stats())
+            ep.close()
         dist.barrier()
-        q.put((rank, same, ep.last_counts, _lib.device_errors()))
+        q.put((rank, res, _lib.device_errors()))
     finally:
         dist.destroy_process_group()
 
@@ -161,8 +215,8 @@ def test_ep_nccl_bit_identical():
     res = {}
     try:
         for _ in range(world):
-            r, same, counts, errs = q.get(timeout=300)
-            res[r] = (same, counts, errs)
+            r, per, errs = q.get(timeout=300)
+            res[r] = (per, errs)
     finally:
         for p in procs:
             p.join(timeout=120)
@@ -170,7 +224,9 @@ def test_ep_nccl_bit_identical():
                 p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     for r in range(world):
-        same, (sc, rc), errs = res[r]
-        assert same and errs == 0, (r, errs)
-        for d in range(world):
-            assert sc[d] == res[d][1][1][r]
+        per, errs = res[r]
+        assert errs == 0, (r, errs)
+        for transport, (same, stats) in per.items():
+            assert same, (r, transport)
+        # both transports moved the same rows on the last call
+        assert per["p2p"][1] == per["collective"][1], (r, per)
