@@ -188,13 +188,18 @@ def bench_prefill(args, world, rank, dev):
     else:
         layers = full
     xs = [synth.make_tokens(T_PREFILL, H, seed=1000 + rank * 10 + i, device=dev) for i in range(nl)]
+    # each layer call runs as one CUDA graph (the public MoELayer.capture; the expert-parallel
+    # layer waits on nothing on the host, so it captures whole as well)
+    caps = [layers[i].capture(T_PREFILL) for i in range(nl)]
+    for i in range(nl):
+        caps[i].x.copy_(xs[i])
     stream = torch.cuda.current_stream(dev)
     step = [0]
 
     def run():
         i = step[0] % nl
         step[0] += 1
-        return layers[i](xs[i]) if world > 1 else layers[i].prefill(xs[i])
+        return caps[i].replay()
 
     for _ in range(args.warmup):
         run()
@@ -210,17 +215,19 @@ def bench_prefill(args, world, rank, dev):
 
     ep = None
     if world > 1:
-        sent, recv = layers[(step[0] - 1) % nl].exchange_stats()
-        t = torch.tensor([recv, sent], dtype=torch.float64, device=dev)
+        st = layers[(step[0] - 1) % nl].exchange_stats()
+        t = torch.tensor([st["received_slots"], st["dispatch_rows"] + st["return_rows"]], dtype=torch.float64,
+                         device=dev)
         tmax, tsum = t.clone(), t.clone()
         torch.distributed.all_reduce(tmax, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.all_reduce(tsum)
         row = H * 2
         ep = {"experts_per_gpu": E // world,
-              "exchange": "per-slot rows pushed to the owners' exchange regions through NVLink peer mappings "
-                          "(dispatch and return kernels, device-side count exchange, no host sync)",
+              "exchange": "NVLink peer stores: token rows once per owner (dispatch kernel), per-slot down rows "
+                          "written to the source by the down GEMM's epilogue; device-side count exchange, no host "
+                          "sync",
               "recv_rows_max_over_mean": round(float(tmax[0] / (tsum[0] / world)), 4),
-              "a2a_bytes_per_step_per_gpu_max": int(2 * tmax[1] * row)}
+              "nvlink_bytes_per_step_per_gpu_max": int(tmax[1] * row)}
 
     # dominant kernel: routed gate/up grouped GEMM + fused SwiGLU (one-GPU form), timed alone
     lay = full[0]
@@ -252,8 +259,7 @@ def bench_prefill(args, world, rank, dev):
     def e2e():
         i = step[0] % nl
         step[0] += 1
-        xd = xh[i].to(dev, non_blocking=True)
-        out = layers[i](xd)
+        out = caps[i](xh[i])                      # pinned host tokens in, graph replay
         outh.copy_(out, non_blocking=True)
     for _ in range(args.warmup):
         e2e()
@@ -261,10 +267,14 @@ def bench_prefill(args, world, rank, dev):
     e2e_ms = max_over_ranks(time_events(e2e, args.steps, stream), world)
     # this library's kernels per layer: top-k, permute (hist, scan, scatter), gate/up, down,
     # combine; the router logits run on cuBLAS and are not counted.  Expert parallel (peer
-    # exchange): top-k, dispatch layout (3), count exchange, dispatch push, wait, receive layout
-    # (head + permute 3), gate/up, down, return push, wait, combine.
-    launches_per_step = 17 if world > 1 else 7
+    # exchange): top-k, dispatch layout (3), token dedup, count exchange, dispatch push, wait,
+    # receive layout (head, permute 3, row destinations), gate/up, down with the return in its
+    # epilogue, signal, wait, combine.
+    launches_per_step = 19 if world > 1 else 7
+    del caps
+    torch.cuda.synchronize()
     if world > 1:
+        barrier(world)
         for lay in layers:
             lay.close()
     return dict(value=value, ms=ms, clocks=clk.summary(), roofline=roofline, layer_tflops=layer_tflops, ep=ep,
@@ -351,7 +361,8 @@ def main():
                           int(os.environ.get("LOCAL_RANK", "0")))
     config = {"workload": "moe_layer_prefill_T4096", "tokens_per_gpu": T_PREFILL, "H": H, "I": I, "E": E,
               "top_k": K_TOP, "w4_group": GS, "shared_expert": "W4, sigmoid gate",
-              "l2": "inputs larger than L2 (0.83 GB weights per layer, 2-layer rotation)"}
+              "l2": "inputs larger than L2 (0.83 GB weights per layer, 2-layer rotation)",
+              "execution": "one CUDA graph per layer call (MoELayer.capture), replayed"}
 
     if args.impl == "reference":
         if rank != 0:

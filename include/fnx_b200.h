@@ -105,54 +105,62 @@ int fnx_ep_gather_rows(const void* src, long long ld_src, long long src_rows, co
 
 /* Peer-memory exchange of the expert-parallel layer (the NVLink replacement of the
  * all-to-all; no counterpart in the reference).  Each of the G ranks (G <= 8, one node)
- * allocates one region of fnx_ep_p2p_region_bytes(G, H, k, T_cap, cap) bytes with
+ * allocates one region of fnx_ep_p2p_region_bytes(G, H, k, T_cap) bytes with
  * fnx_ep_p2p_alloc (zero-filled), exports it with fnx_ep_p2p_export (a 64-byte CUDA IPC
- * handle), and imports every peer's with fnx_ep_p2p_import; fnx_ep_p2p_desc then fills an
+ * handle) and imports every peer's with fnx_ep_p2p_import; fnx_ep_p2p_desc then fills an
  * opaque descriptor of fnx_ep_p2p_desc_bytes() bytes (host memory) from the G base pointers
- * (bases[rank] = its own).  T_cap: most tokens a rank brings to one call; cap: most slot rows
- * a rank can receive (G*T_cap*k always suffices).  Eg = E/G experts per rank.
- * One layer call, on each rank's stream (every rank calls, in the same order):
- *   fnx_ep_p2p_counts(desc, counts)       counts int64 [G] of fnx_ep_dispatch_layout; exchanges
- *                                         them and starts the call's epoch;
- *   fnx_ep_p2p_push(desc, x, T, order, idx)   each slot's token row (owner-major order) to its
- *                                         owner, this rank's own tokens to its own region;
- *   fnx_ep_p2p_wait(desc, 1)              until every rank's rows for this rank have landed;
- *   fnx_ep_p2p_recv_layout(desc, T, order_x, ends_x, pos, ws, ws_bytes)
- *                                         expert-major rows of the owner's grouped launches:
- *                                         expert 0 = the shared expert over its own T tokens
- *                                         (order_x[t] = cap + t), experts 1..Eg the received
- *                                         slots; order_x int64 [T + cap], ends_x int64 [Eg + 1],
- *                                         pos int64 [cap] = each received slot's row in them;
- *   (grouped gate/up with epilogue 4 and down over fnx_ep_p2p_local(desc, 0), M = T + cap)
- *   fnx_ep_p2p_return(desc, yd, yd_rows, pos) each received slot's down row back to its source;
- *   fnx_ep_p2p_wait(desc, 2)              until this rank's rows are all back in
- *                                         fnx_ep_p2p_local(desc, 2) (owner-major, the row map
- *                                         of fnx_ep_dispatch_layout's inverse).
- * Waits are bounded (device error 1 when a peer never arrives); a count beyond cap sets
- * device error 4 and its rows are dropped.  The setup and teardown calls (alloc, free,
+ * (bases[rank] = its own).  T_cap: most tokens a rank brings to one call; Eg = E/G experts
+ * per rank.  Capacities: cap = G*T_cap*k received slots, cap_tok = G*T_cap received token
+ * rows (fnx_ep_p2p_capacity 0 / 1).
+ * One layer call, on each rank's stream (every rank calls, in the same order), after
+ * fnx_ep_dispatch_layout(idx) -> order, inverse, counts:
+ *   fnx_ep_p2p_dedup(desc, order, counts, T, tok_index, tcounts)
+ *       tok_index int32 [T*k]: each slot's token row among the rows sent (a token goes once
+ *       to each owner holding any of its experts); tcounts int64 [G]: token rows per owner;
+ *   fnx_ep_p2p_counts(desc, counts, tcounts)   exchanges the counts, starts the call's epoch;
+ *   fnx_ep_p2p_push(desc, x, T, order, idx, tok_index)
+ *       token rows and per-slot entries (owner-local expert, token row) to their owners, this
+ *       rank's own tokens to its own region (the shared expert's rows);
+ *   fnx_ep_p2p_wait(desc, 1)                  until every rank's rows for this rank landed;
+ *   fnx_ep_p2p_recv_layout(desc, T, order_x, ends_x, pos, rows, sh_out, ws, ws_bytes)
+ *       the owner's expert-major rows: expert 0 = the shared expert over its own T tokens,
+ *       experts 1..Eg the received slots; order_x int64 [T + cap] (token rows of
+ *       fnx_ep_p2p_local(desc, 0)), ends_x int64 [Eg + 1], pos int64 [cap] (each received
+ *       slot's row), rows (pointers) [T + cap]: where each down row goes -- the shared rows
+ *       to sh_out bf16 [T, H], each received slot's to its source's return buffer;
+ *   grouped gate/up (fnx_moe_grouped_w4, epilogue 4, M = T + cap) and down
+ *       (fnx_moe_grouped_w4_rows with out_rows = rows: the return happens in its epilogue);
+ *   fnx_ep_p2p_signal(desc, 2)                the down rows are out;
+ *   fnx_ep_p2p_wait(desc, 2)                  until this rank's rows are all back in
+ *       fnx_ep_p2p_local(desc, 2) (bf16 [T_cap*k, H], owner-major: row inverse[q] is slot q).
+ * Waits are bounded (device error 1 when a peer never arrives); a count beyond a capacity
+ * sets device error 4 and its rows are dropped.  The setup and teardown calls (alloc, free,
  * export, import, close) and fnx_ep_p2p_received allocate or synchronise; the per-call ones
  * follow the conventions at the top of this file. */
-size_t fnx_ep_p2p_region_bytes(int world, int H, int k, int T_cap, long long cap);
+size_t fnx_ep_p2p_region_bytes(int world, int H, int k, int T_cap);
 int fnx_ep_p2p_alloc(size_t bytes, void** ptr);
 int fnx_ep_p2p_free(void* ptr);
 int fnx_ep_p2p_export(void* ptr, void* handle);
 int fnx_ep_p2p_import(const void* handle, void** ptr);
 int fnx_ep_p2p_close(void* ptr);
 size_t fnx_ep_p2p_desc_bytes(void);
-int fnx_ep_p2p_desc(void* desc, int rank, int world, void* const* bases, int H, int k, int T_cap, long long cap,
-                    int Eg);
-/* this rank's buffers: 0 recv_x bf16 [cap + T_cap, H], 1 recv_e int64 [cap],
- * 2 yb bf16 [T_cap*k, H], 3 plan int64 (plan[0] = slots received this call) */
+int fnx_ep_p2p_desc(void* desc, int rank, int world, void* const* bases, int H, int k, int T_cap, int Eg);
+/* this rank's buffers: 0 recv_x bf16 [cap_tok + T_cap, H], 1 recv_e int64 [cap],
+ * 2 yb bf16 [T_cap*k, H], 3 plan int64 (plan[0] = slots received this call), 4 recv_row int64 [cap] */
 void* fnx_ep_p2p_local(const void* desc, int which);
+long long fnx_ep_p2p_capacity(const void* desc, int which);
 /* slots this rank received in its last call (synchronises with the device; for statistics) */
 long long fnx_ep_p2p_received(const void* desc);
-int fnx_ep_p2p_counts(const void* desc, const void* counts, void* stream);
-int fnx_ep_p2p_push(const void* desc, const void* x, int T, const void* order, const void* idx, void* stream);
+int fnx_ep_p2p_dedup(const void* desc, const void* order, const void* counts, int T, void* tok_index, void* tcounts,
+                     void* stream);
+int fnx_ep_p2p_counts(const void* desc, const void* counts, const void* tcounts, void* stream);
+int fnx_ep_p2p_push(const void* desc, const void* x, int T, const void* order, const void* idx, const void* tok_index,
+                    void* stream);
 int fnx_ep_p2p_wait(const void* desc, int phase, void* stream);
+int fnx_ep_p2p_signal(const void* desc, int phase, void* stream);
 size_t fnx_ep_p2p_recv_workspace(const void* desc);
-int fnx_ep_p2p_recv_layout(const void* desc, int T, void* order_x, void* ends_x, void* pos, void* workspace,
-                           size_t ws_bytes, void* stream);
-int fnx_ep_p2p_return(const void* desc, const void* yd, long long yd_rows, const void* pos, void* stream);
+int fnx_ep_p2p_recv_layout(const void* desc, int T, void* order_x, void* ends_x, void* pos, void* rows, void* sh_out,
+                           void* workspace, size_t ws_bytes, void* stream);
 
 /* Load-time repack of the int4pack artifact (w4 int32 [E,K,Nw/8] expert-major, scales bf16
  * [E,K/gs,Nw]; tools/repack_w4a16.py, tools/repack_w4_em.py) into the tile blocks the B200
@@ -182,6 +190,14 @@ int fnx_repack_w4_tiles(const void* w4, const void* scales, void* tiles, int E, 
 int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_rows, const void* row_index, int index_div,
                        const void* tiles, const void* ends, void* out, long long ld_out, int E, int M, int K, int Nw,
                        int epilogue, void* stream);
+
+/* fnx_moe_grouped_w4 with epilogue 0 whose output row r goes to out_rows[r] (a device array of
+ * 16-byte aligned row pointers, bf16 [Nw] each, which may point into peers' memory): the
+ * expert-parallel down projection writing each slot's row straight into its source's return
+ * buffer. */
+int fnx_moe_grouped_w4_rows(const void* act, long long ld_act, long long act_rows, const void* row_index,
+                            int index_div, const void* tiles, const void* ends, void* out_rows, int E, int M, int K,
+                            int Nw, void* stream);
 
 /* DenseW8.__call__ (fnx/engine.py:350-365): y bf16 [M,N] = x bf16 [M,K] . bf16(w8t int8 [K,N]
  * * sc bf16 [G,N]) with fp32 accumulation.  K % 64 == 0, N % 128 == 0. */

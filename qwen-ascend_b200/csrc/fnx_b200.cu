@@ -332,9 +332,11 @@ FNX_API size_t fnx_moe_permute_workspace(int n, int E) {
 
 namespace {
 // stable counting sort of n ids into E buckets of `div` consecutive ids each
-// n_dev: optional device-side entry count (<= n); base: added to ends and inverse.
+// n_dev: optional device-side entry count (<= n); base: added to ends and inverse;
+// row_map: order holds row_map[i] in place of the entry index i.
 int permute_launch(const void* idx, void* order, void* inverse, void* ends, void* counts, int n, int E, int div,
-                   void* workspace, cudaStream_t st, const long long* n_dev = nullptr, long long base = 0) {
+                   void* workspace, cudaStream_t st, const long long* n_dev = nullptr, long long base = 0,
+                   const int64_t* row_map = nullptr) {
     const int chunks = (n + PERM_CHUNK - 1) / PERM_CHUNK;
     int* hist = (int*)workspace;
     if (chunks == 0) {
@@ -346,7 +348,7 @@ int permute_launch(const void* idx, void* order, void* inverse, void* ends, void
     permute_hist_kernel<<<chunks, 256, E * sizeof(int), st>>>((const int64_t*)idx, n, n_dev, E, div, hist);
     permute_scan_kernel<<<1, 1024, 0, st>>>(hist, chunks, E, (int64_t*)ends, (int64_t*)counts, base);
     permute_scatter_kernel<<<chunks, 32, (E + PERM_CHUNK) * sizeof(int), st>>>(
-        (const int64_t*)idx, n, n_dev, E, div, hist, (int64_t*)order, (int64_t*)inverse, base);
+        (const int64_t*)idx, n, n_dev, E, div, hist, (int64_t*)order, (int64_t*)inverse, base, row_map);
     return launch_rc();
 }
 }  // namespace
@@ -397,24 +399,26 @@ FNX_API int fnx_ep_gather_rows(const void* src, long long ld_src, long long src_
 // ------------------------------------------------------------------ peer-memory exchange
 namespace {
 struct EPRegion {
-    size_t flags, cnt, plan, epoch, tickets, recv_e, recv_x, yb, total;
+    size_t flags, cnt, plan, epoch, tickets, recv_e, recv_row, recv_x, yb, sink, total;
 };
-EPRegion ep_region(int H, int k, int T_cap, long long cap) {
+EPRegion ep_region(int H, int k, int T_cap, long long cap, long long cap_tok) {
     EPRegion R{};
     size_t o = 0;
-    R.flags = o;   o += align_up(sizeof(unsigned) * EP_PHASES * 2 * EP_MAX_G, 256);
-    R.cnt = o;     o += align_up(sizeof(long long) * 2 * EP_MAX_G * EP_MAX_G, 256);
-    R.plan = o;    o += align_up(sizeof(long long) * EP_PLAN_LEN, 256);
-    R.epoch = o;   R.tickets = o + 16; o += 256;
-    R.recv_e = o;  o += align_up(sizeof(int64_t) * (size_t)cap, 256);
-    R.recv_x = o;  o += align_up(sizeof(bf16) * (size_t)(cap + T_cap) * H, 256);
-    R.yb = o;      o += align_up(sizeof(bf16) * (size_t)T_cap * k * H, 256);
+    R.flags = o;    o += align_up(sizeof(unsigned) * EP_PHASES * 2 * EP_MAX_G, 256);
+    R.cnt = o;      o += align_up(sizeof(long long) * 2 * EP_MAX_G * EP_MAX_G * 2, 256);
+    R.plan = o;     o += align_up(sizeof(long long) * EP_PLAN_LEN, 256);
+    R.epoch = o;    R.tickets = o + 16; o += 256;
+    R.recv_e = o;   o += align_up(sizeof(int64_t) * (size_t)cap, 256);
+    R.recv_row = o; o += align_up(sizeof(int64_t) * (size_t)cap, 256);
+    R.recv_x = o;   o += align_up(sizeof(bf16) * (size_t)(cap_tok + T_cap) * H, 256);
+    R.yb = o;       o += align_up(sizeof(bf16) * (size_t)T_cap * k * H, 256);
+    R.sink = o;     o += align_up(sizeof(bf16) * (size_t)H, 256);
     R.total = o;
     return R;
 }
-bool ep_shape_ok(int world, int H, int k, int T_cap, long long cap) {
+bool ep_shape_ok(int world, int H, int k, int T_cap) {
     return world >= 1 && world <= EP_MAX_G && H >= 8 && H % 8 == 0 && k >= 1 && k <= 64 && T_cap >= 1 &&
-           cap >= 0 && cap + T_cap <= 0x7fffffffLL && (long long)T_cap * k <= 0x7fffffffLL;
+           (long long)world * T_cap * k + T_cap <= 0x7fffffffLL;
 }
 const EPDesc* ep_desc(const void* d) {
     const EPDesc* e = (const EPDesc*)d;
@@ -422,9 +426,9 @@ const EPDesc* ep_desc(const void* d) {
 }
 }  // namespace
 
-FNX_API size_t fnx_ep_p2p_region_bytes(int world, int H, int k, int T_cap, long long cap) {
-    if (!ep_shape_ok(world, H, k, T_cap, cap)) return 0;
-    return ep_region(H, k, T_cap, cap).total;
+FNX_API size_t fnx_ep_p2p_region_bytes(int world, int H, int k, int T_cap) {
+    if (!ep_shape_ok(world, H, k, T_cap)) return 0;
+    return ep_region(H, k, T_cap, (long long)world * T_cap * k, (long long)world * T_cap).total;
 }
 
 FNX_API int fnx_ep_p2p_alloc(size_t bytes, void** ptr) {
@@ -462,25 +466,27 @@ FNX_API int fnx_ep_p2p_close(void* ptr) { return cudaIpcCloseMemHandle(ptr) == c
 
 FNX_API size_t fnx_ep_p2p_desc_bytes(void) { return sizeof(EPDesc); }
 
-FNX_API int fnx_ep_p2p_desc(void* desc, int rank, int world, void* const* bases, int H, int k, int T_cap,
-                            long long cap, int Eg) {
-    if (!desc || !bases || !ep_shape_ok(world, H, k, T_cap, cap) || rank < 0 || rank >= world || Eg < 1)
-        return FNX_EARG;
+FNX_API int fnx_ep_p2p_desc(void* desc, int rank, int world, void* const* bases, int H, int k, int T_cap, int Eg) {
+    if (!desc || !bases || !ep_shape_ok(world, H, k, T_cap) || rank < 0 || rank >= world || Eg < 1) return FNX_EARG;
     for (int q = 0; q < world; ++q)
         if (!bases[q] || !aligned16(bases[q])) return FNX_EARG;
-    const EPRegion R = ep_region(H, k, T_cap, cap);
     EPDesc d{};
-    d.rank = rank; d.world = world; d.H = H; d.k = k; d.T_cap = T_cap; d.Eg = Eg; d.cap = cap;
+    d.rank = rank; d.world = world; d.H = H; d.k = k; d.T_cap = T_cap; d.Eg = Eg;
+    d.cap = (long long)world * T_cap * k;
+    d.cap_tok = (long long)world * T_cap;
+    const EPRegion R = ep_region(H, k, T_cap, d.cap, d.cap_tok);
     char* own = (char*)bases[rank];
     d.plan = (long long*)(own + R.plan);
     d.epoch = (unsigned*)(own + R.epoch);
     d.tickets = (unsigned*)(own + R.tickets);
+    d.sink = (bf16*)(own + R.sink);
     for (int q = 0; q < world; ++q) {
         char* b = (char*)bases[q];
         d.flags[q] = (unsigned*)(b + R.flags);
         d.cnt[q] = (long long*)(b + R.cnt);
         d.recv_x[q] = (bf16*)(b + R.recv_x);
         d.recv_e[q] = (int64_t*)(b + R.recv_e);
+        d.recv_row[q] = (int64_t*)(b + R.recv_row);
         d.yb[q] = (bf16*)(b + R.yb);
     }
     memcpy(desc, &d, sizeof(d));
@@ -495,8 +501,15 @@ FNX_API void* fnx_ep_p2p_local(const void* desc, int which) {
         case 1: return d->recv_e[d->rank];
         case 2: return d->yb[d->rank];
         case 3: return d->plan;
+        case 4: return d->recv_row[d->rank];
         default: return nullptr;
     }
+}
+
+FNX_API long long fnx_ep_p2p_capacity(const void* desc, int which) {
+    const EPDesc* d = ep_desc(desc);
+    if (!d) return -1;
+    return which == 0 ? d->cap : which == 1 ? d->cap_tok : -1;
 }
 
 FNX_API long long fnx_ep_p2p_received(const void* desc) {
@@ -506,22 +519,33 @@ FNX_API long long fnx_ep_p2p_received(const void* desc) {
     return v;
 }
 
-FNX_API int fnx_ep_p2p_counts(const void* desc, const void* counts, void* stream) {
+FNX_API int fnx_ep_p2p_dedup(const void* desc, const void* order, const void* counts, int T, void* tok_index,
+                             void* tcounts, void* stream) {
     const EPDesc* d = ep_desc(desc);
-    if (!d || !counts) return FNX_EARG;
-    ep_counts_kernel<<<1, 64, 0, (cudaStream_t)stream>>>(*d, (const int64_t*)counts);
+    if (!d || T < 0 || T > d->T_cap || !counts || !tcounts || (T > 0 && (!order || !tok_index))) return FNX_EARG;
+    ep_dedup_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(*d, (const int64_t*)order, (const int64_t*)counts, T * d->k,
+                                                          (int*)tok_index, (int64_t*)tcounts);
     return launch_rc();
 }
 
-FNX_API int fnx_ep_p2p_push(const void* desc, const void* x, int T, const void* order, const void* idx, void* stream) {
+FNX_API int fnx_ep_p2p_counts(const void* desc, const void* counts, const void* tcounts, void* stream) {
     const EPDesc* d = ep_desc(desc);
-    if (!d || T < 0 || T > d->T_cap || (T > 0 && (!x || !order || !idx)) || !aligned16(x)) return FNX_EARG;
+    if (!d || !counts || !tcounts) return FNX_EARG;
+    ep_counts_kernel<<<1, 64, 0, (cudaStream_t)stream>>>(*d, (const int64_t*)counts, (const int64_t*)tcounts);
+    return launch_rc();
+}
+
+FNX_API int fnx_ep_p2p_push(const void* desc, const void* x, int T, const void* order, const void* idx,
+                            const void* tok_index, void* stream) {
+    const EPDesc* d = ep_desc(desc);
+    if (!d || T < 0 || T > d->T_cap || (T > 0 && (!x || !order || !idx || !tok_index)) || !aligned16(x))
+        return FNX_EARG;
     const long long rows = (long long)T * d->k + T;
     long long blocks = (rows + 7) / 8;
     if (blocks < 1) blocks = 1;
     if (blocks > (long long)num_sms() * 4) blocks = (long long)num_sms() * 4;
     ep_push_kernel<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(*d, (const bf16*)x, T, (const int64_t*)order,
-                                                                  (const int64_t*)idx);
+                                                                  (const int64_t*)idx, (const int*)tok_index);
     return launch_rc();
 }
 
@@ -532,28 +556,32 @@ FNX_API int fnx_ep_p2p_wait(const void* desc, int phase, void* stream) {
     return launch_rc();
 }
 
+FNX_API int fnx_ep_p2p_signal(const void* desc, int phase, void* stream) {
+    const EPDesc* d = ep_desc(desc);
+    if (!d || phase < 0 || phase >= EP_PHASES) return FNX_EARG;
+    ep_signal_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(*d, phase);
+    return launch_rc();
+}
+
 FNX_API size_t fnx_ep_p2p_recv_workspace(const void* desc) {
     const EPDesc* d = ep_desc(desc);
     return d ? fnx_moe_permute_workspace((int)d->cap, d->Eg) : 0;
 }
 
-FNX_API int fnx_ep_p2p_recv_layout(const void* desc, int T, void* order_x, void* ends_x, void* pos, void* workspace,
-                                   size_t ws_bytes, void* stream) {
+FNX_API int fnx_ep_p2p_recv_layout(const void* desc, int T, void* order_x, void* ends_x, void* pos, void* rows,
+                                   void* sh_out, void* workspace, size_t ws_bytes, void* stream) {
     const EPDesc* d = ep_desc(desc);
-    if (!d || T < 0 || T > d->T_cap || !order_x || !ends_x || !pos || d->Eg > PERM_MAX_E) return FNX_EARG;
+    if (!d || T < 0 || T > d->T_cap || !order_x || !ends_x || !pos || !rows || !sh_out || !aligned16(sh_out) ||
+        d->Eg > PERM_MAX_E)
+        return FNX_EARG;
     if (ws_bytes < fnx_ep_p2p_recv_workspace(desc)) return FNX_EWORKSPACE;
     cudaStream_t st = (cudaStream_t)stream;
-    ep_head_kernel<<<(T + 255) / 256 > 0 ? (T + 255) / 256 : 1, 256, 0, st>>>((int64_t*)order_x, (int64_t*)ends_x, T,
-                                                                              d->cap);
-    return permute_launch(d->recv_e[d->rank], (int64_t*)order_x + T, pos, (int64_t*)ends_x + 1, nullptr, (int)d->cap,
-                          d->Eg, 1, workspace, st, d->plan + EP_R, T);
-}
-
-FNX_API int fnx_ep_p2p_return(const void* desc, const void* yd, long long yd_rows, const void* pos, void* stream) {
-    const EPDesc* d = ep_desc(desc);
-    if (!d || !yd || !pos || yd_rows < 0 || !aligned16(yd)) return FNX_EARG;
-    ep_return_kernel<<<num_sms() * 4, 256, 0, (cudaStream_t)stream>>>(*d, (const bf16*)yd, yd_rows,
-                                                                      (const int64_t*)pos);
+    ep_head_kernel<<<num_sms() * 2, 256, 0, st>>>(*d, (int64_t*)order_x, (int64_t*)ends_x, (bf16**)rows,
+                                                  (bf16*)sh_out, T);
+    const int rc = permute_launch(d->recv_e[d->rank], (int64_t*)order_x + T, pos, (int64_t*)ends_x + 1, nullptr,
+                                  (int)d->cap, d->Eg, 1, workspace, st, d->plan + EP_R, T, d->recv_row[d->rank]);
+    if (rc) return rc;
+    ep_rows_kernel<<<num_sms() * 2, 256, 0, st>>>(*d, (const int64_t*)pos, T, (bf16**)rows);
     return launch_rc();
 }
 
@@ -576,6 +604,25 @@ FNX_API int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_
     if (rc) return rc;
     if (M == 0) return FNX_OK;
     return gemm_launch(GEMM_W4, epilogue, p, (cudaStream_t)stream);
+}
+
+FNX_API int fnx_moe_grouped_w4_rows(const void* act, long long ld_act, long long act_rows, const void* row_index,
+                                    int index_div, const void* tiles, const void* ends, void* out_rows, int E, int M,
+                                    int K, int Nw, void* stream) {
+    if (!out_rows) return FNX_EARG;
+    GemmParams p{};
+    p.act = (const bf16*)act; p.ld_act = ld_act; p.row_index = (const int64_t*)row_index; p.index_div = index_div;
+    p.act_rows = act_rows;
+    if (act_rows < 0 || act_rows > 0x7fffffffLL || (!row_index && act_rows < M)) return FNX_EARG;
+    p.w = tiles; p.ends = (const int64_t*)ends; p.out = nullptr; p.ld_out = Nw;
+    p.out_rows = (bf16* const*)out_rows;
+    p.E = E; p.M = M; p.K = K; p.Nw = Nw; p.gs = 0;
+    p.m_tiles = Nw / G_BM;
+    p.shared_e = -1;
+    const int rc = gemm_check(GEMM_W4, EPI_PLAIN, p);
+    if (rc) return rc;
+    if (M == 0) return FNX_OK;
+    return gemm_launch(GEMM_W4, EPI_PLAIN, p, (cudaStream_t)stream);
 }
 
 FNX_API int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G,

@@ -53,43 +53,56 @@ __global__ void __launch_bounds__(256) ep_gather_rows_kernel(const bf16* __restr
 }  // namespace fnx
 
 // ======================================================================== peer-memory exchange
-// The same dispatch and return as the all-to-all, moved by this library's kernels through
-// the NVLink peer mappings of the ranks' exchange regions (CUDA IPC; plain loads and stores,
-// no multicast).  Nothing waits on the host: the per-owner counts travel by peer stores
-// behind release/acquire flags, so the layer needs no host synchronisation.
+// The dispatch and return of the all-to-all, moved by this library's kernels through the
+// NVLink peer mappings of the ranks' exchange regions (CUDA IPC; plain loads and stores, no
+// multicast).  Nothing waits on the host: the per-owner counts travel by peer stores behind
+// release/acquire flags, so a layer call is one stream of launches.
+//
+// Dispatch sends each token ONCE per owner that holds any of its k experts (the slots of one
+// token for one owner are consecutive in the owner-major order), plus one small entry per
+// slot (owner-local expert, token row).  The return is per slot: the owner's down GEMM writes
+// each slot's row straight into the source's `yb` through a per-row pointer table, so the
+// source reduces the k rows in the reference's slot order.
 //
 // Every rank's region (one cudaMalloc, zero-filled at setup):
-//   flags   u32  [EP_PHASES][2][EP_MAX_G]   flag[ph][parity][q] = last epoch rank q signalled
-//   cnt     i64  [2][G][G]                  cnt[parity][q][j] = slots of rank q for owner j
-//   recv_x  bf16 [cap + T_cap, H]           received slot rows, then this rank's own tokens
-//   recv_e  i64  [cap]                      owner-local expert of each received slot
-//   yb      bf16 [T_cap * k, H]             returned down rows, owner-major (this rank's slots)
-//   plan    i64  [EP_PLAN_LEN]              local: this step's offsets (below)
-//   epoch   u32, tickets u32[4]             local
-// Epochs count layer calls (the same on every rank); flags and counts alternate between two
-// parities so that a rank one step ahead never overwrites what a peer still reads.
+//   flags    u32  [EP_PHASES][2][EP_MAX_G]    flag[ph][parity][q] = last epoch rank q signalled
+//   cnt      i64  [2][G][G][2]                cnt[parity][q][j] = (slots, tokens) of rank q for owner j
+//   plan     i64  [EP_PLAN_LEN]               local: this call's offsets (below)
+//   epoch    u32, tickets u32[4]              local
+//   recv_e   i64  [cap]                       received slots: owner-local expert
+//   recv_row i64  [cap]                       received slots: token row in recv_x
+//   recv_x   bf16 [cap_tok + T_cap, H]        received token rows, then this rank's own tokens
+//   yb       bf16 [T_cap * k, H]              returned down rows, owner-major (this rank's slots)
+//   sink     bf16 [H]                         target of rows with no valid destination
+// cap = G*T_cap*k slots and cap_tok = G*T_cap token rows always suffice.  Epochs count layer
+// calls (the same on every rank); flags and counts alternate between two parities so that a
+// rank one call ahead never overwrites what a peer still reads.
 namespace fnx {
 
 constexpr int EP_MAX_G = 8;
 enum { EP_PH_CNT = 0, EP_PH_DATA = 1, EP_PH_RET = 2, EP_PHASES = 3 };
 // plan entries
 constexpr int EP_R = 0, EP_EPOCH = 1;
-constexpr int EP_RECV_OFF = 2;                                  // [G+1] prefix of slots received per source
-constexpr int EP_SEND_OFF = EP_RECV_OFF + EP_MAX_G + 1;         // [G] my first row in each owner's recv_x
-constexpr int EP_SRC_START = EP_SEND_OFF + EP_MAX_G;            // [G+1] owner chunks of my owner-major order
-constexpr int EP_RET_OFF = EP_SRC_START + EP_MAX_G + 1;         // [G] first row for me in each source's yb
-constexpr int EP_PLAN_LEN = EP_RET_OFF + EP_MAX_G;
+constexpr int EP_RECV_OFF = 2;                                   // [G+1] prefix of slots received per source
+constexpr int EP_SEND_OFF = EP_RECV_OFF + EP_MAX_G + 1;          // [G] my first slot row in each owner
+constexpr int EP_SRC_START = EP_SEND_OFF + EP_MAX_G;             // [G+1] owner chunks of my owner-major slots
+constexpr int EP_RET_OFF = EP_SRC_START + EP_MAX_G + 1;          // [G] first row for me in each source's yb
+constexpr int EP_TOK_SEND_OFF = EP_RET_OFF + EP_MAX_G;           // [G] my first token row in each owner
+constexpr int EP_TOK_START = EP_TOK_SEND_OFF + EP_MAX_G;         // [G+1] owner chunks of my deduplicated tokens
+constexpr int EP_PLAN_LEN = EP_TOK_START + EP_MAX_G + 1;
 
 struct EPDesc {
     int rank, world, H, k, T_cap, Eg;
-    long long cap;
+    long long cap, cap_tok;
     long long* plan;
     unsigned* epoch;
     unsigned* tickets;
+    bf16* sink;
     unsigned* flags[EP_MAX_G];
     long long* cnt[EP_MAX_G];
     bf16* recv_x[EP_MAX_G];
     int64_t* recv_e[EP_MAX_G];
+    int64_t* recv_row[EP_MAX_G];
     bf16* yb[EP_MAX_G];
 };
 
@@ -134,11 +147,85 @@ FNX_DEV void ep_wait_all(const EPDesc& d, int phase, unsigned e) {
     __syncthreads();
 }
 
-// One block (64 threads): start epoch e, send this rank's per-owner slot counts to every
-// rank, wait for everyone's, and derive this step's offsets.
-__global__ void __launch_bounds__(64) ep_counts_kernel(const EPDesc d, const int64_t* __restrict__ counts) {
+FNX_DEV void ep_load_plan(const EPDesc& d, long long* sp) {
+    for (int i = threadIdx.x; i < EP_PLAN_LEN; i += blockDim.x) sp[i] = d.plan[i];
+    __syncthreads();
+}
+
+// owner chunk holding entry p of a [G+1] prefix array (G <= 8)
+FNX_DEV int ep_chunk(const long long* start, int G, long long p) {
+    int j = 0;
+    while (j + 1 < G && p >= start[j + 1]) ++j;
+    return j;
+}
+
+// One block of 1024 threads: tok_index[p] = the deduplicated token row of owner-major slot p
+// (counted over all owners; a new row starts at each owner chunk and each change of token)
+// and tcounts[j] = the token rows for owner j.  Each warp owns a contiguous range of slots and
+// walks it 32 at a time (coalesced loads, ballot counts): one pass counts the new rows, a scan
+// over the 32 warps gives each range its first row, a second pass writes the rows.
+__global__ void __launch_bounds__(1024) ep_dedup_kernel(const EPDesc d, const int64_t* __restrict__ order,
+                                                        const int64_t* __restrict__ counts, int n,
+                                                        int* __restrict__ tok_index, int64_t* __restrict__ tcounts) {
+    __shared__ long long start[EP_MAX_G + 1];
+    __shared__ int wsum[32], wexcl[32];
+    const int G = d.world, k = d.k, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    if (t == 0) {
+        long long a = 0;
+        for (int j = 0; j < G; ++j) { start[j] = a; a += counts[j]; }
+        start[G] = a;
+    }
+    __syncthreads();
+    const long long per = ((long long)(n + 31) / 32 + 31) / 32 * 32;        // slots per warp, multiple of 32
+    const long long wb = min((long long)n, warp * per), we = min((long long)n, wb + per);
+    auto first = [&](long long p) -> bool {
+        if (p == 0) return true;
+        for (int j = 1; j < G; ++j)
+            if (p == start[j]) return true;
+        return __ldg(order + p) / k != __ldg(order + p - 1) / k;
+    };
+    int cnt = 0;
+    for (long long b = wb; b < we; b += 32) {
+        const long long p = b + lane;
+        cnt += __popc(__ballot_sync(0xffffffffu, p < we && first(p)));
+    }
+    if (lane == 0) wsum[warp] = cnt;
+    __syncthreads();
+    if (warp == 0) {
+        const int v = wsum[lane];
+        int inc = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += u;
+        }
+        wexcl[lane] = inc - v;
+    }
+    __syncthreads();
+    int run = wexcl[warp];
+    for (long long b = wb; b < we; b += 32) {
+        const long long p = b + lane;
+        const bool f = p < we && first(p);
+        const unsigned m = __ballot_sync(0xffffffffu, f);
+        if (p < we) tok_index[p] = run + __popc(m & ((1u << lane) - 1u)) + (f ? 1 : 0) - 1;
+        run += __popc(m);
+    }
+    __syncthreads();
+    if (t == 0) {
+        const int total = n > 0 ? tok_index[n - 1] + 1 : 0;
+        long long us[EP_MAX_G + 1];
+        us[G] = total;
+        for (int j = G - 1; j >= 0; --j) us[j] = start[j] < start[j + 1] ? tok_index[start[j]] : us[j + 1];
+        for (int j = 0; j < G; ++j) tcounts[j] = us[j + 1] - us[j];
+    }
+}
+
+// One block (64 threads): start epoch e, send this rank's per-owner slot and token counts to
+// every rank, wait for everyone's, and derive this call's offsets.
+__global__ void __launch_bounds__(64) ep_counts_kernel(const EPDesc d, const int64_t* __restrict__ counts,
+                                                       const int64_t* __restrict__ tcounts) {
     __shared__ unsigned se;
-    __shared__ long long M[EP_MAX_G][EP_MAX_G];
+    __shared__ long long M[EP_MAX_G][EP_MAX_G], U[EP_MAX_G][EP_MAX_G];
     const int G = d.world, r = d.rank, t = threadIdx.x;
     if (t == 0) se = atomicAdd(d.epoch, 1u) + 1u;
     __syncthreads();
@@ -146,30 +233,41 @@ __global__ void __launch_bounds__(64) ep_counts_kernel(const EPDesc d, const int
     const int par = (int)(e & 1u);
     if (t < G * G) {
         const int q = t / G, j = t % G;
-        d.cnt[q][((long long)par * G + r) * G + j] = counts[j];
+        long long* c = d.cnt[q] + (((long long)par * G + r) * G + j) * 2;
+        c[0] = counts[j];
+        c[1] = tcounts[j];
     }
     __threadfence_system();
     __syncthreads();
     ep_signal_all(d, EP_PH_CNT, e);
     ep_wait_all(d, EP_PH_CNT, e);
-    if (t < G * G) M[t / G][t % G] = ld_relaxed_sys_i64(d.cnt[r] + ((long long)par * G + t / G) * G + t % G);
+    if (t < G * G) {
+        const long long* c = d.cnt[r] + (((long long)par * G + t / G) * G + t % G) * 2;
+        M[t / G][t % G] = ld_relaxed_sys_i64(c);
+        U[t / G][t % G] = ld_relaxed_sys_i64(c + 1);
+    }
     __syncthreads();
     if (t == 0) {
         long long* P = d.plan;
-        long long acc = 0;
-        for (int q = 0; q < G; ++q) { P[EP_RECV_OFF + q] = acc; acc += M[q][r]; }
+        long long acc = 0, tok = 0;
+        for (int q = 0; q < G; ++q) { P[EP_RECV_OFF + q] = acc; acc += M[q][r]; tok += U[q][r]; }
         P[EP_RECV_OFF + G] = acc;
-        if (acc > d.cap) { fnx_flag_error(FNX_DEVERR_OVERFLOW); acc = d.cap; }
+        if (acc > d.cap || tok > d.cap_tok) { fnx_flag_error(FNX_DEVERR_OVERFLOW); acc = min(acc, d.cap); }
         P[EP_R] = acc;
         P[EP_EPOCH] = e;
         for (int j = 0; j < G; ++j) {
-            long long s = 0;
-            for (int q = 0; q < r; ++q) s += M[q][j];
+            long long s = 0, u = 0;
+            for (int q = 0; q < r; ++q) { s += M[q][j]; u += U[q][j]; }
             P[EP_SEND_OFF + j] = s;
+            P[EP_TOK_SEND_OFF + j] = u;
         }
-        acc = 0;
-        for (int j = 0; j < G; ++j) { P[EP_SRC_START + j] = acc; acc += M[r][j]; }
+        acc = tok = 0;
+        for (int j = 0; j < G; ++j) {
+            P[EP_SRC_START + j] = acc; acc += M[r][j];
+            P[EP_TOK_START + j] = tok; tok += U[r][j];
+        }
         P[EP_SRC_START + G] = acc;
+        P[EP_TOK_START + G] = tok;
         for (int q = 0; q < G; ++q) {
             long long s = 0;
             for (int j = 0; j < r; ++j) s += M[q][j];
@@ -209,17 +307,15 @@ FNX_DEV void ep_last_block_signal(const EPDesc& d, unsigned* ticket, int phase, 
     if (last) ep_signal_all(d, phase, e);
 }
 
-FNX_DEV void ep_load_plan(const EPDesc& d, long long* sp) {
-    for (int i = threadIdx.x; i < EP_PLAN_LEN; i += blockDim.x) sp[i] = d.plan[i];
-    __syncthreads();
-}
-
-// Dispatch: slot p of the owner-major order goes to its owner's recv_x row
-// send_off[j] + (p - src_start[j]) (with its owner-local expert in recv_e); this rank's own
-// T tokens go to its own rows cap .. cap+T-1 (the shared expert's rows).  Then DATA.
+// Dispatch.  Slot p of the owner-major order (owner j) writes its entry to j's slot row
+// send_off[j] + (p - src_start[j]): the owner-local expert and the token row
+// tok_send_off[j] + (tok_index[p] - tok_start[j]); the first slot of each token for j also
+// copies the token row there.  This rank's own T tokens go to its rows cap_tok .. cap_tok+T-1
+// (the shared expert's rows).  Then DATA.
 __global__ void __launch_bounds__(256) ep_push_kernel(const EPDesc d, const bf16* __restrict__ x, int T,
                                                       const int64_t* __restrict__ order,
-                                                      const int64_t* __restrict__ idx) {
+                                                      const int64_t* __restrict__ idx,
+                                                      const int* __restrict__ tok_index) {
     __shared__ long long sp[EP_PLAN_LEN];
     ep_load_plan(d, sp);
     const int G = d.world, H = d.H, k = d.k, lane = threadIdx.x & 31;
@@ -227,59 +323,82 @@ __global__ void __launch_bounds__(256) ep_push_kernel(const EPDesc d, const bf16
     const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
     for (long long p = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < n + T; p += warps) {
         if (p < n) {
-            int j = 0;
-            while (j + 1 < G && p >= sp[EP_SRC_START + j + 1]) ++j;
-            const long long row = sp[EP_SEND_OFF + j] + (p - sp[EP_SRC_START + j]);
+            const int j = ep_chunk(sp + EP_SRC_START, G, p);
+            const long long srow = sp[EP_SEND_OFF + j] + (p - sp[EP_SRC_START + j]);
+            const int ti = __ldg(tok_index + p);
+            const long long trow = sp[EP_TOK_SEND_OFF + j] + (ti - sp[EP_TOK_START + j]);
             const long long q = __ldg(order + p);
-            if (row >= d.cap || q < 0 || q >= n) {
-                if (lane == 0) fnx_flag_error(row >= d.cap ? FNX_DEVERR_OVERFLOW : FNX_DEVERR_BADID);
+            if (srow >= d.cap || trow >= d.cap_tok || trow < 0 || q < 0 || q >= n) {
+                if (lane == 0) fnx_flag_error(q < 0 || q >= n ? FNX_DEVERR_BADID : FNX_DEVERR_OVERFLOW);
                 continue;
             }
-            if (lane == 0) d.recv_e[j][row] = __ldg(idx + q) % d.Eg;
-            ep_copy_row(d.recv_x[j] + row * H, x + (q / k) * H, H, lane);
+            if (lane == 0) {
+                d.recv_e[j][srow] = __ldg(idx + q) % d.Eg;
+                d.recv_row[j][srow] = trow;
+            }
+            if (p == sp[EP_SRC_START + j] || __ldg(tok_index + p - 1) != ti)
+                ep_copy_row(d.recv_x[j] + trow * H, x + (q / k) * H, H, lane);
         } else {
             const long long t = p - n;
-            ep_copy_row(d.recv_x[d.rank] + (d.cap + t) * H, x + t * H, H, lane);
+            ep_copy_row(d.recv_x[d.rank] + (d.cap_tok + t) * H, x + t * H, H, lane);
         }
     }
     ep_last_block_signal(d, d.tickets + 0, EP_PH_DATA, (unsigned)sp[EP_EPOCH]);
 }
 
-// Return: received slot s (from source q, j-th of q's) sends its down row yd[pos[s]] to
-// source q's yb row ret_off[q] + j.  Then RET.
-__global__ void __launch_bounds__(256) ep_return_kernel(const EPDesc d, const bf16* __restrict__ yd,
-                                                        long long yd_rows, const int64_t* __restrict__ pos) {
-    __shared__ long long sp[EP_PLAN_LEN];
-    ep_load_plan(d, sp);
-    const int G = d.world, H = d.H, lane = threadIdx.x & 31;
-    const long long R = sp[EP_R];
-    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-    for (long long s = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); s < R; s += warps) {
-        int q = 0;
-        while (q + 1 < G && s >= sp[EP_RECV_OFF + q + 1]) ++q;
-        const long long row = sp[EP_RET_OFF + q] + (s - sp[EP_RECV_OFF + q]);
-        const long long src = __ldg(pos + s);
-        if (src < 0 || src >= yd_rows || row >= (long long)d.T_cap * d.k) {
-            if (lane == 0) fnx_flag_error(FNX_DEVERR_BADID);
-            continue;
-        }
-        ep_copy_row(d.yb[q] + row * H, yd + src * H, H, lane);
-    }
-    ep_last_block_signal(d, d.tickets + 1, EP_PH_RET, (unsigned)sp[EP_EPOCH]);
-}
-
-// One block: wait until every rank signalled `phase` of this step's epoch.
+// One block: wait until every rank signalled `phase` of this call's epoch.
 __global__ void __launch_bounds__(32) ep_wait_kernel(const EPDesc d, int phase) {
     __shared__ long long sp[EP_PLAN_LEN];
     ep_load_plan(d, sp);
     ep_wait_all(d, phase, (unsigned)sp[EP_EPOCH]);
 }
 
-// The owner's expert-major rows start with the shared expert over its own T tokens (expert 0
-// of the grouped launches: order_x[t] = cap + t, ends_x[0] = T).
-__global__ void ep_head_kernel(int64_t* __restrict__ order_x, int64_t* __restrict__ ends_x, int T, long long cap) {
-    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) order_x[t] = cap + t;
+// One block: every prior write of this rank (a finished launch's peer stores included) is made
+// visible system-wide, then `phase` of this call's epoch is signalled to every rank.
+__global__ void __launch_bounds__(32) ep_signal_kernel(const EPDesc d, int phase) {
+    __shared__ long long sp[EP_PLAN_LEN];
+    ep_load_plan(d, sp);
+    __threadfence_system();
+    ep_signal_all(d, phase, (unsigned)sp[EP_EPOCH]);
+}
+
+// Head of the owner's expert-major rows: the shared expert over its own T tokens is expert 0
+// of the grouped launches (order_x[t] = cap_tok + t, ends_x[0] = T, its down rows to
+// sh_out); every other down-row destination starts at the sink.
+__global__ void __launch_bounds__(256) ep_head_kernel(const EPDesc d, int64_t* __restrict__ order_x,
+                                                      int64_t* __restrict__ ends_x, bf16** __restrict__ rows,
+                                                      bf16* __restrict__ sh_out, int T) {
+    const long long total = (long long)T + d.cap;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        if (i < T) {
+            order_x[i] = d.cap_tok + i;
+            rows[i] = sh_out + i * d.H;
+        } else {
+            rows[i] = d.sink;
+        }
+    }
     if (blockIdx.x == 0 && threadIdx.x == 0) ends_x[0] = T;
+}
+
+// Down-row destinations of the received slots: slot s (from source q, the j-th of q's) at
+// expert-major position pos[s] returns to source q's yb row ret_off[q] + j.
+__global__ void __launch_bounds__(256) ep_rows_kernel(const EPDesc d, const int64_t* __restrict__ pos, int T,
+                                                      bf16** __restrict__ rows) {
+    __shared__ long long sp[EP_PLAN_LEN];
+    ep_load_plan(d, sp);
+    const long long R = sp[EP_R];
+    const long long lim = (long long)d.T_cap * d.k;
+    for (long long s = (long long)blockIdx.x * blockDim.x + threadIdx.x; s < R; s += (long long)gridDim.x * blockDim.x) {
+        const int q = ep_chunk(sp + EP_RECV_OFF, d.world, s);
+        const long long row = sp[EP_RET_OFF + q] + (s - sp[EP_RECV_OFF + q]);
+        const long long ps = pos[s];
+        if (ps < T || ps >= T + R || row >= lim) {
+            fnx_flag_error(FNX_DEVERR_BADID);
+            continue;
+        }
+        rows[ps] = d.yb[q] + row * d.H;
+    }
 }
 
 }  // namespace fnx

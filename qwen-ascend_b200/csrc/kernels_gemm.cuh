@@ -89,7 +89,13 @@ struct GemmParams {
     int E, M, K, Nw, gs;
     int m_tiles;                // tiles along the feature dimension
     int shared_e;               // EPI_SWIGLU_MIXED: the shared expert's index
+    bf16* const* out_rows;      // EPI_PLAIN: row r goes to out_rows[r] (e.g. a peer's buffer); null: out
 };
+
+// destination of output row `row` (a 16-byte aligned row of Nw bf16 when out_rows is set)
+FNX_DEV bf16* out_row(const GemmParams& p, long long row) {
+    return p.out_rows ? p.out_rows[row] : p.out + row * p.ld_out;
+}
 
 struct GemmSmem {
     uint64_t a_full[G_MAX_STAGES], b_full[G_MAX_STAGES], empty[G_MAX_STAGES];
@@ -210,11 +216,17 @@ FNX_DEV void epilogue_chunk(const GemmParams& p, const TileInfo& ti, int r, int 
     const int lane = threadIdx.x & 31;
     if (EPI == EPI_PLAIN) {
         const int f = ti.m * G_BM + (PERM ? lane_feature<EPI>(r) : r);
-        bf16* o = p.out + (long long)(ti.row0 + n0) * p.ld_out + f;
         const int lim = ti.nrows - n0;
+        if (p.out_rows) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-            if (i < lim) o[(long long)i * p.ld_out] = f2bf(__uint_as_float(v[i]));
+            for (int i = 0; i < 16; ++i)
+                if (i < lim) out_row(p, ti.row0 + n0 + i)[f] = f2bf(__uint_as_float(v[i]));
+        } else {
+            bf16* o = p.out + (long long)(ti.row0 + n0) * p.ld_out + f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                if (i < lim) o[(long long)i * p.ld_out] = f2bf(__uint_as_float(v[i]));
+        }
     } else {
         // lane pairs (2i, 2i+1) hold gate / up of feature m*64 + r/2 for 16 tokens;
         // the even lane finishes tokens 0..7, the odd lane tokens 8..15.
@@ -261,8 +273,7 @@ FNX_DEV void epilogue_chunk_staged(const GemmParams& p, const TileInfo& ti, int 
             const int c = q * 32 + lane, tok = c >> 2, part = c & 3;
             if (n0 + tok < ti.nrows) {
                 const uint4 val = *reinterpret_cast<const uint4*>(stage + tok * 32 + part * 8);
-                *reinterpret_cast<uint4*>(p.out + (long long)(ti.row0 + n0 + tok) * p.ld_out + ti.m * G_BM + w4 * 32 +
-                                          part * 8) = val;
+                *reinterpret_cast<uint4*>(out_row(p, ti.row0 + n0 + tok) + ti.m * G_BM + w4 * 32 + part * 8) = val;
             }
         }
     } else {

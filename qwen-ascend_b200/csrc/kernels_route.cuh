@@ -133,10 +133,19 @@ __global__ void __launch_bounds__(256) permute_hist_kernel(const int64_t* __rest
     n = perm_count(n, n_dev);
     const int c0 = blockIdx.x * PERM_CHUNK;
     const long long lim = (long long)E * div;
-    for (int i = c0 + threadIdx.x; i < min(n, c0 + PERM_CHUNK); i += blockDim.x) {
-        const long long e = ids[i];
-        if (e >= 0 && e < lim) atomicAdd(&sh[div == 1 ? e : e / div], 1);
-        else fnx_flag_error(FNX_DEVERR_BADID);
+    const int lane = threadIdx.x & 31;
+    // warp-aggregated: one shared atomic per distinct bucket of the warp's 32 ids (few buckets,
+    // e.g. the ranks of the expert-parallel dispatch, would otherwise serialise on one counter)
+    for (int i0 = c0 + (threadIdx.x & ~31); i0 < c0 + PERM_CHUNK; i0 += blockDim.x) {
+        const int i = i0 + lane;
+        int b = -1;
+        if (i < n) {
+            const long long e = ids[i];
+            if (e >= 0 && e < lim) b = (int)(div == 1 ? e : e / div);
+            else fnx_flag_error(FNX_DEVERR_BADID);
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, b);
+        if (b >= 0 && lane == __ffs(peers) - 1) atomicAdd(&sh[b], __popc(peers));
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(long long)blockIdx.x * E + e] = sh[e];
@@ -186,12 +195,12 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int* __restrict__ hi
 
 // pass 3: one warp per chunk walks its entries in order; __match_any_sync gives each
 // entry its rank among equal ids in the same 32-entry batch, so positions are stable.
-// order[pos] = i and inverse[i] = pos_base + pos (the host offsets `order` by pos_base).
+// order[pos] = i (or row_map[i]) and inverse[i] = pos_base + pos (the host offsets `order`).
 __global__ void __launch_bounds__(32) permute_scatter_kernel(const int64_t* __restrict__ ids, int n,
                                                              const long long* __restrict__ n_dev, int E, int div,
                                                              const int* __restrict__ start,
                                                              int64_t* __restrict__ order, int64_t* __restrict__ inverse,
-                                                             long long pos_base) {
+                                                             long long pos_base, const int64_t* __restrict__ row_map) {
     extern __shared__ int cursor[];
     int* sid = cursor + E;                       // this chunk's ids, loaded in one coalesced pass
     const int lane = threadIdx.x;
@@ -222,7 +231,7 @@ __global__ void __launch_bounds__(32) permute_scatter_kernel(const int64_t* __re
         __syncwarp();
         if (good) {
             const long long pos = base + rank;
-            order[pos] = i;
+            order[pos] = row_map ? row_map[i] : i;
             if (inverse) inverse[i] = pos_base + pos;
         } else if (valid && inverse) {
             inverse[i] = -1;          // an id outside [0, E): no row (flagged by the histogram pass)

@@ -35,22 +35,25 @@ SIGNATURES = {
     "fnx_ep_layout_workspace": ([I, I], SZ),
     "fnx_ep_dispatch_layout": ([P, I, I, I, P, P, P, P, SZ, P], I),
     "fnx_ep_gather_rows": ([P, LL, LL, P, I, P, I, P, LL, P, LL, I, P], I),
-    "fnx_ep_p2p_region_bytes": ([I, I, I, I, LL], SZ),
+    "fnx_ep_p2p_region_bytes": ([I, I, I, I], SZ),
     "fnx_ep_p2p_alloc": ([SZ, ctypes.POINTER(P)], I),
     "fnx_ep_p2p_free": ([P], I),
     "fnx_ep_p2p_export": ([P, P], I),
     "fnx_ep_p2p_import": ([P, ctypes.POINTER(P)], I),
     "fnx_ep_p2p_close": ([P], I),
     "fnx_ep_p2p_desc_bytes": ([], SZ),
-    "fnx_ep_p2p_desc": ([P, I, I, ctypes.POINTER(P), I, I, I, LL, I], I),
+    "fnx_ep_p2p_desc": ([P, I, I, ctypes.POINTER(P), I, I, I, I], I),
     "fnx_ep_p2p_local": ([P, I], P),
+    "fnx_ep_p2p_capacity": ([P, I], LL),
     "fnx_ep_p2p_received": ([P], LL),
-    "fnx_ep_p2p_counts": ([P, P, P], I),
-    "fnx_ep_p2p_push": ([P, P, I, P, P, P], I),
+    "fnx_ep_p2p_dedup": ([P, P, P, I, P, P, P], I),
+    "fnx_ep_p2p_counts": ([P, P, P, P], I),
+    "fnx_ep_p2p_push": ([P, P, I, P, P, P, P], I),
     "fnx_ep_p2p_wait": ([P, I, P], I),
+    "fnx_ep_p2p_signal": ([P, I, P], I),
     "fnx_ep_p2p_recv_workspace": ([P], SZ),
-    "fnx_ep_p2p_recv_layout": ([P, I, P, P, P, P, SZ, P], I),
-    "fnx_ep_p2p_return": ([P, P, LL, P, P], I),
+    "fnx_ep_p2p_recv_layout": ([P, I, P, P, P, P, P, P, SZ, P], I),
+    "fnx_moe_grouped_w4_rows": ([P, LL, LL, P, I, P, P, P, I, I, I, I, P], I),
     "fnx_moe_grouped_w4": ([P, LL, LL, P, I, P, P, P, LL] + [I] * 5 + [P], I),
     "fnx_w4_tiles_bytes": ([I] * 3, SZ),
     "fnx_repack_w4_tiles": ([P] * 3 + [I] * 5 + [P], I),

@@ -270,6 +270,13 @@ class MoELayer:
 
     __call__ = forward
 
+    def capture(self, T, device=None):
+        """This layer's call on ``T`` tokens captured into one CUDA graph over static buffers
+        (the reference's graph-level caller, ``FnModel.capture`` ``fnx/model.py:288-358``:
+        three warm-up calls on a side stream, then the capture).  Returns a
+        ``CapturedLayer``; its replay launches the same kernels as a direct call."""
+        return CapturedLayer(self, T, device or self.router_cat.device)
+
     def prefill(self, x, details=False):
         """Grouped path (``fnx/engine.py:1815-1853``) for ``T`` tokens.  The routed and the shared
         expert share one grouped launch per projection; the per-call buffers of the extended
@@ -330,3 +337,34 @@ class MoELayer:
             idx_out.data_ptr(), M, self.H, self.I, self.E, self.k, ws.data_ptr(), ws.numel(), _lib.stream(dev))
         _lib.check(rc, "MoE decode")
         return out, w_out, idx_out
+
+
+class CapturedLayer:
+    """One MoE layer call replayed from a CUDA graph.  ``x`` is the static bf16 ``[T, H]``
+    input and ``out`` the static output; ``replay()`` runs the layer on whatever ``x``
+    holds, ``__call__(x)`` copies ``x`` in first.  The layer's own buffers stay bound to the
+    graph, so one layer object backs one capture at a time."""
+
+    def __init__(self, layer, T, device):
+        self.layer = layer
+        self.x = torch.zeros(T, layer.H, dtype=BF16, device=device)
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                layer(self.x)
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            out = layer(self.x)
+        self.out = out[0] if isinstance(out, tuple) else out
+
+    def replay(self):
+        self.graph.replay()
+        return self.out
+
+    def __call__(self, x):
+        if x.data_ptr() != self.x.data_ptr():
+            self.x.copy_(x.reshape(self.x.shape), non_blocking=True)
+        return self.replay()

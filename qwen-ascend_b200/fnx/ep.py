@@ -54,8 +54,7 @@ class _PeerExchange:
     def __init__(self, rank, world, group, H, k, max_tokens, e_local, device):
         L = _lib.lib()
         self.world, self.group = world, group
-        self.cap = world * max_tokens * k              # every slot of every rank could land here
-        nbytes = L.fnx_ep_p2p_region_bytes(world, H, k, max_tokens, self.cap)
+        nbytes = L.fnx_ep_p2p_region_bytes(world, H, k, max_tokens)
         if not nbytes:
             raise ValueError(f"peer exchange: unsupported shape (world={world}, H={H}, k={k}, T={max_tokens})")
         self.imported = []
@@ -81,7 +80,9 @@ class _PeerExchange:
             self._desc = ctypes.create_string_buffer(L.fnx_ep_p2p_desc_bytes())
             self.desc = ctypes.addressof(self._desc)
             _lib.check(L.fnx_ep_p2p_desc(self.desc, rank, world, (ctypes.c_void_p * world)(*bases), H, k, max_tokens,
-                                         self.cap, e_local), "exchange descriptor")
+                                         e_local), "exchange descriptor")
+        self.cap = L.fnx_ep_p2p_capacity(self.desc, 0)          # received slots
+        self.cap_tok = L.fnx_ep_p2p_capacity(self.desc, 1)      # received token rows
         self.recv_x = L.fnx_ep_p2p_local(self.desc, 0)
         self.yb = L.fnx_ep_p2p_local(self.desc, 2)
 
@@ -160,6 +161,14 @@ class ExpertParallelMoE(MoELayer):
         o.dn_loc = o._arrange(torch.cat([layer.dn_all[lo:hi], layer.dn_all[layer.E:]]))
         o._setup_transport(layer.router_cat.device)
         return o
+
+    def capture(self, T, device=None):
+        """The layer's call on ``T`` tokens as one CUDA graph (``MoELayer.capture``); every
+        rank captures, and replays, in step.  Needs the p2p transport: the collective one
+        reads the exchange counts on the host."""
+        if self.transport != "p2p":
+            raise RuntimeError("ExpertParallelMoE.capture needs transport='p2p'")
+        return super().capture(T, device)
 
     def close(self):
         """Release the peer exchange (collective over the group)."""
@@ -316,41 +325,52 @@ class ExpertParallelMoE(MoELayer):
         Eg, I, cap = self.E_local, self.I, ex.cap
         logits, w, idx, wf = self.route(x)
         order_d, inverse_d, counts = self.dispatch_layout(idx)
-        self.last_counts = counts
-        _lib.check(L.fnx_ep_p2p_counts(D, counts.data_ptr(), st), "EP count exchange")
-        _lib.check(L.fnx_ep_p2p_push(D, x.data_ptr(), T, order_d.data_ptr(), idx.data_ptr(), st), "EP dispatch")
+        tok_index = torch.empty(max(idx.numel(), 1), dtype=torch.int32, device=dev)
+        tcounts = torch.empty(self.world, dtype=I64, device=dev)
+        self.last_counts = (counts, tcounts)
+        _lib.check(L.fnx_ep_p2p_dedup(D, order_d.data_ptr(), counts.data_ptr(), T, tok_index.data_ptr(),
+                                      tcounts.data_ptr(), st), "EP token dedup")
+        _lib.check(L.fnx_ep_p2p_counts(D, counts.data_ptr(), tcounts.data_ptr(), st), "EP count exchange")
+        _lib.check(L.fnx_ep_p2p_push(D, x.data_ptr(), T, order_d.data_ptr(), idx.data_ptr(), tok_index.data_ptr(), st),
+                   "EP dispatch")
         _lib.check(L.fnx_ep_p2p_wait(D, 1, st), "EP dispatch wait")
         M = T + cap
         order_x = torch.empty(M, dtype=I64, device=dev)
         ends_x = torch.empty(Eg + 1, dtype=I64, device=dev)
-        pos = torch.empty(max(cap, 1), dtype=I64, device=dev)
+        pos = torch.empty(cap, dtype=I64, device=dev)
+        rows = torch.empty(M, dtype=I64, device=dev)              # down-row destinations (pointers)
+        sh = torch.empty(max(T, 1), H, dtype=BF16, device=dev)
         wsb = L.fnx_ep_p2p_recv_workspace(D)
         ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
-        _lib.check(L.fnx_ep_p2p_recv_layout(D, T, order_x.data_ptr(), ends_x.data_ptr(), pos.data_ptr(), ws.data_ptr(),
-                                            wsb, st), "EP receive layout")
+        _lib.check(L.fnx_ep_p2p_recv_layout(D, T, order_x.data_ptr(), ends_x.data_ptr(), pos.data_ptr(),
+                                            rows.data_ptr(), sh.data_ptr(), ws.data_ptr(), wsb, st), "EP receive layout")
         a2 = torch.empty(M, I, dtype=BF16, device=dev)
-        _lib.check(L.fnx_moe_grouped_w4(ex.recv_x, H, cap + self.max_tokens, order_x.data_ptr(), 1,
+        _lib.check(L.fnx_moe_grouped_w4(ex.recv_x, H, ex.cap_tok + self.max_tokens, order_x.data_ptr(), 1,
                                         self.gu_loc.data_ptr(), ends_x.data_ptr(), a2.data_ptr(), I, Eg + 1, M, H,
                                         2 * I, EPI_SWIGLU_SHARED_FIRST, st), "grouped W4A16 GEMM")
-        yd = torch.empty(M, H, dtype=BF16, device=dev)
-        _grouped_w4(a2, self.dn_loc, ends_x, yd, E=Eg + 1, M=M, K=I, Nw=H, epilogue=EPI_PLAIN)
-        _lib.check(L.fnx_ep_p2p_return(D, yd.data_ptr(), M, pos.data_ptr(), st), "EP return")
+        _lib.check(L.fnx_moe_grouped_w4_rows(a2.data_ptr(), I, M, None, 1, self.dn_loc.data_ptr(), ends_x.data_ptr(),
+                                             rows.data_ptr(), Eg + 1, M, I, H, st), "grouped W4A16 GEMM (return)")
+        _lib.check(L.fnx_ep_p2p_signal(D, 2, st), "EP return signal")
         _lib.check(L.fnx_ep_p2p_wait(D, 2, st), "EP return wait")
         out = torch.empty(T, H, dtype=BF16, device=dev)
         gate = logits[:, self.E:self.E + 1]
-        _lib.check(L.fnx_moe_combine(ex.yb, wf.data_ptr(), inverse_d.data_ptr(), yd.data_ptr(), gate.data_ptr(),
+        _lib.check(L.fnx_moe_combine(ex.yb, wf.data_ptr(), inverse_d.data_ptr(), sh.data_ptr(), gate.data_ptr(),
                                      logits.stride(0), out.data_ptr(), T, self.k, H, st), "MoE combine")
         return out
 
     def exchange_stats(self):
-        """``(rows sent to other ranks, rows received)`` of the last call (synchronises)."""
+        """Rows this rank moved in its last call (synchronises): ``dispatch_rows`` token rows
+        sent to other ranks, ``return_rows`` slot rows that came back from other ranks,
+        ``received_slots`` slots this rank's experts processed."""
         if self.last_counts is None:
             return None
+        r = self.rank
         if self.transport == "p2p":
-            sc = self.last_counts.cpu().tolist()
-            return sum(sc) - sc[self.rank], int(_lib.lib().fnx_ep_p2p_received(self._p2p.desc))
+            sc, tc = (t.cpu().tolist() for t in self.last_counts)
+            return dict(dispatch_rows=sum(tc) - tc[r], return_rows=sum(sc) - sc[r],
+                        received_slots=int(_lib.lib().fnx_ep_p2p_received(self._p2p.desc)))
         sc, rc = self.last_counts
-        return sum(sc) - sc[self.rank], sum(rc)
+        return dict(dispatch_rows=sum(sc) - sc[r], return_rows=sum(sc) - sc[r], received_slots=sum(rc))
 
     # ---------------------------------------------------------------- one-process emulation
     @staticmethod

@@ -221,3 +221,18 @@ def test_expw4_apply_paths():
     ex2 = ExpW4(w.permute(1, 0, 2).contiguous().to(DEV), s8t.to(DEV), base.to(DEV), gs, expert_major=False)
     assert torch.equal(ex2.w4.cpu(), w)
     assert torch.equal(ex2._scales.cpu().view(torch.int16), O.cached_scales(s8t, base).view(torch.int16))
+
+
+@pytest.mark.parametrize("T", [300, 4])
+def test_captured_layer_replays_the_call(T):
+    """MoELayer.capture: the graph replay gives the direct call's bits, on new inputs too."""
+    t, L, layer = _layer(synth.CFG2, 31)
+    cap = layer.capture(T)
+    for seed in (1, 2):
+        x = synth.make_tokens(T, synth.CFG2.H, seed=seed, device=DEV)
+        ref = layer(x).clone()
+        got = cap(x)
+        assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), seed
+    xh = synth.make_tokens(T, synth.CFG2.H, seed=3).pin_memory()       # host input
+    got = cap(xh).clone()
+    assert torch.equal(got.view(torch.int16), layer(xh.to(DEV)).view(torch.int16))
