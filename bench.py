@@ -256,15 +256,23 @@ def bench_prefill(args, world, rank, dev):
     xh = [xs[i].cpu().pin_memory() for i in range(nl)]
     outh = torch.empty(T_PREFILL, H, dtype=torch.bfloat16).pin_memory()
 
-    def e2e():
-        i = step[0] % nl
-        step[0] += 1
-        out = caps[i](xh[i])                      # pinned host tokens in, graph replay
-        outh.copy_(out, non_blocking=True)
-    for _ in range(args.warmup):
-        e2e()
+    # HostPipeline: batch i+1's tokens go up and batch i-1's output comes down while batch i
+    # runs; every step still copies its own input from and its output to pinned host memory
+    from fnx.engine import HostPipeline
+    pipe = HostPipeline(caps)
+    outs_h = [torch.empty(T_PREFILL, H, dtype=torch.bfloat16).pin_memory() for _ in range(nl)]
+    xs_w = [xh[i % nl] for i in range(args.warmup)]
+    pipe.run(xs_w, [outs_h[i % nl] for i in range(args.warmup)])
     torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(time_events(e2e, args.steps, stream), world)
+    barrier(world)
+    xs_t = [xh[i % nl] for i in range(args.steps)]
+    os_t = [outs_h[i % nl] for i in range(args.steps)]
+    e2e_ms = max_over_ranks(time_events(lambda: pipe.run(xs_t, os_t), 1, stream) / args.steps, world)
+    ref_out = caps[0](xs[0]).cpu()
+    torch.cuda.synchronize()
+    pipe.run([xh[0]], [outh])
+    torch.cuda.synchronize()
+    assert torch.equal(outh.view(torch.int16), ref_out.view(torch.int16)), "host pipeline output differs"
     # this library's kernels per layer: top-k, permute (hist, scan, scatter), gate/up, down,
     # combine; the router logits run on cuBLAS and are not counted.  Expert parallel (peer
     # exchange): top-k, dispatch layout (3), token dedup, count exchange, dispatch push, wait,
@@ -344,6 +352,50 @@ def bench_decode(dev, nl=16, iters=20):
     return res
 
 
+def bench_w8(dev, nw=16, iters=10):
+    """The W8A16 concatenated dense projection (qkv+z fused: K=2048, N=5120, per-channel
+    int8 weights, bf16 scales |N(0, 0.01)|) at M = 1, 16, 256, 4096.  16 distinct weight
+    sets (168 MB, beyond L2) are called in turn inside one CUDA graph; the time per call is
+    the graph's time over its 16 calls."""
+    from fnx.engine import DenseW8
+    K, N = 2048, 5120
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    mats = []
+    for _ in range(nw):
+        q = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int32).to(torch.int8)
+        sc = (torch.randn(N, 1, generator=g, device=dev).abs_() * 0.01).to(torch.bfloat16)
+        mats.append(DenseW8(q, sc))
+    pk, src = peaks()
+    stream = torch.cuda.current_stream(dev)
+    res = {"shape": {"K": K, "N": N, "weights": "int8 per output channel"}, "peak_source": src}
+    for M in (1, 16, 256, 4096):
+        x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+        for w in mats:
+            w(x)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for w in mats:
+                w(x)
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        ms = time_events(gr.replay, iters, stream) / nw
+        nbytes = K * N + 2 * N + 2 * M * K + 2 * M * N
+        flops = 2 * M * K * N
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        tfl = flops / (ms * 1e-3) / 1e12
+        r = {"us": round(ms * 1e3, 2), "achieved_gbs": round(gbs, 1), "achieved_tflops": round(tfl, 1)}
+        if M <= 16:
+            r.update(bound="hbm", frac=round(gbs / pk["hbm_gbs"], 4))
+        else:
+            r.update(bound="tensor", frac=round(tfl / pk["bf16_tflops"], 4))
+        res[f"M{M}"] = r
+        del gr
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -392,6 +444,7 @@ def main():
 
     r = bench_prefill(args, world, rank, dev)
     dec = None if (args.no_decode or world > 1) else bench_decode(dev)
+    w8 = None if (args.no_decode or world > 1) else bench_w8(dev)
     cpu = cpu_baseline(args.cpu_sample) if (rank == 0 and world == 1) else None
     if rank == 0:
         line = {"metric": METRIC, "value": round(r["value"], 1), "unit": "tokens/s", "n_gpus": world,
@@ -401,7 +454,7 @@ def main():
                 "config": dict(config, parallelism=f"ep{world}" if world > 1 else "single GPU",
                                **({"expert_parallel": r["ep"]} if r["ep"] else {})),
                 "clocks": r["clocks"], "e2e": r["e2e"], "gpu_launches": r["gpu_launches"],
-                "roofline": r["roofline"], "layer_tflops": round(r["layer_tflops"], 1), "decode": dec,
+                "roofline": r["roofline"], "layer_tflops": round(r["layer_tflops"], 1), "decode": dec, "w8a16": w8,
                 "cpu_baseline": cpu}
         print(json.dumps(line))
     if world > 1:

@@ -368,3 +368,63 @@ class CapturedLayer:
         if x.data_ptr() != self.x.data_ptr():
             self.x.copy_(x.reshape(self.x.shape), non_blocking=True)
         return self.replay()
+
+
+class HostPipeline:
+    """Layer calls on batches that live in pinned host memory, with the copies overlapped:
+    while batch i's graph replays on the compute stream, batch i+1's input goes up and batch
+    i-1's output comes down on two copy streams (the two directions of the host link run at
+    once).  ``slots`` are ``CapturedLayer`` objects used round-robin (at least two); batch i
+    runs on slot ``i % len(slots)``, so consecutive batches never share static buffers."""
+
+    def __init__(self, slots):
+        if len(slots) < 2:
+            raise ValueError("HostPipeline needs at least two captured slots")
+        self.slots = list(slots)
+        self.device = self.slots[0].x.device
+        self.h2d = torch.cuda.Stream(self.device)
+        self.d2h = torch.cuda.Stream(self.device)
+
+    def run(self, xs_host, outs_host):
+        """``outs_host[i] <- layer(xs_host[i])`` for every i (pinned host tensors); returns
+        when the work is queued (synchronise the device, or the last output's stream, to
+        read the results)."""
+        n, S = len(xs_host), len(self.slots)
+        comp = torch.cuda.current_stream(self.device)
+        ev = lambda: torch.cuda.Event()                       # noqa: E731
+        in_ready, done, out_free = [None] * n, [None] * n, [None] * S
+        start = ev()
+        start.record(comp)
+        self.h2d.wait_event(start)
+        self.d2h.wait_event(start)
+
+        def upload(i):
+            s = self.slots[i % S]
+            if out_free[i % S] is not None:                 # previous user of the slot finished
+                self.h2d.wait_event(out_free[i % S])
+            with torch.cuda.stream(self.h2d):
+                s.x.copy_(xs_host[i].reshape(s.x.shape), non_blocking=True)
+            in_ready[i] = ev()
+            in_ready[i].record(self.h2d)
+
+        if n:
+            upload(0)
+        for i in range(n):
+            s = self.slots[i % S]
+            if i + 1 < n:
+                upload(i + 1)
+            comp.wait_event(in_ready[i])
+            s.replay()
+            done[i] = ev()
+            done[i].record(comp)
+            self.d2h.wait_event(done[i])
+            with torch.cuda.stream(self.d2h):
+                outs_host[i].copy_(s.out, non_blocking=True)
+            out_free[i % S] = ev()
+            out_free[i % S].record(self.d2h)
+            # the slot's next batch waits for out_free[i % S] in upload(), and its replay waits
+            # for that upload, so neither its input nor its output is overwritten early
+        # the caller's stream sees every output copied
+        end = ev()
+        end.record(self.d2h)
+        comp.wait_event(end)

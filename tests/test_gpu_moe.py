@@ -236,3 +236,19 @@ def test_captured_layer_replays_the_call(T):
     xh = synth.make_tokens(T, synth.CFG2.H, seed=3).pin_memory()       # host input
     got = cap(xh).clone()
     assert torch.equal(got.view(torch.int16), layer(xh.to(DEV)).view(torch.int16))
+
+
+def test_host_pipeline_matches_direct_calls():
+    """HostPipeline: 5 host batches through two captured layers, copies overlapped with the
+    replays; every output equals the direct call's."""
+    from fnx.engine import HostPipeline
+    layers = [_layer(synth.CFG2, 40 + i)[2] for i in range(2)]
+    T = 256
+    caps = [lay.capture(T) for lay in layers]
+    xs = [synth.make_tokens(T, synth.CFG2.H, seed=60 + i).pin_memory() for i in range(5)]
+    outs = [torch.empty(T, synth.CFG2.H, dtype=BF16).pin_memory() for _ in range(5)]
+    HostPipeline(caps).run(xs, outs)
+    torch.cuda.synchronize()
+    for i in range(5):
+        ref = layers[i % 2](xs[i].to(DEV)).cpu()
+        assert torch.equal(outs[i].view(torch.int16), ref.view(torch.int16)), i
