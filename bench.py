@@ -275,10 +275,10 @@ def bench_prefill(args, world, rank, dev):
     assert torch.equal(outh.view(torch.int16), ref_out.view(torch.int16)), "host pipeline output differs"
     # this library's kernels per layer: top-k, permute (hist, scan, scatter), gate/up, down,
     # combine; the router logits run on cuBLAS and are not counted.  Expert parallel (peer
-    # exchange): top-k, dispatch layout (3), token dedup, count exchange, dispatch push, wait,
+    # exchange): top-k, dispatch layout (3), token dedup (2), count exchange, dispatch push, wait,
     # receive layout (head, permute 3, row destinations), gate/up, down with the return in its
     # epilogue, signal, wait, combine.
-    launches_per_step = 19 if world > 1 else 7
+    launches_per_step = 20 if world > 1 else 7
     del caps
     torch.cuda.synchronize()
     if world > 1:

@@ -17,6 +17,7 @@
 #include "kernels_gemm_pair.cuh"
 #include "kernels_route.cuh"
 #include "kernels_w4gemv.cuh"
+#include "kernels_w8gemv.cuh"
 
 #define FNX_API extern "C" __attribute__((visibility("default")))
 
@@ -399,7 +400,7 @@ FNX_API int fnx_ep_gather_rows(const void* src, long long ld_src, long long src_
 // ------------------------------------------------------------------ peer-memory exchange
 namespace {
 struct EPRegion {
-    size_t flags, cnt, plan, epoch, tickets, recv_e, recv_row, recv_x, yb, sink, total;
+    size_t flags, cnt, plan, epoch, tickets, bcount, recv_e, recv_row, recv_x, yb, sink, total;
 };
 EPRegion ep_region(int H, int k, int T_cap, long long cap, long long cap_tok) {
     EPRegion R{};
@@ -408,6 +409,7 @@ EPRegion ep_region(int H, int k, int T_cap, long long cap, long long cap_tok) {
     R.cnt = o;      o += align_up(sizeof(long long) * 2 * EP_MAX_G * EP_MAX_G * 2, 256);
     R.plan = o;     o += align_up(sizeof(long long) * EP_PLAN_LEN, 256);
     R.epoch = o;    R.tickets = o + 16; o += 256;
+    R.bcount = o;   o += align_up(sizeof(int) * (size_t)(((long long)T_cap * k + 1023) / 1024 + 1), 256);
     R.recv_e = o;   o += align_up(sizeof(int64_t) * (size_t)cap, 256);
     R.recv_row = o; o += align_up(sizeof(int64_t) * (size_t)cap, 256);
     R.recv_x = o;   o += align_up(sizeof(bf16) * (size_t)(cap_tok + T_cap) * H, 256);
@@ -479,6 +481,7 @@ FNX_API int fnx_ep_p2p_desc(void* desc, int rank, int world, void* const* bases,
     d.plan = (long long*)(own + R.plan);
     d.epoch = (unsigned*)(own + R.epoch);
     d.tickets = (unsigned*)(own + R.tickets);
+    d.bcount = (int*)(own + R.bcount);
     d.sink = (bf16*)(own + R.sink);
     for (int q = 0; q < world; ++q) {
         char* b = (char*)bases[q];
@@ -523,8 +526,12 @@ FNX_API int fnx_ep_p2p_dedup(const void* desc, const void* order, const void* co
                              void* tcounts, void* stream) {
     const EPDesc* d = ep_desc(desc);
     if (!d || T < 0 || T > d->T_cap || !counts || !tcounts || (T > 0 && (!order || !tok_index))) return FNX_EARG;
-    ep_dedup_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(*d, (const int64_t*)order, (const int64_t*)counts, T * d->k,
-                                                          (int*)tok_index, (int64_t*)tcounts);
+    const int n = T * d->k;
+    const int blocks = n > 0 ? (n + 1023) / 1024 : 1;
+    cudaStream_t st = (cudaStream_t)stream;
+    ep_dedup_count_kernel<<<blocks, 1024, 0, st>>>(*d, (const int64_t*)order, (const int64_t*)counts, n);
+    ep_dedup_index_kernel<<<blocks, 1024, 0, st>>>(*d, (const int64_t*)order, (const int64_t*)counts, n,
+                                                   (int*)tok_index, (int64_t*)tcounts);
     return launch_rc();
 }
 
@@ -625,8 +632,60 @@ FNX_API int fnx_moe_grouped_w4_rows(const void* act, long long ld_act, long long
     return gemm_launch(GEMM_W4, EPI_PLAIN, p, (cudaStream_t)stream);
 }
 
+namespace {
+template <int MT>
+int w8_gemv_launch_t(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int gs,
+                     cudaStream_t st) {
+    const size_t smem = w8a16_gemv_smem(MT, K);
+    static bool configured = false;
+    if (!configured) {
+        if (cudaFuncSetAttribute(w8a16_gemv_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return FNX_ELAUNCH;
+        configured = true;
+    }
+    if (smem > (size_t)227 * 1024) return FNX_ESHAPE;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = W8V_CL;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((N + W8V_COLS - 1) / W8V_COLS), W8V_CL, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, w8a16_gemv_kernel<MT>, (const bf16*)x, (const int8_t*)w8t, (const bf16*)sc, (bf16*)y,
+                           M, K, N, gs) != cudaSuccess)
+        return FNX_ELAUNCH;
+    return launch_rc();
+}
+
+bool w8_gemv_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("FNX_W8_GEMV");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+}  // namespace
+
 FNX_API int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G,
                            void* stream) {
+    // M <= 16: the weight-streaming GEMV (cluster K split); larger M: the tcgen05 GEMM
+    if (M >= 1 && M <= W8V_MAXM && G >= 1 && K % G == 0 && K % 64 == 0 && K <= 8192 && N % 4 == 0 &&
+        w8_gemv_enabled()) {
+        const int gs = K / G;
+        cudaStream_t st = (cudaStream_t)stream;
+        if (M == 1) return w8_gemv_launch_t<1>(x, w8t, sc, y, M, K, N, gs, st);
+        if (M == 2) return w8_gemv_launch_t<2>(x, w8t, sc, y, M, K, N, gs, st);
+        if (M <= 4) return w8_gemv_launch_t<4>(x, w8t, sc, y, M, K, N, gs, st);
+        if (M <= 8) return w8_gemv_launch_t<8>(x, w8t, sc, y, M, K, N, gs, st);
+        return w8_gemv_launch_t<16>(x, w8t, sc, y, M, K, N, gs, st);
+    }
     GemmParams p{};
     p.act = (const bf16*)x; p.ld_act = K; p.w = w8t; p.scales = (const bf16*)sc; p.out = (bf16*)y; p.ld_out = N;
     p.act_rows = M;

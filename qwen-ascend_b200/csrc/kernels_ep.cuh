@@ -69,6 +69,7 @@ __global__ void __launch_bounds__(256) ep_gather_rows_kernel(const bf16* __restr
 //   cnt      i64  [2][G][G][2]                cnt[parity][q][j] = (slots, tokens) of rank q for owner j
 //   plan     i64  [EP_PLAN_LEN]               local: this call's offsets (below)
 //   epoch    u32, tickets u32[4]              local
+//   bcount   i32  [ceil(T_cap*k / 1024)]      local: token dedup block counts
 //   recv_e   i64  [cap]                       received slots: owner-local expert
 //   recv_row i64  [cap]                       received slots: token row in recv_x
 //   recv_x   bf16 [cap_tok + T_cap, H]        received token rows, then this rank's own tokens
@@ -97,6 +98,7 @@ struct EPDesc {
     long long* plan;
     unsigned* epoch;
     unsigned* tickets;
+    int* bcount;                    // local: dedup block counts [ceil(T_cap*k / 1024)]
     bf16* sink;
     unsigned* flags[EP_MAX_G];
     long long* cnt[EP_MAX_G];
@@ -159,37 +161,54 @@ FNX_DEV int ep_chunk(const long long* start, int G, long long p) {
     return j;
 }
 
-// One block of 1024 threads: tok_index[p] = the deduplicated token row of owner-major slot p
-// (counted over all owners; a new row starts at each owner chunk and each change of token)
-// and tcounts[j] = the token rows for owner j.  Each warp owns a contiguous range of slots and
-// walks it 32 at a time (coalesced loads, ballot counts): one pass counts the new rows, a scan
-// over the 32 warps gives each range its first row, a second pass writes the rows.
-__global__ void __launch_bounds__(1024) ep_dedup_kernel(const EPDesc d, const int64_t* __restrict__ order,
-                                                        const int64_t* __restrict__ counts, int n,
-                                                        int* __restrict__ tok_index, int64_t* __restrict__ tcounts) {
-    __shared__ long long start[EP_MAX_G + 1];
-    __shared__ int wsum[32], wexcl[32];
-    const int G = d.world, k = d.k, t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    if (t == 0) {
+// Token dedup: tok_index[p] = the deduplicated token row of owner-major slot p (counted over
+// all owners; a new row starts at each owner chunk and at each change of token), and
+// tcounts[j] = the token rows for owner j.  Two launches over blocks of 1024 slots: the first
+// counts each block's new rows, the second adds the counts of the blocks before it to a
+// block-wide scan; its last block (by ticket) derives tcounts.
+FNX_DEV void ep_chunk_starts(const int64_t* counts, int G, long long* start) {
+    if (threadIdx.x == 0) {
         long long a = 0;
         for (int j = 0; j < G; ++j) { start[j] = a; a += counts[j]; }
         start[G] = a;
     }
     __syncthreads();
-    const long long per = ((long long)(n + 31) / 32 + 31) / 32 * 32;        // slots per warp, multiple of 32
-    const long long wb = min((long long)n, warp * per), we = min((long long)n, wb + per);
-    auto first = [&](long long p) -> bool {
-        if (p == 0) return true;
-        for (int j = 1; j < G; ++j)
-            if (p == start[j]) return true;
-        return __ldg(order + p) / k != __ldg(order + p - 1) / k;
-    };
-    int cnt = 0;
-    for (long long b = wb; b < we; b += 32) {
-        const long long p = b + lane;
-        cnt += __popc(__ballot_sync(0xffffffffu, p < we && first(p)));
+}
+FNX_DEV bool ep_first(const int64_t* order, const long long* start, int G, int k, long long p) {
+    if (p == 0) return true;
+    for (int j = 1; j < G; ++j)
+        if (p == start[j]) return true;
+    return __ldg(order + p) / k != __ldg(order + p - 1) / k;
+}
+
+__global__ void __launch_bounds__(1024) ep_dedup_count_kernel(const EPDesc d, const int64_t* __restrict__ order,
+                                                              const int64_t* __restrict__ counts, int n) {
+    __shared__ long long start[EP_MAX_G + 1];
+    ep_chunk_starts(counts, d.world, start);
+    const long long p = (long long)blockIdx.x * 1024 + threadIdx.x;
+    const int c = __syncthreads_count(p < n && ep_first(order, start, d.world, d.k, p));
+    if (threadIdx.x == 0) d.bcount[blockIdx.x] = c;
+}
+
+__global__ void __launch_bounds__(1024) ep_dedup_index_kernel(const EPDesc d, const int64_t* __restrict__ order,
+                                                              const int64_t* __restrict__ counts, int n,
+                                                              int* __restrict__ tok_index,
+                                                              int64_t* __restrict__ tcounts) {
+    __shared__ long long start[EP_MAX_G + 1];
+    __shared__ int wsum[32];
+    __shared__ int base;
+    __shared__ unsigned last;
+    ep_chunk_starts(counts, d.world, start);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        int b = 0;
+        for (int i = 0; i < (int)blockIdx.x; ++i) b += d.bcount[i];
+        base = b;
     }
-    if (lane == 0) wsum[warp] = cnt;
+    const long long p = (long long)blockIdx.x * 1024 + threadIdx.x;
+    const bool f = p < n && ep_first(order, start, d.world, d.k, p);
+    const unsigned m = __ballot_sync(0xffffffffu, f);
+    if (lane == 0) wsum[warp] = __popc(m);
     __syncthreads();
     if (warp == 0) {
         const int v = wsum[lane];
@@ -199,23 +218,26 @@ __global__ void __launch_bounds__(1024) ep_dedup_kernel(const EPDesc d, const in
             const int u = __shfl_up_sync(0xffffffffu, inc, o);
             if (lane >= o) inc += u;
         }
-        wexcl[lane] = inc - v;
+        wsum[lane] = inc - v;
     }
     __syncthreads();
-    int run = wexcl[warp];
-    for (long long b = wb; b < we; b += 32) {
-        const long long p = b + lane;
-        const bool f = p < we && first(p);
-        const unsigned m = __ballot_sync(0xffffffffu, f);
-        if (p < we) tok_index[p] = run + __popc(m & ((1u << lane) - 1u)) + (f ? 1 : 0) - 1;
-        run += __popc(m);
+    if (p < n) tok_index[p] = base + wsum[warp] + __popc(m & ((1u << lane) - 1u)) + (f ? 1 : 0) - 1;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        last = atomicAdd(d.tickets + 2, 1u) == gridDim.x - 1;
+        if (last) {
+            atomicExch(d.tickets + 2, 0u);
+            __threadfence();
+        }
     }
     __syncthreads();
-    if (t == 0) {
-        const int total = n > 0 ? tok_index[n - 1] + 1 : 0;
+    if (last && threadIdx.x == 0) {
+        const int G = d.world;
+        const int total = n > 0 ? __ldcg(tok_index + n - 1) + 1 : 0;
         long long us[EP_MAX_G + 1];
         us[G] = total;
-        for (int j = G - 1; j >= 0; --j) us[j] = start[j] < start[j + 1] ? tok_index[start[j]] : us[j + 1];
+        for (int j = G - 1; j >= 0; --j) us[j] = start[j] < start[j + 1] ? __ldcg(tok_index + start[j]) : us[j + 1];
         for (int j = 0; j < G; ++j) tcounts[j] = us[j + 1] - us[j];
     }
 }

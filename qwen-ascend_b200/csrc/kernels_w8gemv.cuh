@@ -1,0 +1,122 @@
+// Small-M W8A16 dense projection (DenseW8.__call__, fnx/engine.py:350-365, for M <= 16):
+// y [M, N] = x [M, K] . bf16(w8t [K, N] * sc [k / gs, n]) with fp32 accumulation.
+//
+// At M <= 16 the projection is a weight stream (K*N bytes of int8), so it is built as a GEMV:
+// a CTA owns 128 output columns (4 per lane: one 4-byte load per weight row, a warp reads a
+// full 128-byte line) and one eighth of K; its 8 warps split that eighth by rows.  The 8 CTAs
+// of a cluster hold the 8 eighths of K for the same columns and reduce them through
+// distributed shared memory in a fixed order, so the sum is deterministic and needs no
+// global workspace.  Each weight is dequantised once to the exactly rounded bf16(q * s) the
+// reference's antiquant produces, then multiplied into every token's fp32 accumulators.
+#pragma once
+#include "fnx_common.cuh"
+
+namespace fnx {
+
+constexpr int W8V_COLS = 128;      // output columns per CTA
+constexpr int W8V_CL = 8;          // CTAs per cluster (K split)
+constexpr int W8V_MAXM = 16;
+
+FNX_DEV float ld_shared_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+inline size_t w8a16_gemv_smem(int MT, int K) {
+    const int Kc = K / W8V_CL;
+    return sizeof(float) * ((size_t)MT * Kc + (size_t)8 * MT * W8V_COLS + (size_t)MT * W8V_COLS);
+}
+
+// grid (ceil(N / 128), 8), cluster (1, 8, 1), 256 threads.  MT: tokens padded to 1/2/4/8/16.
+// Needs K % 64 == 0, N % 4 == 0, K % gs == 0.
+template <int MT>
+__global__ void __launch_bounds__(256, 2) w8a16_gemv_kernel(const bf16* __restrict__ x, const int8_t* __restrict__ w,
+                                                            const bf16* __restrict__ sc, bf16* __restrict__ y,
+                                                            int M, int K, int N, int gs) {
+    extern __shared__ float sm[];
+    const int Kc = K / W8V_CL;
+    float* xs = sm;                                   // [MT][Kc]
+    float* red = xs + MT * Kc;                        // [8 warps][MT][128]
+    float* cpart = red + 8 * MT * W8V_COLS;           // [MT][128]: this CTA's eighth
+    const int crank = (int)cluster_rank();
+    const int n0 = blockIdx.x * W8V_COLS;
+    const int k0 = crank * Kc;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < MT * Kc; i += blockDim.x) {
+        const int m = i / Kc, kk = i - m * Kc;
+        xs[i] = m < M ? bf2f(x[(long long)m * K + k0 + kk]) : 0.f;
+    }
+    __syncthreads();
+
+    const int col = n0 + lane * 4;
+    const bool ok = col < N;
+    const int rpw = Kc / 8;                           // rows per warp (K % 64 == 0)
+    const int r0 = warp * rpw;
+    float acc[MT][4];
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[m][c] = 0.f;
+    int g_cur = -1;
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int rb = 0; rb < rpw; rb += 8) {
+        uint32_t q[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const long long k = k0 + r0 + rb + i;
+            q[i] = (ok && rb + i < rpw) ? __ldg(reinterpret_cast<const unsigned int*>(w + k * N + col)) : 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (rb + i >= rpw) break;                 // warp-uniform: rows past this warp's share
+            const int kr = r0 + rb + i;               // row within the CTA's eighth
+            const int g = (k0 + kr) / gs;
+            if (g != g_cur) {                         // warp-uniform
+                g_cur = g;
+                if (ok) {
+                    const uint2 sv = __ldg(reinterpret_cast<const uint2*>(sc + (long long)g * N + col));
+                    s[0] = bf_lo(sv.x); s[1] = bf_hi(sv.x); s[2] = bf_lo(sv.y); s[3] = bf_hi(sv.y);
+                }
+            }
+            float wv[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int qi = (int)(signed char)(q[i] >> (8 * c));
+                wv[c] = round_bf(__fmul_rn((float)qi, s[c]));     // bf16(q * s): the product is exact in fp32
+            }
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const float xv = xs[m * Kc + kr];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[m][c] = __fmaf_rn(wv[c], xv, acc[m][c]);
+            }
+        }
+    }
+    // the 8 warps of the CTA, in order
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) red[(warp * MT + m) * W8V_COLS + lane * 4 + c] = acc[m][c];
+    __syncthreads();
+    for (int i = threadIdx.x; i < MT * W8V_COLS; i += blockDim.x) {
+        float v = 0.f;
+#pragma unroll
+        for (int wv = 0; wv < 8; ++wv) v += red[wv * MT * W8V_COLS + i];
+        cpart[i] = v;
+    }
+    cluster_sync_all();
+    // the cluster's 8 eighths of K, in order, by CTA 0
+    if (crank == 0) {
+        for (int i = threadIdx.x; i < MT * W8V_COLS; i += blockDim.x) {
+            float v = cpart[i];
+#pragma unroll
+            for (int r = 1; r < W8V_CL; ++r) v += ld_shared_cluster_f32(mapa_rank(cpart + i, (uint32_t)r));
+            const int m = i / W8V_COLS, n = n0 + (i - m * W8V_COLS);
+            if (m < M && n < N) y[(long long)m * N + n] = f2bf(v);
+        }
+    }
+    cluster_sync_all();                               // peers keep their shared memory until read
+}
+
+}  // namespace fnx

@@ -252,3 +252,22 @@ def test_host_pipeline_matches_direct_calls():
     for i in range(5):
         ref = layers[i % 2](xs[i].to(DEV)).cpu()
         assert torch.equal(outs[i].view(torch.int16), ref.view(torch.int16)), i
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 16, 17])
+@pytest.mark.parametrize("G", [1, 8])
+def test_w8a16_small_m(M, G):
+    """The M <= 16 weight-streaming GEMV (and M = 17 on the tensor-core GEMM) against the
+    oracle's exact dequant + fp64 matmul; partial last column block (N = 648); repeatable."""
+    from fnx.engine import DenseW8
+    K, N = 1024, (648 if M <= 16 else 640)          # the tensor-core GEMM needs N % 128 == 0
+    g = torch.Generator().manual_seed(M * 10 + G)
+    q = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int32).to(torch.int8)
+    sc = (torch.randn(N, G, generator=g).abs() * 0.01).to(BF16)
+    x = torch.randn(M, K, generator=g).to(BF16)
+    w = DenseW8(q.to(DEV), sc.to(DEV))
+    got = w(x.to(DEV))
+    ref = O.dense_w8(x, w.w8t.cpu(), w.sc.cpu())
+    rep = O.tolerance_report(got.cpu(), ref)
+    assert O.within_tolerance(got.cpu(), ref), rep
+    assert torch.equal(w(x.to(DEV)).view(torch.int16), got.view(torch.int16))
