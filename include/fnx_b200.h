@@ -218,7 +218,7 @@ int fnx_moe_combine(void* yd, void* wf, void* inverse, void* sh, void* gate, lon
  * router bf16 [E+1, H] (row E = shared-expert gate), routed and shared experts as the
  * tile blocks of fnx_repack_w4_tiles (gate/up with swiglu=1, down with swiglu=0);
  * out bf16 [M,H], w_out bf16 [M,k], idx_out int64 [M,k] (may be NULL).
- * H % 256 == 0, I % 128 == 0, H, I <= 4096.
+ * H % 256 == 0, I % 128 == 0, H, I <= 4096, E <= 512.
  * workspace: fnx_moe_decode_workspace(M,H,I,E,k) bytes, zero-filled before first use;
  * each completed call leaves it ready for the next.  Calls sharing a workspace must not
  * overlap on the GPU. */

@@ -738,18 +738,15 @@ DecodeLayout decode_layout(int M, int H, int I, int E, int k) {
     DecodeLayout L{};
     L.R = E + 1;
     const int mt = I / 64, kb = H / 64;
-    // K splits (powers of two dividing the k-block count).  An item fetches its k-range
-    // with one bulk copy of at most DEC_CH tile blocks, so splits start there and grow
-    // (>= 2 k-blocks each) until the phase has about one item per resident block: the
-    // shared gate/up shares phase 1 with the router rows, the routed gate/up has phase 2.
+    // K splits (powers of two dividing the k-block count, >= 2 k-blocks per item): the
+    // router rows and the shared gate/up together fill about one item per resident block,
+    // and the routed gate/up is split as far as it still fits in one item per block.
     const int slots = 2 * num_sms();
+    const int rb = (L.R + DEC_ROWS - 1) / DEC_ROWS;
     L.ks1 = 1;
-    while (kb / L.ks1 > DEC_CH && kb % (L.ks1 * 2) == 0) L.ks1 *= 2;
-    while (L.ks1 < 64 && M * mt * L.ks1 < slots / 2 && kb % (L.ks1 * 2) == 0 && kb / (L.ks1 * 2) >= 2) L.ks1 *= 2;
+    while (rb + M * mt * L.ks1 * 2 <= slots && kb % (L.ks1 * 2) == 0 && kb / (L.ks1 * 2) >= 2) L.ks1 *= 2;
     L.ks2 = 1;
-    while (kb / L.ks2 > DEC_CH && kb % (L.ks2 * 2) == 0) L.ks2 *= 2;
-    while (L.ks2 < 64 && M * k * mt * L.ks2 < slots && kb % (L.ks2 * 2) == 0 && kb / (L.ks2 * 2) >= 2)
-        L.ks2 *= 2;
+    while (M * k * mt * L.ks2 * 2 <= slots && kb % (L.ks2 * 2) == 0 && kb / (L.ks2 * 2) >= 2) L.ks2 *= 2;
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
     L.logits = take((size_t)M * L.R * 2);
@@ -761,7 +758,7 @@ DecodeLayout decode_layout(int M, int H, int I, int E, int k) {
     L.act_sh = take((size_t)M * I * 2);
     L.yd = take((size_t)M * k * H * 2);
     L.sh = take((size_t)M * H * 2);
-    L.counters = take((size_t)(1 + M * mt + M * k * mt + H / 128 + 2) * 4);   // + barrier 2, exit ticket
+    L.counters = take(decode_counters(M, H, I, k) * 4);
     L.total = off;
     return L;
 }
@@ -780,7 +777,7 @@ FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu,
                               const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H,
                               int I, int E, int k, void* workspace, size_t ws_bytes, void* stream) {
     if (M < 1 || M > DEC_MAX_M || E < 1 || E > ROUTE_MAX_E || k < 1 || k > 32 || k > E) return FNX_EARG;
-    if (H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K) return FNX_ESHAPE;
+    if (H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K || E > DEC_MAX_E) return FNX_ESHAPE;
     const DecodeLayout L = decode_layout(M, H, I, E, k);
     if (!workspace || ws_bytes < L.total) return FNX_EWORKSPACE;
     if (!aligned16(x) || !aligned16(router) || !aligned16(gu) || !aligned16(dn) || !aligned16(sh_gu) ||
@@ -797,8 +794,8 @@ FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu,
     p.act = (bf16*)(ws + L.act); p.act_sh = (bf16*)(ws + L.act_sh); p.yd = (bf16*)(ws + L.yd); p.sh = (bf16*)(ws + L.sh);
     p.counters = (unsigned*)(ws + L.counters);
     p.M = M; p.H = H; p.I = I; p.E = E; p.k = k; p.R = L.R; p.ks1 = L.ks1; p.ks2 = L.ks2;
-    // one cooperative launch of every block that fits at once (the phases meet at grid
-    // barriers, so all blocks must be resident)
+    // one cooperative launch of every block that fits at once (work items wait for earlier
+    // items of other blocks, so all blocks must be resident)
     static int grid = 0;
     if (!grid) {
         if (cudaFuncSetAttribute(decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM))

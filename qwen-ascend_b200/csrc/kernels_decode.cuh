@@ -1,6 +1,5 @@
-// Decode (M <= 16 tokens) W4A16 MoE layer as one cooperative, HBM-bound GEMV kernel with
-// three phases (router + shared gate/up; routed gate/up + shared down; routed down +
-// combine), described above decode_fused_kernel below.
+// Decode (M <= 16 tokens) W4A16 MoE layer as one cooperative, HBM-bound GEMV kernel that
+// runs as a dataflow over work items (described above decode_fused_kernel below).
 //
 // This is the reference's decode branch (fnx/engine.py:1786-1889: concatenated shared
 // GEMM, softmax/top-k, gather + W4A16 gate/up, fp32 swiglu, Cartesian down,
@@ -21,6 +20,7 @@ namespace fnx {
 constexpr int DEC_THREADS = 256;
 constexpr int DEC_MAX_M = 16;
 constexpr int DEC_MAX_K = 4096;          // largest K (H or I) a block stages in shared memory
+constexpr int DEC_MAX_E = 512;           // routed experts
 constexpr int DEC_CH = 16;               // k-blocks per bulk copy (69.6 KB of shared memory)
 // dynamic shared memory of the decode kernels: one chunk of tile blocks, or D1's eight
 // router rows of H <= DEC_MAX_K bf16
@@ -54,10 +54,18 @@ struct DecodeParams {
 
 FNX_DEV int gu_tiles(const DecodeParams& p) { return p.I / 64; }
 FNX_DEV int dn_tiles(const DecodeParams& p) { return p.H / 128; }
-FNX_DEV unsigned* ctr_d1(const DecodeParams& p) { return p.counters; }
-FNX_DEV unsigned* ctr_sh(const DecodeParams& p) { return p.counters + 1; }                                 // [M * I/64]
-FNX_DEV unsigned* ctr_gu(const DecodeParams& p) { return ctr_sh(p) + p.M * gu_tiles(p); }                 // [M*k * I/64]
-FNX_DEV unsigned* ctr_dn(const DecodeParams& p) { return ctr_gu(p) + p.M * p.k * gu_tiles(p); }           // [H/128]
+// counters (zero between calls): tickets of the K-split groups, then the dataflow counts
+FNX_DEV unsigned* ctr_sh(const DecodeParams& p) { return p.counters; }                                  // [M * I/64]
+FNX_DEV unsigned* ctr_gu(const DecodeParams& p) { return ctr_sh(p) + p.M * gu_tiles(p); }              // [M*k * I/64]
+FNX_DEV unsigned* ctr_router(const DecodeParams& p) { return ctr_gu(p) + p.M * p.k * gu_tiles(p); }    // router items done
+FNX_DEV unsigned* ctr_routed(const DecodeParams& p) { return ctr_router(p) + 1; }                       // routing published
+FNX_DEV unsigned* ctr_shgu_done(const DecodeParams& p) { return ctr_routed(p) + 1; }                    // [M] tiles of act_sh
+FNX_DEV unsigned* ctr_gu_done(const DecodeParams& p) { return ctr_shgu_done(p) + p.M; }                 // [M*k] tiles of act
+FNX_DEV unsigned* ctr_comb(const DecodeParams& p) { return ctr_gu_done(p) + p.M * p.k; }                // [M * H/128]
+FNX_DEV unsigned* ctr_exit(const DecodeParams& p) { return ctr_comb(p) + p.M * dn_tiles(p); }
+inline size_t decode_counters(int M, int H, int I, int k) {
+    return (size_t)M * (I / 64) + (size_t)M * k * (I / 64) + 2 + M + (size_t)M * k + (size_t)M * (H / 128) + 1;
+}
 
 // Last-block ticket: true in exactly one block of a group of `n` blocks, after all of them
 // have published their results; the ticket is re-armed for the next launch.
@@ -145,26 +153,26 @@ FNX_DEV float sum_parts(const float* base, int ks, int r) {
 }
 
 // ------------------------------------------------------------------ the fused decode kernel
-// One cooperative launch: three phases separated by two grid barriers.
-//   phase 1  router + shared-gate logits (eight rows per item) and the shared expert's
-//            gate/up (items (t, m, ks); the last item of a (t, m) group applies its SwiGLU)
-//   barrier  then every block routes the tokens from the logits itself (the same
-//            deterministic top-k, so all blocks agree; block 0 publishes the routing)
-//   phase 2  routed gate/up (items (row, m, ks); the last of a group: fp32 SwiGLU -> act)
-//            and the shared expert's down projection (items (t, m) -> sh)
-//   barrier
-//   phase 3  routed down (items (row, m) -> yd); the last item of output tile m reduces the
-//            k slots of every token in order and merges the gated shared output
-// A block walks the items of a phase with stride gridDim.x, so any resident grid works.
+// One cooperative launch (every block resident) walking work items in this order, each block
+// taking items blockIdx.x, blockIdx.x + gridDim.x, ...:
+//   router rows     router + shared-gate logits, DEC_ROWS rows per item; the block finishing
+//                   the last of them routes every token (top-k once) and publishes it
+//   shared gate/up  (t, m, ks) K-split GEMV items; the last of a (t, m) group applies the
+//                   shared expert's SwiGLU into act_sh and counts the tile for token t
+//   routed gate/up  (row, m, ks) after the routing is published; the last of a group applies
+//                   the fp32 SwiGLU into act and counts the tile for slot row
+//   shared down     (t, m) once all act_sh tiles of token t are counted
+//   routed down     (row, m) once all act tiles of slot row are counted
+// The k routed down rows and the shared down tile of each (token, output tile) meet at a
+// ticket; whichever arrives last combines them (slot-order weighted reduce + gated shared).
+// Items only wait for items earlier in the order, and every block walks its items in order,
+// so the lowest unfinished item can always run: no barrier is needed and none deadlocks.
+// Waits are bounded (FNX_DEVERR_TIMEOUT) like every other spin here.
 
 struct DecodeRouting {
     int idx[DEC_MAX_M * ROUTE_MAX_K];
     float wf[DEC_MAX_M * ROUTE_MAX_K];
 };
-
-FNX_DEV unsigned* ctr_bar1(const DecodeParams& p) { return ctr_d1(p); }
-FNX_DEV unsigned* ctr_bar2(const DecodeParams& p) { return ctr_dn(p) + dn_tiles(p); }
-FNX_DEV unsigned* ctr_exit(const DecodeParams& p) { return ctr_bar2(p) + 1; }
 
 FNX_DEV unsigned ld_acquire_u32(const unsigned* p) {
     unsigned v;
@@ -172,23 +180,26 @@ FNX_DEV unsigned ld_acquire_u32(const unsigned* p) {
     return v;
 }
 
-// All blocks of the grid (co-resident by the cooperative launch); bounded.
-FNX_DEV void grid_barrier(unsigned* ctr, unsigned n) {
-    __syncthreads();
+// thread 0 waits (bounded) until *c >= target; then the block synchronises
+FNX_DEV void wait_count(const unsigned* c, unsigned target) {
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(ctr, 1u);
         const uint64_t t0 = fnx_globaltimer();
-        while (ld_acquire_u32(ctr) < n) {
-            __nanosleep(64);
+        while (ld_acquire_u32(c) < target) {
+            __nanosleep(32);
             if (fnx_globaltimer() - t0 > FNX_WAIT_NS) {
                 fnx_flag_error(FNX_DEVERR_TIMEOUT);
                 break;
             }
         }
-        __threadfence();
     }
     __syncthreads();
+}
+
+// this block's results are visible device-wide before *c counts them
+FNX_DEV void count_done(unsigned* c) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) atomicAdd(c, 1u);
 }
 
 // DEC_ROWS consecutive router rows (rows >= E: the shared-expert gate) and, when it fits,
@@ -212,33 +223,33 @@ FNX_DEV void router_rows(const DecodeParams& p, int item, uint32_t* wbuf, uint64
     phase ^= 1u;
     const int row = warp >> 1, hh = warp & 1;
     if (row < nr) {
-        float acc[DEC_MAX_M];
-#pragma unroll
-        for (int t = 0; t < DEC_MAX_M; ++t) acc[t] = 0.f;
         const bf16* wr = reinterpret_cast<const bf16*>(wbuf) + (long long)row * p.H;
-        for (int c = hh * (p.H / 2) + lane * 8; c < (hh + 1) * (p.H / 2); c += 256) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(wr + c);
-            const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        for (int t0 = 0; t0 < p.M; t0 += 4) {          // tokens four at a time (register pressure)
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int c = hh * (p.H / 2) + lane * 8; c < (hh + 1) * (p.H / 2); c += 256) {
+                const uint4 wv = *reinterpret_cast<const uint4*>(wr + c);
+                const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-            for (int t = 0; t < DEC_MAX_M; ++t) {
-                if (t < p.M) {
-                    const uint4 xv = *reinterpret_cast<const uint4*>(xs + (long long)t * p.H + c);
-                    const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+                for (int tt = 0; tt < 4; ++tt) {
+                    if (t0 + tt < p.M) {
+                        const uint4 xv = *reinterpret_cast<const uint4*>(xs + (long long)(t0 + tt) * p.H + c);
+                        const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        fma_bf_lo(acc[t], ww[i], xx[i]);
-                        fma_bf_hi(acc[t], ww[i], xx[i]);
+                        for (int i = 0; i < 4; ++i) {
+                            fma_bf_lo(acc[tt], ww[i], xx[i]);
+                            fma_bf_hi(acc[tt], ww[i], xx[i]);
+                        }
                     }
                 }
             }
-        }
 #pragma unroll
-        for (int t = 0; t < DEC_MAX_M; ++t) {
-            if (t < p.M) {
-                float v = acc[t];
+            for (int tt = 0; tt < 4; ++tt) {
+                if (t0 + tt < p.M) {
+                    float v = acc[tt];
 #pragma unroll
-                for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-                if (lane == 0) partial[row][hh][t] = v;
+                    for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+                    if (lane == 0) partial[row][hh][t0 + tt] = v;
+                }
             }
         }
     }
@@ -250,79 +261,124 @@ FNX_DEV void router_rows(const DecodeParams& p, int item, uint32_t* wbuf, uint64
     __syncthreads();                       // wbuf and partial are reused by the next item
 }
 
-// Top-k of every token (the router kernel's rule) into shared memory; block 0 publishes.
+// Top-k of every token (the router kernel's rule) into shared memory and the workspace /
+// outputs; run by one block.
 FNX_DEV void route_tokens(const DecodeParams& p, DecodeRouting& R) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int t = warp; t < p.M; t += DEC_THREADS / 32) {
         const bf16* row = p.logits + (long long)t * p.R;
         float my_p, tot;
         int my_i;
+        // E <= DEC_MAX_E (wider routers would hold 64+ keys per lane and spill the kernel)
         if (p.E <= 256) topk_warp<8, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
-        else if (p.E <= 512) topk_warp<16, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
-        else if (p.E <= 1024) topk_warp<32, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
-        else topk_warp<64, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
+        else topk_warp<16, true>(row, p.bias, p.E, p.k, my_p, my_i, tot);
         if (lane < p.k) {
             const bf16 wb = f2bf(my_p / tot);
             const int o = t * p.k + lane;
             R.idx[o] = my_i;
             R.wf[o] = bf2f(wb);
-            if (blockIdx.x == 0) {
-                p.wf[o] = bf2f(wb);
-                p.idx[o] = my_i;
-                if (p.w_out) p.w_out[o] = wb;
-                if (p.idx_out) p.idx_out[o] = my_i;
-            }
+            p.wf[o] = bf2f(wb);
+            p.idx[o] = my_i;
+            if (p.w_out) p.w_out[o] = wb;
+            if (p.idx_out) p.idx_out[o] = my_i;
         }
     }
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(DEC_THREADS) decode_fused_kernel(const DecodeParams p) {
+// the published routing into shared memory (after the flag)
+FNX_DEV void load_routing(const DecodeParams& p, DecodeRouting& R) {
+    wait_count(ctr_routed(p), 1u);
+    for (int i = threadIdx.x; i < p.M * p.k; i += blockDim.x) {
+        R.idx[i] = __ldcg(p.idx + i);
+        R.wf[i] = ld_cg_f32(p.wf + i);
+    }
+    __syncthreads();
+}
+
+// out[t, 128m .. 128m+127]: the slot-order weighted reduce of the k routed rows and the
+// sigmoid-gated shared row (kernels/reduce/reduce.cpp + kernels/post_ops/post_ops.cpp rounding)
+FNX_DEV void combine_tile(const DecodeParams& p, const DecodeRouting& R, int t, int m) {
+    const unsigned short* yd = reinterpret_cast<const unsigned short*>(p.yd);
+    const unsigned short* sh = reinterpret_cast<const unsigned short*>(p.sh);
+    const unsigned short* lg = reinterpret_cast<const unsigned short*>(p.logits);
+    if (threadIdx.x < 128) {
+        const int c = m * 128 + threadIdx.x;
+        float acc = 0.f;
+        for (int j = 0; j < p.k; ++j) {
+            const float y = __uint_as_float((uint32_t)__ldcg(yd + (long long)(t * p.k + j) * p.H + c) << 16);
+            acc = __fadd_rn(acc, round_bf(__fmul_rn(y, R.wf[t * p.k + j])));
+        }
+        const float a = round_bf(acc);
+        const float g = __uint_as_float((uint32_t)__ldcg(lg + (long long)t * p.R + p.E) << 16);
+        const float sg = round_bf(sigmoid_f32(g));
+        const float s = __uint_as_float((uint32_t)__ldcg(sh + (long long)t * p.H + c) << 16);
+        p.out[(long long)t * p.H + c] = f2bf(__fadd_rn(a, round_bf(__fmul_rn(s, sg))));
+    }
+}
+
+__global__ void __launch_bounds__(DEC_THREADS, 2) decode_fused_kernel(const DecodeParams p) {
     extern __shared__ __align__(16) uint32_t wbuf[];
     __shared__ __align__(16) uint32_t xs2[DEC_MAX_K / 2];
     __shared__ float red[128];
     __shared__ uint64_t bar;
     __shared__ DecodeRouting R;
+    __shared__ unsigned s_last;
     uint32_t phase = 0;
+    bool have_routing = false;                          // block-uniform
     const int tid = threadIdx.x;
     const int MT = gu_tiles(p), KB = p.H / 64;          // gate/up: I/64 feature tiles over K = H
     const int MTd = dn_tiles(p), KBd = p.I / 64;        // down: H/128 feature tiles over K = I
     const int RB = (p.R + DEC_ROWS - 1) / DEC_ROWS;
+    const int nsh = p.M * MT * p.ks1, ngu = p.M * p.k * MT * p.ks2, nsd = p.M * MTd, ndn = p.M * p.k * MTd;
+    const int total = RB + nsh + ngu + nsd + ndn;
     init_block_bar(&bar);
 
-    // ---- phase 1: logits, shared gate/up
-    const int n1 = RB + p.M * MT * p.ks1;
-    for (int it = blockIdx.x; it < n1; it += gridDim.x) {
-        if (it < RB) {
-            router_rows(p, it, wbuf, &bar, phase);
+    for (int it = blockIdx.x; it < total; it += gridDim.x) {
+        int b = it;
+        if (b < RB) {                                    // ---- router rows
+            router_rows(p, b, wbuf, &bar, phase);
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) s_last = atomicAdd(ctr_router(p), 1u) == (unsigned)RB - 1;
+            __syncthreads();
+            if (s_last) {                                // every logit is out: route once
+                __threadfence();
+                route_tokens(p, R);
+                __threadfence();
+                __syncthreads();
+                if (tid == 0) atomicExch(ctr_routed(p), 1u);
+                have_routing = true;
+            }
             continue;
         }
-        const int b = it - RB;
-        const int ks = b % p.ks1, m = (b / p.ks1) % MT, t = b / (p.ks1 * MT);
-        const int nkb = KB / p.ks1;
-        tile_dot(p.sh_gu_tw + (long long)m * KB * TILE_BLOCK_WORDS, p.x + (long long)t * p.H, p.H, false, xs2,
-                 ks * nkb, (ks + 1) * nkb, wbuf, &bar, phase, red);
-        float* part = p.part + (((long long)t * MT + m) * p.ks1 + ks) * 128;
-        if (tid < 128) part[tid] = red[tid];
-        if (last_block(ctr_sh(p) + t * MT + m, p.ks1)) {
-            const float* base = p.part + ((long long)t * MT + m) * p.ks1 * 128;
-            if (tid < 64) {
-                // shared expert: bf16(bf16(silu(bf16 g)) * bf16 u)   (fnx/engine.py:1788)
-                const float g = round_bf(sum_parts(base, p.ks1, 2 * tid));
-                const float u = round_bf(sum_parts(base, p.ks1, 2 * tid + 1));
-                p.act_sh[(long long)t * p.I + m * 64 + tid] = f2bf(__fmul_rn(round_bf(silu_f32(g)), u));
+        b -= RB;
+        if (b < nsh) {                                   // ---- shared gate/up
+            const int ks = b % p.ks1, m = (b / p.ks1) % MT, t = b / (p.ks1 * MT);
+            const int nkb = KB / p.ks1;
+            tile_dot(p.sh_gu_tw + (long long)m * KB * TILE_BLOCK_WORDS, p.x + (long long)t * p.H, p.H, false, xs2,
+                     ks * nkb, (ks + 1) * nkb, wbuf, &bar, phase, red);
+            float* part = p.part + (((long long)t * MT + m) * p.ks1 + ks) * 128;
+            if (tid < 128) part[tid] = red[tid];
+            if (last_block(ctr_sh(p) + t * MT + m, p.ks1)) {
+                const float* base = p.part + ((long long)t * MT + m) * p.ks1 * 128;
+                if (tid < 64) {
+                    // shared expert: bf16(bf16(silu(bf16 g)) * bf16 u)   (fnx/engine.py:1788)
+                    const float g = round_bf(sum_parts(base, p.ks1, 2 * tid));
+                    const float u = round_bf(sum_parts(base, p.ks1, 2 * tid + 1));
+                    p.act_sh[(long long)t * p.I + m * 64 + tid] = f2bf(__fmul_rn(round_bf(silu_f32(g)), u));
+                }
+                count_done(ctr_shgu_done(p) + t);
             }
+            continue;
         }
-    }
-    grid_barrier(ctr_bar1(p), gridDim.x);
-    route_tokens(p, R);
-
-    // ---- phase 2: routed gate/up, shared down
-    const int n2a = p.M * p.k * MT * p.ks2;
-    const int n2 = n2a + p.M * MTd;
-    for (int it = blockIdx.x; it < n2; it += gridDim.x) {
-        if (it < n2a) {
-            const int ks = it % p.ks2, m = (it / p.ks2) % MT, row = it / (p.ks2 * MT);
+        b -= nsh;
+        if (!have_routing) {                             // every later item needs the routing
+            load_routing(p, R);
+            have_routing = true;
+        }
+        if (b < ngu) {                                   // ---- routed gate/up
+            const int ks = b % p.ks2, m = (b / p.ks2) % MT, row = b / (p.ks2 * MT);
             const int ex = R.idx[row], t = row / p.k;
             const int nkb = KB / p.ks2;
             tile_dot(p.gu_tw + ((long long)ex * MT + m) * KB * TILE_BLOCK_WORDS, p.x + (long long)t * p.H, p.H, false,
@@ -337,49 +393,36 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_fused_kernel(const DecodeP
                     const float u = round_bf(sum_parts(base, p.ks2, 2 * tid + 1));
                     p.act[(long long)row * p.I + m * 64 + tid] = f2bf(__fmul_rn(silu_f32(g), u));
                 }
+                count_done(ctr_gu_done(p) + row);
             }
-        } else {
-            const int b = it - n2a, m = b % MTd, t = b / MTd;
+            continue;
+        }
+        b -= ngu;
+        int t, m;
+        if (b < nsd) {                                   // ---- shared down
+            m = b % MTd;
+            t = b / MTd;
+            wait_count(ctr_shgu_done(p) + t, (unsigned)MT);
             tile_dot(p.sh_dn_tw + (long long)m * KBd * TILE_BLOCK_WORDS, p.act_sh + (long long)t * p.I, p.I, true, xs2,
                      0, KBd, wbuf, &bar, phase, red);
             if (tid < 128) p.sh[(long long)t * p.H + m * 128 + tid] = f2bf(red[tid]);
+        } else {                                         // ---- routed down
+            b -= nsd;
+            m = b % MTd;
+            const int row = b / MTd;
+            t = row / p.k;
+            const int ex = R.idx[row];
+            wait_count(ctr_gu_done(p) + row, (unsigned)MT);
+            tile_dot(p.dn_tw + ((long long)ex * MTd + m) * KBd * TILE_BLOCK_WORDS, p.act + (long long)row * p.I, p.I,
+                     true, xs2, 0, KBd, wbuf, &bar, phase, red);
+            if (tid < 128) p.yd[(long long)row * p.H + m * 128 + tid] = f2bf(red[tid]);
         }
-    }
-    grid_barrier(ctr_bar2(p), gridDim.x);
-
-    // ---- phase 3: routed down; the last item of each output tile combines it
-    const int nrows = p.M * p.k;
-    const int n3 = nrows * MTd;
-    for (int it = blockIdx.x; it < n3; it += gridDim.x) {
-        const int m = it % MTd, row = it / MTd;
-        const int ex = R.idx[row];
-        tile_dot(p.dn_tw + ((long long)ex * MTd + m) * KBd * TILE_BLOCK_WORDS, p.act + (long long)row * p.I, p.I, true,
-                 xs2, 0, KBd, wbuf, &bar, phase, red);
-        if (tid < 128) p.yd[(long long)row * p.H + m * 128 + tid] = f2bf(red[tid]);
-        if (last_block(ctr_dn(p) + m, nrows)) {
-            const unsigned short* yd = reinterpret_cast<const unsigned short*>(p.yd);
-            const unsigned short* sh = reinterpret_cast<const unsigned short*>(p.sh);
-            const unsigned short* lg = reinterpret_cast<const unsigned short*>(p.logits);
-            for (int i = tid; i < p.M * 128; i += DEC_THREADS) {
-                const int t = i / 128, c = m * 128 + i % 128;
-                float acc = 0.f;
-                for (int j = 0; j < p.k; ++j) {
-                    const float y = __uint_as_float((uint32_t)__ldcg(yd + (long long)(t * p.k + j) * p.H + c) << 16);
-                    acc = __fadd_rn(acc, round_bf(__fmul_rn(y, R.wf[t * p.k + j])));
-                }
-                const float a = round_bf(acc);
-                const float g = __uint_as_float((uint32_t)__ldcg(lg + (long long)t * p.R + p.E) << 16);
-                const float sg = round_bf(sigmoid_f32(g));
-                const float s = __uint_as_float((uint32_t)__ldcg(sh + (long long)t * p.H + c) << 16);
-                p.out[(long long)t * p.H + c] = f2bf(__fadd_rn(a, round_bf(__fmul_rn(s, sg))));
-            }
-        }
+        if (last_block(ctr_comb(p) + t * MTd + m, (unsigned)p.k + 1)) combine_tile(p, R, t, m);
     }
 
-    // ---- the last block to leave re-arms the grid barriers for the next call
-    if (last_block(ctr_exit(p), gridDim.x) && tid == 0) {
-        *ctr_bar1(p) = 0;
-        *ctr_bar2(p) = 0;
+    // ---- the last block to leave re-arms the dataflow counts for the next call
+    if (last_block(ctr_exit(p), gridDim.x)) {
+        for (int i = tid; i < 2 + p.M + p.M * p.k; i += blockDim.x) ctr_router(p)[i] = 0;
     }
 }
 

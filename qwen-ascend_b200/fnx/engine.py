@@ -22,6 +22,7 @@ from . import _lib
 BF16 = torch.bfloat16
 EPI_PLAIN, EPI_SWIGLU_F32, EPI_SWIGLU_BF16, EPI_SWIGLU_MIXED = 0, 1, 2, 3
 DECODE_MAX_TOKENS = 16
+DECODE_MAX_EXPERTS = 512         # the fused decode kernel's router width; wider ones take the grouped path
 
 
 TILE_BLOCK_WORDS = 1088          # 1024 words of int4 + 128 bf16 scales per (tile, k-block)
@@ -264,7 +265,7 @@ class MoELayer:
         if x.dtype != BF16:
             x = x.to(BF16)
         x = x.contiguous()
-        if x.shape[0] <= DECODE_MAX_TOKENS:
+        if x.shape[0] <= DECODE_MAX_TOKENS and self.E <= DECODE_MAX_EXPERTS:
             return self.decode(x)[0]
         return self.prefill(x)
 
