@@ -738,15 +738,23 @@ DecodeLayout decode_layout(int M, int H, int I, int E, int k) {
     DecodeLayout L{};
     L.R = E + 1;
     const int mt = I / 64, kb = H / 64;
-    // K splits (powers of two dividing the k-block count, >= 2 k-blocks per item): the
-    // router rows and the shared gate/up together fill about one item per resident block,
-    // and the routed gate/up is split as far as it still fits in one item per block.
+    // K splits (item i of a group takes k-blocks [i*kb/ks, (i+1)*kb/ks), >= 2 each).  The
+    // router rows and the shared gate/up together fill about one item per resident block.
+    // The routed gate/up split minimises (waves of items) x (k-blocks per item + a fixed
+    // per-item cost, measured at about 16 k-blocks' worth: the copy latency, the partial
+    // sums and the group ticket): the items of one wave run side by side, so a second,
+    // nearly empty wave costs a whole item's time.
     const int slots = 2 * num_sms();
     const int rb = (L.R + DEC_ROWS - 1) / DEC_ROWS;
     L.ks1 = 1;
-    while (rb + M * mt * L.ks1 * 2 <= slots && kb % (L.ks1 * 2) == 0 && kb / (L.ks1 * 2) >= 2) L.ks1 *= 2;
+    while (rb + M * mt * (L.ks1 + 1) <= slots && kb / (L.ks1 + 1) >= 2) L.ks1 += 1;
     L.ks2 = 1;
-    while (M * k * mt * L.ks2 * 2 <= slots && kb % (L.ks2 * 2) == 0 && kb / (L.ks2 * 2) >= 2) L.ks2 *= 2;
+    double best = 1e30;
+    for (int ks = 1; ks <= 32 && kb / ks >= 2; ++ks) {
+        const long long items = (long long)M * k * mt * ks;
+        const double cost = (double)((items + slots - 1) / slots) * ((double)kb / ks + 16.0);
+        if (cost < best - 1e-9) { best = cost; L.ks2 = ks; }
+    }
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
     L.logits = take((size_t)M * L.R * 2);

@@ -84,46 +84,59 @@ FNX_DEV bool last_block(unsigned* ctr, unsigned n) {
 }
 
 // Dot products of the 128 rows of one weight tile with x (bf16 [K], staged into xs2 while
-// the first copy is in flight; x_cg reads it through L2) over k-blocks [kb0, kb1).  The
-// tile blocks of a chunk of <= DEC_CH k-blocks are contiguous in HBM and arrive in shared
-// memory (wbuf) by one bulk copy issued by thread 0, so a block keeps its whole chunk in
-// flight at once; thread (half, r) then takes the chunk's k-blocks half, half + 2, ... of
-// tile row r (conflict-free: consecutive rows are consecutive words) and the two halves are
-// added in a fixed order.  Result in red[r] (shared memory, 128 floats).  `phase` tracks
-// the block's mbarrier across calls.
+// the first copies are in flight; x_cg reads it through L2) over k-blocks [kb0, kb1).  The
+// tile blocks of a chunk of <= DEC_CH k-blocks are contiguous in HBM; thread 0 issues them
+// as DEC_SUB-block bulk copies, each on its own mbarrier, all in flight at once, and the
+// block computes each piece as soon as it lands, so compute overlaps the rest of the copy.
+// Thread (half, r) takes k-block half of each piece of tile row r (conflict-free:
+// consecutive rows are consecutive words) and the two halves are added in a fixed order.
+// Result in red[r] (shared memory, 128 floats).  `phase` holds one parity bit per mbarrier.
+#ifndef FNX_DEC_SUB
+#define FNX_DEC_SUB 8
+#endif
+constexpr int DEC_SUB = FNX_DEC_SUB;             // k-blocks per bulk copy
+constexpr int DEC_NBAR = DEC_CH / DEC_SUB;
 FNX_DEV void tile_dot(const uint32_t* __restrict__ tw, const bf16* x, int K, bool x_cg, uint32_t* xs2, int kb0,
                       int kb1, uint32_t* wbuf, uint64_t* bar, uint32_t& phase, float* red) {
     const int r = threadIdx.x & 127, half = threadIdx.x >> 7;
     float a0 = 0.f, a1 = 0.f;
     for (int c0 = kb0; c0 < kb1; c0 += DEC_CH) {
         const int n = min(DEC_CH, kb1 - c0);
+        const int npieces = (n + DEC_SUB - 1) / DEC_SUB;
         if (threadIdx.x == 0) {
-            mbar_arrive_expect_tx(bar, (uint32_t)n * TILE_BLOCK_BYTES);
-            bulk_load(smem_u32(wbuf), tw + (long long)c0 * TILE_BLOCK_WORDS, (uint32_t)n * TILE_BLOCK_BYTES, bar,
-                      l2_evict_first());
+            for (int s = 0; s < npieces; ++s) {
+                const int nb = min(DEC_SUB, n - s * DEC_SUB);
+                mbar_arrive_expect_tx(bar + s, (uint32_t)nb * TILE_BLOCK_BYTES);
+                bulk_load(smem_u32(wbuf + s * DEC_SUB * TILE_BLOCK_WORDS),
+                          tw + (long long)(c0 + s * DEC_SUB) * TILE_BLOCK_WORDS, (uint32_t)nb * TILE_BLOCK_BYTES,
+                          bar + s, l2_evict_first());
+            }
         }
         if (c0 == kb0) {                  // the input row, while the weights are in flight
             const uint32_t* src = reinterpret_cast<const uint32_t*>(x);
             for (int i = threadIdx.x; i < K / 2; i += blockDim.x) xs2[i] = x_cg ? __ldcg(src + i) : src[i];
             __syncthreads();
         }
-        mbar_wait(bar, phase);            // a timeout is flagged; the block finishes with stale data
-        phase ^= 1u;
-        for (int j = half; j < n; j += 2) {
-            const uint32_t* blk = wbuf + j * TILE_BLOCK_WORDS;
-            const uint32_t s16 = reinterpret_cast<const unsigned short*>(blk + 1024)[r];
-            const uint32_t s2 = s16 | (s16 << 16);
-            const uint4* xq = reinterpret_cast<const uint4*>(xs2 + (c0 + j) * 32);
+        for (int s = 0; s < npieces; ++s) {
+            mbar_wait(bar + s, (phase >> s) & 1u);   // a timeout is flagged; the block finishes with stale data
+            phase ^= 1u << s;
+            const int j = s * DEC_SUB + half;
+            if (j < n) {
+                const uint32_t* blk = wbuf + j * TILE_BLOCK_WORDS;
+                const uint32_t s16 = reinterpret_cast<const unsigned short*>(blk + 1024)[r];
+                const uint32_t s2 = s16 | (s16 << 16);
+                const uint4* xq = reinterpret_cast<const uint4*>(xs2 + (c0 + j) * 32);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const uint32_t w = blk[c * 128 + r];
-                const uint4 xv = xq[c];
-                const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+                for (int c = 0; c < 8; ++c) {
+                    const uint32_t w = blk[c * 128 + r];
+                    const uint4 xv = xq[c];
+                    const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint32_t w2 = tile_pair(w, i, s2);
-                    fma_bf_lo(a0, w2, xx[i]);
-                    fma_bf_hi(a1, w2, xx[i]);
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t w2 = tile_pair(w, i, s2);       // exactly rounded bf16(q * s)
+                        fma_bf_lo(a0, w2, xx[i]);
+                        fma_bf_hi(a1, w2, xx[i]);
+                    }
                 }
             }
         }
@@ -136,10 +149,10 @@ FNX_DEV void tile_dot(const uint32_t* __restrict__ tw, const bf16* x, int K, boo
     __syncthreads();
 }
 
-// The block's bulk-copy mbarrier (initialised once per launch).
-FNX_DEV void init_block_bar(uint64_t* bar) {
+// The block's bulk-copy mbarriers (initialised once per launch).
+FNX_DEV void init_block_bar(uint64_t* bar, int n) {
     if (threadIdx.x == 0) {
-        mbar_init(bar, 1);
+        for (int i = 0; i < n; ++i) mbar_init(bar + i, 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -219,7 +232,7 @@ FNX_DEV void router_rows(const DecodeParams& p, int item, uint32_t* wbuf, uint64
         bulk_load(smem_u32(wbuf), p.router + (long long)e0 * p.H, rbytes, bar, l2_evict_first());
         if (x_in_smem) bulk_load(smem_u32(xs), p.x, xbytes, bar, l2_evict_last());
     }
-    mbar_wait(bar, phase);
+    mbar_wait(bar, phase & 1u);
     phase ^= 1u;
     const int row = warp >> 1, hh = warp & 1;
     if (row < nr) {
@@ -286,6 +299,104 @@ FNX_DEV void route_tokens(const DecodeParams& p, DecodeRouting& R) {
     __syncthreads();
 }
 
+// Top-k of one token by all 8 warps (the decode of a single token): warp w takes a slice of
+// E/8 experts, picks its own top-k by (probability desc, id asc), and warp 0 merges the 8 lists
+// by the same order.  Probabilities are the router kernel's softmax (max, exp, sum in a fixed
+// order, then * 1/sum); NaN counts as 0, so k valid distinct ids are always chosen.
+FNX_DEV void route_one_token_block(const DecodeParams& p, DecodeRouting& R) {
+    __shared__ float s_red[8];
+    __shared__ uint32_t c_key[8][ROUTE_MAX_K];
+    __shared__ int c_id[8][ROUTE_MAX_K];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = (p.E + 7) / 8;                        // experts per warp (<= 64)
+    const unsigned short* row = reinterpret_cast<const unsigned short*>(p.logits);
+    int e[2];
+    float v[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        e[h] = warp * S + h * 32 + lane;
+        v[h] = -INFINITY;
+        if (h * 32 + lane < S && e[h] < p.E) {
+            v[h] = __uint_as_float((uint32_t)__ldcg(row + e[h]) << 16);
+            if (p.bias) v[h] = __fadd_rn(v[h], p.bias[e[h]]);
+        }
+    }
+    float mx = fmaxf(v[0], v[1]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) s_red[warp] = mx;
+    __syncthreads();
+    mx = s_red[0];
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_red[w]);
+    float pr[2], sum;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) pr[h] = v[h] == -INFINITY ? 0.f : expf(__fsub_rn(v[h], mx));
+    sum = __fadd_rn(pr[0], pr[1]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    __syncthreads();                                    // every warp has read s_red (max)
+    if (lane == 0) s_red[warp] = sum;
+    __syncthreads();
+    sum = s_red[0];
+    for (int w = 1; w < 8; ++w) sum = __fadd_rn(sum, s_red[w]);
+    const float inv = 1.0f / sum;
+    uint32_t key[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const float q = __fmul_rn(pr[h], inv);
+        key[h] = (h * 32 + lane < S && e[h] < p.E) ? __float_as_uint(q > 0.f ? q : 0.f) + 1u : 0u;
+    }
+    for (int j = 0; j < p.k; ++j) {                     // this warp's top-k
+        const uint32_t gm = __reduce_max_sync(0xffffffffu, max(key[0], key[1]));
+        const uint32_t cand = key[0] == gm ? (uint32_t)e[0] : (key[1] == gm ? (uint32_t)e[1] : 0xffffffffu);
+        const uint32_t bi = __reduce_min_sync(0xffffffffu, gm ? cand : 0xffffffffu);
+        if (gm && (uint32_t)e[0] == bi) key[0] = 0u;
+        if (gm && (uint32_t)e[1] == bi) key[1] = 0u;
+        if (lane == 0) { c_key[warp][j] = gm; c_id[warp][j] = (int)bi; }
+    }
+    __syncthreads();
+    if (warp == 0) {                                    // merge the 8 lists
+        uint32_t ck[8];
+        int ci[8];
+        const int n = 8 * p.k;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            const int c = s * 32 + lane;
+            ck[s] = c < n ? c_key[c / p.k][c % p.k] : 0u;
+            ci[s] = c < n ? c_id[c / p.k][c % p.k] : 0x7fffffff;
+        }
+        float my_p = 0.f, tot = 0.f;
+        int my_i = 0;
+        for (int j = 0; j < p.k; ++j) {
+            uint32_t lm = 0;
+#pragma unroll
+            for (int s = 0; s < 8; ++s) lm = max(lm, ck[s]);
+            const uint32_t gm = __reduce_max_sync(0xffffffffu, lm);
+            uint32_t cand = 0xffffffffu;
+#pragma unroll
+            for (int s = 0; s < 8; ++s)
+                if (ck[s] == gm && gm) cand = min(cand, (uint32_t)ci[s]);
+            const uint32_t bi = __reduce_min_sync(0xffffffffu, cand);
+#pragma unroll
+            for (int s = 0; s < 8; ++s)
+                if (ck[s] == gm && (uint32_t)ci[s] == bi) ck[s] = 0u;
+            const float bp = gm ? __uint_as_float(gm - 1u) : 0.f;
+            if (lane == j) { my_p = bp; my_i = (int)bi; }
+            tot = __fadd_rn(tot, bp);
+        }
+        if (lane < p.k) {
+            const bf16 wb = f2bf(my_p / tot);
+            R.idx[lane] = my_i;
+            R.wf[lane] = bf2f(wb);
+            p.wf[lane] = bf2f(wb);
+            p.idx[lane] = my_i;
+            if (p.w_out) p.w_out[lane] = wb;
+            if (p.idx_out) p.idx_out[lane] = my_i;
+        }
+    }
+    __syncthreads();
+}
+
 // the published routing into shared memory (after the flag)
 FNX_DEV void load_routing(const DecodeParams& p, DecodeRouting& R) {
     wait_count(ctr_routed(p), 1u);
@@ -321,7 +432,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_fused_kernel(const Deco
     extern __shared__ __align__(16) uint32_t wbuf[];
     __shared__ __align__(16) uint32_t xs2[DEC_MAX_K / 2];
     __shared__ float red[128];
-    __shared__ uint64_t bar;
+    __shared__ uint64_t bar[DEC_NBAR];
     __shared__ DecodeRouting R;
     __shared__ unsigned s_last;
     uint32_t phase = 0;
@@ -332,19 +443,20 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_fused_kernel(const Deco
     const int RB = (p.R + DEC_ROWS - 1) / DEC_ROWS;
     const int nsh = p.M * MT * p.ks1, ngu = p.M * p.k * MT * p.ks2, nsd = p.M * MTd, ndn = p.M * p.k * MTd;
     const int total = RB + nsh + ngu + nsd + ndn;
-    init_block_bar(&bar);
+    init_block_bar(bar, DEC_NBAR);
 
     for (int it = blockIdx.x; it < total; it += gridDim.x) {
         int b = it;
         if (b < RB) {                                    // ---- router rows
-            router_rows(p, b, wbuf, &bar, phase);
+            router_rows(p, b, wbuf, bar, phase);
             __threadfence();
             __syncthreads();
             if (tid == 0) s_last = atomicAdd(ctr_router(p), 1u) == (unsigned)RB - 1;
             __syncthreads();
             if (s_last) {                                // every logit is out: route once
                 __threadfence();
-                route_tokens(p, R);
+                if (p.M == 1) route_one_token_block(p, R);
+                else route_tokens(p, R);
                 __threadfence();
                 __syncthreads();
                 if (tid == 0) atomicExch(ctr_routed(p), 1u);
@@ -355,9 +467,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_fused_kernel(const Deco
         b -= RB;
         if (b < nsh) {                                   // ---- shared gate/up
             const int ks = b % p.ks1, m = (b / p.ks1) % MT, t = b / (p.ks1 * MT);
-            const int nkb = KB / p.ks1;
             tile_dot(p.sh_gu_tw + (long long)m * KB * TILE_BLOCK_WORDS, p.x + (long long)t * p.H, p.H, false, xs2,
-                     ks * nkb, (ks + 1) * nkb, wbuf, &bar, phase, red);
+                     ks * KB / p.ks1, (ks + 1) * KB / p.ks1, wbuf, bar, phase, red);
             float* part = p.part + (((long long)t * MT + m) * p.ks1 + ks) * 128;
             if (tid < 128) part[tid] = red[tid];
             if (last_block(ctr_sh(p) + t * MT + m, p.ks1)) {
@@ -380,9 +491,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_fused_kernel(const Deco
         if (b < ngu) {                                   // ---- routed gate/up
             const int ks = b % p.ks2, m = (b / p.ks2) % MT, row = b / (p.ks2 * MT);
             const int ex = R.idx[row], t = row / p.k;
-            const int nkb = KB / p.ks2;
             tile_dot(p.gu_tw + ((long long)ex * MT + m) * KB * TILE_BLOCK_WORDS, p.x + (long long)t * p.H, p.H, false,
-                     xs2, ks * nkb, (ks + 1) * nkb, wbuf, &bar, phase, red);
+                     xs2, ks * KB / p.ks2, (ks + 1) * KB / p.ks2, wbuf, bar, phase, red);
             float* part = p.part2 + (((long long)row * MT + m) * p.ks2 + ks) * 128;
             if (tid < 128) part[tid] = red[tid];
             if (last_block(ctr_gu(p) + row * MT + m, p.ks2)) {
@@ -404,7 +514,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_fused_kernel(const Deco
             t = b / MTd;
             wait_count(ctr_shgu_done(p) + t, (unsigned)MT);
             tile_dot(p.sh_dn_tw + (long long)m * KBd * TILE_BLOCK_WORDS, p.act_sh + (long long)t * p.I, p.I, true, xs2,
-                     0, KBd, wbuf, &bar, phase, red);
+                     0, KBd, wbuf, bar, phase, red);
             if (tid < 128) p.sh[(long long)t * p.H + m * 128 + tid] = f2bf(red[tid]);
         } else {                                         // ---- routed down
             b -= nsd;
@@ -414,7 +524,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 2) decode_fused_kernel(const Deco
             const int ex = R.idx[row];
             wait_count(ctr_gu_done(p) + row, (unsigned)MT);
             tile_dot(p.dn_tw + ((long long)ex * MTd + m) * KBd * TILE_BLOCK_WORDS, p.act + (long long)row * p.I, p.I,
-                     true, xs2, 0, KBd, wbuf, &bar, phase, red);
+                     true, xs2, 0, KBd, wbuf, bar, phase, red);
             if (tid < 128) p.yd[(long long)row * p.H + m * 128 + tid] = f2bf(red[tid]);
         }
         if (last_block(ctr_comb(p) + t * MTd + m, (unsigned)p.k + 1)) combine_tile(p, R, t, m);
