@@ -92,7 +92,7 @@ FNX_DEV bool last_block(unsigned* ctr, unsigned n) {
 // consecutive rows are consecutive words) and the two halves are added in a fixed order.
 // Result in red[r] (shared memory, 128 floats).  `phase` holds one parity bit per mbarrier.
 #ifndef FNX_DEC_SUB
-#define FNX_DEC_SUB 8
+#define FNX_DEC_SUB 16
 #endif
 constexpr int DEC_SUB = FNX_DEC_SUB;             // k-blocks per bulk copy
 constexpr int DEC_NBAR = DEC_CH / DEC_SUB;
@@ -120,8 +120,8 @@ FNX_DEV void tile_dot(const uint32_t* __restrict__ tw, const bf16* x, int K, boo
         for (int s = 0; s < npieces; ++s) {
             mbar_wait(bar + s, (phase >> s) & 1u);   // a timeout is flagged; the block finishes with stale data
             phase ^= 1u << s;
-            const int j = s * DEC_SUB + half;
-            if (j < n) {
+            const int jend = min(n, (s + 1) * DEC_SUB);
+            for (int j = s * DEC_SUB + half; j < jend; j += 2) {
                 const uint32_t* blk = wbuf + j * TILE_BLOCK_WORDS;
                 const uint32_t s16 = reinterpret_cast<const unsigned short*>(blk + 1024)[r];
                 const uint32_t s2 = s16 | (s16 << 16);
