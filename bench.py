@@ -293,12 +293,33 @@ def bench_prefill(args, world, rank, dev):
 
 
 def profile_case(case, dev):
-    """Two launches of one routed grouped GEMM of the bench workload (one layer, its real
-    routing), nothing else of the grouped-GEMM kind: the small case ncu captures
-    (`-k regex:grouped_gemm -s 1 -c 1` profiles the second launch)."""
+    """Small cases for ncu captures (one layer of the bench workload):
+    gu / dn  two launches of the routed gate/up or down grouped GEMM (its real routing), nothing
+             else of the grouped-GEMM kind (`-k regex:grouped_gemm -s 1 -c 1` takes the second);
+    dec      four decode calls at M=1 (`-k regex:decode_fused -s 2 -c 1` takes the third);
+    ep       three calls of the expert-parallel layer with the peer exchange on one rank
+             (every kernel of the p2p path, the exchange kept on this GPU)."""
     from fnx import synth
     from fnx.engine import EPI_PLAIN, EPI_SWIGLU_F32, _grouped_w4
     lay = make_layers(1, dev)[0]
+    if case == "dec":
+        x = synth.make_tokens(1, H, seed=3, device=dev)
+        for _ in range(4):
+            lay.decode(x)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": case, "ok": True}))
+        return
+    if case == "ep":
+        from fnx.ep import ExpertParallelMoE
+        ep = ExpertParallelMoE.from_layer(lay, 0, 1, transport="p2p")
+        x = synth.make_tokens(T_PREFILL, H, seed=1000, device=dev)
+        for _ in range(3):
+            out = ep(x)
+        torch.cuda.synchronize()
+        ok = bool(torch.equal(out.view(torch.int16), lay.prefill(x).view(torch.int16)))
+        ep.close()
+        print(json.dumps({"profile_case": case, "ok": ok}))
+        return
     x = synth.make_tokens(T_PREFILL, H, seed=1000, device=dev)
     _, idx, _ = lay.topk(lay.logits(x))
     order, _, ends = lay.permute(idx)
@@ -404,8 +425,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=128)
-    ap.add_argument("--profile-case", choices=["gu", "dn"], default=None,
-                    help="run only two launches of the routed gate/up or down GEMM (for ncu captures)")
+    ap.add_argument("--profile-case", choices=["gu", "dn", "dec", "ep"], default=None,
+                    help="run only a small case for ncu captures (see profile_case)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
