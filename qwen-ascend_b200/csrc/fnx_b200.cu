@@ -346,9 +346,25 @@ int permute_launch(const void* idx, void* order, void* inverse, void* ends, void
         if (counts) cudaMemsetAsync(counts, 0, sizeof(int64_t) * E, st);
         return launch_rc();
     }
+    const size_t ssm = permute_scatter_smem(E);
+    static size_t ssm_set = 48 * 1024;
+    if (ssm > ssm_set) {
+        if (cudaFuncSetAttribute(permute_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)permute_scatter_smem(PERM_MAX_E)) != cudaSuccess)
+            return FNX_ELAUNCH;
+        ssm_set = permute_scatter_smem(PERM_MAX_E);
+    }
     permute_hist_kernel<<<chunks, 256, E * sizeof(int), st>>>((const int64_t*)idx, n, n_dev, E, div, hist);
-    permute_scan_kernel<<<1, 1024, 0, st>>>(hist, chunks, E, (int64_t*)ends, (int64_t*)counts, base);
-    permute_scatter_kernel<<<chunks, 32, (E + PERM_CHUNK) * sizeof(int), st>>>(
+    static bool scan_set = false;
+    if (!scan_set) {
+        if (cudaFuncSetAttribute(permute_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)PERM_SCAN_SMEM) != cudaSuccess)
+            return FNX_ELAUNCH;
+        scan_set = true;
+    }
+    permute_scan_kernel<<<1, 1024, permute_scan_smem(chunks, E), st>>>(hist, chunks, E, (int64_t*)ends,
+                                                                       (int64_t*)counts, base);
+    permute_scatter_kernel<<<chunks, 32 * PERM_WARPS, ssm, st>>>(
         (const int64_t*)idx, n, n_dev, E, div, hist, (int64_t*)order, (int64_t*)inverse, base, row_map);
     return launch_rc();
 }

@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(256) moe_merge_kernel(const bf16* __restrict__
 // weighted_reduce mode 2 followed by post_ops.moe_merge (fnx/engine.py:1844-1853),
 // with the same roundings, in one pass over yd.
 template <bool VEC>
-__global__ void __launch_bounds__(256) moe_combine_kernel(const bf16* __restrict__ yd, const float* __restrict__ w,
+__global__ void __launch_bounds__(256, 3) moe_combine_kernel(const bf16* __restrict__ yd, const float* __restrict__ w,
                                                           const int64_t* __restrict__ inverse,
                                                           const bf16* __restrict__ sh, const bf16* __restrict__ gate,
                                                           long long gate_ld, bf16* __restrict__ out, int T, int k,
@@ -126,6 +126,62 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const bf16* __restrict
         float acc[VEC ? 8 : 1];
 #pragma unroll
         for (int j = 0; j < (VEC ? 8 : 1); ++j) acc[j] = 0.f;
+        if (VEC && k <= 16) {
+            // the k row indices and weights first, then the rows four at a time (the shared
+            // row and gate are loaded with the indices)
+            long long rows[16];
+            float s[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                rows[q] = -1;
+                s[q] = 0.f;
+                if (q < k) {
+                    const long long slot = (long long)t * k + q;
+                    rows[q] = inverse ? inverse[slot] : slot;
+                    s[q] = w[slot];
+                }
+            }
+            const long long off = (long long)t * H + c;
+            const uint4 sv = ld_nc_v4(sh + off);
+            const float g = bf2f(gate[(long long)t * gate_ld]);
+#pragma unroll
+            for (int j0 = 0; j0 < 16; j0 += 4) {
+                if (j0 >= k) break;
+                uint4 v[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    v[q] = make_uint4(0, 0, 0, 0);
+                    const long long row = rows[j0 + q];
+                    if (j0 + q < k && row >= 0 && row < (long long)T * k) v[q] = ld_nc_v4(yd + row * H + c);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    if (j0 + q >= k) break;
+                    const long long row = rows[j0 + q];
+                    if (row < 0 || row >= (long long)T * k) {      // an id outside [0, E) left no row
+                        fnx_flag_error(FNX_DEVERR_BADID);
+                        continue;
+                    }
+                    const uint32_t vv[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        acc[2 * e] = __fadd_rn(acc[2 * e], round_bf(__fmul_rn(bf_lo(vv[e]), s[j0 + q])));
+                        acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], round_bf(__fmul_rn(bf_hi(vv[e]), s[j0 + q])));
+                    }
+                }
+            }
+            const float sg = round_bf(sigmoid_f32(g));
+            const uint32_t sa[4] = {sv.x, sv.y, sv.z, sv.w};
+            uint32_t oa[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float lo = __fadd_rn(round_bf(acc[2 * q]), round_bf(__fmul_rn(bf_lo(sa[q]), sg)));
+                const float hi = __fadd_rn(round_bf(acc[2 * q + 1]), round_bf(__fmul_rn(bf_hi(sa[q]), sg)));
+                oa[q] = pack_bf2(lo, hi);
+            }
+            *reinterpret_cast<uint4*>(out + off) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+            continue;
+        }
         // slots in groups of four: all four row loads are issued before the in-order sums
         for (int j0 = 0; j0 < k; j0 += 4) {
             uint4 v[4];

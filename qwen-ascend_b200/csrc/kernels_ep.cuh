@@ -332,8 +332,9 @@ FNX_DEV void ep_last_block_signal(const EPDesc& d, unsigned* ticket, int phase, 
 // Dispatch.  Slot p of the owner-major order (owner j) writes its entry to j's slot row
 // send_off[j] + (p - src_start[j]): the owner-local expert and the token row
 // tok_send_off[j] + (tok_index[p] - tok_start[j]); the first slot of each token for j also
-// copies the token row there.  This rank's own T tokens go to its rows cap_tok .. cap_tok+T-1
-// (the shared expert's rows).  Then DATA.
+// copies the token row there.  Each lane takes one slot (32 slots' loads in flight per warp),
+// then the warp copies the rows of its first slots one after another.  This rank's own T tokens
+// go to its rows cap_tok .. cap_tok+T-1 (the shared expert's rows).  Then DATA.
 __global__ void __launch_bounds__(256) ep_push_kernel(const EPDesc d, const bf16* __restrict__ x, int T,
                                                       const int64_t* __restrict__ order,
                                                       const int64_t* __restrict__ idx,
@@ -343,28 +344,39 @@ __global__ void __launch_bounds__(256) ep_push_kernel(const EPDesc d, const bf16
     const int G = d.world, H = d.H, k = d.k, lane = threadIdx.x & 31;
     const long long n = (long long)T * k;
     const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-    for (long long p = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < n + T; p += warps) {
+    const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    for (long long b = gw * 32; b < n; b += warps * 32) {
+        const long long p = b + lane;
+        bool copy = false;
+        int j = 0;
+        long long trow = 0, src = 0;
         if (p < n) {
-            const int j = ep_chunk(sp + EP_SRC_START, G, p);
+            j = ep_chunk(sp + EP_SRC_START, G, p);
             const long long srow = sp[EP_SEND_OFF + j] + (p - sp[EP_SRC_START + j]);
             const int ti = __ldg(tok_index + p);
-            const long long trow = sp[EP_TOK_SEND_OFF + j] + (ti - sp[EP_TOK_START + j]);
+            trow = sp[EP_TOK_SEND_OFF + j] + (ti - sp[EP_TOK_START + j]);
             const long long q = __ldg(order + p);
             if (srow >= d.cap || trow >= d.cap_tok || trow < 0 || q < 0 || q >= n) {
-                if (lane == 0) fnx_flag_error(q < 0 || q >= n ? FNX_DEVERR_BADID : FNX_DEVERR_OVERFLOW);
-                continue;
-            }
-            if (lane == 0) {
+                fnx_flag_error(q < 0 || q >= n ? FNX_DEVERR_BADID : FNX_DEVERR_OVERFLOW);
+            } else {
                 d.recv_e[j][srow] = __ldg(idx + q) % d.Eg;
                 d.recv_row[j][srow] = trow;
+                copy = p == sp[EP_SRC_START + j] || __ldg(tok_index + p - 1) != ti;
+                src = q / k;
             }
-            if (p == sp[EP_SRC_START + j] || __ldg(tok_index + p - 1) != ti)
-                ep_copy_row(d.recv_x[j] + trow * H, x + (q / k) * H, H, lane);
-        } else {
-            const long long t = p - n;
-            ep_copy_row(d.recv_x[d.rank] + (d.cap_tok + t) * H, x + t * H, H, lane);
+        }
+        unsigned m = __ballot_sync(0xffffffffu, copy);
+        while (m) {
+            const int l = __ffs(m) - 1;
+            m &= m - 1u;
+            const int jj = __shfl_sync(0xffffffffu, j, l);
+            const long long tr = __shfl_sync(0xffffffffu, trow, l);
+            const long long sr = __shfl_sync(0xffffffffu, src, l);
+            ep_copy_row(d.recv_x[jj] + tr * H, x + sr * H, H, lane);
         }
     }
+    for (long long t = gw; t < T; t += warps)
+        ep_copy_row(d.recv_x[d.rank] + (d.cap_tok + t) * H, x + t * H, H, lane);
     ep_last_block_signal(d, d.tickets + 0, EP_PH_DATA, (unsigned)sp[EP_EPOCH]);
 }
 

@@ -265,15 +265,22 @@ FNX_DEV void epilogue_chunk_staged(const GemmParams& p, const TileInfo& ti, int 
                                    uint16_t* stage) {
     const int lane = threadIdx.x & 31;
     if (EPI == EPI_PLAIN) {
+        // destinations first: with per-row pointers their loads overlap the staging below
+        bf16* dst[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int tok = (q * 32 + lane) >> 2;
+            dst[q] = n0 + tok < ti.nrows ? out_row(p, ti.row0 + n0 + tok) : nullptr;
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) stage[i * 32 + lane] = (uint16_t)bf16_bits(f2bf(__uint_as_float(v[i])));
         __syncwarp();
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
             const int c = q * 32 + lane, tok = c >> 2, part = c & 3;
-            if (n0 + tok < ti.nrows) {
+            if (dst[q]) {
                 const uint4 val = *reinterpret_cast<const uint4*>(stage + tok * 32 + part * 8);
-                *reinterpret_cast<uint4*>(out_row(p, ti.row0 + n0 + tok) + ti.m * G_BM + w4 * 32 + part * 8) = val;
+                *reinterpret_cast<uint4*>(dst[q] + ti.m * G_BM + w4 * 32 + part * 8) = val;
             }
         }
     } else {

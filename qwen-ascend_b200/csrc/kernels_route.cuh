@@ -152,12 +152,34 @@ __global__ void __launch_bounds__(256) permute_hist_kernel(const int64_t* __rest
 }
 
 // pass 2 (one block): ends[e] = base + inclusive cumsum of counts; hist[c][e] becomes the
-// starting output position of chunk c's entries for expert e.
+// starting output position of chunk c's entries for expert e.  The histogram is staged in
+// shared memory when it fits (the per-expert walks over the chunks are dependent chains), and
+// the scan over experts is a warp-shuffle scan.
+constexpr size_t PERM_SCAN_SMEM = 160 * 1024;
+inline size_t permute_scan_smem(int nchunks, int E) {
+    const size_t b = sizeof(int) * (size_t)nchunks * E;
+    return b <= PERM_SCAN_SMEM ? b : 0;
+}
+
 __global__ void __launch_bounds__(1024) permute_scan_kernel(int* __restrict__ hist, int nchunks, int E,
                                                             int64_t* __restrict__ ends, int64_t* __restrict__ counts_out,
                                                             long long base) {
-    __shared__ int part[1024];
+    extern __shared__ int hs[];
+    __shared__ int wsum[32];
     __shared__ int carry;
+    const bool staged = (size_t)nchunks * E * sizeof(int) <= PERM_SCAN_SMEM;
+    int* h = staged ? hs : hist;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int tot = nchunks * E;
+    if (staged)                                   // eight loads in flight per thread
+        for (int i0 = threadIdx.x; i0 < tot; i0 += 8 * blockDim.x) {
+            int v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = i0 + u * (int)blockDim.x < tot ? hist[i0 + u * blockDim.x] : 0;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (i0 + u * (int)blockDim.x < tot) hs[i0 + u * blockDim.x] = v[u];
+        }
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
     for (int e0 = 0; e0 < E; e0 += blockDim.x) {
@@ -165,25 +187,35 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int* __restrict__ hi
         int cnt = 0;
         if (e < E)
 #pragma unroll 8
-            for (int c = 0; c < nchunks; ++c) cnt += hist[(long long)c * E + e];
-        part[threadIdx.x] = cnt;
-        __syncthreads();
-        // inclusive Hillis-Steele scan over the block
-        for (int o = 1; o < blockDim.x; o <<= 1) {
-            const int add = threadIdx.x >= o ? part[threadIdx.x - o] : 0;
-            __syncthreads();
-            part[threadIdx.x] += add;
-            __syncthreads();
+            for (int c = 0; c < nchunks; ++c) cnt += h[c * E + e];
+        // inclusive scan over the block: within warps, then over the warp totals
+        int inc = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += u;
         }
-        const int incl = part[threadIdx.x] + carry;
+        if (lane == 31) wsum[warp] = inc;
+        __syncthreads();
+        if (warp == 0) {
+            const int v = wsum[lane];
+            int wi = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= o) wi += u;
+            }
+            wsum[lane] = wi - v;                  // exclusive prefix of the warp totals
+        }
+        __syncthreads();
+        const int incl = carry + wsum[warp] + inc;
         if (e < E) {
             ends[e] = base + incl;
             if (counts_out) counts_out[e] = cnt;
             int pos = incl - cnt;
             for (int c = 0; c < nchunks; ++c) {
-                const long long h = (long long)c * E + e;
-                const int v = hist[h];
-                hist[h] = pos;
+                const int v = h[c * E + e];
+                h[c * E + e] = pos;
                 pos += v;
             }
         }
@@ -191,50 +223,78 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int* __restrict__ hi
         if (threadIdx.x == blockDim.x - 1) carry = incl;
         __syncthreads();
     }
+    if (staged)
+        for (int i = threadIdx.x; i < tot; i += blockDim.x) hist[i] = hs[i];
 }
 
-// pass 3: one warp per chunk walks its entries in order; __match_any_sync gives each
-// entry its rank among equal ids in the same 32-entry batch, so positions are stable.
+// pass 3: one block per chunk; its 8 warps take 128 consecutive entries each.  A first walk
+// counts each warp's entries per bucket (__match_any_sync groups equal ids of a 32-entry batch),
+// the counts are scanned across the warps in order from the chunk's start positions, and a
+// second walk places each warp's entries with its own cursors, so positions stay stable
+// (chunk order, then warp order, then batch order, then lane order).
 // order[pos] = i (or row_map[i]) and inverse[i] = pos_base + pos (the host offsets `order`).
-__global__ void __launch_bounds__(32) permute_scatter_kernel(const int64_t* __restrict__ ids, int n,
-                                                             const long long* __restrict__ n_dev, int E, int div,
-                                                             const int* __restrict__ start,
-                                                             int64_t* __restrict__ order, int64_t* __restrict__ inverse,
-                                                             long long pos_base, const int64_t* __restrict__ row_map) {
-    extern __shared__ int cursor[];
-    int* sid = cursor + E;                       // this chunk's ids, loaded in one coalesced pass
-    const int lane = threadIdx.x;
+constexpr int PERM_WARPS = 8;
+inline size_t permute_scatter_smem(int E) { return sizeof(int) * ((size_t)PERM_WARPS * E + PERM_CHUNK); }
+
+__global__ void __launch_bounds__(32 * PERM_WARPS) permute_scatter_kernel(
+        const int64_t* __restrict__ ids, int n, const long long* __restrict__ n_dev, int E, int div,
+        const int* __restrict__ start, int64_t* __restrict__ order, int64_t* __restrict__ inverse, long long pos_base,
+        const int64_t* __restrict__ row_map) {
+    extern __shared__ int psm[];
+    int* cur = psm;                              // [PERM_WARPS][E]: counts, then cursors
+    int* sid = psm + PERM_WARPS * E;             // [PERM_CHUNK]: bucket of each entry (-1 none)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     n = perm_count(n, n_dev);
     const int c0 = blockIdx.x * PERM_CHUNK;
     if (c0 >= n) return;
     const int c1 = min(n, c0 + PERM_CHUNK);
-    for (int e = lane; e < E; e += 32) cursor[e] = start[(long long)blockIdx.x * E + e];
-#pragma unroll 8
-    for (int i = c0 + lane; i < c1; i += 32) {
+    for (int i = threadIdx.x; i < PERM_WARPS * E; i += blockDim.x) cur[i] = 0;
+    const long long lim = (long long)E * div;
+    for (int i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
         const long long e = ids[i];
-        sid[i - c0] = (e >= 0 && e < (long long)E * div) ? (int)(div == 1 ? e : e / div) : -1;
+        sid[i - c0] = (e >= 0 && e < lim) ? (int)(div == 1 ? e : e / div) : -1;
     }
-    __syncwarp();
-    for (int b = c0; b < c1; b += 32) {
+    __syncthreads();
+    constexpr int PER_WARP = PERM_CHUNK / PERM_WARPS;
+    const int w0 = c0 + warp * PER_WARP, w1 = min(c1, w0 + PER_WARP);
+    int* mine = cur + warp * E;
+    for (int b = w0; b < w0 + PER_WARP; b += 32) {       // counts (warp-private row)
         const int i = b + lane;
-        const bool valid = i < c1;
-        long long e = valid ? sid[i - c0] : -1;
-        const bool good = valid && e >= 0 && e < E;
-        const unsigned act = __ballot_sync(0xffffffffu, good);
-        const int key = good ? (int)e : -1 - lane;       // invalid lanes get unique keys
+        const int bk = i < w1 ? sid[i - c0] : -1;
+        const int key = bk >= 0 ? bk : -1 - lane;        // lanes without a bucket get unique keys
+        const unsigned peers = __match_any_sync(0xffffffffu, key);
+        if (bk >= 0 && lane == __ffs(peers) - 1) mine[bk] += __popc(peers);
+        __syncwarp();
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {  // exclusive scan across the warps
+        int run = start[(long long)blockIdx.x * E + e];
+        for (int w = 0; w < PERM_WARPS; ++w) {
+            const int c = cur[w * E + e];
+            cur[w * E + e] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+    for (int b = w0; b < w0 + PER_WARP; b += 32) {       // placement
+        const int i = b + lane;
+        const bool valid = i < w1;
+        const int bk = valid ? sid[i - c0] : -1;
+        const bool good = bk >= 0;
+        const int key = good ? bk : -1 - lane;
         const unsigned peers = __match_any_sync(0xffffffffu, key);
         const int rank = __popc(peers & ((1u << lane) - 1u));
         int base = 0;
-        if (good) base = cursor[e];
+        if (good) base = mine[bk];
         __syncwarp();
-        if (good && rank == 0) cursor[e] = base + __popc(peers & act);
+        if (good && rank == 0) mine[bk] = base + __popc(peers);
         __syncwarp();
         if (good) {
             const long long pos = base + rank;
             order[pos] = row_map ? row_map[i] : i;
             if (inverse) inverse[i] = pos_base + pos;
         } else if (valid && inverse) {
-            inverse[i] = -1;          // an id outside [0, E): no row (flagged by the histogram pass)
+            inverse[i] = -1;          // an id outside the buckets: no row (flagged by the histogram pass)
         }
     }
 }
