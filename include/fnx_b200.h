@@ -162,6 +162,13 @@ size_t fnx_ep_p2p_recv_workspace(const void* desc);
 int fnx_ep_p2p_recv_layout(const void* desc, int T, void* order_x, void* ends_x, void* pos, void* rows, void* sh_out,
                            void* workspace, size_t ws_bytes, void* stream);
 
+/* The LQP artifact's experts as the int4pack artifact, on the GPU (tools/repack_w4a16.py:41-70,
+ * which needs CANN's npu_convert_weight_to_int4pack): v2o uint8 [E, N, K/2] offset-binary
+ * (byte 64s+j of a row: low nibble W[128s+j] + 8, high nibble W[128s+64+j] + 8) -> w4 int32
+ * [K, E, N/8] (expert_major = 0, the artifact's layout) or [E, K, N/8] (tools/repack_w4_em.py),
+ * nibble t of word j = W[8j+t] two's complement.  N % 8 == 0, K % 128 == 0.  Byte-exact. */
+int fnx_repack_v2o(const void* v2o, int E, int N, int K, int expert_major, void* w4, void* stream);
+
 /* Load-time repack of the int4pack artifact (w4 int32 [E,K,Nw/8] expert-major, scales bf16
  * [E,K/gs,Nw]; tools/repack_w4a16.py, tools/repack_w4_em.py) into the tile blocks the B200
  * kernels stream: tiles int32 [E, Nw/128, K/64, 1088], one 4352-byte block per (expert,

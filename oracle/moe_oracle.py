@@ -65,6 +65,28 @@ def pack_int4pack(q: torch.Tensor) -> torch.Tensor:
     return word.to(torch.int32)
 
 
+def unpack_v2o(v2o: np.ndarray, K: int) -> np.ndarray:
+    """LQP ``v2o`` uint8 ``[m, N, K/2]`` (offset-binary) -> int32 ``[m, N, K]`` in [-8, 7].
+
+    Restates ``unpack_v2`` of ``tools/repack_w4a16.py:41-55``: byte ``64s+j`` of a row holds
+    ``W[128s+j]`` in its low nibble and ``W[128s+64+j]`` in its high nibble, each ``n + 8``."""
+    m, N, _ = v2o.shape
+    S = K // 128
+    p = v2o.astype(np.int16)
+    out = np.empty((m, N, S, 2, 64), dtype=np.int32)
+    out[..., 0, :] = ((p & 15) - 8).reshape(m, N, S, 64)
+    out[..., 1, :] = ((p >> 4) - 8).reshape(m, N, S, 64)
+    return out.reshape(m, N, K)
+
+
+def repack_v2o(v2o: np.ndarray, K: int) -> torch.Tensor:
+    """``tools/repack_w4a16.py:58-70`` restated: the LQP ``v2o`` experts ``[E, N, K/2]`` as the
+    int4pack artifact ``int32 [K, E, N/8]`` (``npu_convert_weight_to_int4pack`` of each
+    expert's ``[K, N]`` values, stored K-major)."""
+    q = torch.from_numpy(unpack_v2o(v2o, K)).to(torch.int8)          # [E, N, K]
+    return pack_int4pack(q.transpose(1, 2)).permute(1, 0, 2).contiguous()
+
+
 def to_expert_major(w4_kmajor: torch.Tensor) -> torch.Tensor:
     """``[K, E, N/8] -> [E, K, N/8]``: the byte-exact transpose of ``tools/repack_w4_em.py:16``."""
     return w4_kmajor.permute(1, 0, 2).contiguous()

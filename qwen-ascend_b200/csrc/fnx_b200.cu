@@ -727,6 +727,14 @@ FNX_API int fnx_bf16_gemm_nt(const void* x, long long ld_x, const void* w, void*
 }
 
 // ======================================================================== load-time repack
+FNX_API int fnx_repack_v2o(const void* v2o, int E, int N, int K, int expert_major, void* w4, void* stream) {
+    if (!v2o || !w4 || E < 1 || N < 8 || N % 8 || K < 128 || K % 128) return FNX_EARG;
+    const long long total = (long long)E * K * (N / 8);
+    repack_v2o_kernel<<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>((const uint8_t*)v2o, E, N, K,
+                                                                             expert_major ? 1 : 0, (int32_t*)w4);
+    return launch_rc();
+}
+
 FNX_API size_t fnx_w4_tiles_bytes(int E, int K, int Nw) {
     if (E < 1 || K < 64 || K % 64 || Nw < 128 || Nw % 128) return 0;
     return (size_t)E * (Nw / 128) * (K / 64) * TILE_BLOCK_BYTES;

@@ -76,4 +76,32 @@ FNX_DEV uint32_t tile_pair(uint32_t word, int i, uint32_t s2) {
     return bmul2(q, s2);
 }
 
+// LQP v2o -> int4pack (tools/repack_w4a16.py:41-70 without CANN): v2o uint8 [E, N, K/2], byte
+// 64s+j of row n = W[n, 128s+j] (low nibble) | W[n, 128s+64+j] (high), each offset by 8.
+// Output word j of (k, e): nibble t = W[8j+t, k] in two's complement (the offset nibble with
+// its top bit flipped); K-major [K, E, N/8], or expert-major [E, K, N/8].  One thread per word.
+__global__ void __launch_bounds__(256) repack_v2o_kernel(const uint8_t* __restrict__ v2o, int E, int N, int K,
+                                                         int expert_major, int32_t* __restrict__ out) {
+    const int nw = N / 8;
+    const long long total = (long long)E * K * nw;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        // consecutive threads take consecutive words j of one (k, e) row of the output
+        const int j = (int)(i % nw);
+        const long long r = i / nw;
+        int k, e;
+        if (expert_major) { e = (int)(r / K); k = (int)(r % K); }
+        else { k = (int)(r / E); e = (int)(r % E); }
+        const long long byte = 64 * (k >> 7) + (k & 63);
+        const int sh = ((k >> 6) & 1) * 4;
+        uint32_t w = 0;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const uint32_t b = v2o[((long long)e * N + 8 * j + t) * (K / 2) + byte];
+            w |= (((b >> sh) & 15u) ^ 8u) << (4 * t);
+        }
+        out[i] = (int32_t)w;
+    }
+}
+
 }  // namespace fnx

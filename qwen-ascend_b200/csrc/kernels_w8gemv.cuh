@@ -14,7 +14,10 @@
 namespace fnx {
 
 constexpr int W8V_COLS = 128;      // output columns per CTA
-constexpr int W8V_CL = 8;          // CTAs per cluster (K split)
+#ifndef FNX_W8V_CL
+#define FNX_W8V_CL 8
+#endif
+constexpr int W8V_CL = FNX_W8V_CL; // CTAs per cluster (K split)
 constexpr int W8V_MAXM = 16;
 
 FNX_DEV float ld_shared_cluster_f32(uint32_t addr) {
@@ -60,15 +63,16 @@ __global__ void __launch_bounds__(256, 2) w8a16_gemv_kernel(const bf16* __restri
         for (int c = 0; c < 4; ++c) acc[m][c] = 0.f;
     int g_cur = -1;
     float s[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int rb = 0; rb < rpw; rb += 8) {
-        uint32_t q[8];
+    constexpr int RB = 8;                             // rows per batch of loads in flight
+    for (int rb = 0; rb < rpw; rb += RB) {
+        uint32_t q[RB];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < RB; ++i) {
             const long long k = k0 + r0 + rb + i;
             q[i] = (ok && rb + i < rpw) ? __ldg(reinterpret_cast<const unsigned int*>(w + k * N + col)) : 0u;
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < RB; ++i) {
             if (rb + i >= rpw) break;                 // warp-uniform: rows past this warp's share
             const int kr = r0 + rb + i;               // row within the CTA's eighth
             const int g = (k0 + kr) / gs;

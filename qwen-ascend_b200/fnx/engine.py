@@ -45,6 +45,22 @@ def repack_w4(w4, scales, swiglu):
     return t
 
 
+def repack_v2o(v2o, K, expert_major=False):
+    """The LQP artifact's experts ``v2o`` uint8 ``[E, N, K/2]`` (offset-binary, byte ``64s+j`` =
+    ``W[128s+j] + 8`` low | ``W[128s+64+j] + 8`` high) as int4pack words: ``int32 [K, E, N/8]``
+    (the layout ``tools/repack_w4a16.py:58-70`` writes, there with CANN's
+    ``npu_convert_weight_to_int4pack``) or ``[E, K, N/8]`` with ``expert_major``
+    (``tools/repack_w4_em.py``).  Byte-exact, on the GPU (``fnx_repack_v2o``)."""
+    _lib.require_cuda(v2o)
+    E, N = v2o.shape[0], v2o.shape[1]
+    shape = (E, K, N // 8) if expert_major else (K, E, N // 8)
+    out = torch.empty(shape, dtype=torch.int32, device=v2o.device)
+    rc = _lib.lib().fnx_repack_v2o(v2o.contiguous().data_ptr(), E, N, K, 1 if expert_major else 0, out.data_ptr(),
+                                   _lib.stream(v2o.device))
+    _lib.check(rc, "v2o repack")
+    return out
+
+
 def _grouped_w4(act, tiles, ends, out, *, E, M, K, Nw, epilogue, row_index=None, index_div=1):
     """Grouped GEMM over the tile blocks of ``repack_w4`` (the SwiGLU epilogues need the
     SwiGLU row order)."""
@@ -74,6 +90,15 @@ class ExpW4:
         self.gs = gs
         self._scales = (s8t.permute(1, 0, 2).to(BF16) * base.to(BF16)[:, None, :]).contiguous()
         self.s8t = self.base = None
+
+    @classmethod
+    def from_lqp(cls, v2o, s8, base, gs):
+        """Experts straight from the LQP artifact (``v2o [E,N,K/2]`` uint8, ``s8 [E,N,G]`` int8,
+        ``base [E,N]`` fp16), with the conversion ``tools/repack_w4a16.py`` does offline: the
+        int4 values repacked on the GPU, ``s8t = s8`` as ``[G,E,N]`` and ``base`` in bf16."""
+        K = v2o.shape[2] * 2
+        w4 = repack_v2o(v2o, K, expert_major=True)
+        return cls(w4, s8.permute(2, 0, 1).contiguous(), base.to(BF16), gs, expert_major=True)
 
     @classmethod
     def from_scales(cls, w4_em, scales, gs):

@@ -65,9 +65,14 @@ def _install_stub():
         n = x.shape[dim] // 2
         return torch.nn.functional.silu(x[..., :n]) * x[..., n:]
 
+    def int4pack(q):
+        # npu_convert_weight_to_int4pack restated (used only by the tools module's import)
+        return O.pack_int4pack(q.to(torch.int8))
+
     stub.npu_weight_quant_batchmatmul = wqbm
     stub.npu_grouped_matmul = gmm
     stub.npu_swiglu = swiglu
+    stub.npu_convert_weight_to_int4pack = int4pack
     sys.modules["torch_npu"] = stub
 
 
@@ -334,11 +339,28 @@ def golden_w4gemv():
     print("w4gemv saved", flush=True)
 
 
+def golden_v2o():
+    """The LQP v2o unpack of ``tools/repack_w4a16.py:41-55`` (the reference function itself, run
+    on random bytes): the layout the GPU v2o -> int4pack repack reads."""
+    _install_stub()
+    spec = importlib.util.spec_from_file_location("ref_repack_w4a16", REF / "tools" / "repack_w4a16.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    rng = np.random.Generator(np.random.PCG64(17))
+    E, N, K = 3, 24, 384
+    v2o = rng.integers(0, 256, size=(E, N, K // 2), dtype=np.uint8)
+    q = mod.unpack_v2(v2o, K)
+    torch.save(dict(v2o=torch.from_numpy(v2o), K=K, q=torch.from_numpy(q)), HERE / "v2o.pt")
+    print("v2o saved", flush=True)
+
+
 PIN = synth.MoEShape(H=256, I=128, E=16, k=4, gs=128)
 
 if __name__ == "__main__":
     torch.set_num_threads(os.cpu_count())
-    which = set(sys.argv[1:]) or {"pin", "cfg1", "decode", "reduce", "w8", "w4gemv", "expq"}
+    which = set(sys.argv[1:]) or {"pin", "cfg1", "decode", "reduce", "w8", "w4gemv", "expq", "v2o"}
+    if "v2o" in which:
+        golden_v2o()
     if "pin" in which:
         golden_grouped("pin_grouped", PIN, T=48, seed=11, xseed=12)
         golden_decode("pin_decode", PIN, seed=11, xseed=13)

@@ -56,6 +56,8 @@ def test_host_side_rejections(lib):
     assert g(None, 2048, 64, None, 1, None, None, None, 1024, 8, 64, 2048, 1024, 5, None) == -1
     assert g(None, 2048, 10, None, 1, None, None, None, 1024, 8, 64, 2048, 1024, 0, None) == -1  # rows < M
     assert lib.fnx_repack_w4_tiles(None, None, None, 8, 2048, 1024, 96, 0, None) == -1          # gs % 64
+    assert lib.fnx_repack_v2o(None, 8, 1024, 2048, 0, None, None) == -1                          # no buffers
+    assert lib.fnx_repack_v2o(8, 8, 1024, 2000, 0, 8, None) == -1                                # K % 128
     assert lib.fnx_w4_tiles_bytes(512, 2048, 1024) == 512 * 8 * 32 * 4352
     assert lib.fnx_w4_tiles_bytes(512, 2048, 1000) == 0
     assert lib.fnx_w4gemv_launch(None, None, None, None, None, None, None, 1024, 100, 10, 20, 2, None) == -1

@@ -194,3 +194,36 @@ def test_w4gemv_goldens(golden):
     ref = O.w4gemv(gd["v2"].numpy(), np.ascontiguousarray(np.transpose(gd["s4"].numpy(), (0, 2, 1))), x,
                    np.arange(3), N, K, 2)
     assert np.abs(ys[1].cpu().numpy() - ref).max() < 1e-4
+
+
+@pytest.mark.parametrize("E,N,K", [(3, 24, 384), (2, 1024, 2048)])
+def test_repack_v2o_bit_exact(E, N, K):
+    """fnx_repack_v2o (K-major and expert-major) equals the oracle's restatement of
+    tools/repack_w4a16.py byte for byte."""
+    from fnx.engine import repack_v2o
+    rng = np.random.Generator(np.random.PCG64(E * N + K))
+    v2o = rng.integers(0, 256, size=(E, N, K // 2), dtype=np.uint8)
+    ref = O.repack_v2o(v2o, K)
+    vd = torch.from_numpy(v2o).to(DEV)
+    assert torch.equal(repack_v2o(vd, K).cpu(), ref)
+    assert torch.equal(repack_v2o(vd, K, expert_major=True).cpu(), ref.permute(1, 0, 2).contiguous())
+
+
+def test_expw4_from_lqp():
+    """ExpW4.from_lqp: the LQP artifact through the GPU repack and the grouped GEMM matches the
+    oracle's dequant matmul of the same values."""
+    from fnx.engine import ExpW4
+    E, N, K, gs = 2, 256, 256, 64
+    rng = np.random.Generator(np.random.PCG64(3))
+    v2o = rng.integers(0, 256, size=(E, N, K // 2), dtype=np.uint8)
+    s8 = rng.integers(1, 127, size=(E, N, K // gs), dtype=np.int8)
+    base = (np.abs(rng.standard_normal((E, N))) * 1e-3).astype(np.float16)
+    w = ExpW4.from_lqp(torch.from_numpy(v2o).to(DEV), torch.from_numpy(s8).to(DEV), torch.from_numpy(base).to(DEV), gs)
+    x = torch.randn(5, K, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16)
+    ends = torch.tensor([3, 5], dtype=torch.int64)
+    got = w.apply_grouped(x.to(DEV), ends.to(DEV)).cpu()
+    q = torch.from_numpy(O.unpack_v2o(v2o, K)).to(torch.int8).transpose(1, 2)        # [E, K, N]
+    scales = (torch.from_numpy(s8).permute(0, 2, 1).to(torch.bfloat16)
+              * torch.from_numpy(base).to(torch.bfloat16)[:, None, :])           # [E, G, N]
+    ref = O.grouped_matmul(x, ends, lambda e: O.deq_w4(q[e], scales[e], gs))
+    assert O.within_tolerance(got, ref), O.tolerance_report(got, ref)

@@ -170,3 +170,15 @@ def test_topk_tie_rule():
     w2 = w.clone()
     assert bool(O.same_topk(idx, w, torch.tensor([[1, 4]]), w2, probs, 2)[0])
     assert not bool(O.same_topk(idx, w, torch.tensor([[1, 3]]), w2, probs, 2)[0])
+
+
+def test_v2o_unpack_and_repack_pinned(golden):
+    """LQP v2o: the oracle's unpack equals the reference's own ``unpack_v2``
+    (``tools/repack_w4a16.py:41-55``) on the fixture, and its int4pack repack round-trips."""
+    g = golden("v2o")
+    v2o, K = g["v2o"].numpy(), g["K"]
+    q = O.unpack_v2o(v2o, K)
+    assert np.array_equal(q, g["q"].numpy())
+    art = O.repack_v2o(v2o, K)                                    # [K, E, N/8]
+    back = O.unpack_int4pack(art.permute(1, 0, 2))                # [E, K, N]
+    assert torch.equal(back.transpose(1, 2).to(torch.int32), torch.from_numpy(q))
