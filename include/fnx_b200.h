@@ -53,7 +53,15 @@ int fnx_w4gemv_launch(void* p4, void* s4t, void* xe, void* xo, void* y, void* db
 int fnx_w4gemv_launch_layers(void** p4, void** s4t, void** x, void** y, int nL, int N, int K, int nExp, int nblk,
                              int lay, void* dbg, void* stream);
 
+/* replaces kernels/inject/inject.cpp:26 (fnx/native_inject.py:9-28): H = 2560, HC = 4.
+ * out[t, b*H + c] = bf16(h[t, b*H + c] + bf16(y[t, c] * g[t, b])), h/out bf16 [batch, HC*H],
+ * y bf16 [batch, H], g bf16 [batch, HC]. */
+int fnx_inject(void* h, void* y, void* g, void* out, int batch, void* stream);
+
 /* ---- widened forms of the reference kernels (shapes the AscendC kernels hard-code) ---- */
+
+/* fnx_inject for any H % 8 == 0 and HC <= 64. */
+int fnx_inject_ex(void* h, void* y, void* g, void* out, int batch, int H, int HC, void* stream);
 
 /* fnx_gather_pair with any slot count; ids outside [0,E) copy zeros and set device error 2
  * (E <= 0 disables the check). */
@@ -220,6 +228,13 @@ int fnx_bf16_gemm_nt(const void* x, long long ld_x, const void* w, void* y, long
  * [T*k] (or NULL), sh bf16 [T,H], gate bf16 at gate[t * gate_ld] -> out bf16 [T,H]. */
 int fnx_moe_combine(void* yd, void* wf, void* inverse, void* sh, void* gate, long long gate_ld, void* out, int T, int k,
                     int H, void* stream);
+
+/* fnx_moe_combine followed by the residual inject of the layer (fnx/engine.py:1945-1946:
+ * `y = _moe(mixed); return inject(h, inj, y)`) in the same pass: out_hyper [T, HC*H] =
+ * inject(hyper, inj, y) with y the combined output (also stored to `out` unless it is NULL).
+ * k <= 16, H % 8 == 0, HC <= 64. */
+int fnx_moe_combine_inject(void* yd, void* wf, void* inverse, void* sh, void* gate, long long gate_ld, void* hyper,
+                           void* inj, void* out_hyper, void* out, int T, int k, int H, int HC, void* stream);
 
 /* Whole decode MoE layer for M <= 16 tokens (fnx/engine.py:1786-1889 decode branch):
  * router bf16 [E+1, H] (row E = shared-expert gate), routed and shared experts as the

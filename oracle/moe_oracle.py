@@ -289,6 +289,18 @@ def sigmoid_bf16(g: torch.Tensor) -> torch.Tensor:
     return torch.sigmoid(g.to(F32)).to(BF16)
 
 
+def inject(hyper: torch.Tensor, inj: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """``inject`` (``fnx/engine.py:859-877``; ``kernels/inject/inject.cpp:14-20``):
+    ``out[t, b*H + c] = bf16(hyper[t, b*H + c] + bf16(y[t, c] * inj[t, b]))`` over the HC
+    branches, fp32 arithmetic with both roundings."""
+    B = hyper.shape[0]
+    HC = inj.reshape(B, -1).shape[1]
+    H = y.reshape(B, -1).shape[1]
+    h = hyper.reshape(B, HC, H).to(F32)
+    p = (y.reshape(B, 1, H).to(F32) * inj.reshape(B, HC, 1).to(F32)).to(BF16).to(F32)
+    return (h + p).to(BF16).reshape(hyper.shape)
+
+
 def moe_merge(experts: torch.Tensor, shared: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
     """``bf16(e + bf16(sh * bf16(sigmoid(g))))`` (``kernels/post_ops/post_ops.cpp:72-90``);
     ``gate`` holds one value per row."""

@@ -309,6 +309,35 @@ FNX_API int fnx_moe_combine(void* yd, void* wf, void* inverse, void* sh, void* g
     return launch_rc();
 }
 
+// inject (kernels/inject/inject.cpp:26): hyper [B, HC*H], y [B, H], gate [B, HC] bf16
+FNX_API int fnx_inject_ex(void* h, void* y, void* g, void* out, int batch, int H, int HC, void* stream) {
+    if (batch < 1 || H < 8 || H % 8 || HC < 1 || HC > 64 || !h || !y || !g || !out) return FNX_EARG;
+    if (!aligned16(h) || !aligned16(y) || !aligned16(out)) return FNX_EALIGN;
+    inject_kernel<<<grid_for((long long)batch * (H / 8), 256), 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)h, (const bf16*)y, (const bf16*)g, (bf16*)out, batch, H, HC);
+    return launch_rc();
+}
+
+FNX_API int fnx_inject(void* h, void* y, void* g, void* out, int batch, void* stream) {
+    return fnx_inject_ex(h, y, g, out, batch, 2560, 4, stream);
+}
+
+FNX_API int fnx_moe_combine_inject(void* yd, void* wf, void* inverse, void* sh, void* gate, long long gate_ld,
+                                   void* hyper, void* inj, void* out_hyper, void* out, int T, int k, int H, int HC,
+                                   void* stream) {
+    if (T < 0 || k < 1 || k > 16 || H < 8 || H % 8 || gate_ld < 1 || HC < 1 || HC > 64 || !hyper || !inj ||
+        !out_hyper)
+        return FNX_EARG;
+    if (!aligned16(yd) || !aligned16(sh) || !aligned16(hyper) || !aligned16(out_hyper) || (out && !aligned16(out)))
+        return FNX_EALIGN;
+    if (T == 0) return FNX_OK;
+    const int grid = grid_for((long long)T * (H / 8), 256);
+    moe_combine_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)yd, (const float*)wf, (const int64_t*)inverse, (const bf16*)sh, (const bf16*)gate, gate_ld,
+        (bf16*)out, T, k, H, (const bf16*)hyper, (const bf16*)inj, (bf16*)out_hyper, HC);
+    return launch_rc();
+}
+
 // ======================================================================== routing
 FNX_API int fnx_router_topk(void* logits, long long ld, void* bias, void* w_out, void* idx_out, void* wf_out, int T,
                             int E, int k, void* stream) {

@@ -110,13 +110,55 @@ __global__ void __launch_bounds__(256) moe_merge_kernel(const bf16* __restrict__
 // out[t,c] = bf16( bf16(sum_j fp32(bf16(w[t*k+j] * yd[row(t,j), c]))) + bf16(sh[t,c] * bf16(sigmoid(g[t]))) )
 // row(t,j) = inverse[t*k+j] (or t*k+j); g[t] = gate[t * gate_ld].  The reference's
 // weighted_reduce mode 2 followed by post_ops.moe_merge (fnx/engine.py:1844-1853),
-// with the same roundings, in one pass over yd.
+// with the same roundings, in one pass over yd (the kernel follows the inject helpers).
+
+// inject of 8 columns [c, c+8) of token t for every branch: y (bf16 pairs) * inj[t, b], rounded
+// to bf16, added to hyper in fp32 and rounded (kernels/inject/inject.cpp:14-20).
+FNX_DEV void inject_vec(const bf16* hyper, const bf16* inj, bf16* out_hyper, long long t, int c, int H, int HC,
+                        const uint32_t (&ya)[4]) {
+    for (int b = 0; b < HC; ++b) {
+        const float gv = bf2f(inj[t * HC + b]);
+        const long long o = (t * HC + b) * (long long)H + c;
+        const uint4 hv = ld_nc_v4(hyper + o);
+        const uint32_t ha[4] = {hv.x, hv.y, hv.z, hv.w};
+        uint32_t oa[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float lo = __fadd_rn(bf_lo(ha[q]), round_bf(__fmul_rn(bf_lo(ya[q]), gv)));
+            const float hi = __fadd_rn(bf_hi(ha[q]), round_bf(__fmul_rn(bf_hi(ya[q]), gv)));
+            oa[q] = pack_bf2(lo, hi);
+        }
+        *reinterpret_cast<uint4*>(out_hyper + o) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+    }
+}
+
+// Standalone inject: out [B, HC*H] from hyper [B, HC*H], y [B, H], inj [B, HC] (H % 8 == 0).
+__global__ void __launch_bounds__(256) inject_kernel(const bf16* __restrict__ hyper, const bf16* __restrict__ y,
+                                                     const bf16* __restrict__ inj, bf16* __restrict__ out, int B,
+                                                     int H, int HC) {
+    const int per_row = H / 8;
+    const long long total = (long long)B * per_row;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long t = i / per_row;
+        const int c = (int)(i % per_row) * 8;
+        const uint4 yv = ld_nc_v4(y + t * H + c);
+        const uint32_t ya[4] = {yv.x, yv.y, yv.z, yv.w};
+        inject_vec(hyper, inj, out, t, c, H, HC, ya);
+    }
+}
+
+// The combine.  With `hyper` (the fused inject of fnx/engine.py:859-877): out_hyper[t, b*H + c] =
+// bf16(hyper[t, b*H + c] + bf16(y[t, c] * inj[t, b])) for the HC branches, y the combined
+// output (also written to `out` when it is not null).  Needs the vector path (H % 8, k <= 16).
 template <bool VEC>
 __global__ void __launch_bounds__(256, 3) moe_combine_kernel(const bf16* __restrict__ yd, const float* __restrict__ w,
                                                           const int64_t* __restrict__ inverse,
                                                           const bf16* __restrict__ sh, const bf16* __restrict__ gate,
                                                           long long gate_ld, bf16* __restrict__ out, int T, int k,
-                                                          int H) {
+                                                          int H, const bf16* __restrict__ hyper = nullptr,
+                                                          const bf16* __restrict__ inj = nullptr,
+                                                          bf16* __restrict__ out_hyper = nullptr, int HC = 0) {
     const int per_row = VEC ? H / 8 : H;
     const long long total = (long long)T * per_row;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -179,7 +221,8 @@ __global__ void __launch_bounds__(256, 3) moe_combine_kernel(const bf16* __restr
                 const float hi = __fadd_rn(round_bf(acc[2 * q + 1]), round_bf(__fmul_rn(bf_hi(sa[q]), sg)));
                 oa[q] = pack_bf2(lo, hi);
             }
-            *reinterpret_cast<uint4*>(out + off) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+            if (out) *reinterpret_cast<uint4*>(out + off) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+            if (hyper) inject_vec(hyper, inj, out_hyper, t, c, H, HC, oa);
             continue;
         }
         // slots in groups of four: all four row loads are issued before the in-order sums

@@ -29,6 +29,9 @@ SIGNATURES = {
     "fnx_gather_pair": ([P] * 5 + [I] * 3 + [P], I),
     "fnx_gather_pair_ex": ([P] * 5 + [I] * 5 + [P], I),
     "fnx_moe_combine": ([P] * 5 + [LL, P, I, I, I, P], I),
+    "fnx_moe_combine_inject": ([P] * 5 + [LL, P, P, P, P, I, I, I, I, P], I),
+    "fnx_inject": ([P] * 4 + [I, P], I),
+    "fnx_inject_ex": ([P] * 4 + [I, I, I, P], I),
     "fnx_router_topk": ([P, LL, P, P, P, P, I, I, I, P], I),
     "fnx_moe_permute_workspace": ([I, I], SZ),
     "fnx_moe_permute": ([P] * 5 + [I, I, P, SZ, P], I),

@@ -303,7 +303,26 @@ class MoELayer:
         ``CapturedLayer``; its replay launches the same kernels as a direct call."""
         return CapturedLayer(self, T, device or self.router_cat.device)
 
-    def prefill(self, x, details=False):
+    def moe_inject(self, x, hyper, inj):
+        """The MoE half of a layer's tail, ``inject(h, inj, self._moe(mixed))``
+        (``fnx/engine.py:1945-1946``): ``hyper`` bf16 ``[b, 1, HC*H]`` (the hyper-connection
+        state), ``inj`` bf16 ``[b, 1, HC]``; returns the new state.  The grouped path applies
+        the inject inside the combine pass; the decode path runs it after the fused layer."""
+        from . import native_inject
+        x2 = x.reshape(-1, self.H)
+        if x2.dtype != BF16:
+            x2 = x2.to(BF16)
+        x2 = x2.contiguous()
+        hyper, inj = hyper.contiguous(), inj.contiguous()
+        if x2.shape[0] <= DECODE_MAX_TOKENS and self.E <= DECODE_MAX_EXPERTS:
+            y = self.decode(x2)[0]
+            out = native_inject.inject(hyper, inj, y.view(x2.shape[0], 1, self.H))
+            if out is None:
+                raise ValueError("moe_inject: unsupported hyper / inj shapes")
+            return out
+        return self.prefill(x2, inject=(hyper, inj))
+
+    def prefill(self, x, details=False, inject=None):
         """Grouped path (``fnx/engine.py:1815-1853``) for ``T`` tokens.  The routed and the shared
         expert share one grouped launch per projection; the per-call buffers of the extended
         permutation are cached per token count (calls on one layer must not overlap)."""
@@ -330,8 +349,19 @@ class MoELayer:
         yd = torch.empty(M + T, H, dtype=BF16, device=dev)
         _grouped_w4(act, self.dn_all, ends_x, yd, E=E + 1, M=M + T, K=I, Nw=H, epilogue=EPI_PLAIN)
         sh_act, sh = act[M:], yd[M:]
-        out = torch.empty(T, H, dtype=BF16, device=dev)
         gate = logits[:, E:E + 1]
+        if inject is not None:              # combine + residual inject in one pass
+            hyper, inj = inject
+            HC = inj.numel() // T
+            if hyper.numel() != T * HC * H:
+                raise ValueError("prefill inject: hyper must hold T * HC * H values")
+            out_h = torch.empty_like(hyper)
+            rc = _lib.lib().fnx_moe_combine_inject(yd.data_ptr(), wf.data_ptr(), inverse.data_ptr(), sh.data_ptr(),
+                                                   gate.data_ptr(), logits.stride(0), hyper.data_ptr(), inj.data_ptr(),
+                                                   out_h.data_ptr(), None, T, k, H, HC, _lib.stream(dev))
+            _lib.check(rc, "MoE combine + inject")
+            return out_h
+        out = torch.empty(T, H, dtype=BF16, device=dev)
         rc = _lib.lib().fnx_moe_combine(yd.data_ptr(), wf.data_ptr(), inverse.data_ptr(), sh.data_ptr(),
                                         gate.data_ptr(), logits.stride(0), out.data_ptr(), T, k, H, _lib.stream(dev))
         _lib.check(rc, "MoE combine")

@@ -354,13 +354,29 @@ def golden_v2o():
     print("v2o saved", flush=True)
 
 
+def golden_inject():
+    """``inject`` (``fnx/engine.py:859-877``, the torch path) on random bf16 tensors at the
+    reference's production width (H=2560, HC=4): ``hyper + y * inj`` broadcast over branches."""
+    E = ref_engine(synth.PROD)
+    g = torch.Generator().manual_seed(23)
+    b = 3
+    hyper = torch.randn(b, 1, E.HC * E.H, generator=g).to(torch.bfloat16)
+    inj = (2 * torch.rand(b, 1, E.HC, generator=g)).to(torch.bfloat16)
+    y = torch.randn(b, 1, E.H, generator=g).to(torch.bfloat16)
+    out = E.inject(hyper, inj, y)
+    torch.save(dict(hyper=hyper, inj=inj, y=y, out=out, H=int(E.H), HC=int(E.HC)), HERE / "inject.pt")
+    print("inject saved", flush=True)
+
+
 PIN = synth.MoEShape(H=256, I=128, E=16, k=4, gs=128)
 
 if __name__ == "__main__":
     torch.set_num_threads(os.cpu_count())
-    which = set(sys.argv[1:]) or {"pin", "cfg1", "decode", "reduce", "w8", "w4gemv", "expq", "v2o"}
+    which = set(sys.argv[1:]) or {"pin", "cfg1", "decode", "reduce", "w8", "w4gemv", "expq", "v2o", "inject"}
     if "v2o" in which:
         golden_v2o()
+    if "inject" in which:
+        golden_inject()
     if "pin" in which:
         golden_grouped("pin_grouped", PIN, T=48, seed=11, xseed=12)
         golden_decode("pin_decode", PIN, seed=11, xseed=13)

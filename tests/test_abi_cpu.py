@@ -57,6 +57,10 @@ def test_host_side_rejections(lib):
     assert g(None, 2048, 10, None, 1, None, None, None, 1024, 8, 64, 2048, 1024, 0, None) == -1  # rows < M
     assert lib.fnx_repack_w4_tiles(None, None, None, 8, 2048, 1024, 96, 0, None) == -1          # gs % 64
     assert lib.fnx_repack_v2o(None, 8, 1024, 2048, 0, None, None) == -1                          # no buffers
+    assert lib.fnx_inject(None, None, None, None, 0, None) == -1                                  # batch 0
+    assert lib.fnx_inject_ex(8, 8, 8, 8, 1, 100, 4, None) == -1                                   # H % 8
+    ci = lib.fnx_moe_combine_inject
+    assert ci(None, None, None, None, None, 1, 8, 8, 8, None, 4, 17, 2048, 4, None) == -1        # k > 16
     assert lib.fnx_repack_v2o(8, 8, 1024, 2000, 0, 8, None) == -1                                # K % 128
     assert lib.fnx_w4_tiles_bytes(512, 2048, 1024) == 512 * 8 * 32 * 4352
     assert lib.fnx_w4_tiles_bytes(512, 2048, 1000) == 0

@@ -271,3 +271,44 @@ def test_w8a16_small_m(M, G):
     rep = O.tolerance_report(got.cpu(), ref)
     assert O.within_tolerance(got.cpu(), ref), rep
     assert torch.equal(w(x.to(DEV)).view(torch.int16), got.view(torch.int16))
+
+
+
+@pytest.mark.parametrize("B,H,HC", [(3, 2560, 4), (5, 2048, 4), (2, 256, 3)])
+def test_inject_bit_exact(B, H, HC):
+    """native_inject.inject (fnx_inject_ex) against the oracle, bit for bit."""
+    from fnx import native_inject
+    g = torch.Generator().manual_seed(B * H + HC)
+    hyper = torch.randn(B, 1, HC * H, generator=g).to(BF16)
+    inj = (2 * torch.rand(B, 1, HC, generator=g)).to(BF16)
+    y = torch.randn(B, 1, H, generator=g).to(BF16)
+    got = native_inject.inject(hyper.to(DEV), inj.to(DEV), y.to(DEV))
+    assert torch.equal(got.cpu().view(torch.int16), O.inject(hyper, inj, y).view(torch.int16))
+    assert native_inject.inject(hyper.to(DEV), inj.to(DEV), y.to(DEV)[:, :, :-8].contiguous()) is None
+
+
+def test_inject_reference_shim(golden):
+    """fnx_inject (the reference's shim signature, H=2560, HC=4) on the reference's own golden."""
+    g = golden("inject")
+    hyper, inj, y = (g[n].to(DEV) for n in ("hyper", "inj", "y"))
+    out = torch.empty_like(hyper)
+    rc = _lib.lib().fnx_inject(hyper.data_ptr(), y.data_ptr(), inj.data_ptr(), out.data_ptr(), hyper.shape[0],
+                               _lib.stream(hyper.device))
+    assert rc == 0
+    assert torch.equal(out.cpu().view(torch.int16), g["out"].view(torch.int16))
+
+
+@pytest.mark.parametrize("T", [300, 2])
+def test_moe_inject_fused(T):
+    """MoELayer.moe_inject: the combine + inject pass (prefill) and decode + inject equal the
+    layer's output injected separately."""
+    from fnx import native_inject
+    t, L, layer = _layer(synth.CFG2, 51)
+    HC, H = 4, synth.CFG2.H
+    x = synth.make_tokens(T, H, seed=5, device=DEV)
+    g = torch.Generator(device=DEV).manual_seed(6)
+    hyper = torch.randn(T, 1, HC * H, generator=g, device=DEV).to(BF16)
+    inj = (2 * torch.rand(T, 1, HC, generator=g, device=DEV)).to(BF16)
+    got = layer.moe_inject(x, hyper, inj)
+    ref = native_inject.inject(hyper, inj, layer(x).view(T, 1, H))
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))

@@ -182,3 +182,10 @@ def test_v2o_unpack_and_repack_pinned(golden):
     art = O.repack_v2o(v2o, K)                                    # [K, E, N/8]
     back = O.unpack_int4pack(art.permute(1, 0, 2))                # [E, K, N]
     assert torch.equal(back.transpose(1, 2).to(torch.int32), torch.from_numpy(q))
+
+
+def test_inject_pinned(golden):
+    """The oracle's inject equals the reference's ``inject`` (torch path) bit for bit."""
+    g = golden("inject")
+    got = O.inject(g["hyper"], g["inj"], g["y"])
+    assert torch.equal(got.view(torch.int16), g["out"].view(torch.int16))
