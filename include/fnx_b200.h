@@ -58,7 +58,26 @@ int fnx_w4gemv_launch_layers(void** p4, void** s4t, void** x, void** y, int nL, 
  * y bf16 [batch, H], g bf16 [batch, HC]. */
 int fnx_inject(void* h, void* y, void* g, void* out, int batch, void* stream);
 
+/* replaces kernels/post_ops/post_ops.cpp:25 (fnx/post_ops.py:22-26): the hyper-connection
+ * activation of gated_residual (fnx/engine.py:832-851).  x bf16 [batch, 324] (320 mix + 4
+ * inject columns) -> m = bf16(silu(bf16(x/4))) [batch, 320], g = bf16(2*bf16(sigmoid(bf16(x/4))))
+ * [batch, 4].  mode bit 0: sigmoid as a rounded reciprocal; bit 1: silu as v * sigmoid. */
+int fnx_hc_activation(void* x, void* m, void* g, int batch, int mode, void* stream);
+
+/* replaces kernels/post_ops/post_ops.cpp:50 (fnx/post_ops.py:27-30): the branch mix of
+ * gated_residual (fnx/engine.py:838-845).  x (hn), l (logits) bf16 [batch, 4*2560] ->
+ * y bf16 [batch, 2560] = bf16(sum_b bf16(bf16(sigmoid(l_b)) * x_b) / 4). */
+int fnx_hc_sigmoid_reduce(void* x, void* l, void* y, int batch, void* stream);
+
 /* ---- widened forms of the reference kernels (shapes the AscendC kernels hard-code) ---- */
+
+/* fnx_hc_activation with n_mix low-rank and HC inject columns. */
+int fnx_hc_activation_ex(void* x, void* m, void* g, int batch, int n_mix, int HC, int mode, void* stream);
+/* fnx_hc_sigmoid_reduce for any H and HC branches. */
+int fnx_hc_sigmoid_reduce_ex(void* x, void* l, void* y, int batch, int H, int HC, void* stream);
+/* rms_norm(x, w, gs=H) of fnx/engine.py:156-190 on hyper-connection rows: x, out bf16
+ * [batch, HC*H]; every group of H normalised in fp32, times (1 + w) (w bf16 [HC*H]). */
+int fnx_hc_rms_norm(void* x, void* w, void* out, int batch, int H, int HC, float eps, void* stream);
 
 /* fnx_inject for any H % 8 == 0 and HC <= 64. */
 int fnx_inject_ex(void* h, void* y, void* g, void* out, int batch, int H, int HC, void* stream);

@@ -301,6 +301,42 @@ def inject(hyper: torch.Tensor, inj: torch.Tensor, y: torch.Tensor) -> torch.Ten
     return (h + p).to(BF16).reshape(hyper.shape)
 
 
+def hc_rms_norm(x: torch.Tensor, w: torch.Tensor, H: int, eps: float = 1e-6) -> torch.Tensor:
+    """``rms_norm(x, w, gs=H)`` torch path (``fnx/engine.py:183-190``): groups of H in fp32,
+    ``x * rsqrt(mean(x^2) + eps) * (1 + w)``, back to bf16."""
+    xf = x.float()
+    xg = xf.view(*xf.shape[:-1], -1, H)
+    out = (xg * torch.rsqrt(xg.pow(2).mean(-1, keepdim=True) + eps)).flatten(-2)
+    return (out * (1.0 + w.float())).to(BF16)
+
+
+def hc_activation(di: torch.Tensor, HC: int):
+    """The activation of ``gated_residual`` (``fnx/engine.py:832-851``, torch path):
+    ``mix = silu(dp / HC)``, ``inj = 2 * sigmoid(ip / HC)`` on bf16 tensors."""
+    dp, ip = di[..., :-HC], di[..., -HC:]
+    return F.silu(dp / HC), 2.0 * torch.sigmoid(ip / HC)
+
+
+def hc_mix_reduce(hn: torch.Tensor, logits: torch.Tensor, HC: int) -> torch.Tensor:
+    """``(sigmoid(logits) * hn)`` averaged over the HC branches (``fnx/engine.py:838-845``)."""
+    b = hn.shape[0]
+    H = hn.shape[-1] // HC
+    mix = torch.sigmoid(logits)
+    return (mix.view(b, 1, HC, H) * hn.view(b, 1, HC, H)).mean(dim=-2).view(b, 1, H)
+
+
+def gated_residual(h: torch.Tensor, norm_w: torch.Tensor, w_di: torch.Tensor, w_up: torch.Tensor, HC: int,
+                   H: int):
+    """``gated_residual(h, hc_norm_w, w_di, w_up, None, n_inj=HC)`` (``fnx/engine.py:818-857``,
+    torch path, bf16 CPU linears): returns ``(mixed [b,1,H], inj [b,1,HC])``."""
+    b = h.shape[0]
+    hn = hc_rms_norm(h, norm_w, H)
+    di = F.linear(hn, w_di)
+    mix, inj = hc_activation(di, HC)
+    logits = F.linear(mix, w_up)
+    return hc_mix_reduce(hn, logits, HC), inj.view(b, 1, HC)
+
+
 def moe_merge(experts: torch.Tensor, shared: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
     """``bf16(e + bf16(sh * bf16(sigmoid(g))))`` (``kernels/post_ops/post_ops.cpp:72-90``);
     ``gate`` holds one value per row."""

@@ -15,6 +15,7 @@
 #include "kernels_ep.cuh"
 #include "kernels_gemm.cuh"
 #include "kernels_gemm_pair.cuh"
+#include "kernels_hc.cuh"
 #include "kernels_route.cuh"
 #include "kernels_w4gemv.cuh"
 #include "kernels_w8gemv.cuh"
@@ -336,6 +337,39 @@ FNX_API int fnx_moe_combine_inject(void* yd, void* wf, void* inverse, void* sh, 
         (const bf16*)yd, (const float*)wf, (const int64_t*)inverse, (const bf16*)sh, (const bf16*)gate, gate_ld,
         (bf16*)out, T, k, H, (const bf16*)hyper, (const bf16*)inj, (bf16*)out_hyper, HC);
     return launch_rc();
+}
+
+// ------------------------------------------------------------------ hyper-connection mix
+FNX_API int fnx_hc_rms_norm(void* x, void* w, void* out, int batch, int H, int HC, float eps, void* stream) {
+    if (batch < 0 || H < 1 || HC < 1 || !(eps >= 0.f) || (batch > 0 && (!x || !w || !out))) return FNX_EARG;
+    if (batch == 0) return FNX_OK;
+    hc_rms_norm_kernel<<<batch * HC, 256, 0, (cudaStream_t)stream>>>((const bf16*)x, (const bf16*)w, (bf16*)out, H,
+                                                                      HC, eps);
+    return launch_rc();
+}
+
+FNX_API int fnx_hc_activation_ex(void* x, void* m, void* g, int batch, int n_mix, int HC, int mode, void* stream) {
+    if (batch < 1 || n_mix < 1 || HC < 1 || mode < 0 || mode > 3 || !x || !m || !g) return FNX_EARG;
+    hc_activation_kernel<<<grid_for((long long)batch * (n_mix + HC), 256), 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)x, (bf16*)m, (bf16*)g, batch, n_mix, HC, mode);
+    return launch_rc();
+}
+
+// kernels/post_ops/post_ops.cpp:25: di [batch, 324] -> mixed [batch, 320], gates [batch, 4]
+FNX_API int fnx_hc_activation(void* x, void* m, void* g, int batch, int mode, void* stream) {
+    return fnx_hc_activation_ex(x, m, g, batch, 320, 4, mode, stream);
+}
+
+FNX_API int fnx_hc_sigmoid_reduce_ex(void* x, void* l, void* y, int batch, int H, int HC, void* stream) {
+    if (batch < 1 || H < 1 || HC < 1 || !x || !l || !y) return FNX_EARG;
+    hc_sigmoid_reduce_kernel<<<grid_for((long long)batch * H, 256), 256, 0, (cudaStream_t)stream>>>(
+        (const bf16*)x, (const bf16*)l, (bf16*)y, batch, H, HC);
+    return launch_rc();
+}
+
+// kernels/post_ops/post_ops.cpp:50: values, logits [batch, 10240] -> mixed [batch, 2560]
+FNX_API int fnx_hc_sigmoid_reduce(void* x, void* l, void* y, int batch, void* stream) {
+    return fnx_hc_sigmoid_reduce_ex(x, l, y, batch, 2560, 4, stream);
 }
 
 // ======================================================================== routing

@@ -31,6 +31,11 @@ SIGNATURES = {
     "fnx_moe_combine": ([P] * 5 + [LL, P, I, I, I, P], I),
     "fnx_moe_combine_inject": ([P] * 5 + [LL, P, P, P, P, I, I, I, I, P], I),
     "fnx_inject": ([P] * 4 + [I, P], I),
+    "fnx_hc_rms_norm": ([P] * 3 + [I, I, I, ctypes.c_float, P], I),
+    "fnx_hc_activation": ([P] * 3 + [I, I, P], I),
+    "fnx_hc_activation_ex": ([P] * 3 + [I] * 4 + [P], I),
+    "fnx_hc_sigmoid_reduce": ([P] * 3 + [I, P], I),
+    "fnx_hc_sigmoid_reduce_ex": ([P] * 3 + [I] * 3 + [P], I),
     "fnx_inject_ex": ([P] * 4 + [I, I, I, P], I),
     "fnx_router_topk": ([P, LL, P, P, P, P, I, I, I, P], I),
     "fnx_moe_permute_workspace": ([I, I], SZ),

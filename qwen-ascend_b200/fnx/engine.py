@@ -71,6 +71,32 @@ def _grouped_w4(act, tiles, ends, out, *, E, M, K, Nw, epilogue, row_index=None,
     return out
 
 
+def gated_residual(h, hc_norm_w, w_down, w_up, w_inj=None, n_inj=0, hc=4, eps=1e-6):
+    """The hyper-connection mix that produces a layer's MoE input (``fnx/engine.py:818-857``):
+    ``h`` bf16 ``[b, 1, hc*H]`` -> ``(mixed [b, 1, H], inj [b, 1, hc])``.  ``w_down`` bf16
+    ``[r (+ hc), hc*H]`` (with ``n_inj == hc`` its last rows are the inject weights, as the
+    reference's loader concatenates them), ``w_up`` bf16 ``[hc*H, r]``, ``w_inj`` bf16
+    ``[hc, hc*H]`` when not concatenated.  RMSNorm, activation and branch mix run on this
+    library's kernels with the reference's roundings; the two small GEMMs are library GEMMs."""
+    from . import post_ops
+    b, HCH = h.shape[0], h.shape[-1]
+    H = HCH // hc
+    h2 = h.reshape(b, HCH).contiguous()
+    hn = torch.empty_like(h2)
+    rc = _lib.lib().fnx_hc_rms_norm(h2.data_ptr(), hc_norm_w.contiguous().data_ptr(), hn.data_ptr(), b, H, hc, eps,
+                                    _lib.stream(h.device))
+    _lib.check(rc, "hyper-connection rms_norm")
+    if not n_inj:
+        if w_inj is None:
+            raise ValueError("gated_residual: pass w_inj, or w_down with the inject rows and n_inj = hc")
+        w_down = torch.cat([w_down, w_inj])
+    di = torch.mm(hn, w_down.t())
+    mix, inj = post_ops.activate(di.view(b, 1, -1).contiguous(), hc)
+    logits = torch.mm(mix.view(b, -1), w_up.t())
+    mixed = post_ops.mix_reduce(hn.view(b, 1, HCH), logits.view(b, 1, HCH).contiguous(), hc)
+    return mixed, inj
+
+
 class ExpW4:
     """Experts in the W4A16 artifact layout (``tools/repack_w4a16.py``):
     ``w4`` int32 ``[K, E, N/8]`` (or ``[E, K, N/8]`` with ``expert_major``), ``s8t`` int8

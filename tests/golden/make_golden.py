@@ -368,15 +368,37 @@ def golden_inject():
     print("inject saved", flush=True)
 
 
+def golden_hc():
+    """``gated_residual`` (``fnx/engine.py:818-857``, torch path, with the concatenated
+    down+inject weight as the loader builds it) at H=256, HC=4, low rank 32: the step that
+    produces the MoE input ``mixed`` and the inject gates."""
+    E = ref_engine(synth.PROD)
+    g = torch.Generator().manual_seed(29)
+    # a narrow instance of the production shape (H=2560, LOWRANK=320) keeps the fixture small;
+    # gated_residual reads H and HC from the module and the low rank from the weights
+    H, HC, LR, b = 256, int(E.HC), 32, 3
+    E.H = H
+    h = torch.randn(b, 1, HC * H, generator=g).to(torch.bfloat16)
+    norm_w = (0.1 * torch.randn(HC * H, generator=g)).to(torch.bfloat16)
+    w_di = (torch.randn(LR + HC, HC * H, generator=g) / (HC * H) ** 0.5).to(torch.bfloat16)
+    w_up = (torch.randn(HC * H, LR, generator=g) / LR ** 0.5).to(torch.bfloat16)
+    mixed, inj = E.gated_residual(h, norm_w, w_di, w_up, None, n_inj=HC)
+    torch.save(dict(h=h, norm_w=norm_w, w_di=w_di, w_up=w_up, mixed=mixed, inj=inj, H=H, HC=HC, LR=LR),
+               HERE / "hc.pt")
+    print("hc saved", flush=True)
+
+
 PIN = synth.MoEShape(H=256, I=128, E=16, k=4, gs=128)
 
 if __name__ == "__main__":
     torch.set_num_threads(os.cpu_count())
-    which = set(sys.argv[1:]) or {"pin", "cfg1", "decode", "reduce", "w8", "w4gemv", "expq", "v2o", "inject"}
+    which = set(sys.argv[1:]) or {"pin", "cfg1", "decode", "reduce", "w8", "w4gemv", "expq", "v2o", "inject", "hc"}
     if "v2o" in which:
         golden_v2o()
     if "inject" in which:
         golden_inject()
+    if "hc" in which:
+        golden_hc()
     if "pin" in which:
         golden_grouped("pin_grouped", PIN, T=48, seed=11, xseed=12)
         golden_decode("pin_decode", PIN, seed=11, xseed=13)

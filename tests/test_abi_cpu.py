@@ -59,6 +59,10 @@ def test_host_side_rejections(lib):
     assert lib.fnx_repack_v2o(None, 8, 1024, 2048, 0, None, None) == -1                          # no buffers
     assert lib.fnx_inject(None, None, None, None, 0, None) == -1                                  # batch 0
     assert lib.fnx_inject_ex(8, 8, 8, 8, 1, 100, 4, None) == -1                                   # H % 8
+    assert lib.fnx_hc_activation(None, None, None, 0, 0, None) == -1                             # batch 0
+    assert lib.fnx_hc_activation(8, 8, 8, 1, 4, None) == -1                                      # mode 4
+    assert lib.fnx_hc_sigmoid_reduce_ex(8, 8, 8, 1, 2560, 0, None) == -1                         # HC 0
+    assert lib.fnx_hc_rms_norm(8, 8, 8, 1, 0, 4, 1e-6, None) == -1                               # H 0
     ci = lib.fnx_moe_combine_inject
     assert ci(None, None, None, None, None, 1, 8, 8, 8, None, 4, 17, 2048, 4, None) == -1        # k > 16
     assert lib.fnx_repack_v2o(8, 8, 1024, 2000, 0, 8, None) == -1                                # K % 128

@@ -227,3 +227,66 @@ def test_expw4_from_lqp():
               * torch.from_numpy(base).to(torch.bfloat16)[:, None, :])           # [E, G, N]
     ref = O.grouped_matmul(x, ends, lambda e: O.deq_w4(q[e], scales[e], gs))
     assert O.within_tolerance(got, ref), O.tolerance_report(got, ref)
+
+
+
+def _ordered(t):
+    b = t.contiguous().view(torch.int16).to(torch.int32)
+    return torch.where(b < 0, -(b & 0x7FFF), b)          # bf16 bit patterns in value order (+0 == -0)
+
+
+def _ulp_ok(got, ref, min_exact=0.99):
+    d = (_ordered(got) - _ordered(ref)).abs()
+    return int(d.max()) <= 1 and float((d == 0).float().mean()) >= min_exact
+
+
+@pytest.mark.parametrize("b,H,HC,LR", [(3, 2560, 4, 320), (5, 256, 4, 32), (2, 512, 3, 64)])
+def test_hyper_connection_kernels(b, H, HC, LR):
+    """rms_norm (its own sum order: within 1 bf16 ulp), the activation and the branch mix
+    (CUDA expf: within 1 ulp) against the oracle's torch path on the same inputs."""
+    from fnx import post_ops
+    g = torch.Generator().manual_seed(b * H + HC)
+    h = torch.randn(b, HC * H, generator=g).to(torch.bfloat16)
+    w = (0.1 * torch.randn(HC * H, generator=g)).to(torch.bfloat16)
+    hn = torch.empty(b, HC * H, dtype=torch.bfloat16, device=DEV)
+    rc = _lib.lib().fnx_hc_rms_norm(h.to(DEV).data_ptr(), w.to(DEV).data_ptr(), hn.data_ptr(), b, H, HC, 1e-6,
+                                    _lib.stream(hn.device))
+    assert rc == 0
+    assert _ulp_ok(hn.cpu(), O.hc_rms_norm(h, w, H))
+    di = (3 * torch.randn(b, 1, LR + HC, generator=g)).to(torch.bfloat16)
+    mix, inj = post_ops.activate(di.to(DEV), HC)
+    rmix, rinj = O.hc_activation(di, HC)
+    assert _ulp_ok(mix.cpu(), rmix, 0.97) and _ulp_ok(inj.cpu(), rinj, 0.5)
+    logits = (2 * torch.randn(b, 1, HC * H, generator=g)).to(torch.bfloat16)
+    vals = torch.randn(b, 1, HC * H, generator=g).to(torch.bfloat16)
+    mixed = post_ops.mix_reduce(vals.to(DEV), logits.to(DEV), HC)
+    assert _ulp_ok(mixed.cpu(), O.hc_mix_reduce(vals, logits, HC), 0.97)
+
+
+def test_hyper_connection_reference_shims():
+    """fnx_hc_activation / fnx_hc_sigmoid_reduce with the reference shims' fixed shapes."""
+    from fnx import post_ops
+    g = torch.Generator().manual_seed(8)
+    di = (3 * torch.randn(2, 324, generator=g)).to(torch.bfloat16).to(DEV)
+    m = torch.empty(2, 320, dtype=torch.bfloat16, device=DEV)
+    gt = torch.empty(2, 4, dtype=torch.bfloat16, device=DEV)
+    L, st = _lib.lib(), _lib.stream(di.device)
+    assert L.fnx_hc_activation(di.data_ptr(), m.data_ptr(), gt.data_ptr(), 2, 0, st) == 0
+    rm, rg = post_ops.activate(di.view(2, 1, 324), 4)
+    assert torch.equal(m, rm.view(2, 320)) and torch.equal(gt, rg.view(2, 4))
+    x = torch.randn(2, 10240, generator=g).to(torch.bfloat16).to(DEV)
+    lg = torch.randn(2, 10240, generator=g).to(torch.bfloat16).to(DEV)
+    y = torch.empty(2, 2560, dtype=torch.bfloat16, device=DEV)
+    assert L.fnx_hc_sigmoid_reduce(x.data_ptr(), lg.data_ptr(), y.data_ptr(), 2, st) == 0
+    assert torch.equal(y, post_ops.mix_reduce(x.view(2, 1, 10240), lg.view(2, 1, 10240), 4).view(2, 2560))
+
+
+def test_gated_residual_end_to_end(golden):
+    """engine.gated_residual on the reference golden's inputs: the GEMMs run on the GPU's
+    library, so within tolerance of the reference's output."""
+    from fnx.engine import gated_residual
+    g = golden("hc")
+    mixed, inj = gated_residual(g["h"].to(DEV), g["norm_w"].to(DEV), g["w_di"].to(DEV), g["w_up"].to(DEV),
+                                n_inj=g["HC"], hc=g["HC"])
+    assert O.within_tolerance(mixed.cpu(), g["mixed"]), O.tolerance_report(mixed.cpu(), g["mixed"])
+    assert int((_ordered(inj.cpu()) - _ordered(g["inj"])).abs().max()) <= 2

@@ -189,3 +189,12 @@ def test_inject_pinned(golden):
     g = golden("inject")
     got = O.inject(g["hyper"], g["inj"], g["y"])
     assert torch.equal(got.view(torch.int16), g["out"].view(torch.int16))
+
+
+def test_gated_residual_pinned(golden):
+    """The oracle's gated_residual (rms_norm, linears, activation, branch mix) equals the
+    reference's function (torch path) bit for bit."""
+    g = golden("hc")
+    mixed, inj = O.gated_residual(g["h"], g["norm_w"], g["w_di"], g["w_up"], g["HC"], g["H"])
+    assert torch.equal(mixed.view(torch.int16), g["mixed"].view(torch.int16))
+    assert torch.equal(inj.view(torch.int16), g["inj"].view(torch.int16))
