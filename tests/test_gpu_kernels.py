@@ -244,13 +244,14 @@ def _ulp_ok(got, ref, min_exact=0.99):
 def test_hyper_connection_kernels(b, H, HC, LR):
     """rms_norm (its own sum order: within 1 bf16 ulp), the activation and the branch mix
     (CUDA expf: within 1 ulp) against the oracle's torch path on the same inputs."""
-    from fnx import post_ops
+    from fnx import _lib as fl, post_ops
     g = torch.Generator().manual_seed(b * H + HC)
     h = torch.randn(b, HC * H, generator=g).to(torch.bfloat16)
     w = (0.1 * torch.randn(HC * H, generator=g)).to(torch.bfloat16)
     hn = torch.empty(b, HC * H, dtype=torch.bfloat16, device=DEV)
-    rc = _lib.lib().fnx_hc_rms_norm(h.to(DEV).data_ptr(), w.to(DEV).data_ptr(), hn.data_ptr(), b, H, HC, 1e-6,
-                                    _lib.stream(hn.device))
+    hd, wd = h.to(DEV), w.to(DEV)                       # alive until the kernel has read them
+    rc = fl.lib().fnx_hc_rms_norm(hd.data_ptr(), wd.data_ptr(), hn.data_ptr(), b, H, HC, 1e-6, fl.stream(hn.device))
+    torch.cuda.synchronize()
     assert rc == 0
     assert _ulp_ok(hn.cpu(), O.hc_rms_norm(h, w, H))
     di = (3 * torch.randn(b, 1, LR + HC, generator=g)).to(torch.bfloat16)
@@ -265,12 +266,12 @@ def test_hyper_connection_kernels(b, H, HC, LR):
 
 def test_hyper_connection_reference_shims():
     """fnx_hc_activation / fnx_hc_sigmoid_reduce with the reference shims' fixed shapes."""
-    from fnx import post_ops
+    from fnx import _lib as fl, post_ops
     g = torch.Generator().manual_seed(8)
     di = (3 * torch.randn(2, 324, generator=g)).to(torch.bfloat16).to(DEV)
     m = torch.empty(2, 320, dtype=torch.bfloat16, device=DEV)
     gt = torch.empty(2, 4, dtype=torch.bfloat16, device=DEV)
-    L, st = _lib.lib(), _lib.stream(di.device)
+    L, st = fl.lib(), fl.stream(di.device)
     assert L.fnx_hc_activation(di.data_ptr(), m.data_ptr(), gt.data_ptr(), 2, 0, st) == 0
     rm, rg = post_ops.activate(di.view(2, 1, 324), 4)
     assert torch.equal(m, rm.view(2, 320)) and torch.equal(gt, rg.view(2, 4))
