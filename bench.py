@@ -298,9 +298,23 @@ def profile_case(case, dev):
              else of the grouped-GEMM kind (`-k regex:grouped_gemm -s 1 -c 1` takes the second);
     dec      four decode calls at M=1 (`-k regex:decode_fused -s 2 -c 1` takes the third);
     ep       three calls of the expert-parallel layer with the peer exchange on one rank
-             (every kernel of the p2p path, the exchange kept on this GPU)."""
+             (every kernel of the p2p path, the exchange kept on this GPU);
+    w8       four W8A16 projections at M=1 (K=2048, N=5120; `-k regex:w8a16 -s 2 -c 1`)."""
     from fnx import synth
     from fnx.engine import EPI_PLAIN, EPI_SWIGLU_F32, _grouped_w4
+    if case == "w8":
+        from fnx.engine import DenseW8
+        g = torch.Generator(device=dev)
+        g.manual_seed(7)
+        q = torch.randint(-127, 128, (5120, 2048), generator=g, device=dev, dtype=torch.int32).to(torch.int8)
+        sc = (torch.randn(5120, 1, generator=g, device=dev).abs_() * 0.01).to(torch.bfloat16)
+        w = DenseW8(q, sc)
+        x = torch.randn(1, 2048, generator=g, device=dev).to(torch.bfloat16)
+        for _ in range(4):
+            w(x)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": case, "ok": True}))
+        return
     lay = make_layers(1, dev)[0]
     if case == "dec":
         x = synth.make_tokens(1, H, seed=3, device=dev)
@@ -425,7 +439,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=128)
-    ap.add_argument("--profile-case", choices=["gu", "dn", "dec", "ep"], default=None,
+    ap.add_argument("--profile-case", choices=["gu", "dn", "dec", "ep", "w8"], default=None,
                     help="run only a small case for ncu captures (see profile_case)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

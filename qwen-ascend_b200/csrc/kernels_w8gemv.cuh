@@ -28,7 +28,17 @@ FNX_DEV float ld_shared_cluster_f32(uint32_t addr) {
 
 inline size_t w8a16_gemv_smem(int MT, int K) {
     const int Kc = K / W8V_CL;
-    return sizeof(float) * ((size_t)MT * Kc + (size_t)8 * MT * W8V_COLS + (size_t)MT * W8V_COLS);
+    return sizeof(uint16_t) * (size_t)MT * Kc + sizeof(float) * ((size_t)8 * MT * W8V_COLS + (size_t)MT * W8V_COLS);
+}
+
+// two signed bytes (bytes b and b+1 of w, already xor 0x80) -> their exact values as bf16x2
+FNX_DEV uint32_t i8pair_bf16x2(uint32_t wx, int b) {
+    // 0x4B0000uu = 2^23 + u as fp32; minus 2^23 + 128 leaves the signed value exactly
+    const float lo = __int_as_float(__byte_perm(wx, 0x4B000000u, 0x7640 + b)) - 8388736.0f;
+    const float hi = __int_as_float(__byte_perm(wx, 0x4B000000u, 0x7641 + b)) - 8388736.0f;
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
 }
 
 // grid (ceil(N / 128), 8), cluster (1, 8, 1), 256 threads.  MT: tokens padded to 1/2/4/8/16.
@@ -39,16 +49,17 @@ __global__ void __launch_bounds__(256, 2) w8a16_gemv_kernel(const bf16* __restri
                                                             int M, int K, int N, int gs) {
     extern __shared__ float sm[];
     const int Kc = K / W8V_CL;
-    float* xs = sm;                                   // [MT][Kc]
-    float* red = xs + MT * Kc;                        // [8 warps][MT][128]
-    float* cpart = red + 8 * MT * W8V_COLS;           // [MT][128]: this CTA's eighth
+    uint16_t* xs = reinterpret_cast<uint16_t*>(sm);                 // [MT][Kc] bf16 bits
+    float* red = sm + (MT * Kc + 1) / 2;                              // [8 warps][MT][128]
+    float* cpart = red + 8 * MT * W8V_COLS;                           // [MT][128]: this CTA's eighth
     const int crank = (int)cluster_rank();
     const int n0 = blockIdx.x * W8V_COLS;
     const int k0 = crank * Kc;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const unsigned short* xb = reinterpret_cast<const unsigned short*>(x);
     for (int i = threadIdx.x; i < MT * Kc; i += blockDim.x) {
         const int m = i / Kc, kk = i - m * Kc;
-        xs[i] = m < M ? bf2f(x[(long long)m * K + k0 + kk]) : 0.f;
+        xs[i] = m < M ? xb[(long long)m * K + k0 + kk] : (uint16_t)0;
     }
     __syncthreads();
 
@@ -61,8 +72,14 @@ __global__ void __launch_bounds__(256, 2) w8a16_gemv_kernel(const bf16* __restri
     for (int m = 0; m < MT; ++m)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[m][c] = 0.f;
-    int g_cur = -1;
-    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    // the scale group and where it ends (no division per row)
+    int g = (k0 + r0) / gs;
+    int g_end = (g + 1) * gs - k0;                    // first row (CTA-relative) of the next group
+    uint32_t s01 = 0, s23 = 0;
+    if (ok) {
+        const uint2 sv = __ldg(reinterpret_cast<const uint2*>(sc + (long long)g * N + col));
+        s01 = sv.x; s23 = sv.y;
+    }
     constexpr int RB = 8;                             // rows per batch of loads in flight
     for (int rb = 0; rb < rpw; rb += RB) {
         uint32_t q[RB];
@@ -75,25 +92,25 @@ __global__ void __launch_bounds__(256, 2) w8a16_gemv_kernel(const bf16* __restri
         for (int i = 0; i < RB; ++i) {
             if (rb + i >= rpw) break;                 // warp-uniform: rows past this warp's share
             const int kr = r0 + rb + i;               // row within the CTA's eighth
-            const int g = (k0 + kr) / gs;
-            if (g != g_cur) {                         // warp-uniform
-                g_cur = g;
+            if (kr >= g_end) {                        // warp-uniform
+                ++g;
+                g_end += gs;
                 if (ok) {
                     const uint2 sv = __ldg(reinterpret_cast<const uint2*>(sc + (long long)g * N + col));
-                    s[0] = bf_lo(sv.x); s[1] = bf_hi(sv.x); s[2] = bf_lo(sv.y); s[3] = bf_hi(sv.y);
+                    s01 = sv.x; s23 = sv.y;
                 }
             }
-            float wv[4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int qi = (int)(signed char)(q[i] >> (8 * c));
-                wv[c] = round_bf(__fmul_rn((float)qi, s[c]));     // bf16(q * s): the product is exact in fp32
-            }
+            const uint32_t qx = q[i] ^ 0x80808080u;
+            const uint32_t w01 = bmul2(i8pair_bf16x2(qx, 0), s01);      // bf16(q * s), exact rounding
+            const uint32_t w23 = bmul2(i8pair_bf16x2(qx, 2), s23);
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
-                const float xv = xs[m * Kc + kr];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) acc[m][c] = __fmaf_rn(wv[c], xv, acc[m][c]);
+                const uint32_t xv = (uint32_t)xs[m * Kc + kr];
+                const uint32_t x2 = xv | (xv << 16);
+                fma_bf_lo(acc[m][0], w01, x2);
+                fma_bf_hi(acc[m][1], w01, x2);
+                fma_bf_lo(acc[m][2], w23, x2);
+                fma_bf_hi(acc[m][3], w23, x2);
             }
         }
     }

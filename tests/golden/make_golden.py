@@ -1,13 +1,13 @@
 """Generate golden vectors by running the reference's own Python code on CPU.
 
-Run in the build container, where the reference tree is mounted (default
-``/root/reference``, or ``$FNX_REFERENCE``)::
+Run where the reference tree is available (its location in ``$FNX_REFERENCE``, or the
+build container's mount by default)::
 
     python tests/golden/make_golden.py
 
 The reference imports ``torch_npu`` at module load; a stub module is injected whose
-three closed CANN operators (``npu_weight_quant_batchmatmul``, ``npu_grouped_matmul``,
-``npu_swiglu``) are restated on CPU by the oracle.  Everything else -- ``FnLayer._moe``
+closed CANN operators (``npu_weight_quant_batchmatmul``, ``npu_grouped_matmul``,
+``npu_swiglu``, ``npu_convert_weight_to_int4pack``) are restated on CPU by the oracle.  Everything else -- ``FnLayer._moe``
 routing / permutation / inverse / combine fallbacks, ``ExpW4._wcat/_scat``, ``ExpQ``
 packing and torch dequant + bmm, ``DenseW8`` layout, ``QW`` torch dequant and
 ``W4GemvOp.to_v2_layout`` -- is the reference's unmodified code.
