@@ -80,7 +80,10 @@ __global__ void __launch_bounds__(256, 2) w8a16_gemv_kernel(const bf16* __restri
         const uint2 sv = __ldg(reinterpret_cast<const uint2*>(sc + (long long)g * N + col));
         s01 = sv.x; s23 = sv.y;
     }
-    constexpr int RB = 8;                             // rows per batch of loads in flight
+#ifndef FNX_W8V_RB
+#define FNX_W8V_RB 8
+#endif
+    constexpr int RB = FNX_W8V_RB;                    // rows per batch of loads in flight
     for (int rb = 0; rb < rpw; rb += RB) {
         uint32_t q[RB];
 #pragma unroll
