@@ -87,6 +87,37 @@ def repack_v2o(v2o: np.ndarray, K: int) -> torch.Tensor:
     return pack_int4pack(q.transpose(1, 2)).permute(1, 0, 2).contiguous()
 
 
+def expq_deq(v2o: torch.Tensor, s8: torch.Tensor, base: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    """The selected experts of an LQP artifact dequantised, bf16 ``[k, N, K]``:
+    ``bf16((n' - 8) * bf16(bf16(s8[e, n, k // gs]) * bf16(base[e, n])))`` -- ``ExpQ._deq_v2``
+    (``fnx/engine.py:503-565``, default flags) with its lo/hi halves put back in k order."""
+    K = v2o.shape[2] * 2
+    q = torch.from_numpy(unpack_v2o(v2o.index_select(0, idx).numpy(), K))       # [k, N, K]
+    k, N = q.shape[0], q.shape[1]
+    G = s8.shape[-1]
+    s = s8.index_select(0, idx).to(BF16) * base.index_select(0, idx).to(BF16).unsqueeze(-1)
+    return (q.to(BF16).view(k, N, G, K // G) * s.unsqueeze(-1)).reshape(k, N, K)
+
+
+def expq_halves(w: torch.Tensor):
+    """``[k, N, K]`` -> the ``(wlo, whi)`` pair ``_deq_v2`` returns: k in ``[128s, 128s+64)`` and
+    ``[128s+64, 128s+128)`` of every 128-block, each ``[k, N, K/2]``."""
+    k, N, K = w.shape
+    v = w.view(k, N, K // 128, 2, 64)
+    return v[..., 0, :].reshape(k, N, K // 2), v[..., 1, :].reshape(k, N, K // 2)
+
+
+def expq_matmul(xb: torch.Tensor, v2o: torch.Tensor, s8: torch.Tensor, base: torch.Tensor, idx: torch.Tensor,
+                acc: torch.dtype = torch.float64) -> torch.Tensor:
+    """``ExpQ.matmul`` (``fnx/engine.py:567-572``): row j of ``xb [k, 1, K]`` times expert
+    ``idx[j]`` -> bf16 ``[k, N]``.  The reference adds two bf16 GEMMs over the lo/hi halves
+    (``_gemm2``, ``fnx/engine.py:772-776``), rounding three times; as a specification the
+    oracle accumulates exactly and rounds once (as :func:`w4a16_matmul`)."""
+    w = expq_deq(v2o, s8, base, idx)
+    x = xb.reshape(w.shape[0], w.shape[2])
+    return torch.einsum("jk,jnk->jn", x.to(acc), w.to(acc)).to(F32).to(BF16)
+
+
 def to_expert_major(w4_kmajor: torch.Tensor) -> torch.Tensor:
     """``[K, E, N/8] -> [E, K, N/8]``: the byte-exact transpose of ``tools/repack_w4_em.py:16``."""
     return w4_kmajor.permute(1, 0, 2).contiguous()

@@ -4,6 +4,8 @@ Mirrors the reference's MoE/quant section of ``fnx/engine.py``:
 
 * ``ExpW4``  (reference ``fnx/engine.py:619-753``): int4pack experts + bf16 group scales;
   ``apply`` / ``apply_diag`` / ``apply_grouped`` run the tcgen05 grouped GEMM.
+* ``ExpQ``   (reference ``fnx/engine.py:411-616``): experts from int4 values or straight from
+  the LQP ``v2o`` artifact; ``matmul`` runs the same grouped GEMM per selected expert.
 * ``DenseW8`` (reference ``fnx/engine.py:297-384``): int8 ``[K, N]`` + bf16 ``[G, N]``
   scales, N-concatenation by ``merge``; calls run the W8A16 kernels.
 * ``MoELayer`` (reference ``FnLayer._moe``, ``fnx/engine.py:1782-1930``): shared expert,
@@ -176,6 +178,74 @@ class ExpW4:
         out = torch.empty(x.shape[0], self.N, dtype=BF16, device=x.device)
         return _grouped_w4(x.to(BF16).contiguous(), self.tiles(), group_ends.contiguous(), out, E=self.E,
                            M=x.shape[0], K=self.K, Nw=self.N, epilogue=EPI_PLAIN)
+
+
+def _values_to_v2o(q):
+    """int8 ``[E, N, K]`` values in [-8, 7] -> the LQP ``v2o`` bytes ``[E, N, K/2]`` (byte
+    ``64s+j`` = ``W[128s+j] + 8`` low | ``W[128s+64+j] + 8`` high), on q's device."""
+    E, N, K = q.shape
+    v = (q.to(torch.int16) + 8).to(torch.uint8).view(E, N, K // 128, 2, 64)
+    return (v[..., 0, :] | (v[..., 1, :] << 4)).reshape(E, N, K // 2).contiguous()
+
+
+class ExpQ:
+    """Experts given as int4 values or as the LQP artifact (reference ``ExpQ``,
+    ``fnx/engine.py:411-616``): ``ExpQ(q, s, gs, packed=True, base=None)`` with ``q`` int8
+    ``[E, N, K]`` in [-8, 7] and scales ``s [E, N, K/gs]`` (times ``base [E, N]`` when given),
+    or ``ExpQ.from_packed(qv2, s8, base, dev)`` straight from the artifact's offset-binary
+    ``v2o [E, N, K/2]``, int8 ``s8 [E, N, G]`` and fp16 ``base [E, N]``.  The real weight is
+    ``bf16(q * bf16(bf16(s) * bf16(base)))`` as in ``_deq_v2`` (``fnx/engine.py:503-565``).
+
+    ``matmul(xb, idx)``: row j of ``xb [k, 1, K]`` times expert ``idx[j]`` -> bf16 ``[k, N]``.
+    The reference dequantises the selected experts with torch ops and adds two bf16 GEMMs over
+    the lo/hi halves of every 128-k block (``_gemm2``, ``fnx/engine.py:772-776``).  Here the
+    values are repacked once on the GPU into the W4A16 tile blocks and every call is one
+    fp32-accumulated tcgen05 GEMM rounded once, so results agree with the reference's within
+    the floating-point tolerance, not bit for bit; no dequantised weight is ever stored.
+    ``packed`` is accepted for signature compatibility (storage is always 4-bit)."""
+
+    def __init__(self, q, s, gs, packed=True, base=None):
+        _lib.require_cuda(q, s)
+        self.gs, self.K, self.N = gs, q.shape[-1], q.shape[1]
+        if self.K % 128:
+            raise ValueError(f"ExpQ: K={self.K} is not a multiple of 128")
+        self.packed, self.dev = True, q.device
+        self._init(_values_to_v2o(q), s, base)
+
+    def _init(self, v2o, s, base):
+        sc = s.to(BF16)
+        if base is not None:
+            sc = sc * base.to(BF16).unsqueeze(-1)
+        w4 = repack_v2o(v2o, self.K, expert_major=True)
+        self.w = ExpW4.from_scales(w4, sc.permute(0, 2, 1).contiguous(), self.gs)
+        self.w.tiles()
+        self.w.w4 = self.w._scales = None           # the tile blocks carry both
+
+    @classmethod
+    def from_packed(cls, qv2, s8, base, dev):
+        """``fnx/engine.py:478-501``: ``gs`` is inferred from the artifact (``K / G``)."""
+        o = cls.__new__(cls)
+        o.dev = torch.device(dev)
+        o.N, o.K = qv2.shape[1], qv2.shape[2] * 2
+        if o.K % 128:
+            raise ValueError(f"ExpQ: K={o.K} is not a multiple of 128")
+        o.gs, o.packed = o.K // s8.shape[-1], True
+        v2o = qv2.to(o.dev)
+        _lib.require_cuda(v2o)
+        o._init(v2o, s8.to(o.dev), None if base is None else base.to(o.dev))
+        return o
+
+    def matmul(self, xb, idx):
+        x = xb.reshape(-1, self.K)
+        idx = idx.to(self.dev)
+        if x.shape[0] != idx.numel():
+            raise ValueError(f"ExpQ.matmul: {x.shape[0]} rows for {idx.numel()} expert ids")
+        return self.w.apply_diag(x, idx)
+
+    def to_host_offload(self):
+        """Host offload is not part of this build (weights stay in HBM); returns False, as the
+        reference does when there is nothing to offload."""
+        return False
 
 
 class DenseW8:

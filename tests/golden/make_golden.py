@@ -354,6 +354,29 @@ def golden_v2o():
     print("v2o saved", flush=True)
 
 
+def golden_expq_packed():
+    """``ExpQ.from_packed`` (``fnx/engine.py:478-501``) on random LQP tensors and its ``matmul``
+    (``_deq_v2`` + ``_gemm2``, ``fnx/engine.py:503-572,772-776``), default flags: the torch
+    dequant path built straight from the artifact, at 64- and 128-wide scale groups.  The
+    dequantised lo/hi halves are kept as SHA-256 digests, the products in full."""
+    E = ref_engine(synth.CFG1)
+    rng = np.random.Generator(np.random.PCG64(31))
+    nE, N, K = 3, 256, 384
+    idx = torch.tensor([2, 0, 2, 1])                    # a repeated expert, one left out
+    cases = {}
+    for gs in (64, 128):
+        v2o = torch.from_numpy(rng.integers(0, 256, size=(nE, N, K // 2), dtype=np.uint8))
+        s8 = torch.from_numpy(rng.integers(1, 128, size=(nE, N, K // gs), dtype=np.int8))
+        base = torch.from_numpy((np.abs(rng.standard_normal((nE, N))) * 1e-3 + 1e-4).astype(np.float16))
+        xb = torch.from_numpy(rng.standard_normal((idx.numel(), 1, K), dtype=np.float32)).to(torch.bfloat16)
+        q = E.ExpQ.from_packed(v2o, s8, base, "cpu")
+        wlo, whi = q._deq_v2(idx)
+        y = q.matmul(xb, idx)
+        cases[f"g{gs}"] = dict(v2o=v2o, s8=s8, base=base, xb=xb, y=y, wlo_sha=sha(wlo), whi_sha=sha(whi))
+    torch.save(dict(K=K, N=N, E=nE, idx=idx, cases=cases), HERE / "expq_packed.pt")
+    print("expq_packed saved", flush=True)
+
+
 def golden_inject():
     """``inject`` (``fnx/engine.py:859-877``, the torch path) on random bf16 tensors at the
     reference's production width (H=2560, HC=4): ``hyper + y * inj`` broadcast over branches."""
@@ -407,6 +430,7 @@ if __name__ == "__main__":
     if "expq" in which:
         golden_expq("cfg1_expq", synth.CFG1, T=64, seed=0, xseed=1)
         golden_expq("pin_expq_decode", PIN, T=1, seed=11, xseed=13)
+        golden_expq_packed()
     if "decode" in which:
         golden_decode("cfg2_decode", synth.CFG2, seed=2, xseed=3)
     if "reduce" in which:

@@ -117,3 +117,17 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setenv("FNX_B200_SO", str(tmp_path / "missing.so"))
     with pytest.raises(OSError):
         _lib.lib()
+
+
+def test_expq_value_packer_matches_artifact(golden):
+    """ExpQ(q, ...) turns int4 values into the LQP v2o bytes before the GPU repack: the
+    packer reproduces the reference's artifact bytes from their unpacked values, and a
+    CPU-resident ExpQ is refused (no CPU path)."""
+    import torch
+    import oracle as O
+    from fnx.engine import ExpQ, _values_to_v2o
+    g = golden("v2o")
+    q = torch.from_numpy(O.unpack_v2o(g["v2o"].numpy(), g["K"])).to(torch.int8)
+    assert torch.equal(_values_to_v2o(q), g["v2o"])
+    with pytest.raises(RuntimeError):
+        ExpQ(q, torch.ones(q.shape[0], q.shape[1], g["K"] // 64, dtype=torch.int8), 64)

@@ -229,6 +229,27 @@ def test_expw4_from_lqp():
     assert O.within_tolerance(got, ref), O.tolerance_report(got, ref)
 
 
+@pytest.mark.parametrize("gs", [64, 128])
+def test_expq_from_packed_golden(golden, gs):
+    """ExpQ.from_packed + matmul (the reference's ``ExpQ`` surface) on the reference's own
+    fixture: within tolerance of the reference's three-rounding torch result, and close to
+    the oracle's once-rounded specification; the value constructor gives the same bits."""
+    from fnx.engine import ExpQ
+    g = golden("expq_packed")
+    c, idx = g["cases"][f"g{gs}"], g["idx"]
+    q = ExpQ.from_packed(c["v2o"], c["s8"], c["base"], DEV)
+    assert (q.K, q.N, q.gs) == (g["K"], g["N"], gs)
+    got = q.matmul(c["xb"].to(DEV), idx).cpu()
+    r = O.tolerance_report(got, c["y"])
+    assert r["rel_l2"] < 5e-3 and r["max_abs_norm"] < 2e-2, r
+    spec = O.expq_matmul(c["xb"], c["v2o"], c["s8"], c["base"], idx)
+    r = O.tolerance_report(got, spec)
+    assert r["rel_l2"] < 1e-3 and r["exact_fraction"] > 0.9, r
+    vals = torch.from_numpy(O.unpack_v2o(c["v2o"].numpy(), g["K"])).to(torch.int8)
+    q2 = ExpQ(vals.to(DEV), c["s8"].to(DEV), gs, base=c["base"].to(DEV))
+    assert bits_equal(q2.matmul(c["xb"].to(DEV), idx.to(DEV)), got)
+    assert q.to_host_offload() is False
+
 
 def _ordered(t):
     b = t.contiguous().view(torch.int16).to(torch.int32)

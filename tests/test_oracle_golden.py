@@ -184,6 +184,21 @@ def test_v2o_unpack_and_repack_pinned(golden):
     assert torch.equal(back.transpose(1, 2).to(torch.int32), torch.from_numpy(q))
 
 
+@pytest.mark.parametrize("gs", [64, 128])
+def test_expq_packed_pinned(golden, gs):
+    """``ExpQ.from_packed`` + ``matmul`` (the reference's torch dequant path straight from the
+    LQP tensors): the oracle's dequantised halves equal the reference's bit for bit, and its
+    once-rounded product agrees with the reference's three-rounding one within tolerance."""
+    g = golden("expq_packed")
+    c = g["cases"][f"g{gs}"]
+    w = O.expq_deq(c["v2o"], c["s8"], c["base"], g["idx"])
+    wlo, whi = O.expq_halves(w)
+    assert sha(wlo) == c["wlo_sha"] and sha(whi) == c["whi_sha"]
+    y = O.expq_matmul(c["xb"], c["v2o"], c["s8"], c["base"], g["idx"])
+    r = O.tolerance_report(y, c["y"])
+    assert r["rel_l2"] < 5e-3 and r["max_abs_norm"] < 2e-2, r
+
+
 def test_inject_pinned(golden):
     """The oracle's inject equals the reference's ``inject`` (torch path) bit for bit."""
     g = golden("inject")
