@@ -132,7 +132,10 @@ def max_over_ranks(v, world):
 
 
 # ------------------------------------------------------------------ CPU baseline
-def cpu_baseline(sample_tokens=128, seed=0):
+_CPU_INPUTS = {}
+
+
+def cpu_baseline(sample_tokens=512, seed=0):
     """The oracle port of the reference's torch path on this host's cores: one MoE layer
     over ``sample_tokens`` tokens with fp32 accumulation, dequantising every touched
     expert inside the timed region (as the reference's ExpQ path does per call)."""
@@ -140,8 +143,10 @@ def cpu_baseline(sample_tokens=128, seed=0):
     from fnx import synth
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    t = synth.make_layer(synth.CFG2, seed=seed)
-    x = synth.make_tokens(sample_tokens, H, seed=seed + 1)
+    key = (seed, sample_tokens)
+    if key not in _CPU_INPUTS:                  # synthesis stays outside the timed region
+        _CPU_INPUTS[key] = (synth.make_layer(synth.CFG2, seed=seed), synth.make_tokens(sample_tokens, H, seed=seed + 1))
+    t, x = _CPU_INPUTS[key]
     t0 = time.perf_counter()
     L = O.Layer(t, GS)
     O.moe_forward(x, L, K_TOP, acc=torch.float32)
@@ -438,7 +443,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-decode", action="store_true")
-    ap.add_argument("--cpu-sample", type=int, default=128)
+    ap.add_argument("--cpu-sample", type=int, default=512,
+                    help="tokens per CPU-baseline sample (both arms; about 10 s of CPU work per sample)")
     ap.add_argument("--profile-case", choices=["gu", "dn", "dec", "ep", "w8"], default=None,
                     help="run only a small case for ncu captures (see profile_case)")
     args = ap.parse_args()

@@ -712,35 +712,38 @@ FNX_API int fnx_moe_grouped_w4_rows(const void* act, long long ld_act, long long
 }
 
 namespace {
-template <int MT>
+template <int MT, int CL>
 int w8_gemv_launch_t(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int gs,
                      cudaStream_t st) {
-    const size_t smem = w8a16_gemv_smem(MT, K);
+    const size_t smem = w8a16_gemv_smem(MT, CL, K);
     static bool configured = false;
-    if (!configured) {
-        if (cudaFuncSetAttribute(w8a16_gemv_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
+    if (!configured) {                                // once, for the largest K accepted (8192)
+        if (cudaFuncSetAttribute(w8a16_gemv_kernel<MT, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)w8a16_gemv_smem(MT, CL, 8192)) != cudaSuccess)
             return FNX_ELAUNCH;
         configured = true;
     }
-    if (smem > (size_t)227 * 1024) return FNX_ESHAPE;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = W8V_CL;
+    attr[0].val.clusterDim.y = CL;
     attr[0].val.clusterDim.z = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((N + W8V_COLS - 1) / W8V_COLS), W8V_CL, 1);
+    cfg.gridDim = dim3((unsigned)((N + W8V_COLS - 1) / W8V_COLS), CL, 1);
     cfg.blockDim = dim3(256, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, w8a16_gemv_kernel<MT>, (const bf16*)x, (const int8_t*)w8t, (const bf16*)sc, (bf16*)y,
-                           M, K, N, gs) != cudaSuccess)
+    if (cudaLaunchKernelEx(&cfg, w8a16_gemv_kernel<MT, CL>, (const bf16*)x, (const int8_t*)w8t, (const bf16*)sc,
+                           (bf16*)y, M, K, N, gs) != cudaSuccess)
         return FNX_ELAUNCH;
     return launch_rc();
 }
+
+#ifndef FNX_W8V_CL16
+#define FNX_W8V_CL16 4
+#endif
 
 bool w8_gemv_enabled() {
     static int v = -1;
@@ -759,11 +762,11 @@ FNX_API int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void*
         w8_gemv_enabled()) {
         const int gs = K / G;
         cudaStream_t st = (cudaStream_t)stream;
-        if (M == 1) return w8_gemv_launch_t<1>(x, w8t, sc, y, M, K, N, gs, st);
-        if (M == 2) return w8_gemv_launch_t<2>(x, w8t, sc, y, M, K, N, gs, st);
-        if (M <= 4) return w8_gemv_launch_t<4>(x, w8t, sc, y, M, K, N, gs, st);
-        if (M <= 8) return w8_gemv_launch_t<8>(x, w8t, sc, y, M, K, N, gs, st);
-        return w8_gemv_launch_t<16>(x, w8t, sc, y, M, K, N, gs, st);
+        if (M == 1) return w8_gemv_launch_t<1, 8>(x, w8t, sc, y, M, K, N, gs, st);
+        if (M == 2) return w8_gemv_launch_t<2, 8>(x, w8t, sc, y, M, K, N, gs, st);
+        if (M <= 4) return w8_gemv_launch_t<4, 8>(x, w8t, sc, y, M, K, N, gs, st);
+        if (M <= 8) return w8_gemv_launch_t<8, 8>(x, w8t, sc, y, M, K, N, gs, st);
+        return w8_gemv_launch_t<16, FNX_W8V_CL16>(x, w8t, sc, y, M, K, N, gs, st);
     }
     GemmParams p{};
     p.act = (const bf16*)x; p.ld_act = K; p.w = w8t; p.scales = (const bf16*)sc; p.out = (bf16*)y; p.ld_out = N;

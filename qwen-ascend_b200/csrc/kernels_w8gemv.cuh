@@ -7,17 +7,21 @@
 // of a cluster hold the 8 eighths of K for the same columns and reduce them through
 // distributed shared memory in a fixed order, so the sum is deterministic and needs no
 // global workspace.  Each weight is dequantised once to the exactly rounded bf16(q * s) the
-// reference's antiquant produces, then multiplied into every token's fp32 accumulators.
+// reference's antiquant produces, then multiplied into every token's fp32 accumulators.  The
+// tokens are staged in shared memory as fp32, token-minor, so one 16-byte load serves four
+// tokens and each product is a plain fp32 FMA.  The first two batches of weight rows are
+// requested before the tokens are staged, and every batch is requested one batch ahead of its
+// use.
 #pragma once
 #include "fnx_common.cuh"
+
+#ifndef FNX_W8V_DB
+#define FNX_W8V_DB 1
+#endif
 
 namespace fnx {
 
 constexpr int W8V_COLS = 128;      // output columns per CTA
-#ifndef FNX_W8V_CL
-#define FNX_W8V_CL 8
-#endif
-constexpr int W8V_CL = FNX_W8V_CL; // CTAs per cluster (K split)
 constexpr int W8V_MAXM = 16;
 
 FNX_DEV float ld_shared_cluster_f32(uint32_t addr) {
@@ -26,9 +30,9 @@ FNX_DEV float ld_shared_cluster_f32(uint32_t addr) {
     return v;
 }
 
-inline size_t w8a16_gemv_smem(int MT, int K) {
-    const int Kc = K / W8V_CL;
-    return sizeof(uint16_t) * (size_t)MT * Kc + sizeof(float) * ((size_t)8 * MT * W8V_COLS + (size_t)MT * W8V_COLS);
+inline size_t w8a16_gemv_smem(int MT, int CL, int K) {
+    const int Kc = K / CL;
+    return sizeof(float) * ((size_t)Kc * MT + (size_t)8 * MT * W8V_COLS + (size_t)MT * W8V_COLS);
 }
 
 // two signed bytes (bytes b and b+1 of w, already xor 0x80) -> their exact values as bf16x2
@@ -41,37 +45,37 @@ FNX_DEV uint32_t i8pair_bf16x2(uint32_t wx, int b) {
     return r;
 }
 
-// grid (ceil(N / 128), 8), cluster (1, 8, 1), 256 threads.  MT: tokens padded to 1/2/4/8/16.
-// Needs K % 64 == 0, N % 4 == 0, K % gs == 0.
-template <int MT>
-__global__ void __launch_bounds__(256, 2) w8a16_gemv_kernel(const bf16* __restrict__ x, const int8_t* __restrict__ w,
-                                                            const bf16* __restrict__ sc, bf16* __restrict__ y,
-                                                            int M, int K, int N, int gs) {
+// grid (ceil(N / 128), CL), cluster (1, CL, 1), 256 threads.  MT: tokens padded to 1/2/4/8/16.
+// Needs K % 64 == 0, N % 4 == 0, K % gs == 0.  Up to 8 tokens a CTA fits in 80 registers, so
+// three CTAs share an SM and the N = 5120 grid (320 CTAs) runs in one wave.
+template <int MT, int CL>
+__global__ void __launch_bounds__(256, (MT <= 8 ? 3 : 2))
+    w8a16_gemv_kernel(const bf16* __restrict__ x, const int8_t* __restrict__ w, const bf16* __restrict__ sc,
+                      bf16* __restrict__ y, int M, int K, int N, int gs) {
     extern __shared__ float sm[];
-    const int Kc = K / W8V_CL;
-    uint16_t* xs = reinterpret_cast<uint16_t*>(sm);                 // [MT][Kc] bf16 bits
-    float* red = sm + (MT * Kc + 1) / 2;                              // [8 warps][MT][128]
+    const int Kc = K / CL;
+    float* xs = sm;                                                   // [Kc][MT] tokens as fp32
+    float* red = sm + Kc * MT;                                        // [8 warps][MT][128]
     float* cpart = red + 8 * MT * W8V_COLS;                           // [MT][128]: this CTA's eighth
     const int crank = (int)cluster_rank();
     const int n0 = blockIdx.x * W8V_COLS;
     const int k0 = crank * Kc;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const unsigned short* xb = reinterpret_cast<const unsigned short*>(x);
-    for (int i = threadIdx.x; i < MT * Kc; i += blockDim.x) {
-        const int m = i / Kc, kk = i - m * Kc;
-        xs[i] = m < M ? xb[(long long)m * K + k0 + kk] : (uint16_t)0;
-    }
-    __syncthreads();
-
     const int col = n0 + lane * 4;
     const bool ok = col < N;
     const int rpw = Kc / 8;                           // rows per warp (K % 64 == 0)
     const int r0 = warp * rpw;
-    float acc[MT][4];
+#ifndef FNX_W8V_RB
+#define FNX_W8V_RB 8
+#endif
+    constexpr int RB = FNX_W8V_RB;                    // rows per batch of loads
+    auto load = [&](uint32_t (&q)[RB], int rb) {
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[m][c] = 0.f;
+        for (int i = 0; i < RB; ++i) {
+            const long long k = k0 + r0 + rb + i;
+            q[i] = (ok && rb + i < rpw) ? __ldg(reinterpret_cast<const unsigned int*>(w + k * N + col)) : 0u;
+        }
+    };
     // the scale group and where it ends (no division per row)
     int g = (k0 + r0) / gs;
     int g_end = (g + 1) * gs - k0;                    // first row (CTA-relative) of the next group
@@ -80,17 +84,26 @@ __global__ void __launch_bounds__(256, 2) w8a16_gemv_kernel(const bf16* __restri
         const uint2 sv = __ldg(reinterpret_cast<const uint2*>(sc + (long long)g * N + col));
         s01 = sv.x; s23 = sv.y;
     }
-#ifndef FNX_W8V_RB
-#define FNX_W8V_RB 8
+    // the first weight rows are requested before the tokens are staged
+    uint32_t qa[RB], qb[RB];
+    load(qa, 0);
+#if FNX_W8V_DB
+    load(qb, RB);
 #endif
-    constexpr int RB = FNX_W8V_RB;                    // rows per batch of loads in flight
-    for (int rb = 0; rb < rpw; rb += RB) {
-        uint32_t q[RB];
+
+    const unsigned short* xb = reinterpret_cast<const unsigned short*>(x);
+    for (int i = threadIdx.x; i < MT * Kc; i += blockDim.x) {
+        const int m = i / Kc, kk = i - m * Kc;
+        xs[kk * MT + m] = m < M ? __uint_as_float((uint32_t)xb[(long long)m * K + k0 + kk] << 16) : 0.f;
+    }
+    __syncthreads();
+
+    float acc[MT][4];
 #pragma unroll
-        for (int i = 0; i < RB; ++i) {
-            const long long k = k0 + r0 + rb + i;
-            q[i] = (ok && rb + i < rpw) ? __ldg(reinterpret_cast<const unsigned int*>(w + k * N + col)) : 0u;
-        }
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[m][c] = 0.f;
+    auto consume = [&](const uint32_t (&q)[RB], int rb) {
 #pragma unroll
         for (int i = 0; i < RB; ++i) {
             if (rb + i >= rpw) break;                 // warp-uniform: rows past this warp's share
@@ -106,17 +119,48 @@ __global__ void __launch_bounds__(256, 2) w8a16_gemv_kernel(const bf16* __restri
             const uint32_t qx = q[i] ^ 0x80808080u;
             const uint32_t w01 = bmul2(i8pair_bf16x2(qx, 0), s01);      // bf16(q * s), exact rounding
             const uint32_t w23 = bmul2(i8pair_bf16x2(qx, 2), s23);
+            // bf16 -> fp32 is exact, so an fp32 FMA of the two gives the product exactly and
+            // rounds the sum once
+            const float wf[4] = {__uint_as_float(w01 << 16), __uint_as_float(w01 & 0xffff0000u),
+                                 __uint_as_float(w23 << 16), __uint_as_float(w23 & 0xffff0000u)};
+            const float* xr = xs + kr * MT;
+            if constexpr (MT >= 4) {
 #pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                const uint32_t xv = (uint32_t)xs[m * Kc + kr];
-                const uint32_t x2 = xv | (xv << 16);
-                fma_bf_lo(acc[m][0], w01, x2);
-                fma_bf_hi(acc[m][1], w01, x2);
-                fma_bf_lo(acc[m][2], w23, x2);
-                fma_bf_hi(acc[m][3], w23, x2);
+                for (int m = 0; m < MT; m += 4) {
+                    const float4 xv = *reinterpret_cast<const float4*>(xr + m);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        acc[m][c] = __fmaf_rn(wf[c], xv.x, acc[m][c]);
+                        acc[m + 1][c] = __fmaf_rn(wf[c], xv.y, acc[m + 1][c]);
+                        acc[m + 2][c] = __fmaf_rn(wf[c], xv.z, acc[m + 2][c]);
+                        acc[m + 3][c] = __fmaf_rn(wf[c], xv.w, acc[m + 3][c]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    const float xv = xr[m];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) acc[m][c] = __fmaf_rn(wf[c], xv, acc[m][c]);
+                }
             }
         }
+    };
+#if FNX_W8V_DB
+    // two batches in flight: the next one is requested before the current one is used
+    for (int rb = 0; rb < rpw; rb += 2 * RB) {
+        consume(qa, rb);
+        if (rb + 2 * RB < rpw) load(qa, rb + 2 * RB);
+        if (rb + RB < rpw) consume(qb, rb + RB);
+        if (rb + 3 * RB < rpw) load(qb, rb + 3 * RB);
     }
+#else
+    for (int rb = 0; rb < rpw; rb += RB) {
+        if (rb) load(qa, rb);
+        consume(qa, rb);
+    }
+    (void)qb;
+#endif
     // the 8 warps of the CTA, in order
 #pragma unroll
     for (int m = 0; m < MT; ++m)
@@ -135,7 +179,7 @@ __global__ void __launch_bounds__(256, 2) w8a16_gemv_kernel(const bf16* __restri
         for (int i = threadIdx.x; i < MT * W8V_COLS; i += blockDim.x) {
             float v = cpart[i];
 #pragma unroll
-            for (int r = 1; r < W8V_CL; ++r) v += ld_shared_cluster_f32(mapa_rank(cpart + i, (uint32_t)r));
+            for (int r = 1; r < CL; ++r) v += ld_shared_cluster_f32(mapa_rank(cpart + i, (uint32_t)r));
             const int m = i / W8V_COLS, n = n0 + (i - m * W8V_COLS);
             if (m < M && n < N) y[(long long)m * N + n] = f2bf(v);
         }
