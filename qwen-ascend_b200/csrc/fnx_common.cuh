@@ -112,6 +112,19 @@ FNX_DEV uint32_t bmul2(uint32_t a, uint32_t b) {
     return r;
 }
 
+// int8 weights without integer-to-float conversions: byte b of wx (a word of int8 values with
+// their sign bits flipped, w ^ 0x80808080) as its exact fp32 value.  0x4B0000uu is 2^23 + u as
+// fp32; taking 2^23 + 128 from it leaves u - 128, the signed byte.
+FNX_DEV float i8x_f32(uint32_t wx, int b) {
+    return __int_as_float(__byte_perm(wx, 0x4B000000u, 0x7640 + b)) - 8388736.0f;
+}
+// two exact small integers as bf16x2 (lo in the low half)
+FNX_DEV uint32_t ints_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
 // acc += bf16 a * bf16 b, product and sum in fp32 (mixed-precision FMA, sm_100).
 FNX_DEV void fma_bf_lo(float& acc, uint32_t a2, uint32_t b2) {
     asm("{\n .reg .b16 a, b, u;\n mov.b32 {a, u}, %1;\n mov.b32 {b, u}, %2;\n"

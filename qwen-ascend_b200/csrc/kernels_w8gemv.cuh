@@ -37,12 +37,7 @@ inline size_t w8a16_gemv_smem(int MT, int CL, int K) {
 
 // two signed bytes (bytes b and b+1 of w, already xor 0x80) -> their exact values as bf16x2
 FNX_DEV uint32_t i8pair_bf16x2(uint32_t wx, int b) {
-    // 0x4B0000uu = 2^23 + u as fp32; minus 2^23 + 128 leaves the signed value exactly
-    const float lo = __int_as_float(__byte_perm(wx, 0x4B000000u, 0x7640 + b)) - 8388736.0f;
-    const float hi = __int_as_float(__byte_perm(wx, 0x4B000000u, 0x7641 + b)) - 8388736.0f;
-    uint32_t r;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-    return r;
+    return ints_bf16x2(i8x_f32(wx, b), i8x_f32(wx, b + 1));
 }
 
 // grid (ceil(N / 128), CL), cluster (1, CL, 1), 256 threads.  MT: tokens padded to 1/2/4/8/16.
