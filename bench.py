@@ -135,7 +135,7 @@ def max_over_ranks(v, world):
 _CPU_INPUTS = {}
 
 
-def cpu_baseline(sample_tokens=2048, seed=0):
+def cpu_baseline(sample_tokens=T_PREFILL, seed=0):
     """The oracle port of the reference's torch path on this host's cores: one MoE layer
     over ``sample_tokens`` tokens with fp32 accumulation, dequantising every touched
     expert inside the timed region (as the reference's ExpQ path does per call)."""
@@ -443,8 +443,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-decode", action="store_true")
-    ap.add_argument("--cpu-sample", type=int, default=2048,
-                    help="tokens per CPU-baseline sample (both arms; about 10 s of CPU work per sample)")
+    ap.add_argument("--cpu-sample", type=int, default=T_PREFILL,
+                    help="tokens per CPU-baseline sample (both arms; default the whole T=4096 batch)")
     ap.add_argument("--profile-case", choices=["gu", "dn", "dec", "ep", "w8"], default=None,
                     help="run only a small case for ncu captures (see profile_case)")
     args = ap.parse_args()

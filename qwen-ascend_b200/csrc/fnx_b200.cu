@@ -755,11 +755,37 @@ bool w8_gemv_enabled() {
 }
 }  // namespace
 
-FNX_API int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G,
-                           void* stream) {
+namespace {
+// Split-K factor of the tcgen05 W8 GEMM: with one token tile the launch has only N / 128 tiles,
+// too few for 148 SMs.  Each tile streams its k-blocks one stage after another, so the cost is
+// modelled as (rounds of tiles over the SMs) x (k-blocks per tile), the smaller split winning a
+// tie; the fp32 partials are kept no larger than the weights (s * M * 4 <= K).
+int w8_ksplit(int M, int K, int N) {
+    const int KB = K / G_BK;
+    const long long tiles = (long long)((M + G_BN - 1) / G_BN) * (N / G_BM);
+    const long long nsm = num_sms();
+    int best = 1;
+    long long best_cost = (tiles + nsm - 1) / nsm * KB;
+    for (int s = 2; s <= 16; ++s) {
+        if (KB % s || KB / s < 2 || (long long)s * M * 4 > K) continue;
+        const long long cost = (tiles * s + nsm - 1) / nsm * (KB / s);
+        if (cost < best_cost) {
+            best = s;
+            best_cost = cost;
+        }
+    }
+    return best;
+}
+
+bool w8_gemv_route(int M, int K, int N, int G) {
+    return M >= 1 && M <= W8V_MAXM && G >= 1 && K % G == 0 && K % 64 == 0 && K <= 8192 && N % 4 == 0 &&
+           w8_gemv_enabled();
+}
+
+int w8a16_gemm_impl(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G, void* ws,
+                    size_t ws_bytes, void* stream) {
     // M <= 16: the weight-streaming GEMV (cluster K split); larger M: the tcgen05 GEMM
-    if (M >= 1 && M <= W8V_MAXM && G >= 1 && K % G == 0 && K % 64 == 0 && K <= 8192 && N % 4 == 0 &&
-        w8_gemv_enabled()) {
+    if (w8_gemv_route(M, K, N, G)) {
         const int gs = K / G;
         cudaStream_t st = (cudaStream_t)stream;
         if (M == 1) return w8_gemv_launch_t<1, 8>(x, w8t, sc, y, M, K, N, gs, st);
@@ -777,7 +803,39 @@ FNX_API int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void*
     if (rc) return rc;
     if (N % 8) return FNX_ESHAPE;
     if (M == 0) return FNX_OK;
+    if (ws) {
+        const int s = w8_ksplit(M, K, N);
+        if (s > 1) {
+            if (!aligned16(ws)) return FNX_EALIGN;
+            if (ws_bytes < (size_t)s * M * N * sizeof(float)) return FNX_EWORKSPACE;
+            p.ksplit = s;
+            p.partial = (float*)ws;
+            const int r = gemm_launch(GEMM_W8, EPI_PLAIN, p, (cudaStream_t)stream);
+            if (r) return r;
+            const long long n4 = (long long)M * (N / 4);
+            splitk_reduce_kernel<<<grid_for(n4, 256), 256, 0, (cudaStream_t)stream>>>(p.partial, p.out, p.ld_out, M,
+                                                                                      N, s);
+            return launch_rc();
+        }
+    }
     return gemm_launch(GEMM_W8, EPI_PLAIN, p, (cudaStream_t)stream);
+}
+}  // namespace
+
+FNX_API int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G,
+                           void* stream) {
+    return w8a16_gemm_impl(x, w8t, sc, y, M, K, N, G, nullptr, 0, stream);
+}
+
+FNX_API size_t fnx_w8a16_gemm_workspace(int M, int K, int N, int G) {
+    if (M < 1 || K < G_BK || K % G_BK || N < G_BM || N % G_BM || w8_gemv_route(M, K, N, G)) return 0;
+    const int s = w8_ksplit(M, K, N);
+    return s > 1 ? (size_t)s * M * N * sizeof(float) : 0;
+}
+
+FNX_API int fnx_w8a16_gemm_ws(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G,
+                              void* ws, size_t ws_bytes, void* stream) {
+    return w8a16_gemm_impl(x, w8t, sc, y, M, K, N, G, ws, ws_bytes, stream);
 }
 
 FNX_API int fnx_bf16_gemm_nt(const void* x, long long ld_x, const void* w, void* y, long long ld_y, int M, int K, int N,

@@ -90,7 +90,14 @@ struct GemmParams {
     int m_tiles;                // tiles along the feature dimension
     int shared_e;               // EPI_SWIGLU_MIXED: the shared expert's index
     bf16* const* out_rows;      // EPI_PLAIN: row r goes to out_rows[r] (e.g. a peer's buffer); null: out
+    // split-K (GEMM_W8, EPI_PLAIN): ksplit > 1 cuts K into ksplit equal ranges, each a tile of
+    // its own; the epilogue writes fp32 partials [ksplit][M][Nw] to `partial` and a separate
+    // pass sums them in split order (deterministic).  0 or 1: no split.
+    int ksplit;
+    float* partial;
 };
+
+FNX_DEV int gemm_ksplit(const GemmParams& p) { return p.ksplit > 1 ? p.ksplit : 1; }
 
 // destination of output row `row` (a 16-byte aligned row of Nw bf16 when out_rows is set)
 FNX_DEV bf16* out_row(const GemmParams& p, long long row) {
@@ -111,6 +118,7 @@ struct GemmSmem {
 
 struct TileInfo {
     int e, m, row0, nrows;
+    int ks;            // split-K range of the single-CTA kernel (0 without a split)
 };
 
 FNX_DEV bool decode_tile(const GemmSmem& S, const GemmParams& p, int tile, TileInfo& ti) {
@@ -121,10 +129,13 @@ FNX_DEV bool decode_tile(const GemmSmem& S, const GemmParams& p, int tile, TileI
         if (S.tile_start[mid] <= tile) lo = mid; else hi = mid;
     }
     const int e = lo;
+    const int ksplit = gemm_ksplit(p);
     const int local = tile - S.tile_start[e];
-    const int chunk = local / p.m_tiles;
+    ti.ks = local % ksplit;                        // the K ranges of one output tile are adjacent
+    const int l2 = local / ksplit;
+    const int chunk = l2 / p.m_tiles;
     ti.e = e;
-    ti.m = local % p.m_tiles;
+    ti.m = l2 % p.m_tiles;
     const long long begin = min((long long)p.M, (long long)(p.ends ? (e ? p.ends[e - 1] : 0) : 0));
     const long long end = min((long long)p.M, (long long)(p.ends ? p.ends[e] : p.M));
     ti.row0 = (int)begin + chunk * G_BN;
@@ -256,6 +267,37 @@ FNX_DEV void epilogue_chunk(const GemmParams& p, const TileInfo& ti, int r, int 
     }
 }
 
+// Split-K epilogue (EPI_PLAIN): this K range's fp32 sums for 16 tokens of accumulator lane r,
+// into partial[ks][row][feature] (summed in split order by splitk_reduce_kernel).
+template <bool PERM>
+FNX_DEV void epilogue_partial(const GemmParams& p, const TileInfo& ti, int r, int n0, const uint32_t (&v)[16]) {
+    const int f = ti.m * G_BM + (PERM ? lane_feature<EPI_PLAIN>(r) : r);
+    const int lim = ti.nrows - n0;
+    float* o = p.partial + ((long long)ti.ks * p.M + ti.row0 + n0) * p.Nw + f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+        if (i < lim) o[(long long)i * p.Nw] = __uint_as_float(v[i]);
+}
+
+// y[row, f] = bf16(sum over s = 0..ksplit-1 of partial[s][row][f]) in that order; 4 features per
+// thread (Nw % 4 == 0).
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ partial, bf16* __restrict__ out,
+                                                            long long ld_out, int M, int Nw, int ksplit) {
+    const long long n4 = (long long)M * (Nw / 4);
+    const long long plane = (long long)M * Nw;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        const long long row = i / (Nw / 4);
+        const int c = (int)(i - row * (Nw / 4)) * 4;
+        float4 a = __ldcs(reinterpret_cast<const float4*>(partial + row * Nw + c));
+        for (int s = 1; s < ksplit; ++s) {
+            const float4 b = __ldcs(reinterpret_cast<const float4*>(partial + s * plane + row * Nw + c));
+            a.x = __fadd_rn(a.x, b.x); a.y = __fadd_rn(a.y, b.y); a.z = __fadd_rn(a.z, b.z); a.w = __fadd_rn(a.w, b.w);
+        }
+        const uint2 o = make_uint2(pack_bf2(a.x, a.y), pack_bf2(a.z, a.w));
+        *reinterpret_cast<uint2*>(out + row * ld_out + c) = o;
+    }
+}
+
 // Staged form for tile-ordered rows (the W4 kernels): the warp's 32 accumulator lanes x 16
 // tokens go through a 1 KB shared buffer so that global stores are 16-byte vectors along
 // the feature dimension (one token row segment per 4 or 2 lanes) instead of 2-byte
@@ -365,7 +407,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                 const long long begin = min((long long)p.M, (long long)(p.ends ? (e ? p.ends[e - 1] : 0) : 0));
                 const long long end = min((long long)p.M, (long long)(p.ends ? p.ends[e] : p.M));
                 const long long cnt = end > begin ? end - begin : 0;   // malformed ends -> no tiles
-                n = (int)((cnt + G_BN - 1) / G_BN) * p.m_tiles;
+                n = (int)((cnt + G_BN - 1) / G_BN) * p.m_tiles * gemm_ksplit(p);
             }
             int incl = n;
 #pragma unroll
@@ -392,6 +434,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
     tc_fence_after();
     const uint32_t tmem = S.tmem_base;
     const int KB = p.K / G_BK;
+    const int KBt = KB / gemm_ksplit(p);        // k-blocks per tile (the host checks KB % ksplit == 0)
 
     if (warp == 0 || warp >= 16) {
         // ------------------------------------------------ B loaders
@@ -429,11 +472,11 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
             }
             const int npad = (ti.nrows + 15) & ~15;
             const int c = lane & 7;               // 16-byte chunk of the 128-byte row slice
-            for (int kb = 0; kb < KB; ++kb, ++it) {
+            for (int kb = 0; kb < KBt; ++kb, ++it) {
                 const int s = it % C::STAGES;
                 if (!mbar_wait(&S.empty[s], ((it / C::STAGES) & 1) ^ 1)) { S.abort = 1; ok = false; break; }
                 const uint32_t bt = smem_u32(b_tiles + s * G_B_BYTES);
-                const bf16* kbase = p.act + kb * G_BK + c * 8;
+                const bf16* kbase = p.act + (ti.ks * KBt + kb) * G_BK + c * 8;
                 // one instruction copies 4 whole 128-byte row slices (8 lanes per row), so each
                 // touches 4 cache lines instead of 32
 #pragma unroll
@@ -454,7 +497,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer (whole warp, one elected lane issues)
         const int my_tiles = S.total_tiles > (int)blockIdx.x ? (S.total_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-        const int total_stages = my_tiles * KB;
+        const int total_stages = my_tiles * KBt;
         int j = 0;
         uint32_t pack = 0;          // lane L: (token rows / 16 - 1) of tiles 8L .. 8L+7 of the epoch
         for (int i = 0; i < my_tiles; ++i) {
@@ -474,7 +517,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
             const int ab = i & 1;
             const uint32_t idesc = idesc_bf16_f32(G_BM, (int)n16 * 16);
             const uint32_t d = tmem + ab * G_BN;
-            for (int kb = 0; kb < KB; ++kb, ++j) {
+            for (int kb = 0; kb < KBt; ++kb, ++j) {
                 const int s = j % C::STAGES;
                 named_bar_sync(G_BAR_FULL, 64);
                 tc_fence_after();
@@ -490,7 +533,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                                       sdesc_kmajor_sw128(b0 + kk * 32), idesc, (kb | kk) ? 1u : 0u);
                     }
                     umma_commit(&S.empty[s]);
-                    if (kb == KB - 1) umma_commit(&S.acc_full[ab]);
+                    if (kb == KBt - 1) umma_commit(&S.acc_full[ab]);
                 }
                 __syncwarp();
                 if (j + 1 < total_stages) named_bar_arrive(G_BAR_TAKEN, 64);
@@ -520,12 +563,12 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                                   bytes, &S.raw_full[os], stream_once);
                     }
                 } else if (MODE == GEMM_BF16) {
-                    for (int kb = 0; kb < KB; ++kb, ++it) {
+                    for (int kb = 0; kb < KBt; ++kb, ++it) {
                         const int s = it % C::STAGES;
                         if (!mbar_wait(&S.empty[s], ((it / C::STAGES) & 1) ^ 1)) { ok = false; break; }
                         mbar_arrive_expect_tx(&S.a_full[s], G_A_BYTES);
-                        tma_load_2d(smem_u32(a_tiles + s * G_A_BYTES), &p.tmap_a, &S.a_full[s], kb * G_BK,
-                                    ti.e * p.Nw + ti.m * G_BM);
+                        tma_load_2d(smem_u32(a_tiles + s * G_A_BYTES), &p.tmap_a, &S.a_full[s],
+                                    (ti.ks * KBt + kb) * G_BK, ti.e * p.Nw + ti.m * G_BM);
                     }
                 }
                 if (!ok) { S.abort = 1; break; }
@@ -546,7 +589,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                 const bool ok = mbar_wait(&S.acc_empty[ab], ((i >> 1) & 1) ^ 1);
                 if (!__all_sync(0xffffffffu, ok)) { dead = true; S.abort = 1; }
             }
-            for (int kb = 0; kb < KB; ++kb, ++j) {
+            for (int kb = 0; kb < KBt; ++kb, ++j) {
                 const int s = j % C::STAGES;
                 const uint32_t ph = (j / C::STAGES) & 1;
                 dead = __any_sync(0xffffffffu, dead || S.abort);
@@ -574,7 +617,10 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                 uint32_t v[16];
                 tmem_ld16(tmem + ((uint32_t)(e4 * 32) << 16) + ab * G_BN + n0, v);
                 tmem_ld_wait();
-                epilogue_chunk<EPI, MODE == GEMM_W8>(p, ti, r, n0, v);
+                if (EPI == EPI_PLAIN && p.ksplit > 1)
+                    epilogue_partial<MODE == GEMM_W8>(p, ti, r, n0, v);
+                else
+                    epilogue_chunk<EPI, MODE == GEMM_W8>(p, ti, r, n0, v);
             }
             tc_fence_before();
             __syncwarp();
@@ -590,7 +636,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
         for (int tile = blockIdx.x; ok && !S.abort; tile += gridDim.x) {
             TileInfo ti;
             if (!decode_tile(S, p, tile, ti)) break;
-            for (int kb = 0; kb < KB; ++kb, ++it) {
+            for (int kb = 0; kb < KBt; ++kb, ++it) {
                 const int s = it % C::STAGES;
                 if (MODE == GEMM_W4) {
                     const int os = op % G_R_OPS;
@@ -618,7 +664,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                     }
                 } else if ((it & 1) == grp) {
                     if (!mbar_wait(&S.empty[s], ((it / C::STAGES) & 1) ^ 1)) { ok = false; break; }
-                    produce_a_w8<EPI>(p, ti, kb, a_tiles + s * G_A_BYTES, t);
+                    produce_a_w8<EPI>(p, ti, ti.ks * KBt + kb, a_tiles + s * G_A_BYTES, t);
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&S.a_full[s]);

@@ -67,6 +67,8 @@ SIGNATURES = {
     "fnx_w4_tiles_bytes": ([I] * 3, SZ),
     "fnx_repack_w4_tiles": ([P] * 3 + [I] * 5 + [P], I),
     "fnx_w8a16_gemm": ([P] * 4 + [I] * 4 + [P], I),
+    "fnx_w8a16_gemm_workspace": ([I] * 4, SZ),
+    "fnx_w8a16_gemm_ws": ([P] * 4 + [I] * 4 + [P, SZ, P], I),
     "fnx_bf16_gemm_nt": ([P, LL, P, P, LL, I, I, I, P], I),
     "fnx_moe_decode_workspace": ([I] * 5, SZ),
     "fnx_moe_decode_w4": ([P] * 10 + [I] * 5 + [P, SZ, P], I),

@@ -277,9 +277,14 @@ class DenseW8:
         sh = x.shape
         x2 = (x if x.dtype == BF16 else x.to(BF16)).reshape(-1, sh[-1]).contiguous()
         _lib.require_cuda(x2, self.w8t)
-        y = torch.empty(x2.shape[0], self.N, dtype=BF16, device=x2.device)
-        rc = _lib.lib().fnx_w8a16_gemm(x2.data_ptr(), self.w8t.data_ptr(), self.sc.data_ptr(), y.data_ptr(),
-                                       x2.shape[0], self.K, self.N, self.sc.shape[0], _lib.stream(x2.device))
+        L = _lib.lib()
+        M, G = x2.shape[0], self.sc.shape[0]
+        y = torch.empty(M, self.N, dtype=BF16, device=x2.device)
+        # split-K partials for mid-sized M (stream-ordered by the caching allocator)
+        nws = L.fnx_w8a16_gemm_workspace(M, self.K, self.N, G)
+        ws = torch.empty(nws, dtype=torch.uint8, device=x2.device) if nws else None
+        rc = L.fnx_w8a16_gemm_ws(x2.data_ptr(), self.w8t.data_ptr(), self.sc.data_ptr(), y.data_ptr(), M, self.K,
+                                 self.N, G, _lib.ptr(ws), nws, _lib.stream(x2.device))
         _lib.check(rc, "W8A16 GEMM")
         return y if x.dim() <= 2 else y.view(*sh[:-1], self.N)
 

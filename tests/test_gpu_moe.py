@@ -312,3 +312,43 @@ def test_moe_inject_fused(T):
     got = layer.moe_inject(x, hyper, inj)
     ref = native_inject.inject(hyper, inj, layer(x).view(T, 1, H))
     assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("M", [17, 48, 128, 200])
+@pytest.mark.parametrize("G", [1, 16])
+def test_w8a16_split_k(M, G):
+    """fnx_w8a16_gemm_ws: where one token tile leaves the tensor-core GEMM too few tiles, K is
+    split into fp32 partials summed in split order.  Split and unsplit entry points both match
+    the oracle; the split result repeats bit for bit; a short workspace is refused."""
+    from fnx import _lib as fl
+    L = fl.lib()
+    K, N = 1024, 640
+    g = torch.Generator().manual_seed(M * 7 + G)
+    q = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int32).to(torch.int8)
+    sc = (torch.randn(N, G, generator=g).abs() * 0.01).to(BF16)
+    x = torch.randn(M, K, generator=g).to(BF16)
+    from fnx.engine import DenseW8
+    w = DenseW8(q.to(DEV), sc.to(DEV))
+    xd = x.to(DEV)
+    nws = L.fnx_w8a16_gemm_workspace(M, K, N, G)
+    assert (nws > 0) == (M <= 128)                 # 5 feature tiles: split while the partials stay small
+    ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=DEV)
+    ref = O.dense_w8(x, w.w8t.cpu(), w.sc.cpu())
+    outs = []
+    for split in (True, True, False):
+        y = torch.full((M, N), float("nan"), dtype=BF16, device=DEV)
+        if split:
+            rc = L.fnx_w8a16_gemm_ws(xd.data_ptr(), w.w8t.data_ptr(), w.sc.data_ptr(), y.data_ptr(), M, K, N, G,
+                                     ws.data_ptr(), nws, fl.stream(xd.device))
+        else:
+            rc = L.fnx_w8a16_gemm(xd.data_ptr(), w.w8t.data_ptr(), w.sc.data_ptr(), y.data_ptr(), M, K, N, G,
+                                  fl.stream(xd.device))
+        assert rc == 0
+        outs.append(y.cpu())
+        assert O.within_tolerance(outs[-1], ref), O.tolerance_report(outs[-1], ref)
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    assert torch.equal(w(xd).cpu().view(torch.int16), outs[0].view(torch.int16))    # DenseW8 takes the split
+    if nws:
+        rc = L.fnx_w8a16_gemm_ws(xd.data_ptr(), w.w8t.data_ptr(), w.sc.data_ptr(), y.data_ptr(), M, K, N, G,
+                                 ws.data_ptr(), nws - 4, fl.stream(xd.device))
+        assert rc == -5
