@@ -238,9 +238,10 @@ int fnx_moe_grouped_w4_rows(const void* act, long long ld_act, long long act_row
 int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G, void* stream);
 
 /* fnx_w8a16_gemm with a caller workspace: where one token tile leaves the GEMM too few tiles for
- * the SMs (M up to about 128), K is split and the fp32 partials [s, M, N] go to ws, then are
- * summed in split order (deterministic).  ws: 16-byte aligned, at least
- * fnx_w8a16_gemm_workspace(M, K, N, G) bytes (0: no split for this shape; ws may be NULL). */
+ * the SMs (M from 9 to about 128), K is split and the fp32 partials [s, M, N] go to ws, then are
+ * summed in split order (deterministic); M <= 8 stays on the weight-streaming GEMV.  ws:
+ * 16-byte aligned, at least fnx_w8a16_gemm_workspace(M, K, N, G) bytes (0: no split for this
+ * shape; ws may be NULL). */
 size_t fnx_w8a16_gemm_workspace(int M, int K, int N, int G);
 int fnx_w8a16_gemm_ws(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G, void* ws,
                       size_t ws_bytes, void* stream);

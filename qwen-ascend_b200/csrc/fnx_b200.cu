@@ -777,15 +777,26 @@ int w8_ksplit(int M, int K, int N) {
     return best;
 }
 
-bool w8_gemv_route(int M, int K, int N, int G) {
-    return M >= 1 && M <= W8V_MAXM && G >= 1 && K % G == 0 && K % 64 == 0 && K <= 8192 && N % 4 == 0 &&
-           w8_gemv_enabled();
+// Shapes the tcgen05 W8 GEMM takes (gemm_check's rules for one group of W8 weights).
+bool w8_gemm_shape(int K, int N, int G) {
+    return G >= 1 && K % G == 0 && K >= G_BK && K % G_BK == 0 && (K / G) % G_BK == 0 && N >= G_BM && N % G_BM == 0;
+}
+
+// The weight-streaming GEMV takes M <= 16 on the plain entry point.  With a workspace the
+// split-K GEMM is faster from 9 tokens on (the GEMV's 16-token form: 31 us at K=2048, N=5120;
+// the split GEMM: about 18 us), so there the GEMV keeps M <= 8, and M <= 16 only for shapes the
+// GEMM does not take.
+bool w8_gemv_route(int M, int K, int N, int G, bool split_path) {
+    const bool ok = M >= 1 && M <= W8V_MAXM && G >= 1 && K % G == 0 && K % 64 == 0 && K <= 8192 && N % 4 == 0 &&
+                    w8_gemv_enabled();
+    if (!ok) return false;
+    return !split_path || M <= 8 || !w8_gemm_shape(K, N, G);
 }
 
 int w8a16_gemm_impl(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G, void* ws,
-                    size_t ws_bytes, void* stream) {
-    // M <= 16: the weight-streaming GEMV (cluster K split); larger M: the tcgen05 GEMM
-    if (w8_gemv_route(M, K, N, G)) {
+                    size_t ws_bytes, bool split_path, void* stream) {
+    // small M: the weight-streaming GEMV (cluster K split); larger M: the tcgen05 GEMM
+    if (w8_gemv_route(M, K, N, G, split_path)) {
         const int gs = K / G;
         cudaStream_t st = (cudaStream_t)stream;
         if (M == 1) return w8_gemv_launch_t<1, 8>(x, w8t, sc, y, M, K, N, gs, st);
@@ -824,18 +835,18 @@ int w8a16_gemm_impl(const void* x, const void* w8t, const void* sc, void* y, int
 
 FNX_API int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G,
                            void* stream) {
-    return w8a16_gemm_impl(x, w8t, sc, y, M, K, N, G, nullptr, 0, stream);
+    return w8a16_gemm_impl(x, w8t, sc, y, M, K, N, G, nullptr, 0, false, stream);
 }
 
 FNX_API size_t fnx_w8a16_gemm_workspace(int M, int K, int N, int G) {
-    if (M < 1 || K < G_BK || K % G_BK || N < G_BM || N % G_BM || w8_gemv_route(M, K, N, G)) return 0;
+    if (M < 1 || !w8_gemm_shape(K, N, G) || w8_gemv_route(M, K, N, G, true)) return 0;
     const int s = w8_ksplit(M, K, N);
     return s > 1 ? (size_t)s * M * N * sizeof(float) : 0;
 }
 
 FNX_API int fnx_w8a16_gemm_ws(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G,
                               void* ws, size_t ws_bytes, void* stream) {
-    return w8a16_gemm_impl(x, w8t, sc, y, M, K, N, G, ws, ws_bytes, stream);
+    return w8a16_gemm_impl(x, w8t, sc, y, M, K, N, G, ws, ws_bytes, true, stream);
 }
 
 FNX_API int fnx_bf16_gemm_nt(const void* x, long long ld_x, const void* w, void* y, long long ld_y, int M, int K, int N,

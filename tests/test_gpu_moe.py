@@ -314,7 +314,7 @@ def test_moe_inject_fused(T):
     assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
 
 
-@pytest.mark.parametrize("M", [17, 48, 128, 200])
+@pytest.mark.parametrize("M", [12, 17, 48, 128, 200])
 @pytest.mark.parametrize("G", [1, 16])
 def test_w8a16_split_k(M, G):
     """fnx_w8a16_gemm_ws: where one token tile leaves the tensor-core GEMM too few tiles, K is
