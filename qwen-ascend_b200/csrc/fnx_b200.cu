@@ -26,14 +26,24 @@ using namespace fnx;
 
 namespace {
 
+// Launch set-up (function attributes, occupancy, SM counts) belongs to a device, and one process
+// may drive several GPUs (layers placed on different devices), so it is cached per device.
+constexpr int FNX_MAX_DEVICES = 64;
+inline int current_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= FNX_MAX_DEVICES) dev = 0;
+    return dev;
+}
+
 int num_sms() {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    static int sms[FNX_MAX_DEVICES] = {};
+    const int dev = current_device();
+    if (!sms[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        sms[dev] = n;
     }
-    return sms;
+    return sms[dev];
 }
 
 inline int launch_rc() {
@@ -143,12 +153,13 @@ int make_map_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dt, int e
 template <int MODE, int EPI>
 int gemm_launch_t(GemmParams& p, cudaStream_t st) {
     const size_t smem = grouped_gemm_smem_bytes(MODE);
-    static bool configured = false;
-    if (!configured) {
+    static bool configured[FNX_MAX_DEVICES] = {};
+    const int dev = current_device();
+    if (!configured[dev]) {
         if (cudaFuncSetAttribute(grouped_gemm_kernel<MODE, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem) != cudaSuccess)
             return FNX_ELAUNCH;
-        configured = true;
+        configured[dev] = true;
     }
     int rc = FNX_OK;
     if (MODE == GEMM_BF16) {
@@ -165,7 +176,8 @@ int gemm_launch_t(GemmParams& p, cudaStream_t st) {
 template <int EPI>
 int gemm_pair_launch_t(GemmParams& p, cudaStream_t st) {
     const size_t smem = grouped_gemm_pair_smem_bytes();
-    static int clusters = 0;
+    static int clusters_of[FNX_MAX_DEVICES] = {};
+    int& clusters = clusters_of[current_device()];
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -410,20 +422,21 @@ int permute_launch(const void* idx, void* order, void* inverse, void* ends, void
         return launch_rc();
     }
     const size_t ssm = permute_scatter_smem(E);
-    static size_t ssm_set = 48 * 1024;
-    if (ssm > ssm_set) {
+    static bool ssm_set[FNX_MAX_DEVICES] = {};
+    const int dev = current_device();
+    if (ssm > 48 * 1024 && !ssm_set[dev]) {
         if (cudaFuncSetAttribute(permute_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)permute_scatter_smem(PERM_MAX_E)) != cudaSuccess)
             return FNX_ELAUNCH;
-        ssm_set = permute_scatter_smem(PERM_MAX_E);
+        ssm_set[dev] = true;
     }
     permute_hist_kernel<<<chunks, 256, E * sizeof(int), st>>>((const int64_t*)idx, n, n_dev, E, div, hist);
-    static bool scan_set = false;
-    if (!scan_set) {
+    static bool scan_set[FNX_MAX_DEVICES] = {};
+    if (!scan_set[dev]) {
         if (cudaFuncSetAttribute(permute_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)PERM_SCAN_SMEM) != cudaSuccess)
             return FNX_ELAUNCH;
-        scan_set = true;
+        scan_set[dev] = true;
     }
     permute_scan_kernel<<<1, 1024, permute_scan_smem(chunks, E), st>>>(hist, chunks, E, (int64_t*)ends,
                                                                        (int64_t*)counts, base);
@@ -716,12 +729,13 @@ template <int MT, int CL>
 int w8_gemv_launch_t(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int gs,
                      cudaStream_t st) {
     const size_t smem = w8a16_gemv_smem(MT, CL, K);
-    static bool configured = false;
-    if (!configured) {                                // once, for the largest K accepted (8192)
+    static bool configured[FNX_MAX_DEVICES] = {};
+    const int dev = current_device();
+    if (!configured[dev]) {                           // once per device, for the largest K accepted (8192)
         if (cudaFuncSetAttribute(w8a16_gemv_kernel<MT, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)w8a16_gemv_smem(MT, CL, 8192)) != cudaSuccess)
             return FNX_ELAUNCH;
-        configured = true;
+        configured[dev] = true;
     }
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -963,7 +977,8 @@ FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu,
     p.M = M; p.H = H; p.I = I; p.E = E; p.k = k; p.R = L.R; p.ks1 = L.ks1; p.ks2 = L.ks2;
     // one cooperative launch of every block that fits at once (work items wait for earlier
     // items of other blocks, so all blocks must be resident)
-    static int grid = 0;
+    static int grid_of[FNX_MAX_DEVICES] = {};
+    int& grid = grid_of[current_device()];
     if (!grid) {
         if (cudaFuncSetAttribute(decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM))
             return FNX_ELAUNCH;

@@ -352,3 +352,30 @@ def test_w8a16_split_k(M, G):
         rc = L.fnx_w8a16_gemm_ws(xd.data_ptr(), w.w8t.data_ptr(), w.sc.data_ptr(), y.data_ptr(), M, K, N, G,
                                  ws.data_ptr(), nws - 4, fl.stream(xd.device))
         assert rc == -5
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs in one process")
+def test_two_devices_one_process():
+    """One process driving two GPUs (layers placed on different devices): every kernel's launch
+    set-up is per device, so the second device runs the same prefill, decode and W8A16 paths
+    and, the kernels being deterministic, returns the same bits as the first."""
+    from fnx import _lib as fl
+    from fnx.engine import DenseW8, MoELayer
+    shape = synth.CFG1
+    g = torch.Generator().manual_seed(5)
+    q = torch.randint(-127, 128, (640, 1024), generator=g, dtype=torch.int32).to(torch.int8)
+    sc = (torch.randn(640, 1, generator=g).abs() * 0.01).to(BF16)
+    xw = {M: torch.randn(M, 1024, generator=g).to(BF16) for M in (1, 12, 300)}
+    res = []
+    for d in (0, 1):
+        dev = torch.device("cuda", d)
+        with torch.cuda.device(dev):
+            layer = MoELayer.from_synth(synth.make_layer(shape, seed=3, device=dev), shape)
+            out = [layer(synth.make_tokens(T, shape.H, seed=9, device=dev)).cpu() for T in (96, 2)]
+            w = DenseW8(q.to(dev), sc.to(dev))
+            out += [w(xw[M].to(dev)).cpu() for M in (1, 12, 300)]
+            torch.cuda.synchronize(dev)
+            assert fl.device_errors() == 0
+        res.append(out)
+    for a, b in zip(*res):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
