@@ -93,6 +93,22 @@ def test_workspace_sizes(lib):
     assert 0 < n1 < n16 < 64 << 20
 
 
+def test_w8_split_workspace_sizes(lib):
+    """The W8A16 split-K workspace: none where the GEMV serves (M <= 8) or where the GEMM has
+    enough tiles (M = 200), s * M * N fp32 partials with s dividing K/64 in between, none for
+    shapes the tensor-core GEMM does not take.  (Sizes only: nothing runs without a GPU; the
+    split chosen assumes the 148 SMs of a B200 when no device is visible.)"""
+    K, N = 2048, 5120
+    assert lib.fnx_w8a16_gemm_workspace(8, K, N, 1) == 0
+    assert lib.fnx_w8a16_gemm_workspace(200, K, N, 1) == 0
+    for M in (9, 16, 64, 128):
+        n = lib.fnx_w8a16_gemm_workspace(M, K, N, 1)
+        s, rem = divmod(n, M * N * 4)
+        assert rem == 0 and s > 1 and (K // 64) % s == 0 and s * M * 4 <= K, (M, n)
+    assert lib.fnx_w8a16_gemm_workspace(16, K, 648, 1) == 0       # N % 128: the GEMV keeps M <= 16
+    assert lib.fnx_w8a16_gemm_workspace(16, K, N, 64) == 0        # 32-wide scale groups: GEMV as well
+
+
 def test_python_wrappers_return_none_for_unsupported():
     import torch
     from fnx import expert_gather, moe_epilogue, post_ops, weighted_reduce
