@@ -304,17 +304,18 @@ def profile_case(case, dev):
     dec      four decode calls at M=1 (`-k regex:decode_fused -s 2 -c 1` takes the third);
     ep       three calls of the expert-parallel layer with the peer exchange on one rank
              (every kernel of the p2p path, the exchange kept on this GPU);
-    w8       four W8A16 projections at M=1 (K=2048, N=5120; `-k regex:w8a16 -s 2 -c 1`)."""
+    w8       four W8A16 projections at M=1 (K=2048, N=5120; `-k regex:w8a16 -s 2 -c 1`);
+    w8s      four at M=16, the split-K tensor-core GEMM and its reduce (`-s 4 -c 4` takes the last two)."""
     from fnx import synth
     from fnx.engine import EPI_PLAIN, EPI_SWIGLU_F32, _grouped_w4
-    if case == "w8":
+    if case in ("w8", "w8s"):
         from fnx.engine import DenseW8
         g = torch.Generator(device=dev)
         g.manual_seed(7)
         q = torch.randint(-127, 128, (5120, 2048), generator=g, device=dev, dtype=torch.int32).to(torch.int8)
         sc = (torch.randn(5120, 1, generator=g, device=dev).abs_() * 0.01).to(torch.bfloat16)
         w = DenseW8(q, sc)
-        x = torch.randn(1, 2048, generator=g, device=dev).to(torch.bfloat16)
+        x = torch.randn(1 if case == "w8" else 16, 2048, generator=g, device=dev).to(torch.bfloat16)
         for _ in range(4):
             w(x)
         torch.cuda.synchronize()
@@ -445,7 +446,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=T_PREFILL,
                     help="tokens per CPU-baseline sample (both arms; default the whole T=4096 batch)")
-    ap.add_argument("--profile-case", choices=["gu", "dn", "dec", "ep", "w8"], default=None,
+    ap.add_argument("--profile-case", choices=["gu", "dn", "dec", "ep", "w8", "w8s"], default=None,
                     help="run only a small case for ncu captures (see profile_case)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

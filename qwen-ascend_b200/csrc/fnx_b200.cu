@@ -780,7 +780,7 @@ int w8_ksplit(int M, int K, int N) {
     const long long nsm = num_sms();
     int best = 1;
     long long best_cost = (tiles + nsm - 1) / nsm * KB;
-    for (int s = 2; s <= 16; ++s) {
+    for (int s = 2; s <= SPLITK_MAX; ++s) {
         if (KB % s || KB / s < 2 || (long long)s * M * 4 > K) continue;
         const long long cost = (tiles * s + nsm - 1) / nsm * (KB / s);
         if (cost < best_cost) {
@@ -838,8 +838,12 @@ int w8a16_gemm_impl(const void* x, const void* w8t, const void* sc, void* y, int
             const int r = gemm_launch(GEMM_W8, EPI_PLAIN, p, (cudaStream_t)stream);
             if (r) return r;
             const long long n4 = (long long)M * (N / 4);
-            splitk_reduce_kernel<<<grid_for(n4, 256), 256, 0, (cudaStream_t)stream>>>(p.partial, p.out, p.ld_out, M,
-                                                                                      N, s);
+            const dim3 grid(grid_for(n4, 256));
+            cudaStream_t st = (cudaStream_t)stream;
+            if (s <= 2) splitk_reduce_kernel<2><<<grid, 256, 0, st>>>(p.partial, p.out, p.ld_out, M, N, s);
+            else if (s <= 4) splitk_reduce_kernel<4><<<grid, 256, 0, st>>>(p.partial, p.out, p.ld_out, M, N, s);
+            else if (s <= 8) splitk_reduce_kernel<8><<<grid, 256, 0, st>>>(p.partial, p.out, p.ld_out, M, N, s);
+            else splitk_reduce_kernel<SPLITK_MAX><<<grid, 256, 0, st>>>(p.partial, p.out, p.ld_out, M, N, s);
             return launch_rc();
         }
     }

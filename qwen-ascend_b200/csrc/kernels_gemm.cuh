@@ -280,7 +280,11 @@ FNX_DEV void epilogue_partial(const GemmParams& p, const TileInfo& ti, int r, in
 }
 
 // y[row, f] = bf16(sum over s = 0..ksplit-1 of partial[s][row][f]) in that order; 4 features per
-// thread (Nw % 4 == 0).
+// thread (Nw % 4 == 0), ksplit <= KMAX.  Every partial of a thread is requested before the first
+// is added, so the loads overlap instead of forming a chain; KMAX (2, 4, 8, 16: the smallest that
+// holds ksplit) keeps the registers to what the split needs.
+constexpr int SPLITK_MAX = 16;
+template <int KMAX>
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ partial, bf16* __restrict__ out,
                                                             long long ld_out, int M, int Nw, int ksplit) {
     const long long n4 = (long long)M * (Nw / 4);
@@ -288,10 +292,16 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
         const long long row = i / (Nw / 4);
         const int c = (int)(i - row * (Nw / 4)) * 4;
-        float4 a = __ldcs(reinterpret_cast<const float4*>(partial + row * Nw + c));
-        for (int s = 1; s < ksplit; ++s) {
-            const float4 b = __ldcs(reinterpret_cast<const float4*>(partial + s * plane + row * Nw + c));
-            a.x = __fadd_rn(a.x, b.x); a.y = __fadd_rn(a.y, b.y); a.z = __fadd_rn(a.z, b.z); a.w = __fadd_rn(a.w, b.w);
+        float4 b[KMAX];
+#pragma unroll
+        for (int s = 0; s < KMAX; ++s)
+            if (s < ksplit) b[s] = __ldcs(reinterpret_cast<const float4*>(partial + s * plane + row * Nw + c));
+        float4 a = b[0];
+#pragma unroll
+        for (int s = 1; s < KMAX; ++s) {
+            if (s >= ksplit) break;
+            a.x = __fadd_rn(a.x, b[s].x); a.y = __fadd_rn(a.y, b[s].y); a.z = __fadd_rn(a.z, b[s].z);
+            a.w = __fadd_rn(a.w, b[s].w);
         }
         const uint2 o = make_uint2(pack_bf2(a.x, a.y), pack_bf2(a.z, a.w));
         *reinterpret_cast<uint2*>(out + row * ld_out + c) = o;
