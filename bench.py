@@ -220,6 +220,15 @@ def bench_prefill(args, world, rank, dev):
 
     ep = None
     if world > 1:
+        # multi-GPU parity: this rank's tokens through the expert-parallel layer (graph replay)
+        # against the one-GPU layer holding all experts, bit for bit, on every rank
+        got = caps[0](xs[0]).clone()
+        ref = full[0].prefill(xs[0])
+        same = torch.tensor([1 if torch.equal(got.view(torch.int16), ref.view(torch.int16)) else 0],
+                            dtype=torch.int32, device=dev)
+        torch.distributed.all_reduce(same, op=torch.distributed.ReduceOp.MIN)
+        ep_bit_identical = bool(same.item())
+        del got, ref
         st = layers[(step[0] - 1) % nl].exchange_stats()
         t = torch.tensor([st["received_slots"], st["dispatch_rows"] + st["return_rows"]], dtype=torch.float64,
                          device=dev)
@@ -231,6 +240,7 @@ def bench_prefill(args, world, rank, dev):
               "exchange": "NVLink peer stores: token rows once per owner (dispatch kernel), per-slot down rows "
                           "written to the source by the down GEMM's epilogue; device-side count exchange, no host "
                           "sync",
+              "bit_identical_to_one_gpu": ep_bit_identical,
               "recv_rows_max_over_mean": round(float(tmax[0] / (tsum[0] / world)), 4),
               "nvlink_bytes_per_step_per_gpu_max": int(tmax[1] * row)}
 
@@ -251,8 +261,8 @@ def bench_prefill(args, world, rank, dev):
     roofline = {"kernel": "grouped_gemm_pair_kernel<SwiGLU> (routed gate/up)", "bound": "tensor",
                 "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(achieved / pk["bf16_tflops"], 4), "peak_source": f"{src} bf16 burst",
-                # dram__bytes_read.sum + dram__bytes_write.sum of this launch (587.6 + 8.1 MB),
-                # ncu capture of `bench.py --profile-case gu`, profiles/grouped_gemm_pair_gate_up_T4096.md
+                # dram__bytes_read.sum + dram__bytes_write.sum of this launch (587.6 + 8.1 MB) from one
+                # ncu capture of `bench.py --profile-case gu`
                 "traffic": 595.7e6, "traffic_unit": "B", "ms_per_launch": round(gu_ms, 4),
                 "algorithmic_flops_per_launch": gu_flops}
     layer_tflops = prefill_flops(T_PREFILL) / (ms * 1e-3) / 1e12
@@ -495,6 +505,7 @@ def main():
                 "data": "synthetic (seeded; shapes/distributions of the workload definition)",
                 "config": dict(config, parallelism=f"ep{world}" if world > 1 else "single GPU",
                                **({"expert_parallel": r["ep"]} if r["ep"] else {})),
+                **({"ep_bit_identical": r["ep"]["bit_identical_to_one_gpu"]} if r["ep"] else {}),
                 "clocks": r["clocks"], "e2e": r["e2e"], "gpu_launches": r["gpu_launches"],
                 "roofline": r["roofline"], "layer_tflops": round(r["layer_tflops"], 1), "decode": dec, "w8a16": w8,
                 "cpu_baseline": cpu}

@@ -807,8 +807,14 @@ bool w8_gemv_route(int M, int K, int N, int G, bool split_path) {
     return !split_path || M <= 8 || !w8_gemm_shape(K, N, G);
 }
 
+inline bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
 int w8a16_gemm_impl(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G, void* ws,
                     size_t ws_bytes, bool split_path, void* stream) {
+    // Both routes load x and the weights in 16-byte vectors, the scales as 8-byte pairs and
+    // store y as 8-byte quads (the split-K reduce): reject misaligned pointers before either
+    // route launches.
+    if (M > 0 && (!aligned16(x) || !aligned16(w8t) || !aligned8(sc) || !aligned8(y))) return FNX_EALIGN;
     // small M: the weight-streaming GEMV (cluster K split); larger M: the tcgen05 GEMM
     if (w8_gemv_route(M, K, N, G, split_path)) {
         const int gs = K / G;
@@ -950,7 +956,7 @@ DecodeLayout decode_layout(int M, int H, int I, int E, int k) {
 }  // namespace
 
 FNX_API size_t fnx_moe_decode_workspace(int M, int H, int I, int E, int k) {
-    if (M < 1 || M > DEC_MAX_M || H < 1 || I < 1 || E < 1 || k < 1) return 0;
+    if (M < 1 || M > DEC_MAX_M || H < 256 || I < 128 || E < 1 || k < 1) return 0;
     return decode_layout(M, H, I, E, k).total;
 }
 
@@ -962,7 +968,8 @@ FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu,
                               const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H,
                               int I, int E, int k, void* workspace, size_t ws_bytes, void* stream) {
     if (M < 1 || M > DEC_MAX_M || E < 1 || E > ROUTE_MAX_E || k < 1 || k > 32 || k > E) return FNX_EARG;
-    if (H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K || E > DEC_MAX_E) return FNX_ESHAPE;
+    if (H < 256 || I < 128 || H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K || E > DEC_MAX_E)
+        return FNX_ESHAPE;
     const DecodeLayout L = decode_layout(M, H, I, E, k);
     if (!workspace || ws_bytes < L.total) return FNX_EWORKSPACE;
     if (!aligned16(x) || !aligned16(router) || !aligned16(gu) || !aligned16(dn) || !aligned16(sh_gu) ||
@@ -1053,22 +1060,26 @@ namespace {
 // Device address of the scratch array for the current device.  In host code the array's
 // name is only a host-side stand-in, so the address is looked up once per device (with
 // that device current) and cached.
+// The cache has one slot per device, as the library's other per-device launch caches; host
+// threads that make their first calls at the same time store the same address (atomically).
 void* noalloc_scratch(int* rc) {
-    static void* addr[64] = {};
+    static void* addr[FNX_MAX_DEVICES] = {};
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= FNX_MAX_DEVICES) {
         *rc = FNX_ELAUNCH;
         return nullptr;
     }
-    if (!addr[dev]) {
+    void* cached = __atomic_load_n(&addr[dev], __ATOMIC_ACQUIRE);
+    if (!cached) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_fnx_noalloc_scratch) != cudaSuccess || p == nullptr) {
             *rc = FNX_ELAUNCH;
             return nullptr;
         }
-        addr[dev] = p;
+        __atomic_store_n(&addr[dev], p, __ATOMIC_RELEASE);
+        cached = p;
     }
-    return addr[dev];
+    return cached;
 }
 }  // namespace
 
@@ -1083,7 +1094,8 @@ FNX_API int fnx_moe_decode_w4_noalloc(const void* x, const void* router, const v
                                       const void* sh_gu, const void* sh_dn, const void* bias, void* out, void* w_out,
                                       void* idx_out, int M, int H, int I, int E, int k, void* stream) {
     if (M < 1 || M > DEC_MAX_M || E < 1 || E > ROUTE_MAX_E || k < 1 || k > 32 || k > E) return FNX_EARG;
-    if (H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K) {
+    if (H < 256 || I < 128 || H % 256 || I % 128) return FNX_ESHAPE;
+    if (H > DEC_MAX_K || I > DEC_MAX_K) {
         const DecodeLayout L0 = decode_layout(M, H, I, E, k);
         return L0.total > FNX_NOALLOC_SCRATCH_BYTES ? FNX_EWORKSPACE : FNX_ESHAPE;
     }

@@ -423,14 +423,20 @@ class MoELayer:
             return out
         return self.prefill(x2, inject=(hyper, inj))
 
-    def prefill(self, x, details=False, inject=None):
+    def prefill(self, x, details=False, inject=None, logits=None):
         """Grouped path (``fnx/engine.py:1815-1853``) for ``T`` tokens.  The routed and the shared
         expert share one grouped launch per projection; the per-call buffers of the extended
-        permutation are cached per token count (calls on one layer must not overlap)."""
+        permutation are cached per token count (calls on one layer must not overlap).
+        ``logits``: bf16 ``[T, >= E+1]`` router logits (columns ``[0, E)``) and shared-expert gate
+        (column ``E``) computed elsewhere, in place of this layer's router GEMM."""
         T, H, I, k, E = x.shape[0], self.H, self.I, self.k, self.E
         dev = x.device
         M = T * k
-        logits = self.logits(x)
+        if logits is None:
+            logits = self.logits(x)
+        elif logits.dtype != BF16 or logits.dim() != 2 or logits.shape[0] != T or logits.shape[1] <= E \
+                or logits.stride(1) != 1 or logits.device != dev:
+            raise ValueError("prefill: logits must be bf16 [T, >= E+1], row-major, on x's device")
         w, idx, wf = self.topk(logits)
         # expert-major rows of the routed experts, then the shared expert (expert E) over all
         # T tokens: its rows M .. M+T-1 read token t (row index t*k, divided by k)

@@ -1,9 +1,8 @@
 """Generate golden vectors by running the reference's own Python code on CPU.
 
-Run where the reference tree is available (its location in ``$FNX_REFERENCE``, or the
-build container's mount by default)::
+Run where the reference tree is available, with its location in ``$FNX_REFERENCE``::
 
-    python tests/golden/make_golden.py
+    FNX_REFERENCE=<path of the qwen-ascend tree> python tests/golden/make_golden.py
 
 The reference imports ``torch_npu`` at module load; a stub module is injected whose
 closed CANN operators (``npu_weight_quant_batchmatmul``, ``npu_grouped_matmul``,
@@ -31,7 +30,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("FNX_REFERENCE", "/root/reference"))
+if not os.environ.get("FNX_REFERENCE"):
+    raise SystemExit("make_golden.py: set FNX_REFERENCE to the reference (qwen-ascend) source tree")
+REF = Path(os.environ["FNX_REFERENCE"])
 
 
 def _load(name, path):
@@ -191,7 +192,9 @@ def lin_outputs(rec, shape):
     return sh, gu[:, 2 * I:2 * I + 1].contiguous(), gu[:, 2 * I + 1:].contiguous()
 
 
-def golden_grouped(name, shape, T, seed, xseed):
+def golden_grouped(name, shape, T, seed, xseed, light=False):
+    """The grouped prefill branch; ``light`` keeps the routing, permutation and output only
+    (not the shared-expert rows), for the larger token counts."""
     E = ref_engine(shape)
     t = synth.make_layer(shape, seed=seed)
     x = synth.make_tokens(T, shape.H, seed=xseed)
@@ -201,7 +204,7 @@ def golden_grouped(name, shape, T, seed, xseed):
     w_raw, idx = rec["topk"]
     g = dict(kind="grouped", shape=list(map(int, (shape.H, shape.I, shape.E, shape.k, shape.gs))),
              T=T, seed=seed, xseed=xseed, input_sha=sha(*t.values(), x),
-             logits=logits, gate=gate, sh=sh, probs_topk=w_raw, idx=idx, out=out,
+             logits=logits, gate=gate, sh=None if light else sh, probs_topk=w_raw, idx=idx, out=out,
              order=rec["argsort"][0], inverse=rec["argsort"][1] if len(rec["argsort"]) > 1 else None,
              ends=rec["grouped_in"][0][1])
     if T * shape.k <= 256:
@@ -415,7 +418,7 @@ PIN = synth.MoEShape(H=256, I=128, E=16, k=4, gs=128)
 
 if __name__ == "__main__":
     torch.set_num_threads(os.cpu_count())
-    which = set(sys.argv[1:]) or {"pin", "cfg1", "decode", "reduce", "w8", "w4gemv", "expq", "v2o", "inject", "hc"}
+    which = set(sys.argv[1:]) or {"pin", "cfg1", "cfg2", "decode", "reduce", "w8", "w4gemv", "expq", "v2o", "inject", "hc"}
     if "v2o" in which:
         golden_v2o()
     if "inject" in which:
@@ -427,6 +430,9 @@ if __name__ == "__main__":
         golden_decode("pin_decode", PIN, seed=11, xseed=13)
     if "cfg1" in which:
         golden_grouped("cfg1_grouped", synth.CFG1, T=64, seed=0, xseed=1)
+    if "cfg2" in which:
+        # the prefill configuration's layer shape (E=512, top-10) at 512 tokens
+        golden_grouped("cfg2_grouped_T512", synth.CFG2, T=512, seed=2, xseed=5, light=True)
     if "expq" in which:
         golden_expq("cfg1_expq", synth.CFG1, T=64, seed=0, xseed=1)
         golden_expq("pin_expq_decode", PIN, T=1, seed=11, xseed=13)

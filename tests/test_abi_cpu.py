@@ -72,6 +72,22 @@ def test_host_side_rejections(lib):
     assert lib.fnx_w4gemv_launch(None, None, None, None, None, None, None, 1024, 2048, 10, 20, 3, None) == -1
     assert lib.fnx_moe_decode_w4(*([None] * 10), 17, 2048, 512, 512, 10, None, 0, None) == -1
     assert lib.fnx_moe_decode_w4(*([None] * 10), 1, 2048, 512, 512, 10, None, 0, None) == -5
+    # H or I of zero or below: rejected as shapes by all three decode entry points, and no
+    # workspace size (a negative H would wrap the layout's offsets; I = 0 leaves groups that
+    # never complete)
+    for Hb, Ib in ((0, 512), (-256, 512), (2048, 0), (2048, -128), (128, 512), (2048, 64)):
+        assert lib.fnx_moe_decode_w4(*([None] * 10), 1, Hb, Ib, 512, 10, None, 1 << 30, None) == -2, (Hb, Ib)
+        assert lib.fnx_moe_decode_w4_noalloc(*([None] * 10), 1, Hb, Ib, 512, 10, None) == -2, (Hb, Ib)
+        assert lib.fnx_moe_decode_workspace(1, Hb, Ib, 512, 10) == 0, (Hb, Ib)
+    # W8A16: misaligned x / weights / scales / output are refused before either route (the GEMV
+    # at M <= 16 and the tensor-core GEMM) launches
+    w8 = lib.fnx_w8a16_gemm
+    for M in (1, 300):
+        assert w8(0x1008, 0x2000, 0x3000, 0x4000, M, 2048, 5120, 1, None) == -3, M     # x: 8 of 16 bytes
+        assert w8(0x1000, 0x2004, 0x3000, 0x4000, M, 2048, 5120, 1, None) == -3, M     # w8t
+        assert w8(0x1000, 0x2000, 0x3004, 0x4000, M, 2048, 5120, 1, None) == -3, M     # scales
+        assert w8(0x1000, 0x2000, 0x3000, 0x4002, M, 2048, 5120, 1, None) == -3, M     # y
+        assert lib.fnx_w8a16_gemm_ws(0x1000, 0x2000, 0x3000, 0x4002, M, 2048, 5120, 1, None, 0, None) == -3
     # expert-parallel dispatch layout and row gather
     d = lib.fnx_ep_dispatch_layout
     assert d(None, 40960, 512, 3, None, None, None, None, 0, None) == -1          # E % G
@@ -106,6 +122,10 @@ def test_w8_split_workspace_sizes(lib):
         s, rem = divmod(n, M * N * 4)
         assert rem == 0 and s > 1 and (K // 64) % s == 0 and s * M * 4 <= K, (M, n)
     assert lib.fnx_w8a16_gemm_workspace(16, K, 648, 1) == 0       # N % 128: the GEMV keeps M <= 16
+    # splits that are not powers of two (K/64 = 24 or 48 k-blocks); the GPU tests run these cases
+    for M, K2, s_want in ((12, 1536, 12), (64, 1536, 6), (100, 1536, 3), (64, 3072, 12)):
+        n = lib.fnx_w8a16_gemm_workspace(M, K2, 640, 1)
+        assert n == s_want * M * 640 * 4, (M, K2, n)
     assert lib.fnx_w8a16_gemm_workspace(16, K, N, 64) == 0        # 32-wide scale groups: GEMV as well
 
 

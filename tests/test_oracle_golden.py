@@ -45,14 +45,16 @@ def canonical_rows(t, order):
     return out
 
 
-@pytest.mark.parametrize("name", ["pin_grouped", "cfg1_grouped"])
+@pytest.mark.parametrize("name", ["pin_grouped", "cfg1_grouped", "cfg2_grouped_T512"])
 def test_grouped_layer(golden, name):
     g = golden(name)
     shp, t, x = load_case(g)
     L = O.Layer(t, shp.gs)
     sh, gate, logits = O.shared_and_logits(x, L)
     assert bits_equal(logits, g["logits"])
-    assert bits_equal(sh, g["sh"]) and bits_equal(gate, g["gate"])
+    assert bits_equal(gate, g["gate"])
+    if g["sh"] is not None:                 # the larger fixtures keep no shared-expert rows
+        assert bits_equal(sh, g["sh"])
     w, idx, probs = O.route(logits, shp.k)
     # reference weights: renormalise the top-k probabilities it selected
     wr = (g["probs_topk"] / g["probs_topk"].sum(-1, keepdim=True)).to(BF16)
