@@ -266,6 +266,13 @@ def bench_prefill(args, world, rank, dev):
                 "traffic": 595.7e6, "traffic_unit": "B", "ms_per_launch": round(gu_ms, 4),
                 "algorithmic_flops_per_launch": gu_flops}
     layer_tflops = prefill_flops(T_PREFILL) / (ms * 1e-3) / 1e12
+    # the router + shared-gate logits GEMM ([T, 2048] x [640, 2048]^T): this library's tcgen05 GEMM
+    # (what the layer runs) beside cuBLAS on the same operands
+    rg = {}
+    for name, native in (("native", True), ("cublas", False)):
+        for _ in range(3):
+            lay.logits(xs[0], native=native)
+        rg[f"{name}_us"] = round(time_events(lambda: lay.logits(xs[0], native=native), 20, stream) * 1e3, 2)
 
     # end to end through the public API with host buffers
     xh = [xs[i].cpu().pin_memory() for i in range(nl)]
@@ -288,12 +295,11 @@ def bench_prefill(args, world, rank, dev):
     pipe.run([xh[0]], [outh])
     torch.cuda.synchronize()
     assert torch.equal(outh.view(torch.int16), ref_out.view(torch.int16)), "host pipeline output differs"
-    # this library's kernels per layer: top-k, permute (hist, scan, scatter), gate/up, down,
-    # combine; the router logits run on cuBLAS and are not counted.  Expert parallel (peer
-    # exchange): top-k, dispatch layout (3), token dedup (2), count exchange, dispatch push, wait,
-    # receive layout (head, permute 3, row destinations), gate/up, down with the return in its
-    # epilogue, signal, wait, combine.
-    launches_per_step = 20 if world > 1 else 7
+    # this library's kernels per layer: router logits GEMM, top-k, permute (hist, scan, scatter),
+    # gate/up, down, combine.  Expert parallel (peer exchange): router GEMM, top-k, dispatch layout
+    # (3), token dedup (2), count exchange, dispatch push, wait, receive layout (head, permute 3,
+    # row destinations), gate/up, down with the return in its epilogue, signal, wait, combine.
+    launches_per_step = 21 if world > 1 else 8
     del caps
     torch.cuda.synchronize()
     if world > 1:
@@ -301,10 +307,77 @@ def bench_prefill(args, world, rank, dev):
         for lay in layers:
             lay.close()
     return dict(value=value, ms=ms, clocks=clk.summary(), roofline=roofline, layer_tflops=layer_tflops, ep=ep,
+                router_gemm=rg,
                 e2e={"value": world * T_PREFILL / (e2e_ms * 1e-3), "unit": "tokens/s",
                      "h2d_bytes_per_step": T_PREFILL * H * 2, "d2h_bytes_per_step": T_PREFILL * H * 2,
                      "ms_per_step": round(e2e_ms, 4)},
                 gpu_launches=launches_per_step * args.steps)
+
+
+def bench_ep_stack(args, world, rank, dev, n_layers=48, T=8192, steps=2, warmup=1):
+    """The expert-parallel stack of the workload definition: 48 independently seeded layers of the
+    prefill shape (E=512, top-10, H=2048, I=512, W4 g128), T=8192 tokens per GPU, router logits
+    biased by a Zipf(1.1) expert popularity (so the experts, and with them the owner GPUs, are
+    unevenly loaded).  Rank r keeps experts [r*E/N, (r+1)*E/N) of every layer; the layers share one
+    peer exchange and run one after another on the rank's tokens (each layer gets the same input:
+    the stack times the MoE path, not a model, and the model's residuals and norms are not part of
+    it).  Reports tokens/s over the stack, NVLink bytes per GPU per step, and the load imbalance
+    (max / mean received rows over the GPUs, and max / mean rows per expert)."""
+    from fnx import synth
+    from fnx.engine import MoELayer
+    bias = synth.zipf_bias(E, 1.1).to(dev)
+    layers, shared = [], None
+    for i in range(n_layers):
+        full = MoELayer.from_synth(synth.make_layer(synth.CFG2, seed=5000 + i, device=dev), synth.CFG2, bias=bias)
+        if world > 1:
+            from fnx.ep import ExpertParallelMoE
+            lay = ExpertParallelMoE.from_layer(full, rank, world, transport="p2p", max_tokens=T, exchange=shared)
+            shared = lay.exchange
+            del full
+        else:
+            lay = full
+        layers.append(lay)
+    torch.cuda.empty_cache()
+    x = synth.make_tokens(T, H, seed=9000 + rank, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for lay in layers:
+            lay(x)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(time_events(step, steps, stream), world)
+    # routing skew: rows per expert in layer 0 on this rank's tokens
+    _, idx, _ = layers[0].topk(layers[0].logits(x))
+    per_expert = torch.bincount(idx.reshape(-1), minlength=E).double()
+    res = {"layers": n_layers, "tokens_per_gpu": T, "routing_bias": "zipf(1.1) over a seeded expert ranking",
+           "inputs": "the same seeded tokens into every layer", "ms_per_step": round(ms, 3),
+           "tokens_per_s": round(world * T / (ms * 1e-3), 1), "ms_per_layer": round(ms / n_layers, 4),
+           "experts_per_gpu": E // world,
+           "expert_rows_max_over_mean_layer0": round(float(per_expert.max() / per_expert.mean()), 3)}
+    if world > 1:
+        sends = torch.stack([lay.last_counts[0] for lay in layers]).to(torch.float64)       # [L, world] slots sent
+        toks = torch.stack([lay.last_counts[1] for lay in layers]).to(torch.float64)        # [L, world] token rows
+        recv = sends.clone()
+        torch.distributed.all_reduce(recv)
+        imb = recv.max(dim=1).values / recv.mean(dim=1)
+        moved = (toks.sum(1) - toks[:, rank]) + (sends.sum(1) - sends[:, rank])             # rows out + rows back
+        mx = torch.tensor([float(moved.sum()) * H * 2], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        res.update(recv_rows_max_over_mean_mean=round(float(imb.mean()), 4),
+                   recv_rows_max_over_mean_max=round(float(imb.max()), 4),
+                   nvlink_bytes_per_step_per_gpu_max=int(mx.item()))
+        torch.cuda.synchronize()
+        barrier(world)
+        for lay in layers[1:]:
+            lay.close()
+        layers[0].close()
+    del layers
+    torch.cuda.empty_cache()
+    return res
 
 
 def profile_case(case, dev):
@@ -454,6 +527,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-stack", action="store_true", help="skip the 48-layer expert-parallel stack")
     ap.add_argument("--cpu-sample", type=int, default=T_PREFILL,
                     help="tokens per CPU-baseline sample (both arms; default the whole T=4096 batch)")
     ap.add_argument("--profile-case", choices=["gu", "dn", "dec", "ep", "w8", "w8s"], default=None,
@@ -495,6 +569,7 @@ def main():
         return
 
     r = bench_prefill(args, world, rank, dev)
+    stack = None if args.no_stack else bench_ep_stack(args, world, rank, dev)
     dec = None if (args.no_decode or world > 1) else bench_decode(dev)
     w8 = None if (args.no_decode or world > 1) else bench_w8(dev)
     cpu = cpu_baseline(args.cpu_sample) if (rank == 0 and world == 1) else None
@@ -507,7 +582,8 @@ def main():
                                **({"expert_parallel": r["ep"]} if r["ep"] else {})),
                 **({"ep_bit_identical": r["ep"]["bit_identical_to_one_gpu"]} if r["ep"] else {}),
                 "clocks": r["clocks"], "e2e": r["e2e"], "gpu_launches": r["gpu_launches"],
-                "roofline": r["roofline"], "layer_tflops": round(r["layer_tflops"], 1), "decode": dec, "w8a16": w8,
+                "roofline": r["roofline"], "layer_tflops": round(r["layer_tflops"], 1),
+                "router_gemm": r["router_gemm"], "ep_stack": stack, "decode": dec, "w8a16": w8,
                 "cpu_baseline": cpu}
         print(json.dumps(line))
     if world > 1:

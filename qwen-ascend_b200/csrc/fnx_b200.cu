@@ -12,6 +12,7 @@
 #include "fnx_common.cuh"
 #include "kernels_combine.cuh"
 #include "kernels_decode.cuh"
+#include "kernels_decode2.cuh"
 #include "kernels_ep.cuh"
 #include "kernels_gemm.cuh"
 #include "kernels_gemm_pair.cuh"
@@ -236,7 +237,10 @@ int gemm_launch(int mode, int epi, GemmParams& p, cudaStream_t st) {
 int gemm_check(int mode, int epi, const GemmParams& p) {
     if (p.E < 1 || p.E > G_MAX_E || p.M < 0 || p.K < G_BK || p.K % G_BK || p.Nw < 1) return FNX_EARG;
     if (mode == GEMM_W8 && (p.gs < G_BK || p.gs % G_BK || p.K % p.gs)) return FNX_ESHAPE;
-    if (epi == EPI_PLAIN ? p.Nw % G_BM : (p.Nw % 128)) return FNX_ESHAPE;
+    // bf16 weights: any width (the last tile's rows past Nw read the tensor map's zero fill and
+    // are not stored); the quantised layouts come in whole 128-feature tiles
+    if (mode != GEMM_BF16 && (epi == EPI_PLAIN ? p.Nw % G_BM : (p.Nw % 128))) return FNX_ESHAPE;
+    if (!p.out_rows && p.ld_out < (epi == EPI_PLAIN ? p.Nw : p.Nw / 2)) return FNX_EARG;
     if (p.ld_act % 8 || !aligned16(p.act) || !aligned16(p.w) || (p.scales && !aligned16(p.scales))) return FNX_EALIGN;
     if (p.row_index && p.index_div < 1) return FNX_EARG;
     return FNX_OK;
@@ -878,7 +882,7 @@ FNX_API int fnx_bf16_gemm_nt(const void* x, long long ld_x, const void* w, void*
     GemmParams p{};
     p.act = (const bf16*)x; p.ld_act = ld_x; p.w = w; p.out = (bf16*)y; p.ld_out = ld_y;
     p.act_rows = M;
-    p.E = 1; p.M = M; p.K = K; p.Nw = N; p.gs = K; p.m_tiles = N / G_BM;
+    p.E = 1; p.M = M; p.K = K; p.Nw = N; p.gs = K; p.m_tiles = (N + G_BM - 1) / G_BM;
     const int rc = gemm_check(GEMM_BF16, EPI_PLAIN, p);
     if (rc) return rc;
     if (M == 0) return FNX_OK;
@@ -915,22 +919,66 @@ namespace {
 struct DecodeLayout {
     size_t logits, wf, idx, part, part2, act, act_sh, yd, sh, counters, total;
     int ks1, ks2, R;
+    // streaming kernel: the launch counter at offset 0, tagged words, the exit ticket last
+    // (`counters`: the part that must be zero before the first call)
+    size_t tlog, tpart, tpart2, tyd, tsh;
 };
+
+// FNX_DECODE_V1=1 selects the first decode kernel (decode_fused_kernel: one bulk-copy chunk per
+// item, routing by one CTA) in place of the streaming one, for comparisons.
+bool decode_v1() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("FNX_DECODE_V1");
+        v = (e && e[0] == '1') ? 1 : 0;
+    }
+    return v == 1;
+}
+
+int env_int(const char* name, int dflt) {
+    const char* e = getenv(name);
+    return e && *e ? atoi(e) : dflt;
+}
 
 DecodeLayout decode_layout(int M, int H, int I, int E, int k) {
     DecodeLayout L{};
     L.R = E + 1;
     const int mt = I / 64, kb = H / 64;
-    // K splits (item i of a group takes k-blocks [i*kb/ks, (i+1)*kb/ks), >= 2 each).  The
-    // router rows and the shared gate/up together fill about one item per resident block.
-    // The routed gate/up split minimises (waves of items) x (k-blocks per item + a fixed
-    // per-item cost, measured at about 16 k-blocks' worth: the copy latency, the partial
-    // sums and the group ticket): the items of one wave run side by side, so a second,
-    // nearly empty wave costs a whole item's time.
     const int slots = 2 * num_sms();
-    const int rb = (L.R + DEC_ROWS - 1) / DEC_ROWS;
+    // K splits: item i of a group takes k-blocks [i*kb/ks, (i+1)*kb/ks).  The router rows and the
+    // shared gate/up (both before the routing is known) together fill about one item per
+    // resident CTA.
+    const int rows = decode_v1() ? DEC_ROWS : d2_router_rows(H);
+    const int rb = (L.R + rows - 1) / rows;
     L.ks1 = 1;
     while (rb + M * mt * (L.ks1 + 1) <= slots && kb / (L.ks1 + 1) >= 2) L.ks1 += 1;
+    if (!decode_v1()) {
+        // streaming kernel: the routed gate/up is split into at most one item per resident CTA
+        // (no CTA holds two items of the critical gate/up phase), never finer than a down item
+        const int cap = kb / (I / 64) >= 1 ? kb / (I / 64) : 1;
+        const long long groups = (long long)M * k * mt;
+        L.ks2 = (int)(slots / groups);                 // about one gate/up item per resident CTA
+        if (L.ks2 < 2 && M <= 4) L.ks2 = 2;            // 2 to 4 tokens: halves (measured 46.7 against 50.0 us at M = 4)
+        if (L.ks2 > cap) L.ks2 = cap;
+        if (L.ks2 < 1) L.ks2 = 1;
+        const int e1 = env_int("FNX_DEC_KS1", 0), e2 = env_int("FNX_DEC_KS2", 0);
+        if (e1 >= 1 && kb / e1 >= 1) L.ks1 = e1;
+        if (e2 >= 1 && kb / e2 >= 1) L.ks2 = e2;
+        size_t off = 0;
+        auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
+        take(sizeof(unsigned));                                  // launch counter, offset 0
+        L.tlog = take((size_t)M * L.R * 8);
+        L.tpart = take((size_t)M * mt * L.ks1 * 128 * 8);
+        L.tpart2 = take((size_t)M * k * mt * L.ks2 * 128 * 8);
+        L.tyd = take((size_t)M * k * (H / 2) * 8);
+        L.tsh = take((size_t)M * (H / 2) * 8);
+        L.counters = take(sizeof(unsigned));                     // exit ticket
+        L.total = off;
+        return L;
+    }
+    // one copy per item: the routed gate/up split minimises (waves of items) x (k-blocks per
+    // item + a fixed per-item cost, measured at about 16 k-blocks' worth: the copy latency, the
+    // partial sums and the group ticket)
     L.ks2 = 1;
     double best = 1e30;
     for (int ks = 1; ks <= 32 && kb / ks >= 2; ++ks) {
@@ -973,9 +1021,46 @@ FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu,
     const DecodeLayout L = decode_layout(M, H, I, E, k);
     if (!workspace || ws_bytes < L.total) return FNX_EWORKSPACE;
     if (!aligned16(x) || !aligned16(router) || !aligned16(gu) || !aligned16(dn) || !aligned16(sh_gu) ||
-        !aligned16(sh_dn))
+        !aligned16(sh_dn) || !aligned16(workspace) || (reinterpret_cast<uintptr_t>(out) & 3u))
         return FNX_EALIGN;
     uint8_t* ws = (uint8_t*)workspace;
+    if (!decode_v1()) {
+        StreamParams q{};
+        q.x = (const bf16*)x; q.router = (const bf16*)router;
+        q.gu_tw = (const uint32_t*)gu; q.dn_tw = (const uint32_t*)dn;
+        q.sh_gu_tw = (const uint32_t*)sh_gu; q.sh_dn_tw = (const uint32_t*)sh_dn;
+        q.out = (bf16*)out; q.w_out = (bf16*)w_out; q.idx_out = (int64_t*)idx_out; q.bias = (const float*)bias;
+        q.epoch = (unsigned*)ws;
+        q.exit = (unsigned*)(ws + L.counters);
+        q.tlog = (tword*)(ws + L.tlog); q.tpart = (tword*)(ws + L.tpart); q.tpart2 = (tword*)(ws + L.tpart2);
+        q.tyd = (tword*)(ws + L.tyd); q.tsh = (tword*)(ws + L.tsh);
+        q.M = M; q.H = H; q.I = I; q.E = E; q.k = k; q.R = L.R; q.ks1 = L.ks1; q.ks2 = L.ks2;
+        // one cooperative launch of every block that fits at once (work items wait for earlier
+        // items of other blocks, so all blocks must be resident)
+        static int grid2_of[FNX_MAX_DEVICES] = {};
+        int& grid2 = grid2_of[current_device()];
+        if (!grid2) {
+            if (cudaFuncSetAttribute(decode_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, D2_SMEM))
+                return FNX_ELAUNCH;
+            int per_sm = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_stream_kernel, D2_THREADS, D2_SMEM) ||
+                per_sm < 1)
+                return FNX_ELAUNCH;
+            grid2 = per_sm * num_sms();
+        }
+        cudaLaunchAttribute attr2[1];
+        attr2[0].id = cudaLaunchAttributeCooperative;
+        attr2[0].val.cooperative = 1;
+        cudaLaunchConfig_t cfg2 = {};
+        cfg2.gridDim = dim3(grid2);
+        cfg2.blockDim = dim3(D2_THREADS);
+        cfg2.dynamicSmemBytes = D2_SMEM;
+        cfg2.stream = (cudaStream_t)stream;
+        cfg2.attrs = attr2;
+        cfg2.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg2, decode_stream_kernel, q) != cudaSuccess) return FNX_ELAUNCH;
+        return launch_rc();
+    }
     DecodeParams p{};
     p.x = (const bf16*)x; p.router = (const bf16*)router;
     p.gu_tw = (const uint32_t*)gu; p.dn_tw = (const uint32_t*)dn;

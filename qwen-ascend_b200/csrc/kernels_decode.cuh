@@ -128,7 +128,7 @@ FNX_DEV void tile_dot(const uint32_t* __restrict__ tw, const bf16* x, int K, boo
                 const uint4* xq = reinterpret_cast<const uint4*>(xs2 + (c0 + j) * 32);
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
-                    const uint32_t w = blk[c * 128 + r];
+                    const uint32_t w = blk[tile_word(c, r)];
                     const uint4 xv = xq[c];
                     const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll

@@ -181,7 +181,7 @@ FNX_DEV void produce_a_w4(const uint8_t* raw, int r, uint32_t (&a)[32]) {
     const uint32_t s2 = s16 | (s16 << 16);
     uint32_t wv[8];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) wv[c] = rw[c * 128 + r];
+    for (int c = 0; c < 8; ++c) wv[c] = rw[tile_word(c, r)];
 #pragma unroll
     for (int c = 0; c < 8; ++c)
 #pragma unroll
@@ -227,6 +227,7 @@ FNX_DEV void epilogue_chunk(const GemmParams& p, const TileInfo& ti, int r, int 
     const int lane = threadIdx.x & 31;
     if (EPI == EPI_PLAIN) {
         const int f = ti.m * G_BM + (PERM ? lane_feature<EPI>(r) : r);
+        if (f >= p.Nw) return;                    // the last tile of a width that is not a multiple of 128
         const int lim = ti.nrows - n0;
         if (p.out_rows) {
 #pragma unroll

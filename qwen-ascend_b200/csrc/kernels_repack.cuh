@@ -7,9 +7,13 @@
 // Output t  int32 [E, MT, K/64, TILE_BLOCK_WORDS]: one 4352-byte block per (expert e,
 //        feature tile m, k-block kb), contiguous along kb, so a tile's whole K range is one
 //        linear stream and consecutive k-blocks can be fetched by one bulk copy:
-//          word c*128 + r (c < 8, r < 128): the 8 weights W[kb*64 + 8c + i, f(m, r)] of tile
-//            row r as offset-binary nibbles (q + 8) in the order i = 0,2,4,6,1,3,5,7, so
-//            that ((word >> 4i) & 0x000f000f) yields the pair (k = 8c+2i, 8c+2i+1);
+//          word tile_word(c, r) = c*128 + (r ^ 8*(c%4)) (c < 8, r < 128): the 8 weights
+//            W[kb*64 + 8c + i, f(m, r)] of tile row r as offset-binary nibbles (q + 8) in the
+//            order i = 0,2,4,6,1,3,5,7, so that ((word >> 4i) & 0x000f000f) yields the pair
+//            (k = 8c+2i, 8c+2i+1).  The XOR swizzle keeps both access patterns free of
+//            shared-memory bank conflicts: one thread per tile row reading word c (the GEMM's
+//            dequant warps), and the mma fragment order of the decode GEMV, where the four
+//            threads of a fragment group read words c = 0..3 (and 4..7) of the same row;
 //          half-word 2048 + r: the scale of tile row r for the group holding k-block kb
 //            (repeated in every k-block of a group when gs > 64).
 // Tile rows: PLAIN  f(m, r) = 128m + r                                 (MT = Nw / 128)
@@ -23,6 +27,9 @@ namespace fnx {
 
 constexpr int TILE_BLOCK_WORDS = 1024 + 64;                 // 4096 B of weights + 256 B of scales
 constexpr int TILE_BLOCK_BYTES = TILE_BLOCK_WORDS * 4;      // 4352
+
+// Position of word c (8 consecutive k) of tile row r inside a tile block.
+FNX_DEV int tile_word(int c, int r) { return c * 128 + (r ^ ((c & 3) << 3)); }
 
 FNX_DEV int tile_feature(int m, int r, int Nw, bool swiglu) {
     return swiglu ? ((r & 1) ? Nw / 2 : 0) + 64 * m + (r >> 1) : 128 * m + r;
@@ -44,7 +51,7 @@ __global__ void __launch_bounds__(256) repack_w4_tiles_kernel(const uint32_t* __
         const int e = (int)(rest / MT);
         uint32_t out = 0;
         if (wd < 1024) {
-            const int r = wd & 127, c = wd >> 7;
+            const int c = wd >> 7, r = (wd & 127) ^ ((c & 3) << 3);     // tile_word's inverse
             const int f = tile_feature(m, r, Nw, swiglu != 0);
             const int k0 = kb * 64 + 8 * c;
             const uint32_t* src = w + ((long long)e * K + k0) * nw8 + (f >> 3);

@@ -73,13 +73,35 @@ def _grouped_w4(act, tiles, ends, out, *, E, M, K, Nw, epilogue, row_index=None,
     return out
 
 
+def mm_nt(x, w):
+    """``x [M, K] @ w[N, K]^T`` -> bf16 ``[M, N]`` on this library's tcgen05 bf16 GEMM
+    (``fnx_bf16_gemm_nt``: fp32 accumulation, one rounding).  K is zero-padded to a multiple of
+    64 when it is not one (exact: the padding adds zero products)."""
+    _lib.require_cuda(x, w)
+    x = (x if x.dtype == BF16 else x.to(BF16)).contiguous()
+    w = (w if w.dtype == BF16 else w.to(BF16)).contiguous()
+    M, K = x.shape
+    N = w.shape[0]
+    Kp = (K + 63) // 64 * 64
+    if Kp != K:
+        x = torch.nn.functional.pad(x, (0, Kp - K))
+        w = torch.nn.functional.pad(w, (0, Kp - K))
+    out = torch.empty(M, N, dtype=BF16, device=x.device)
+    if M:
+        rc = _lib.lib().fnx_bf16_gemm_nt(x.data_ptr(), x.stride(0), w.data_ptr(), out.data_ptr(), N, M, Kp, N,
+                                         _lib.stream(x.device))
+        _lib.check(rc, "bf16 GEMM")
+    return out
+
+
 def gated_residual(h, hc_norm_w, w_down, w_up, w_inj=None, n_inj=0, hc=4, eps=1e-6):
     """The hyper-connection mix that produces a layer's MoE input (``fnx/engine.py:818-857``):
     ``h`` bf16 ``[b, 1, hc*H]`` -> ``(mixed [b, 1, H], inj [b, 1, hc])``.  ``w_down`` bf16
     ``[r (+ hc), hc*H]`` (with ``n_inj == hc`` its last rows are the inject weights, as the
     reference's loader concatenates them), ``w_up`` bf16 ``[hc*H, r]``, ``w_inj`` bf16
     ``[hc, hc*H]`` when not concatenated.  RMSNorm, activation and branch mix run on this
-    library's kernels with the reference's roundings; the two small GEMMs are library GEMMs."""
+    library's kernels with the reference's roundings, the two small GEMMs on its tcgen05 bf16
+    GEMM (``mm_nt``)."""
     from . import post_ops
     b, HCH = h.shape[0], h.shape[-1]
     H = HCH // hc
@@ -92,9 +114,9 @@ def gated_residual(h, hc_norm_w, w_down, w_up, w_inj=None, n_inj=0, hc=4, eps=1e
         if w_inj is None:
             raise ValueError("gated_residual: pass w_inj, or w_down with the inject rows and n_inj = hc")
         w_down = torch.cat([w_down, w_inj])
-    di = torch.mm(hn, w_down.t())
+    di = mm_nt(hn, w_down)
     mix, inj = post_ops.activate(di.view(b, 1, -1).contiguous(), hc)
-    logits = torch.mm(mix.view(b, -1), w_up.t())
+    logits = mm_nt(mix.view(b, -1), w_up)
     mixed = post_ops.mix_reduce(hn.view(b, 1, HCH), logits.view(b, 1, HCH).contiguous(), hc)
     return mixed, inj
 
@@ -349,10 +371,11 @@ class MoELayer:
         return sum(t.numel() * t.element_size() for t in (self.gu_all, self.dn_all, self.router_cat))
 
     # ---------------------------------------------------------------- routing
-    def logits(self, x, native=False):
-        """bf16 ``[T, R_pad]``: router logits in columns ``[0, E)``, shared gate in column E.
-        A plain bf16 GEMM (fp32 accumulation), run by cuBLAS; ``native`` runs the library's
-        own tcgen05 bf16 GEMM instead."""
+    def logits(self, x, native=True):
+        """bf16 ``[T, R_pad]``: router logits in columns ``[0, E)``, shared gate in column E:
+        one bf16 GEMM over the concatenated router (fp32 accumulation, rounded once) on this
+        library's tcgen05 bf16 GEMM.  ``native=False`` runs the same product on cuBLAS, for
+        comparisons."""
         if not native:
             return torch.mm(x, self.router_cat.t())
         T = x.shape[0]

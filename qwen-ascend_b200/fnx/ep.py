@@ -54,6 +54,7 @@ class _PeerExchange:
     def __init__(self, rank, world, group, H, k, max_tokens, e_local, device):
         L = _lib.lib()
         self.world, self.group = world, group
+        self.H, self.k, self.max_tokens, self.e_local = H, k, max_tokens, e_local
         nbytes = L.fnx_ep_p2p_region_bytes(world, H, k, max_tokens)
         if not nbytes:
             raise ValueError(f"peer exchange: unsupported shape (world={world}, H={H}, k={k}, T={max_tokens})")
@@ -141,16 +142,32 @@ class ExpertParallelMoE(MoELayer):
             return torch.cat([tiles[-1:], tiles[:-1]]).contiguous()
         return tiles
 
-    def _setup_transport(self, device):
+    def _setup_transport(self, device, exchange=None):
+        self._own_p2p = exchange is None
         if self.transport == "p2p":
-            self._p2p = _PeerExchange(self.rank, self.world, self.group, self.H, self.k, self.max_tokens,
-                                      self.E_local, device)
+            if exchange is not None:
+                if (exchange.world != self.world or exchange.H != self.H or exchange.k != self.k
+                        or exchange.max_tokens < self.max_tokens or exchange.e_local != self.E_local):
+                    raise ValueError("ExpertParallelMoE: the shared exchange was made for another shape")
+                self._p2p = exchange
+            else:
+                self._p2p = _PeerExchange(self.rank, self.world, self.group, self.H, self.k, self.max_tokens,
+                                          self.E_local, device)
+
+    @property
+    def exchange(self):
+        """The peer exchange (p2p transport), for other layers of the same stack to share."""
+        return self._p2p
 
     @classmethod
-    def from_layer(cls, layer: MoELayer, rank, world, group=None, transport="auto", max_tokens=4096):
+    def from_layer(cls, layer: MoELayer, rank, world, group=None, transport="auto", max_tokens=4096,
+                   exchange=None):
         """This rank's shard of a one-device ``MoELayer`` (its tile blocks are copied, so the
         full layer may be dropped afterwards).  Collective over the group when the transport
-        is ``"p2p"`` (the ranks exchange their regions' IPC handles)."""
+        is ``"p2p"`` (the ranks exchange their regions' IPC handles).  ``exchange``: the peer
+        exchange of another layer of the same shape, to share (the layers of a stack run one
+        after another, and the exchange's device-side call epochs order them); the layer that
+        made it releases it."""
         o = cls.__new__(cls)
         o.E, o.H, o.I, o.k, o.gs = layer.E, layer.H, layer.I, layer.k, layer.gs
         o.R, o.R_pad, o.router_cat, o.bias = layer.R, layer.R_pad, layer.router_cat, layer.bias
@@ -159,7 +176,7 @@ class ExpertParallelMoE(MoELayer):
         lo, hi = rank * o.E_local, (rank + 1) * o.E_local
         o.gu_loc = o._arrange(torch.cat([layer.gu_all[lo:hi], layer.gu_all[layer.E:]]))
         o.dn_loc = o._arrange(torch.cat([layer.dn_all[lo:hi], layer.dn_all[layer.E:]]))
-        o._setup_transport(layer.router_cat.device)
+        o._setup_transport(layer.router_cat.device, exchange)
         return o
 
     def capture(self, T, device=None):
@@ -171,10 +188,10 @@ class ExpertParallelMoE(MoELayer):
         return super().capture(T, device)
 
     def close(self):
-        """Release the peer exchange (collective over the group)."""
-        if self._p2p is not None:
+        """Release the peer exchange if this layer made it (collective over the group)."""
+        if self._p2p is not None and getattr(self, "_own_p2p", True):
             self._p2p.close()
-            self._p2p = None
+        self._p2p = None
 
     # ---------------------------------------------------------------- stages
     def route(self, x):

@@ -66,6 +66,9 @@ def tile_unpack(t, K, N, gs, swiglu):
     E, MT, KB = t.shape[:3]
     G = K // gs
     words = (t[..., :1024].to(torch.int64) & 0xFFFFFFFF).reshape(E, MT, KB, 8, 128)
+    # word c of tile row r sits at position r ^ 8*(c % 4) of row c (the bank swizzle)
+    c_idx = torch.arange(8)[:, None]
+    words = words[..., c_idx, torch.arange(128)[None, :] ^ (8 * (c_idx % 4))]
     bs = t[..., 1024:].contiguous().view(torch.int16).view(BF16)     # [E, MT, KB, 128]
     per = gs // 64
     for g in range(G):
