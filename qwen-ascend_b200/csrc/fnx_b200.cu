@@ -16,6 +16,7 @@
 #include "kernels_ep.cuh"
 #include "kernels_gemm.cuh"
 #include "kernels_gemm_pair.cuh"
+#include "kernels_gemm_bf16.cuh"
 #include "kernels_hc.cuh"
 #include "kernels_route.cuh"
 #include "kernels_w4gemv.cuh"
@@ -113,7 +114,7 @@ EncodeTiledFn encode_fn() {
 struct MapKey {
     const void* ptr;
     int dtype, swz;
-    unsigned long long d0, d1;
+    unsigned long long d0, d1, stride;
     unsigned b0, b1;
 };
 struct MapEntry {
@@ -125,10 +126,12 @@ struct MapEntry {
 // 2-D tiled map: inner dimension d0 (contiguous, elements), outer d1 rows, box {b0, b1}.
 // Cached per (pointer, shape) -- weights are long-lived, so repeated calls reuse maps.
 int make_map_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dt, int esize, unsigned long long d0,
-                unsigned long long d1, unsigned b0, unsigned b1, CUtensorMapSwizzle swz) {
+                unsigned long long d1, unsigned b0, unsigned b1, CUtensorMapSwizzle swz,
+                unsigned long long stride_bytes = 0) {
     static MapEntry cache[64];
     static int next = 0;
-    const MapKey k{ptr, (int)dt, (int)swz, d0, d1, b0, b1};
+    if (!stride_bytes) stride_bytes = d0 * (unsigned long long)esize;
+    const MapKey k{ptr, (int)dt, (int)swz, d0, d1, stride_bytes, b0, b1};
     for (auto& e : cache)
         if (e.used && memcmp(&e.key, &k, sizeof(k)) == 0) {
             *out = e.map;
@@ -137,7 +140,7 @@ int make_map_2d(CUtensorMap* out, const void* ptr, CUtensorMapDataType dt, int e
     EncodeTiledFn fn = encode_fn();
     if (!fn) return FNX_EDRIVER;
     const cuuint64_t dims[2] = {d0, d1};
-    const cuuint64_t strides[1] = {d0 * (cuuint64_t)esize};
+    const cuuint64_t strides[1] = {(cuuint64_t)stride_bytes};
     const cuuint32_t box[2] = {b0, b1};
     const cuuint32_t estr[2] = {1, 1};
     if (fn(out, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
@@ -185,7 +188,7 @@ int gemm_pair_launch_t(GemmParams& p, cudaStream_t st) {
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.blockDim = dim3(G_THREADS);
+    cfg.blockDim = dim3(P_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
@@ -877,16 +880,56 @@ FNX_API int fnx_w8a16_gemm_ws(const void* x, const void* w8t, const void* sc, vo
     return w8a16_gemm_impl(x, w8t, sc, y, M, K, N, G, ws, ws_bytes, true, stream);
 }
 
+namespace {
+template <int BN>
+int gemm_bf16_tma_launch_t(const void* x, long long ld_x, const void* w, void* y, long long ld_y, int M, int K, int N,
+                           cudaStream_t st) {
+    const size_t smem = gemm_bf16_tma_smem<BN>();
+    static bool configured[FNX_MAX_DEVICES] = {};
+    const int dev = current_device();
+    if (!configured[dev]) {
+        if (cudaFuncSetAttribute(gemm_bf16_tma_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return FNX_ELAUNCH;
+        configured[dev] = true;
+    }
+    TGemmParams p{};
+    int rc = make_map_2d(&p.ta, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (unsigned long long)K, (unsigned long long)M,
+                         T_BK, T_BM, CU_TENSOR_MAP_SWIZZLE_128B, (unsigned long long)ld_x * 2);
+    if (rc) return rc;
+    rc = make_map_2d(&p.tb, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (unsigned long long)K, (unsigned long long)N, T_BK,
+                     BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    p.out = (bf16*)y; p.ld_out = ld_y; p.M = M; p.N = N; p.K = K;
+    const int tiles = ((M + T_BM - 1) / T_BM) * ((N + BN - 1) / BN);
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    gemm_bf16_tma_kernel<BN><<<grid, T_THREADS, smem, st>>>(p);
+    return launch_rc();
+}
+}  // namespace
+
+// y [M, N] (row stride ld_y) = x [M, K] (row stride ld_x) @ w [N, K]^T, bf16 in and out, fp32
+// accumulation: the TMA-fed tcgen05 GEMM (kernels_gemm_bf16.cuh); 160-feature tiles when N is a
+// multiple of 160 (the router's 640 rows: 128 tiles at T = 4096, one wave), 128 otherwise.
 FNX_API int fnx_bf16_gemm_nt(const void* x, long long ld_x, const void* w, void* y, long long ld_y, int M, int K, int N,
                              void* stream) {
-    GemmParams p{};
-    p.act = (const bf16*)x; p.ld_act = ld_x; p.w = w; p.out = (bf16*)y; p.ld_out = ld_y;
-    p.act_rows = M;
-    p.E = 1; p.M = M; p.K = K; p.Nw = N; p.gs = K; p.m_tiles = (N + G_BM - 1) / G_BM;
-    const int rc = gemm_check(GEMM_BF16, EPI_PLAIN, p);
-    if (rc) return rc;
+    if (M < 0 || K < T_BK || K % T_BK || N < 1 || ld_x < K || ld_y < N) return FNX_EARG;
+    if (!aligned16(x) || !aligned16(w) || ld_x % 8) return FNX_EALIGN;
     if (M == 0) return FNX_OK;
-    return gemm_launch(GEMM_BF16, EPI_PLAIN, p, (cudaStream_t)stream);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (M < T_BM || N < 128) {
+        // fewer rows than one TMA box: the single-CTA kernel (weights by TMA, the few token rows
+        // gathered by its loader warps)
+        GemmParams p{};
+        p.act = (const bf16*)x; p.ld_act = ld_x; p.w = w; p.out = (bf16*)y; p.ld_out = ld_y;
+        p.act_rows = M;
+        p.E = 1; p.M = M; p.K = K; p.Nw = N; p.gs = K; p.m_tiles = (N + G_BM - 1) / G_BM;
+        const int rc = gemm_check(GEMM_BF16, EPI_PLAIN, p);
+        if (rc) return rc;
+        return gemm_launch(GEMM_BF16, EPI_PLAIN, p, st);
+    }
+    if (N % 160 == 0) return gemm_bf16_tma_launch_t<160>(x, ld_x, w, y, ld_y, M, K, N, st);
+    return gemm_bf16_tma_launch_t<128>(x, ld_x, w, y, ld_y, M, K, N, st);
 }
 
 // ======================================================================== load-time repack

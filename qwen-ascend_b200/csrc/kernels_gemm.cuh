@@ -188,6 +188,27 @@ FNX_DEV void produce_a_w4(const uint8_t* raw, int r, uint32_t (&a)[32]) {
         for (int i = 0; i < 4; ++i) a[4 * c + i] = tile_pair(wv[c], i, s2);
 }
 
+// produce_a_w4 straight into tensor memory in two halves of 16 columns (words 0-3, then 4-7):
+// half the registers live at once, so the 32 independent conversion chains of a row interleave
+// instead of queueing behind a 32-register fragment.
+FNX_DEV void produce_store_w4(const uint8_t* raw, int r, uint32_t taddr) {
+    const uint32_t* rw = reinterpret_cast<const uint32_t*>(raw);
+    const uint32_t s16 = reinterpret_cast<const uint16_t*>(raw + G_RAW_W)[r];
+    const uint32_t s2 = s16 | (s16 << 16);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        uint32_t wv[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) wv[c] = rw[tile_word(4 * half + c, r)];
+        uint32_t a[16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[4 * c + i] = tile_pair(wv[c], i, s2);
+        tmem_st16(taddr + 16 * half, a);
+    }
+}
+
 // W8: same block shape, int8 weights read directly (L2-resident dense projections).
 template <int EPI>
 FNX_DEV void produce_a_w8(const GemmParams& p, const TileInfo& ti, int kb, uint8_t* a_tile, int t) {
@@ -656,9 +677,8 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                         const bool got = mbar_wait(&S.raw_full[os], rph) &&
                                          mbar_wait(&S.empty[s], ((it / C::STAGES) & 1) ^ 1);
                         if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-                        uint32_t a[32];
-                        produce_a_w4(raw_tiles + (os * G_OPK + kb % G_OPK) * G_RAW_BYTES, t, a);
-                        tmem_st32(tmem + ((uint32_t)(q * 32) << 16) + C::A_COL0 + s * 32, a);
+                        produce_store_w4(raw_tiles + (os * G_OPK + kb % G_OPK) * G_RAW_BYTES, t,
+                                         tmem + ((uint32_t)(q * 32) << 16) + C::A_COL0 + s * 32);
                         tmem_st_wait();
                         tc_fence_before();
                         __syncwarp();

@@ -37,6 +37,18 @@ constexpr int P_STAGES = 4;                          // A stages in tensor memor
 #define FNX_PAIR_ROPS 5
 #endif
 constexpr int P_BSTAGES = FNX_PAIR_BSTAGES;
+// Producers: two groups of eight warps take alternate stages; inside a group, warp w converts
+// k-block (w / 4) % 2 of the stage for tensor-memory lane quarter w % 4.  One group of four warps
+// per stage (each converting both k-blocks) spent ~1400 cycles per stage on the conversion, a
+// latency two groups could not hide (clock-stamped: an MMA stage every ~1120 cycles against 339
+// of tensor work); splitting the k-blocks over two warps halves that latency.
+#ifndef FNX_PAIR_PROD
+#define FNX_PAIR_PROD 8
+#endif
+constexpr int P_PROD = FNX_PAIR_PROD;                // producer warps: 8 .. 8 + P_PROD - 1 (8 or 16)
+constexpr int P_KPW = P_KS * 8 / P_PROD;             // k-blocks of a stage each producer warp converts
+constexpr int P_LOADER0 = 8 + P_PROD;                // loader warps 0 and P_LOADER0 .. P_LOADER0 + 2
+constexpr int P_THREADS = 32 * (P_LOADER0 + G_LOADERS - 1);   // 27 warps
 constexpr int P_BN_HALF = G_BN / 2;                  // token rows per CTA per tile
 constexpr int P_B_SUB = P_BN_HALF * G_BK * 2;        // 8 KB: one k-block of this CTA's token rows
 constexpr int P_B_BYTES = P_KS * P_B_SUB;            // 16 KB per stage
@@ -45,6 +57,7 @@ constexpr uint32_t P_TMEM_COLS = 512;
 constexpr uint32_t P_A_COL0 = 2 * G_BN;
 constexpr uint32_t P_A_COLS = 32 * P_KS;             // tensor-memory columns of one A stage
 static_assert(G_OPK % P_KS == 0, "a copy holds whole stages");
+static_assert(P_KS == 2 && (P_PROD == 8 || P_PROD == 16), "producer groups of 4 or 8 warps over 2 k-blocks");
 static_assert(P_STAGES <= G_MAX_STAGES && P_BSTAGES <= G_MAX_STAGES && P_R_OPS <= G_MAX_R_OPS &&
                   P_A_COL0 + P_STAGES * P_A_COLS <= P_TMEM_COLS,
               "budget");
@@ -70,7 +83,7 @@ FNX_DEV bool decode_pair_tile(const GemmSmem& S, const GemmParams& p, int tile, 
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(P_THREADS, 1) grouped_gemm_pair_kernel(const __grid_constant__ GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* b_tiles = base;
@@ -87,7 +100,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
     // (b_full / b_empty / peer_full)
     if (tid == 0) {
         for (int s = 0; s < P_STAGES; ++s) {
-            mbar_init(&S.a_full[s], 4);
+            mbar_init(&S.a_full[s], P_PROD / 2);     // the eight warps of the stage's group
             mbar_init(&S.empty[s], 1);
         }
         for (int s = 0; s < P_BSTAGES; ++s) {
@@ -97,7 +110,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
         }
         for (int s = 0; s < P_R_OPS; ++s) {
             mbar_init(&S.raw_full[s], 1);
-            mbar_init(&S.raw_empty[s], 8);
+            mbar_init(&S.raw_empty[s], P_PROD);      // every producer warp releases every copy
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&S.acc_full[b], 1);
@@ -112,11 +125,11 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
         tmem_relinquish_pair();
     }
     {
-        __shared__ int warp_sums[G_THREADS / 32];
+        __shared__ int warp_sums[P_THREADS / 32];
         __shared__ int carry;
         if (tid == 0) carry = 0;
         __syncthreads();
-        for (int e0 = 0; e0 < p.E; e0 += G_THREADS) {
+        for (int e0 = 0; e0 < p.E; e0 += P_THREADS) {
             const int e = e0 + tid;
             int n = 0;
             if (e < p.E) {
@@ -137,7 +150,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
             for (int w = 0; w < warp; ++w) before += warp_sums[w];
             if (e < p.E) S.tile_start[e] = before + incl - n;
             __syncthreads();
-            if (tid == G_THREADS - 1) carry = before + incl;
+            if (tid == P_THREADS - 1) carry = before + incl;
             __syncthreads();
         }
         if (tid == 0) {
@@ -155,9 +168,9 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
     const int KB = p.K / G_BK;
     const int KS = KB / P_KS;                            // stages per tile (K % 128 == 0)
 
-    if (warp == 0 || warp >= 16) {
+    if (warp == 0 || warp >= P_LOADER0) {
         // ------------------------------------------------ B loaders: this CTA's half of the chunk rows
-        const int lw = warp == 0 ? 0 : warp - 15;
+        const int lw = warp == 0 ? 0 : warp - P_LOADER0 + 1;
         const uint64_t keep = l2_evict_last();
         int it = 0;
         bool ok = true;
@@ -348,10 +361,11 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
                 else mbar_arrive_remote_relaxed(mapa_rank(&S.acc_empty[ab], 0));
             }
         }
-    } else if (warp >= 8) {
+    } else if (warp >= 8 && warp < 8 + P_PROD) {
         // ------------------------------------------------ A producers (this CTA's feature tile)
-        const int grp = (warp - 8) >> 2;
-        const int q = warp & 3;
+        const int grp = (warp - 8) / (P_PROD / 2);
+        const int q = warp & 3;                          // the tensor-memory lane quarter warp % 4 reaches
+        const int h0 = (((warp - 8) >> 2) % (P_PROD / 8)) * P_KPW;   // the first k-block of the stage it converts
         const int t = q * 32 + lane;
         int it = 0, op = 0;
         bool ok = true;
@@ -368,11 +382,9 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_pair_kernel(const _
                                      mbar_wait_cluster(&S.empty[s], ((it / P_STAGES) & 1) ^ 1);
                     if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
 #pragma unroll
-                    for (int h = 0; h < P_KS; ++h) {
-                        uint32_t a[32];
-                        produce_a_w4(raw_tiles + (os * G_OPK + (kb0 + h) % G_OPK) * G_RAW_BYTES, t, a);
-                        tmem_st32(tmem + ((uint32_t)(q * 32) << 16) + P_A_COL0 + s * P_A_COLS + h * 32, a);
-                    }
+                    for (int h = h0; h < h0 + P_KPW; ++h)
+                        produce_store_w4(raw_tiles + (os * G_OPK + (kb0 + h) % G_OPK) * G_RAW_BYTES, t,
+                                         tmem + ((uint32_t)(q * 32) << 16) + P_A_COL0 + s * P_A_COLS + h * 32);
                     tmem_st_wait();
                     tc_fence_before();
                     __syncwarp();
