@@ -141,7 +141,7 @@ def cpu_baseline(sample_tokens=T_PREFILL, seed=0):
     expert inside the timed region (as the reference's ExpQ path does per call)."""
     import oracle as O
     from fnx import synth
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) or 1
     torch.set_num_threads(threads)
     key = (seed, sample_tokens)
     if key not in _CPU_INPUTS:                  # synthesis stays outside the timed region
@@ -154,6 +154,18 @@ def cpu_baseline(sample_tokens=T_PREFILL, seed=0):
     return {"value": sample_tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"{sample_tokens} tokens through one layer of the T=4096 configuration (E=512, top-10): "
                       f"oracle port of FnLayer._moe, fp32 accumulation, per-call dequantisation; {dt:.1f} s"}
+
+
+def cpu_baseline_median(sample_tokens=T_PREFILL, runs=3, warm=1):
+    """``cpu_baseline`` after ``warm`` untimed calls (first-touch allocation, thread-pool start),
+    the median of ``runs`` timed calls, as the reference arm measures it."""
+    for _ in range(warm):
+        cpu_baseline(sample_tokens)
+    rs = [cpu_baseline(sample_tokens) for _ in range(runs)]
+    v = statistics.median(r["value"] for r in rs)
+    r = dict(rs[0], value=v)
+    r["sample"] += f"; median of {runs} calls after {warm} untimed"
+    return r
 
 
 # ------------------------------------------------------------------ B200 arm
@@ -300,6 +312,11 @@ def bench_prefill(args, world, rank, dev):
     # (3), token dedup (2), count exchange, dispatch push, wait, receive layout (head, permute 3,
     # row destinations), gate/up, down with the return in its epilogue, signal, wait, combine.
     launches_per_step = 21 if world > 1 else 8
+    # the host link's ceiling for e2e: both directions at once (the pipeline's copies overlap the
+    # replays), so a step takes at least the device step and each direction's copy time
+    link = bench_host_link(world, dev, T_PREFILL * H * 2)
+    link_ms = max(ms, T_PREFILL * H * 2 / (link["duplex_gbs"] * 1e9) * 1e3)
+    link["e2e_ceiling_tokens_per_s"] = round(world * T_PREFILL / (link_ms * 1e-3), 1)
     del caps
     torch.cuda.synchronize()
     if world > 1:
@@ -310,8 +327,49 @@ def bench_prefill(args, world, rank, dev):
                 router_gemm=rg,
                 e2e={"value": world * T_PREFILL / (e2e_ms * 1e-3), "unit": "tokens/s",
                      "h2d_bytes_per_step": T_PREFILL * H * 2, "d2h_bytes_per_step": T_PREFILL * H * 2,
-                     "ms_per_step": round(e2e_ms, 4)},
+                     "ms_per_step": round(e2e_ms, 4), "host_link": link},
                 gpu_launches=launches_per_step * args.steps)
+
+
+def bench_host_link(world, dev, nbytes, iters=20):
+    """Host-link bandwidth with the bench's own kind of buffers (pinned host, allocated after
+    the NUMA binding): ``nbytes`` up alone, down alone, and both directions at once on two
+    streams (as ``HostPipeline`` runs them), every rank copying at the same time.  GB/s of the
+    slowest rank (time max over ranks)."""
+    hin = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    hout = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    din = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    dout = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    sa, sb = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    comp = torch.cuda.current_stream(dev)
+
+    def timed(up, down):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record(comp)
+        for st, on, fn in ((sa, up, lambda: din.copy_(hin, non_blocking=True)),
+                           (sb, down, lambda: hout.copy_(dout, non_blocking=True))):
+            if not on:
+                continue
+            st.wait_event(ev[0])
+            with torch.cuda.stream(st):
+                for _ in range(iters):
+                    fn()
+        ev[1].record(sa)
+        ev[2].record(sb)
+        comp.wait_event(ev[1])
+        comp.wait_event(ev[2])
+        torch.cuda.synchronize()
+        return max(ev[0].elapsed_time(ev[1]) if up else 0.0, ev[0].elapsed_time(ev[2]) if down else 0.0)
+
+    res = {}
+    for name, up, down in (("h2d", True, False), ("d2h", False, True), ("duplex", True, True)):
+        timed(up, down)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = max_over_ranks(timed(up, down), world)
+        res[f"{name}_gbs"] = round(nbytes * iters / (ms * 1e-3) / 1e9, 1)
+    res["bytes_per_copy"] = nbytes
+    return res
 
 
 def bench_ep_stack(args, world, rank, dev, n_layers=48, T=8192, steps=2, warmup=1):
@@ -520,6 +578,56 @@ def bench_w8(dev, nw=16, iters=10):
     return res
 
 
+def bench_apply(dev, ncalls=16, iters=20):
+    """ExpW4.apply at M=1, the reference's drop-in decode entry (one token times its top-10
+    experts of the E=512 gate/up bank, K=H=2048, N=2I=1024).  16 calls with different expert
+    sets (178 MB of tile blocks, beyond L2) run in one CUDA graph; the expert-id path (the
+    experts read in place) is timed beside the earlier form that copied the selected tile
+    blocks out first (index_select, then the GEMM on the copy)."""
+    from fnx.engine import ExpW4, EPI_PLAIN, _grouped_w4
+    from fnx import _lib
+    K, N, G = H, 2 * I, H // GS
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    w4 = torch.randint(-2 ** 31, 2 ** 31 - 1, (E, K, N // 8), generator=g, device=dev, dtype=torch.int32)
+    sc = (torch.rand(E, G, N, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    ex = ExpW4.from_scales(w4, sc, GS)
+    del w4, sc
+    ex.tiles()
+    ex.w4 = ex._scales = None          # only the tile blocks are read
+    ids = [torch.randperm(E, generator=g, device=dev)[:K_TOP].contiguous() for _ in range(ncalls)]
+    x = torch.randn(1, K, generator=g, device=dev).to(torch.bfloat16)
+    ends = torch.arange(1, K_TOP + 1, device=dev, dtype=torch.int64)
+    rows = torch.zeros(K_TOP, device=dev, dtype=torch.int64)
+    outc = torch.empty(K_TOP, N, dtype=torch.bfloat16, device=dev)
+
+    def copied(i):
+        sel = ex.tiles().index_select(0, ids[i]).contiguous()
+        _grouped_w4(x, sel, ends, outc, E=K_TOP, M=K_TOP, K=K, Nw=N, epilogue=EPI_PLAIN, row_index=rows)
+
+    stream = torch.cuda.current_stream(dev)
+    pk, src = peaks()
+    per_expert = int(_lib.lib().fnx_w4_tiles_bytes(1, K, N))
+    nbytes = K_TOP * per_expert + 2 * K + 2 * K_TOP * N
+    res = {"M": 1, "experts": K_TOP, "K": K, "N": N, "bytes_per_call": nbytes, "peak_source": src}
+    for name, fn in (("in_place", lambda i: ex.apply(x, ids[i])), ("copy_then_gemm", copied)):
+        for i in range(ncalls):
+            fn(i)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for i in range(ncalls):
+                fn(i)
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        us = time_events(gr.replay, iters, stream) * 1e3 / ncalls
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[name] = {"us": round(us, 2), "achieved_gbs": round(gbs, 1), "frac_hbm": round(gbs / pk["hbm_gbs"], 4)}
+        del gr
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -562,6 +670,11 @@ def main():
     world, rank, local = dist_setup(args)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    # pinned host buffers on the GPU's NUMA node: the GPU part of the run is bound to the CPUs
+    # local to this rank's GPU; the CPU baseline afterwards gets every CPU back
+    from fnx.hostmem import bind_to_device
+    all_cpus = os.sched_getaffinity(0)
+    numa = bind_to_device(dev)
     import __graft_entry__
     __graft_entry__.build()
     if args.profile_case:
@@ -572,7 +685,9 @@ def main():
     stack = None if args.no_stack else bench_ep_stack(args, world, rank, dev)
     dec = None if (args.no_decode or world > 1) else bench_decode(dev)
     w8 = None if (args.no_decode or world > 1) else bench_w8(dev)
-    cpu = cpu_baseline(args.cpu_sample) if (rank == 0 and world == 1) else None
+    app = None if (args.no_decode or world > 1) else bench_apply(dev)
+    os.sched_setaffinity(0, all_cpus)
+    cpu = cpu_baseline_median(args.cpu_sample) if (rank == 0 and world == 1) else None
     if rank == 0:
         line = {"metric": METRIC, "value": round(r["value"], 1), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"], 4),
@@ -581,9 +696,9 @@ def main():
                 "config": dict(config, parallelism=f"ep{world}" if world > 1 else "single GPU",
                                **({"expert_parallel": r["ep"]} if r["ep"] else {})),
                 **({"ep_bit_identical": r["ep"]["bit_identical_to_one_gpu"]} if r["ep"] else {}),
-                "clocks": r["clocks"], "e2e": r["e2e"], "gpu_launches": r["gpu_launches"],
+                "clocks": r["clocks"], "e2e": dict(r["e2e"], numa=numa), "gpu_launches": r["gpu_launches"],
                 "roofline": r["roofline"], "layer_tflops": round(r["layer_tflops"], 1),
-                "router_gemm": r["router_gemm"], "ep_stack": stack, "decode": dec, "w8a16": w8,
+                "router_gemm": r["router_gemm"], "ep_stack": stack, "decode": dec, "w8a16": w8, "expw4_apply": app,
                 "cpu_baseline": cpu}
         print(json.dumps(line))
     if world > 1:

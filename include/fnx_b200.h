@@ -199,8 +199,8 @@ int fnx_repack_v2o(const void* v2o, int E, int N, int K, int expert_major, void*
 /* Load-time repack of the int4pack artifact (w4 int32 [E,K,Nw/8] expert-major, scales bf16
  * [E,K/gs,Nw]; tools/repack_w4a16.py, tools/repack_w4_em.py) into the tile blocks the B200
  * kernels stream: tiles int32 [E, Nw/128, K/64, 1088], one 4352-byte block per (expert,
- * feature tile m, k-block kb), contiguous along kb.  Word c*128 + r (c < 8) holds the 8 weights
- * k = 64kb+8c..+7 of tile row r as offset-binary nibbles in the order 0,2,4,6,1,3,5,7; bf16
+ * feature tile m, k-block kb), contiguous along kb.  Word c*128 + (r ^ 8*(c%4)) (c < 8) holds the 8
+ * weights k = 64kb+8c..+7 of tile row r as offset-binary nibbles in the order 0,2,4,6,1,3,5,7; bf16
  * 2048 + r (words 1024..1087) is row r's scale for the group holding kb (repeated in each
  * k-block of a group).  swiglu=1 orders tile rows as gate/up pairs (row 2i: gate feature
  * 64m+i, row 2i+1: up feature Nw/2+64m+i); swiglu=0: row r = 128m+r.
@@ -233,6 +233,18 @@ int fnx_moe_grouped_w4_rows(const void* act, long long ld_act, long long act_row
                             int index_div, const void* tiles, const void* ends, void* out_rows, int E, int M, int K,
                             int Nw, void* stream);
 
+/* fnx_moe_grouped_w4 (epilogues 0-2) over a selection of experts read in place, for ExpW4.apply /
+ * apply_diag (fnx/engine.py:691-721, whose reference form copies the selected experts out with
+ * expert_gather first): group e multiplies the tile blocks of expert expert_ids[e] (int64 [E])
+ * of the E_w experts in `tiles`; an id outside [0, E_w) reads expert 0 and sets device error 2. */
+int fnx_moe_grouped_w4_sel(const void* act, long long ld_act, long long act_rows, const void* row_index,
+                           int index_div, const void* tiles, int E_w, const void* expert_ids, const void* ends,
+                           void* out, long long ld_out, int E, int M, int K, int Nw, int epilogue, void* stream);
+
+/* W4GemvOp.weighted_sum (fnx/w4gemv_op.py:252-264): out fp32 [N] = sum over e of w[e] * y[e, :],
+ * y fp32 [nE, N], w fp32 [nE] on the device; products rounded, summed in expert order. */
+int fnx_weighted_sum_f32(const void* y, const void* w, void* out, int nE, int N, void* stream);
+
 /* DenseW8.__call__ (fnx/engine.py:350-365): y bf16 [M,N] = x bf16 [M,K] . bf16(w8t int8 [K,N]
  * * sc bf16 [G,N]) with fp32 accumulation.  K % 64 == 0, N % 128 == 0. */
 int fnx_w8a16_gemm(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G, void* stream);
@@ -246,8 +258,10 @@ size_t fnx_w8a16_gemm_workspace(int M, int K, int N, int G);
 int fnx_w8a16_gemm_ws(const void* x, const void* w8t, const void* sc, void* y, int M, int K, int N, int G, void* ws,
                       size_t ws_bytes, void* stream);
 
-/* bf16 GEMM y [M, N] = x [M, K] . w [N, K]^T (the router / concatenated shared GEMM,
- * fnx/engine.py:1787).  N % 128 == 0. */
+/* bf16 GEMM y [M, N] = x [M, K] . w [N, K]^T with fp32 accumulation (the router / concatenated
+ * shared GEMM, fnx/engine.py:1787; the hyper-connection mix's GEMMs, fnx/engine.py:818-857):
+ * both operands by TMA into a tcgen05 pipeline.  K % 64 == 0, ld_x % 8 == 0, x and w 16-byte
+ * aligned; any N (the last feature tile is partial). */
 int fnx_bf16_gemm_nt(const void* x, long long ld_x, const void* w, void* y, long long ld_y, int M, int K, int N,
                      void* stream);
 
@@ -269,9 +283,10 @@ int fnx_moe_combine_inject(void* yd, void* wf, void* inverse, void* sh, void* ga
  * tile blocks of fnx_repack_w4_tiles (gate/up with swiglu=1, down with swiglu=0);
  * out bf16 [M,H], w_out bf16 [M,k], idx_out int64 [M,k] (may be NULL).
  * H % 256 == 0, I % 128 == 0, H, I <= 4096, E <= 512.
- * workspace: fnx_moe_decode_workspace(M,H,I,E,k) bytes, zero-filled before first use;
- * each completed call leaves it ready for the next.  Calls sharing a workspace must not
- * overlap on the GPU. */
+ * workspace: fnx_moe_decode_workspace(M,H,I,E,k) bytes, 16-byte aligned, zero-filled before
+ * its first use and never cleared afterwards (its first word counts the calls made on it; the
+ * values one call hands between CTAs carry that call's tag).  out 4-byte aligned.  Calls sharing
+ * a workspace must not overlap on the GPU. */
 size_t fnx_moe_decode_workspace(int M, int H, int I, int E, int k);
 int fnx_moe_decode_w4(const void* x, const void* router, const void* gu, const void* dn, const void* sh_gu,
                       const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H, int I,

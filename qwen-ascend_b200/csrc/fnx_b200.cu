@@ -712,6 +712,37 @@ FNX_API int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_
     return gemm_launch(GEMM_W4, epilogue, p, (cudaStream_t)stream);
 }
 
+// fnx_moe_grouped_w4 over a selection of experts read in place: group e (rows [ends[e-1], ends[e]))
+// multiplies the tile blocks of expert expert_ids[e] of the E_w experts in `tiles` (no copy of the
+// selected experts, as ExpW4.apply / apply_diag need).
+FNX_API int fnx_moe_grouped_w4_sel(const void* act, long long ld_act, long long act_rows, const void* row_index,
+                                   int index_div, const void* tiles, int E_w, const void* expert_ids, const void* ends,
+                                   void* out, long long ld_out, int E, int M, int K, int Nw, int epilogue,
+                                   void* stream) {
+    if (!expert_ids || E_w < 1 || epilogue < 0 || epilogue > 2) return FNX_EARG;
+    GemmParams p{};
+    p.act = (const bf16*)act; p.ld_act = ld_act; p.row_index = (const int64_t*)row_index; p.index_div = index_div;
+    p.act_rows = act_rows;
+    if (act_rows < 0 || act_rows > 0x7fffffffLL || (!row_index && act_rows < M)) return FNX_EARG;
+    p.w = tiles; p.ends = (const int64_t*)ends; p.out = (bf16*)out; p.ld_out = ld_out;
+    p.E = E; p.M = M; p.K = K; p.Nw = Nw; p.gs = 0;
+    p.expert_ids = (const int64_t*)expert_ids;
+    p.E_w = E_w;
+    p.shared_e = -1;
+    p.m_tiles = epilogue == EPI_PLAIN ? Nw / G_BM : (Nw / 2) / 64;
+    const int rc = gemm_check(GEMM_W4, epilogue, p);
+    if (rc) return rc;
+    if (M == 0) return FNX_OK;
+    return gemm_launch(GEMM_W4, epilogue, p, (cudaStream_t)stream);
+}
+
+FNX_API int fnx_weighted_sum_f32(const void* y, const void* w, void* out, int nE, int N, void* stream) {
+    if (nE < 1 || N < 1 || !y || !w || !out) return FNX_EARG;
+    weighted_sum_f32_kernel<<<grid_for(N, 256), 256, 0, (cudaStream_t)stream>>>((const float*)y, (const float*)w,
+                                                                             (float*)out, nE, N);
+    return launch_rc();
+}
+
 FNX_API int fnx_moe_grouped_w4_rows(const void* act, long long ld_act, long long act_rows, const void* row_index,
                                     int index_div, const void* tiles, const void* ends, void* out_rows, int E, int M,
                                     int K, int Nw, void* stream) {

@@ -336,4 +336,15 @@ __global__ void __launch_bounds__(256) gather_pair_kernel(const uint8_t* __restr
     }
 }
 
+// out[n] = sum over e in order of fp32(w[e] * y[e, n]) (W4GemvOp.weighted_sum, fnx/w4gemv_op.py:252-264:
+// the expert outputs of one token weighted and summed); four columns per thread when aligned.
+__global__ void __launch_bounds__(256) weighted_sum_f32_kernel(const float* __restrict__ y, const float* __restrict__ w,
+                                                               float* __restrict__ out, int nE, int N) {
+    for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < N; n += gridDim.x * blockDim.x) {
+        float acc = 0.f;
+        for (int e = 0; e < nE; ++e) acc = __fadd_rn(acc, __fmul_rn(__ldg(w + e), __ldg(y + (long long)e * N + n)));
+        out[n] = acc;
+    }
+}
+
 }  // namespace fnx

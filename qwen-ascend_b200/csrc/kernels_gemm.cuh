@@ -95,7 +95,22 @@ struct GemmParams {
     // pass sums them in split order (deterministic).  0 or 1: no split.
     int ksplit;
     float* partial;
+    // W4: group e multiplies the tile blocks of expert expert_ids[e] of the E_w experts in `w`
+    // (null: expert e), so a selection of experts is read in place instead of being copied out
+    const int64_t* expert_ids;
+    int E_w;
 };
+
+// The expert whose tile blocks group e reads (an id outside [0, E_w) is flagged, and read as 0).
+FNX_DEV long long weight_expert(const GemmParams& p, int e) {
+    if (!p.expert_ids) return e;
+    const long long w = p.expert_ids[e];
+    if (w < 0 || w >= p.E_w) {
+        fnx_flag_error(FNX_DEVERR_BADID);
+        return 0;
+    }
+    return w;
+}
 
 FNX_DEV int gemm_ksplit(const GemmParams& p) { return p.ksplit > 1 ? p.ksplit : 1; }
 
@@ -585,7 +600,7 @@ __global__ void __launch_bounds__(G_THREADS, 1) grouped_gemm_kernel(const __grid
                 bool ok = true;
                 if (MODE == GEMM_W4) {
                     const uint8_t* tsrc = reinterpret_cast<const uint8_t*>(p.w) +
-                                          ((long long)ti.e * p.m_tiles + ti.m) * KB * (long long)G_RAW_BYTES;
+                                          (weight_expert(p, ti.e) * p.m_tiles + ti.m) * KB * (long long)G_RAW_BYTES;
                     for (int kb0 = 0; kb0 < KB; kb0 += G_OPK, ++op) {
                         const int os = op % G_R_OPS;
                         if (!mbar_wait(&S.raw_empty[os], ((op / G_R_OPS) & 1) ^ 1)) { ok = false; break; }

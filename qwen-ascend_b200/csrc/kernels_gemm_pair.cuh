@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) grouped_gemm_pair_kernel(const _
                 if (!decode_pair_tile(S, p, tile, rank, ti)) break;
                 bool ok = true;
                 const uint8_t* tsrc = reinterpret_cast<const uint8_t*>(p.w) +
-                                      ((long long)ti.e * p.m_tiles + ti.m) * KB * (long long)G_RAW_BYTES;
+                                      (weight_expert(p, ti.e) * p.m_tiles + ti.m) * KB * (long long)G_RAW_BYTES;
                 for (int kb0 = 0; kb0 < KB; kb0 += G_OPK, ++op) {
                     const int os = op % P_R_OPS;
                     if (!mbar_wait(&S.raw_empty[os], ((op / P_R_OPS) & 1) ^ 1)) { ok = false; break; }

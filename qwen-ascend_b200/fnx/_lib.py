@@ -63,6 +63,8 @@ SIGNATURES = {
     "fnx_ep_p2p_recv_layout": ([P, I, P, P, P, P, P, P, SZ, P], I),
     "fnx_moe_grouped_w4_rows": ([P, LL, LL, P, I, P, P, P, I, I, I, I, P], I),
     "fnx_moe_grouped_w4": ([P, LL, LL, P, I, P, P, P, LL] + [I] * 5 + [P], I),
+    "fnx_moe_grouped_w4_sel": ([P, LL, LL, P, I, P, I, P, P, P, LL] + [I] * 5 + [P], I),
+    "fnx_weighted_sum_f32": ([P, P, P, I, I, P], I),
     "fnx_repack_v2o": ([P, I, I, I, I, P, P], I),
     "fnx_w4_tiles_bytes": ([I] * 3, SZ),
     "fnx_repack_w4_tiles": ([P] * 3 + [I] * 5 + [P], I),

@@ -173,27 +173,60 @@ class ExpW4:
             self._tiles = t
         return t
 
-    def _selected(self, ids):
-        return self.tiles().index_select(0, ids).contiguous()
+    def _groups(self, k, M, device):
+        """Cached group ends and the source row of every grouped row (row m of every group
+        reads x[m]) for k groups of M rows each (the reference keeps ``_dg``/``_ends`` for the
+        same purpose, ``fnx/engine.py:661-669``)."""
+        cache = self.__dict__.setdefault("_group_cache", {})
+        key = (k, M, str(device))
+        g = cache.get(key)
+        if g is None:
+            ends = torch.arange(1, k + 1, device=device, dtype=torch.int64) * M
+            rows = torch.arange(k * M, device=device, dtype=torch.int64) % M
+            g = cache[key] = (ends, rows)
+        return g
+
+    def _ids(self, ids, device):
+        if isinstance(ids, torch.Tensor):
+            return ids.to(device=device, dtype=torch.int64).contiguous().view(-1)
+        return torch.tensor(ids, dtype=torch.int64, device=device).view(-1)
+
+    def _sel(self, x, ids, out, k, M, rows_per_group, diagonal=False):
+        """Grouped GEMM over experts ``ids`` read in place from the cached tile blocks (an
+        expert-id table, no copy of the selected experts).  ``diagonal``: grouped row j reads
+        x[j] (no row index)."""
+        ends, rows = self._groups(k, rows_per_group, x.device)
+        if diagonal:
+            rows = None
+        rc = _lib.lib().fnx_moe_grouped_w4_sel(x.data_ptr(), x.stride(0), x.shape[0], _lib.ptr(rows), 1,
+                                               self.tiles().data_ptr(), self.E, ids.data_ptr(), ends.data_ptr(),
+                                               out.data_ptr(), out.stride(0), k, M, self.K, self.N, EPI_PLAIN,
+                                               _lib.stream(x.device))
+        _lib.check(rc, "grouped W4A16 GEMM (selected experts)")
+        return out
 
     def apply(self, x, ids):
         """x ``[M, K]`` bf16, ids ``[k]`` -> ``[M, k*N]``: every row times every selected expert."""
-        M, k = x.shape[0], ids.numel()
-        w = self._selected(ids)
-        rows = torch.arange(k * M, device=x.device, dtype=torch.int64) % M
-        ends = torch.arange(1, k + 1, device=x.device, dtype=torch.int64) * M
+        M = x.shape[0]
+        x = (x if x.dtype == BF16 else x.to(BF16)).contiguous()
+        ids = self._ids(ids, x.device)
+        k = ids.numel()
         out = torch.empty(k * M, self.N, dtype=BF16, device=x.device)
-        _grouped_w4(x.to(BF16).contiguous(), w, ends, out, E=k, M=k * M, K=self.K, Nw=self.N,
-                    epilogue=EPI_PLAIN, row_index=rows)
+        if k and M:
+            self._sel(x, ids, out, k, k * M, M)
         return out.view(k, M, self.N).transpose(0, 1).reshape(M, k * self.N)
 
     def apply_diag(self, x, ids):
         """Row j of x uses expert ids[j] -> ``[k, N]`` (the diagonal of the Cartesian product)."""
         k = x.shape[0]
-        w = self._selected(ids)
-        ends = torch.arange(1, k + 1, device=x.device, dtype=torch.int64)
+        x = (x if x.dtype == BF16 else x.to(BF16)).contiguous()
+        ids = self._ids(ids, x.device)
+        if ids.numel() != k:
+            raise ValueError(f"apply_diag: {ids.numel()} expert ids for {k} rows")
         out = torch.empty(k, self.N, dtype=BF16, device=x.device)
-        return _grouped_w4(x.to(BF16).contiguous(), w, ends, out, E=k, M=k, K=self.K, Nw=self.N, epilogue=EPI_PLAIN)
+        if k:
+            self._sel(x, ids, out, k, k, 1, diagonal=True)
+        return out
 
     def apply_grouped(self, x, group_ends, host_ends=None):
         """Rows sorted by expert (cumulative ``group_ends`` over all E experts)."""
@@ -561,7 +594,11 @@ class HostPipeline:
     while batch i's graph replays on the compute stream, batch i+1's input goes up and batch
     i-1's output comes down on two copy streams (the two directions of the host link run at
     once).  ``slots`` are ``CapturedLayer`` objects used round-robin (at least two); batch i
-    runs on slot ``i % len(slots)``, so consecutive batches never share static buffers."""
+    runs on slot ``i % len(slots)``.  A slot's input buffer is refilled once its previous
+    batch's replay is done (that replay is the only reader of the input), and its next replay
+    waits until the previous output has been copied out, so the upload of batch i+1 does not
+    wait for the download of batch i-1: per batch the pipeline takes the longest of the replay,
+    the upload and the download, not the replay or their sum."""
 
     def __init__(self, slots):
         if len(slots) < 2:
@@ -578,7 +615,7 @@ class HostPipeline:
         n, S = len(xs_host), len(self.slots)
         comp = torch.cuda.current_stream(self.device)
         ev = lambda: torch.cuda.Event()                       # noqa: E731
-        in_ready, done, out_free = [None] * n, [None] * n, [None] * S
+        in_ready, done, out_free = [None] * n, [None] * n, [None] * n
         start = ev()
         start.record(comp)
         self.h2d.wait_event(start)
@@ -586,8 +623,8 @@ class HostPipeline:
 
         def upload(i):
             s = self.slots[i % S]
-            if out_free[i % S] is not None:                 # previous user of the slot finished
-                self.h2d.wait_event(out_free[i % S])
+            if i >= S:                                      # the slot's previous replay read its input
+                self.h2d.wait_event(done[i - S])
             with torch.cuda.stream(self.h2d):
                 s.x.copy_(xs_host[i].reshape(s.x.shape), non_blocking=True)
             in_ready[i] = ev()
@@ -600,16 +637,16 @@ class HostPipeline:
             if i + 1 < n:
                 upload(i + 1)
             comp.wait_event(in_ready[i])
+            if i >= S:                                      # the slot's previous output is copied out
+                comp.wait_event(out_free[i - S])
             s.replay()
             done[i] = ev()
             done[i].record(comp)
             self.d2h.wait_event(done[i])
             with torch.cuda.stream(self.d2h):
                 outs_host[i].copy_(s.out, non_blocking=True)
-            out_free[i % S] = ev()
-            out_free[i % S].record(self.d2h)
-            # the slot's next batch waits for out_free[i % S] in upload(), and its replay waits
-            # for that upload, so neither its input nor its output is overwritten early
+            out_free[i] = ev()
+            out_free[i].record(self.d2h)
         # the caller's stream sees every output copied
         end = ev()
         end.record(self.d2h)

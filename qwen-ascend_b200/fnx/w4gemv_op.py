@@ -128,9 +128,21 @@ class W4GemvOp:
 
     @staticmethod
     def weighted_sum(y_dev, w):
-        """sum_e w_e * y_e (``fnx/w4gemv_op.py:252-264``)."""
+        """sum_e w_e * y_e (``fnx/w4gemv_op.py:252-264``): one kernel, fp32 products rounded
+        and summed in expert order.  y ``[nE, N]`` (cast to fp32 if needed), w ``[nE]``."""
+        _lib.require_cuda(y_dev)
+        y = (y_dev if y_dev.dtype == torch.float32 else y_dev.float()).contiguous()
         if isinstance(w, torch.Tensor):
-            wt = w.to(device=y_dev.device, dtype=torch.float32)
+            wt = w.to(device=y.device, dtype=torch.float32).contiguous().view(-1)
         else:
-            wt = torch.from_numpy(np.asarray(w, dtype=np.float32)).to(y_dev.device)
-        return (y_dev * wt.view(-1, 1)).sum(dim=0)
+            wt = torch.from_numpy(np.asarray(w, dtype=np.float32).reshape(-1)).to(y.device)
+        nE, N = y.shape
+        if wt.numel() != nE:
+            raise ValueError(f"weighted_sum: {wt.numel()} weights for {nE} rows")
+        if nE == 0 or N == 0:
+            return torch.zeros(N, dtype=torch.float32, device=y.device)
+        out = torch.empty(N, dtype=torch.float32, device=y.device)
+        rc = _lib.lib().fnx_weighted_sum_f32(y.data_ptr(), wt.data_ptr(), out.data_ptr(), nE, N,
+                                             _lib.stream(y.device))
+        _lib.check(rc, "weighted sum")
+        return out

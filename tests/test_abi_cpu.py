@@ -55,6 +55,14 @@ def test_host_side_rejections(lib):
     assert g(None, 2048, 64, None, 1, None, None, None, 1024, 8, 64, 2048, 1000, 0, None) == -2
     assert g(None, 2048, 64, None, 1, None, None, None, 1024, 8, 64, 2048, 1024, 5, None) == -1
     assert g(None, 2048, 10, None, 1, None, None, None, 1024, 8, 64, 2048, 1024, 0, None) == -1  # rows < M
+    # the expert-id form: an id table and E_w >= 1 required, epilogues 0-2 only, then the same rules
+    gs = lib.fnx_moe_grouped_w4_sel
+    assert gs(None, 2048, 64, None, 1, None, 8, None, None, None, 1024, 8, 64, 2048, 1024, 0, None) == -1
+    assert gs(None, 2048, 64, None, 1, None, 0, 8, None, None, 1024, 8, 64, 2048, 1024, 0, None) == -1
+    assert gs(None, 2048, 64, None, 1, None, 8, 8, None, None, 1024, 8, 64, 2048, 1024, 3, None) == -1
+    assert gs(None, 2048, 64, None, 1, None, 8, 8, None, None, 1024, 8, 64, 2048, 1000, 0, None) == -2
+    assert lib.fnx_weighted_sum_f32(8, 8, 8, 0, 100, None) == -1                                 # no experts
+    assert lib.fnx_weighted_sum_f32(None, 8, 8, 4, 100, None) == -1                              # no y
     assert lib.fnx_repack_w4_tiles(None, None, None, 8, 2048, 1024, 96, 0, None) == -1          # gs % 64
     assert lib.fnx_repack_v2o(None, 8, 1024, 2048, 0, None, None) == -1                          # no buffers
     assert lib.fnx_inject(None, None, None, None, 0, None) == -1                                  # batch 0

@@ -226,6 +226,63 @@ def test_expw4_apply_paths():
     assert torch.equal(ex2._scales.cpu().view(torch.int16), O.cached_scales(s8t, base).view(torch.int16))
 
 
+@pytest.mark.parametrize("M", [1, 3])
+def test_expw4_apply_reads_experts_in_place(M):
+    """apply/apply_diag hand the grouped GEMM an expert-id table: the result has the bits of the
+    GEMM over a copied selection, and a warm M=1 call launches the GEMM and nothing else (no
+    gather of tile blocks, no index tensors built per call)."""
+    from fnx.engine import ExpW4, _grouped_w4, EPI_PLAIN
+    E, K, N, gs = 16, 512, 256, 128
+    w, s = _w4(E, K, N, gs, seed=21)
+    ex = ExpW4.from_scales(w.to(DEV), s.to(DEV), gs)
+    ids = torch.tensor([5, 0, 15, 5], dtype=torch.int64, device=DEV)
+    k = ids.numel()
+    x = torch.randn(M, K).to(BF16).to(DEV)
+    y = ex.apply(x, ids)
+    sel = ex.tiles().index_select(0, ids).contiguous()
+    rows = torch.arange(k * M, device=DEV, dtype=torch.int64) % M
+    ends = torch.arange(1, k + 1, device=DEV, dtype=torch.int64) * M
+    ref = torch.empty(k * M, N, dtype=BF16, device=DEV)
+    _grouped_w4(x, sel, ends, ref, E=k, M=k * M, K=K, Nw=N, epilogue=EPI_PLAIN, row_index=rows)
+    ref = ref.view(k, M, N).transpose(0, 1).reshape(M, k * N)
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+    xd = torch.randn(k, K).to(BF16).to(DEV)
+    yd = ex.apply_diag(xd, ids)
+    refd = torch.empty(k, N, dtype=BF16, device=DEV)
+    _grouped_w4(xd, sel, torch.arange(1, k + 1, device=DEV, dtype=torch.int64), refd, E=k, M=k, K=K, Nw=N,
+                epilogue=EPI_PLAIN)
+    assert torch.equal(yd.view(torch.int16), refd.view(torch.int16))
+    if M == 1:
+        torch.cuda.synchronize()
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+            ex.apply(x, ids)
+            torch.cuda.synchronize()
+        names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+        assert len(names) == 1 and "grouped_gemm" in names[0], names
+    # an id outside [0, E) reads expert 0 and raises the device error flag
+    torch.cuda.synchronize()
+    _lib.device_errors()
+    ex.apply(x, torch.tensor([2, E], dtype=torch.int64, device=DEV))
+    torch.cuda.synchronize()
+    assert _lib.device_errors() & 2
+
+
+def test_weighted_sum_kernel():
+    """W4GemvOp.weighted_sum: one kernel, products rounded and summed in expert order."""
+    from fnx.w4gemv_op import W4GemvOp
+    g = torch.Generator().manual_seed(5)
+    y = torch.randn(6, 3000, generator=g)
+    w = torch.rand(6, generator=g)
+    got = W4GemvOp.weighted_sum(y.to(DEV), w.to(DEV)).cpu()
+    ref = torch.zeros(3000)
+    for e in range(6):
+        ref = ref + w[e] * y[e]
+    assert torch.equal(got, ref)
+    got2 = W4GemvOp.weighted_sum(y.to(DEV), w.tolist()).cpu()
+    assert torch.equal(got2, ref)
+    assert torch.equal(W4GemvOp.weighted_sum(y[:0].to(DEV), []).cpu(), torch.zeros(3000))
+
+
 @pytest.mark.parametrize("T", [300, 4])
 def test_captured_layer_replays_the_call(T):
     """MoELayer.capture: the graph replay gives the direct call's bits, on new inputs too."""
