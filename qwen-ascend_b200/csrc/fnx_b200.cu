@@ -208,6 +208,16 @@ int gemm_pair_launch_t(GemmParams& p, cudaStream_t st) {
     return launch_rc();
 }
 
+// FNX_GEMM_B_TMA=0 keeps the gathering loaders for contiguous token rows too (for comparisons).
+bool b_tma_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("FNX_GEMM_B_TMA");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
+}
+
 // FNX_GEMM_PAIR=0 selects the single-CTA W4 kernel (for comparisons).
 bool pair_enabled() {
     static int on = -1;
@@ -221,6 +231,18 @@ bool pair_enabled() {
 int gemm_launch(int mode, int epi, GemmParams& p, cudaStream_t st) {
     if (mode == GEMM_W4 && p.m_tiles % 2 == 0 && p.K % (G_BK * P_KS) == 0 && p.ld_out % 8 == 0 && aligned16(p.out) &&
         pair_enabled()) {
+        // contiguous token rows (no row index): the pair kernel loads them by TMA
+        p.b_tma = 0;
+        if (!p.row_index && p.act_rows >= 32 && b_tma_enabled()) {
+            const unsigned long long rows = (unsigned long long)p.act_rows;
+            int rc = make_map_2d(&p.tmap_b32, p.act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (unsigned long long)p.K, rows,
+                                 G_BK, 32, CU_TENSOR_MAP_SWIZZLE_128B, (unsigned long long)p.ld_act * 2);
+            if (!rc)
+                rc = make_map_2d(&p.tmap_b8, p.act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (unsigned long long)p.K, rows,
+                                 G_BK, 8, CU_TENSOR_MAP_SWIZZLE_128B, (unsigned long long)p.ld_act * 2);
+            if (rc) return rc;
+            p.b_tma = 1;
+        }
         if (epi == EPI_PLAIN) return gemm_pair_launch_t<EPI_PLAIN>(p, st);
         if (epi == EPI_SWIGLU_F32) return gemm_pair_launch_t<EPI_SWIGLU_F32>(p, st);
         if (epi == EPI_SWIGLU_MIXED) return gemm_pair_launch_t<EPI_SWIGLU_MIXED>(p, st);

@@ -46,7 +46,7 @@ enum GemmEpi { EPI_PLAIN = 0, EPI_SWIGLU_F32 = 1, EPI_SWIGLU_BF16 = 2, EPI_SWIGL
 constexpr int G_BM = 128;          // weight features per tile (UMMA M)
 constexpr int G_BK = 64;           // k per stage (one 128-byte swizzle row of bf16)
 constexpr int G_BN = 128;          // max token rows per tile
-constexpr int G_MAX_STAGES = 8;
+constexpr int G_MAX_STAGES = 10;
 // Raw int4 ring: G_R_OPS slots of G_OPK tile blocks.  One bulk copy fills a slot with up to
 // G_OPK consecutive k-blocks of a tile (17 KB): a bulk copy costs the copy engine a few
 // hundred cycles however small it is, so 4 KB copies cap the stream near 4.5 TB/s.
@@ -99,6 +99,11 @@ struct GemmParams {
     // (null: expert e), so a selection of experts is read in place instead of being copied out
     const int64_t* expert_ids;
     int E_w;
+    // CTA-pair W4 kernel without a row index: the token rows of a tile are contiguous, so one thread
+    // loads them by TMA (act [act_rows, K], boxes of 32 and 8 rows x 64 k, 128-byte swizzle) in
+    // place of the gathering loader warps
+    int b_tma;
+    CUtensorMap tmap_b32, tmap_b8;
 };
 
 // The expert whose tile blocks group e reads (an id outside [0, E_w) is flagged, and read as 0).

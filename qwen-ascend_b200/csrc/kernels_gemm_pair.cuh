@@ -27,7 +27,14 @@ namespace fnx {
 // A stage carries P_KS k-blocks (128 k): every hand-off between the roles costs a few hundred
 // cycles of latency however little work the stage holds, so stages hold two k-blocks.
 constexpr int P_KS = 2;
-constexpr int P_STAGES = 4;                          // A stages in tensor memory: 8 k-blocks in flight
+// Token rows per pair tile.  Tensor memory holds the two accumulators (P_BN columns each) and the A
+// ring (64 columns per stage) in 512 columns, so narrower token tiles buy a deeper A ring: 128 rows
+// leave 4 stages (8 k-blocks in flight), 96 leave 5.
+#ifndef FNX_PAIR_BN
+#define FNX_PAIR_BN 128
+#endif
+constexpr int P_BN = FNX_PAIR_BN;
+constexpr int P_STAGES = (512 - 2 * P_BN) / 64;      // A stages in tensor memory
 // Token tiles have their own, deeper ring: their path (gather issue + L2 latency + hand-offs)
 // is the longest of the stage loop, so it runs further ahead than the TMEM-bound A ring.
 #ifndef FNX_PAIR_BSTAGES
@@ -49,14 +56,15 @@ constexpr int P_PROD = FNX_PAIR_PROD;                // producer warps: 8 .. 8 +
 constexpr int P_KPW = P_KS * 8 / P_PROD;             // k-blocks of a stage each producer warp converts
 constexpr int P_LOADER0 = 8 + P_PROD;                // loader warps 0 and P_LOADER0 .. P_LOADER0 + 2
 constexpr int P_THREADS = 32 * (P_LOADER0 + G_LOADERS - 1);   // 27 warps
-constexpr int P_BN_HALF = G_BN / 2;                  // token rows per CTA per tile
+constexpr int P_BN_HALF = P_BN / 2;                  // token rows per CTA per tile
 constexpr int P_B_SUB = P_BN_HALF * G_BK * 2;        // 8 KB: one k-block of this CTA's token rows
 constexpr int P_B_BYTES = P_KS * P_B_SUB;            // 16 KB per stage
 constexpr int P_R_OPS = FNX_PAIR_ROPS;               // raw ring: copies of 4 tile blocks (17 KB each)
 constexpr uint32_t P_TMEM_COLS = 512;
-constexpr uint32_t P_A_COL0 = 2 * G_BN;
+constexpr uint32_t P_A_COL0 = 2 * P_BN;
 constexpr uint32_t P_A_COLS = 32 * P_KS;             // tensor-memory columns of one A stage
 static_assert(G_OPK % P_KS == 0, "a copy holds whole stages");
+static_assert(P_BN % 32 == 0 && P_BN <= G_BN && P_BN_HALF % (4 * G_LOADERS) == 0, "token tile: whole loader rounds");
 static_assert(P_KS == 2 && (P_PROD == 8 || P_PROD == 16), "producer groups of 4 or 8 warps over 2 k-blocks");
 static_assert(P_STAGES <= G_MAX_STAGES && P_BSTAGES <= G_MAX_STAGES && P_R_OPS <= G_MAX_R_OPS &&
                   P_A_COL0 + P_STAGES * P_A_COLS <= P_TMEM_COLS,
@@ -77,8 +85,8 @@ FNX_DEV bool decode_pair_tile(const GemmSmem& S, const GemmParams& p, int tile, 
     ti.m = 2 * (local % pairs) + (int)rank;
     const long long begin = min((long long)p.M, (long long)(p.ends ? (e ? p.ends[e - 1] : 0) : 0));
     const long long end = min((long long)p.M, (long long)(p.ends ? p.ends[e] : p.M));
-    ti.row0 = (int)begin + (local / pairs) * G_BN;
-    ti.nrows = (int)min((long long)G_BN, end - ti.row0);
+    ti.row0 = (int)begin + (local / pairs) * P_BN;
+    ti.nrows = (int)min((long long)P_BN, end - ti.row0);
     return true;
 }
 
@@ -104,7 +112,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) grouped_gemm_pair_kernel(const _
             mbar_init(&S.empty[s], 1);
         }
         for (int s = 0; s < P_BSTAGES; ++s) {
-            mbar_init(&S.b_full[s], 32 * G_LOADERS);
+            mbar_init(&S.b_full[s], p.b_tma ? 1 : 32 * G_LOADERS);
             mbar_init(&S.b_empty[s], 1);
             mbar_init(&S.peer_full[s], 1);
         }
@@ -136,7 +144,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) grouped_gemm_pair_kernel(const _
                 const long long begin = min((long long)p.M, (long long)(p.ends ? (e ? p.ends[e - 1] : 0) : 0));
                 const long long end = min((long long)p.M, (long long)(p.ends ? p.ends[e] : p.M));
                 const long long cnt = end > begin ? end - begin : 0;
-                n = (int)((cnt + G_BN - 1) / G_BN) * (p.m_tiles / 2);
+                n = (int)((cnt + P_BN - 1) / P_BN) * (p.m_tiles / 2);
             }
             int incl = n;
 #pragma unroll
@@ -168,7 +176,40 @@ __global__ void __launch_bounds__(P_THREADS, 1) grouped_gemm_pair_kernel(const _
     const int KB = p.K / G_BK;
     const int KS = KB / P_KS;                            // stages per tile (K % 128 == 0)
 
-    if (warp == 0 || warp >= P_LOADER0) {
+    if ((warp == 0 || warp >= P_LOADER0) && p.b_tma) {
+        // ------------------------------------------------ B by TMA: this CTA's rows of the chunk are
+        // act rows row0 + rank * hp .. + hp - 1 (contiguous); boxes of 32, then 8 rows land at
+        // 1024-byte aligned offsets of the stage in the layout the gathering loaders write
+        if (warp == 0 && lane == 0) {
+            tma_prefetch_desc(&p.tmap_b32);
+            tma_prefetch_desc(&p.tmap_b8);
+            int it = 0;
+            for (int tile = cid; !S.abort; tile += ncl) {
+                TileInfo ti;
+                if (!decode_pair_tile(S, p, tile, rank, ti)) break;
+                const int hp = ((ti.nrows + 15) & ~15) / 2;
+                const int r0 = ti.row0 + (int)rank * hp;
+                bool ok = true;
+                for (int ks = 0; ks < KS; ++ks, ++it) {
+                    const int s = it % P_BSTAGES;
+                    if (!mbar_wait_cluster(&S.b_empty[s], ((it / P_BSTAGES) & 1) ^ 1)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&S.b_full[s], (uint32_t)(P_KS * hp * G_BK * 2));
+#pragma unroll
+                    for (int h = 0; h < P_KS; ++h) {
+                        uint8_t* bt = b_tiles + s * P_B_BYTES + h * P_B_SUB;
+                        const int x = (ks * P_KS + h) * G_BK;
+                        int n = 0;
+                        for (; n + 32 <= hp; n += 32)
+                            tma_load_2d(smem_u32(bt + n * G_BK * 2), &p.tmap_b32, &S.b_full[s], x, r0 + n);
+                        for (; n < hp; n += 8)
+                            tma_load_2d(smem_u32(bt + n * G_BK * 2), &p.tmap_b8, &S.b_full[s], x, r0 + n);
+                    }
+                }
+                if (!ok) { S.abort = 1; break; }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 0 || warp >= P_LOADER0) {
         // ------------------------------------------------ B loaders: this CTA's half of the chunk rows
         const int lw = warp == 0 ? 0 : warp - P_LOADER0 + 1;
         const uint64_t keep = l2_evict_last();
@@ -180,9 +221,9 @@ __global__ void __launch_bounds__(P_THREADS, 1) grouped_gemm_pair_kernel(const _
             const int npad = (ti.nrows + 15) & ~15;
             const int hp = npad / 2;                       // rows per CTA, a multiple of 8
             const int rbase = (int)rank * hp;
-            int src_row[P_BN_HALF / 32];                   // lane L: local rows L, L+32
+            int src_row[(P_BN_HALF + 31) / 32];            // lane L: local rows L, L+32
 #pragma unroll
-            for (int i = 0; i < P_BN_HALF / 32; ++i) {
+            for (int i = 0; i < (P_BN_HALF + 31) / 32; ++i) {
                 const int n = lane + 32 * i;
                 long long src = -1;
                 if (n < hp && rbase + n < ti.nrows) {
@@ -247,7 +288,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) grouped_gemm_pair_kernel(const _
                 const uint32_t n16 = ((__shfl_sync(0xffffffffu, pack, loc >> 3) >> (4 * (loc & 7))) & 15u) + 1u;
                 const int ab = i & 1;
                 const uint32_t idesc = idesc_bf16_f32(2 * G_BM, (int)n16 * 16);
-                const uint32_t d = tmem + ab * G_BN;
+                const uint32_t d = tmem + ab * P_BN;
                 for (int ks = 0; ks < KS; ++ks, ++j) {
                     const int s = j % P_STAGES, sb = j % P_BSTAGES;
                     named_bar_sync(G_BAR_FULL, 64);
@@ -349,7 +390,7 @@ __global__ void __launch_bounds__(P_THREADS, 1) grouped_gemm_pair_kernel(const _
             const int npad = (ti.nrows + 15) & ~15;
             for (int n0 = 0; n0 < npad; n0 += 16) {
                 uint32_t v[16];
-                tmem_ld16(tmem + ((uint32_t)(e4 * 32) << 16) + ab * G_BN + n0, v);
+                tmem_ld16(tmem + ((uint32_t)(e4 * 32) << 16) + ab * P_BN + n0, v);
                 tmem_ld_wait();
                 epilogue_chunk_staged<EPI>(p, ti, e4, n0, v, epi_stage + e4 * 512);
             }
