@@ -338,6 +338,7 @@ FNX_API int fnx_gather_pair(void* w, void* s, void* ids, void* ow, void* os, int
 FNX_API int fnx_moe_combine(void* yd, void* wf, void* inverse, void* sh, void* gate, long long gate_ld, void* out, int T,
                             int k, int H, void* stream) {
     if (T < 0 || k < 1 || k > 64 || H < 1 || gate_ld < 1) return FNX_EARG;
+    if ((long long)T * k > 0x7fffffffLL) return FNX_ESHAPE;
     if (T == 0) return FNX_OK;
     const bool vec = H % 8 == 0 && aligned16(yd) && aligned16(sh) && aligned16(out);
     const int grid = grid_for((long long)T * (vec ? H / 8 : H), 256);
@@ -372,6 +373,7 @@ FNX_API int fnx_moe_combine_inject(void* yd, void* wf, void* inverse, void* sh, 
         return FNX_EARG;
     if (!aligned16(yd) || !aligned16(sh) || !aligned16(hyper) || !aligned16(out_hyper) || (out && !aligned16(out)))
         return FNX_EALIGN;
+    if ((long long)T * k > 0x7fffffffLL) return FNX_ESHAPE;
     if (T == 0) return FNX_OK;
     const int grid = grid_for((long long)T * (H / 8), 256);
     moe_combine_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(
@@ -450,9 +452,9 @@ int permute_launch(const void* idx, void* order, void* inverse, void* ends, void
         if (counts) cudaMemsetAsync(counts, 0, sizeof(int64_t) * E, st);
         return launch_rc();
     }
+    const int dev = current_device();
     const size_t ssm = permute_scatter_smem(E);
     static bool ssm_set[FNX_MAX_DEVICES] = {};
-    const int dev = current_device();
     if (ssm > 48 * 1024 && !ssm_set[dev]) {
         if (cudaFuncSetAttribute(permute_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)permute_scatter_smem(PERM_MAX_E)) != cudaSuccess)

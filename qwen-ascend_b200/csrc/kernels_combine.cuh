@@ -151,16 +151,29 @@ __global__ void __launch_bounds__(256) inject_kernel(const bf16* __restrict__ hy
 // The combine.  With `hyper` (the fused inject of fnx/engine.py:859-877): out_hyper[t, b*H + c] =
 // bf16(hyper[t, b*H + c] + bf16(y[t, c] * inj[t, b])) for the HC branches, y the combined
 // output (also written to `out` when it is not null).  Needs the vector path (H % 8, k <= 16).
+// Vector path: a thread owns 8 columns of one token.  When a token's columns fill whole warps
+// (H % 256 == 0) lane q < k of the warp loads slot q's row index and weight once and the warp
+// shares them by shuffles as they are used; the k rows are requested FNX_COMBINE_G at a time
+// before the in-order sums (T*k < 2^31 rows, checked by the host).
+#ifndef FNX_COMBINE_G
+#define FNX_COMBINE_G 4
+#endif
+#ifndef FNX_COMBINE_MINB
+#define FNX_COMBINE_MINB 4
+#endif
 template <bool VEC>
-__global__ void __launch_bounds__(256, 3) moe_combine_kernel(const bf16* __restrict__ yd, const float* __restrict__ w,
+__global__ void __launch_bounds__(256, FNX_COMBINE_MINB) moe_combine_kernel(const bf16* __restrict__ yd, const float* __restrict__ w,
                                                           const int64_t* __restrict__ inverse,
                                                           const bf16* __restrict__ sh, const bf16* __restrict__ gate,
                                                           long long gate_ld, bf16* __restrict__ out, int T, int k,
                                                           int H, const bf16* __restrict__ hyper = nullptr,
                                                           const bf16* __restrict__ inj = nullptr,
                                                           bf16* __restrict__ out_hyper = nullptr, int HC = 0) {
+    constexpr int G = FNX_COMBINE_G;
     const int per_row = VEC ? H / 8 : H;
     const long long total = (long long)T * per_row;
+    const bool warp_token = VEC && (per_row & 31) == 0;      // a warp's items share one token
+    const long long nrows = (long long)T * k;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
         const int t = (int)(i / per_row);
@@ -169,46 +182,59 @@ __global__ void __launch_bounds__(256, 3) moe_combine_kernel(const bf16* __restr
 #pragma unroll
         for (int j = 0; j < (VEC ? 8 : 1); ++j) acc[j] = 0.f;
         if (VEC && k <= 16) {
-            // the k row indices and weights first, then the rows four at a time (the shared
-            // row and gate are loaded with the indices)
-            long long rows[16];
-            float s[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                rows[q] = -1;
-                s[q] = 0.f;
-                if (q < k) {
-                    const long long slot = (long long)t * k + q;
-                    rows[q] = inverse ? inverse[slot] : slot;
-                    s[q] = w[slot];
+            // warp_token: lane q < k holds slot q's row and weight; otherwise each thread reads them
+            int my_r = -1;
+            float my_w = 0.f;
+            if (warp_token) {
+                const int lane = threadIdx.x & 31;
+                if (lane < k) {
+                    const long long slot = (long long)t * k + lane;
+                    const long long r = inverse ? inverse[slot] : slot;
+                    my_r = (r >= 0 && r < nrows) ? (int)r : -1;
+                    my_w = w[slot];
                 }
             }
             const long long off = (long long)t * H + c;
             const uint4 sv = ld_nc_v4(sh + off);
             const float g = bf2f(gate[(long long)t * gate_ld]);
 #pragma unroll
-            for (int j0 = 0; j0 < 16; j0 += 4) {
+            for (int j0 = 0; j0 < 16; j0 += G) {
                 if (j0 >= k) break;
-                uint4 v[4];
+                int r[G];
+                float sw[G];
+                uint4 v[G];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    v[q] = make_uint4(0, 0, 0, 0);
-                    const long long row = rows[j0 + q];
-                    if (j0 + q < k && row >= 0 && row < (long long)T * k) v[q] = ld_nc_v4(yd + row * H + c);
+                for (int q = 0; q < G; ++q) {
+                    const int j = j0 + q;
+                    r[q] = -1;
+                    sw[q] = 0.f;
+                    if (warp_token) {
+                        r[q] = __shfl_sync(0xffffffffu, my_r, j & 31);
+                        sw[q] = __shfl_sync(0xffffffffu, my_w, j & 31);
+                    } else if (j < k) {
+                        const long long slot = (long long)t * k + j;
+                        const long long rr = inverse ? inverse[slot] : slot;
+                        r[q] = (rr >= 0 && rr < nrows) ? (int)rr : -1;
+                        sw[q] = w[slot];
+                    }
                 }
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int q = 0; q < G; ++q) {
+                    v[q] = make_uint4(0, 0, 0, 0);
+                    if (j0 + q < k && r[q] >= 0) v[q] = ld_nc_v4(yd + (long long)r[q] * H + c);
+                }
+#pragma unroll
+                for (int q = 0; q < G; ++q) {
                     if (j0 + q >= k) break;
-                    const long long row = rows[j0 + q];
-                    if (row < 0 || row >= (long long)T * k) {      // an id outside [0, E) left no row
+                    if (r[q] < 0) {                                // an id outside [0, E) left no row
                         fnx_flag_error(FNX_DEVERR_BADID);
                         continue;
                     }
                     const uint32_t vv[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        acc[2 * e] = __fadd_rn(acc[2 * e], round_bf(__fmul_rn(bf_lo(vv[e]), s[j0 + q])));
-                        acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], round_bf(__fmul_rn(bf_hi(vv[e]), s[j0 + q])));
+                        acc[2 * e] = __fadd_rn(acc[2 * e], round_bf(__fmul_rn(bf_lo(vv[e]), sw[q])));
+                        acc[2 * e + 1] = __fadd_rn(acc[2 * e + 1], round_bf(__fmul_rn(bf_hi(vv[e]), sw[q])));
                     }
                 }
             }
