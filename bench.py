@@ -442,7 +442,8 @@ def profile_case(case, dev):
     """Small cases for ncu captures (one layer of the bench workload):
     gu / dn  two launches of the routed gate/up or down grouped GEMM (its real routing), nothing
              else of the grouped-GEMM kind (`-k regex:grouped_gemm -s 1 -c 1` takes the second);
-    dec      four decode calls at M=1 (`-k regex:decode_fused -s 2 -c 1` takes the third);
+             before them one router logits GEMM (`-k regex:gemm_bf16_tma -c 1`);
+    dec      four decode calls at M=1 (`-k regex:decode_stream -s 2 -c 1` takes the third);
     ep       three calls of the expert-parallel layer with the peer exchange on one rank
              (every kernel of the p2p path, the exchange kept on this GPU);
     w8       four W8A16 projections at M=1 (K=2048, N=5120; `-k regex:w8a16 -s 2 -c 1`);
