@@ -100,14 +100,18 @@ FNX_DEV tword ld_tag(const tword* p) {
     return v;
 }
 // One thread waits (bounded) until the word at p carries `tag`, backing off exponentially from
-// 32 to 512 ns between reads, so that many waiting CTAs do not flood the L2 with polls.
+// 32 to FNX_D2_BACKOFF_MAX ns between reads, so that many waiting CTAs do not flood the L2 with
+// polls.
+#ifndef FNX_D2_BACKOFF_MAX
+#define FNX_D2_BACKOFF_MAX 64
+#endif
 FNX_DEV void poll_tag(const tword* p, uint32_t tag, volatile int* dead) {
     if (*dead || (uint32_t)(ld_tag(p) >> 32) == tag) return;
     const uint64_t t0 = fnx_globaltimer();
     unsigned ns = 32;
     while (true) {
         __nanosleep(ns);
-        if (ns < 512) ns <<= 1;
+        if (ns < FNX_D2_BACKOFF_MAX) ns <<= 1;
         if ((uint32_t)(ld_tag(p) >> 32) == tag || *dead) return;
         if (fnx_globaltimer() - t0 > FNX_WAIT_NS) {
             fnx_flag_error(FNX_DEVERR_TIMEOUT);
@@ -132,7 +136,7 @@ FNX_DEV void read_tagged(tword (&v)[N], const tword* p0, long long stride, int n
         for (int i = 0; i < N; ++i) ok &= (uint32_t)(v[i] >> 32) == tag;
         if (ok || *dead) return;
         __nanosleep(ns);
-        if (ns < 512) ns <<= 1;
+        if (ns < FNX_D2_BACKOFF_MAX) ns <<= 1;
 #pragma unroll
         for (int i = 0; i < N; ++i)
             if ((uint32_t)(v[i] >> 32) != tag) v[i] = ld_tag(p0 + i * stride);
@@ -270,24 +274,13 @@ FNX_DEV int d2_stages(const D2Item& d) {
 // identically given the same logits: (probability desc, id asc), k distinct valid ids, weights
 // bf16(p / sum of the k selected p in slot order).  The logits are read as they arrive (tagged).
 //
-// Selection: the probability keys within a factor 16 of the largest fall into 64 bins of 2^19
-// key units (4.4 % in probability); if the smallest set of whole bins holding >= k keys holds at
-// most 32, those candidates are ranked exactly at once (a key's rank is the number of candidates
-// above it, or equal with a lower id) -- the same selection and order as the sequential rule.
-// Otherwise (the k-th key more than a factor 16 below the first, or a crowded last bin) the
-// sequential rounds of topk_warp run.
+// Selection: topk_select (kernels_route.cuh), the binned candidate ranking with the sequential
+// rounds as its fallback -- the same selection and order as router_topk_kernel.
 constexpr int D2_RPER = 16;                           // experts per lane (E <= 512)
-constexpr int D2_RBINS = 64;
-struct D2RouteScratch {
-    int hist[D2_RBINS];
-    uint32_t ck[32];
-    int ci[32];
-    float prob[ROUTE_MAX_K];
-    int sid[ROUTE_MAX_K];
-};
+constexpr int D2_RBINS = 64;                          // the selection's bins (d2_route_block)
 
 FNX_DEV void d2_route_warp(const StreamParams& p, DecodeRouting& R, int t, uint32_t tag, volatile int* dead,
-                           D2RouteScratch& W) {
+                           TopkScratch& W) {
     const int lane = threadIdx.x & 31;
     const tword* row = p.tlog + (long long)t * p.R;
     tword wv[D2_RPER];
@@ -319,103 +312,14 @@ FNX_DEV void d2_route_warp(const StreamParams& p, DecodeRouting& R, int t, uint3
     for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
     const float inv = 1.0f / sum;
     uint32_t key[D2_RPER];
-    uint32_t lmax = 0;
 #pragma unroll
     for (int i = 0; i < D2_RPER; ++i) {
         const float pr = __fmul_rn(v[i], inv);
         key[i] = (i * 32 + lane) < p.E ? __float_as_uint(pr > 0.f ? pr : 0.f) + 1u : 0u;
-        lmax = max(lmax, key[i]);
     }
-    // ---- fast selection
-    const uint32_t kmax = __reduce_max_sync(0xffffffffu, lmax);
-    W.hist[lane] = 0;
-    W.hist[lane + 32] = 0;
-    __syncwarp();
-#pragma unroll
-    for (int i = 0; i < D2_RPER; ++i) {
-        const uint32_t dist = kmax - key[i];
-        if (key[i] && (dist >> 19) < (uint32_t)D2_RBINS) atomicAdd(&W.hist[dist >> 19], 1);
-    }
-    __syncwarp();
-    const int c0 = W.hist[2 * lane], c1 = W.hist[2 * lane + 1];
-    int incl = c0 + c1;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-    }
-    const int excl = incl - c0 - c1;
-    const bool hit0 = excl + c0 >= p.k, hit1 = incl >= p.k;
-    const unsigned bal = __ballot_sync(0xffffffffu, hit0 || hit1);
-    int bstar = -1, cnt = 0;
-    if (bal) {
-        const int l = __ffs(bal) - 1;
-        bstar = __shfl_sync(0xffffffffu, hit0 ? 2 * lane : 2 * lane + 1, l);
-        cnt = __shfl_sync(0xffffffffu, hit0 ? excl + c0 : incl, l);
-    }
-    float my_p = 0.f, tot = 0.f;
-    int my_i = 0;
-    if (bstar >= 0 && cnt <= 32) {
-        // compact the candidates (bin <= bstar) into slots 0..cnt-1, then rank them all at once
-        int mine = 0;
-#pragma unroll
-        for (int i = 0; i < D2_RPER; ++i) mine += (key[i] && ((kmax - key[i]) >> 19) <= (uint32_t)bstar) ? 1 : 0;
-        int off = mine;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, off, o);
-            if (lane >= o) off += y;
-        }
-        off -= mine;
-#pragma unroll
-        for (int i = 0; i < D2_RPER; ++i) {
-            if (key[i] && ((kmax - key[i]) >> 19) <= (uint32_t)bstar) {
-                W.ck[off] = key[i];
-                W.ci[off] = i * 32 + lane;
-                ++off;
-            }
-        }
-        __syncwarp();
-        const uint32_t mk = lane < cnt ? W.ck[lane] : 0u;
-        const int mi = lane < cnt ? W.ci[lane] : 0x7fffffff;
-        int rank = 0;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const uint32_t kj = __shfl_sync(0xffffffffu, mk, j);
-            const int ij = __shfl_sync(0xffffffffu, mi, j);
-            rank += (kj > mk || (kj == mk && ij < mi)) ? 1 : 0;
-        }
-        if (lane < cnt && rank < p.k) {
-            W.prob[rank] = __uint_as_float(mk - 1u);
-            W.sid[rank] = mi;
-        }
-        __syncwarp();
-        for (int j = 0; j < p.k; ++j) tot = __fadd_rn(tot, W.prob[j]);
-        if (lane < p.k) {
-            my_p = W.prob[lane];
-            my_i = W.sid[lane];
-        }
-        __syncwarp();
-    } else {
-        // ---- sequential rounds (topk_warp's): highest key, lowest id on ties
-        for (int j = 0; j < p.k; ++j) {
-            uint32_t lm = 0;
-#pragma unroll
-            for (int i = 0; i < D2_RPER; ++i) lm = max(lm, key[i]);
-            const uint32_t gm = __reduce_max_sync(0xffffffffu, lm);
-            uint32_t cand = 0xffffffffu;
-#pragma unroll
-            for (int i = D2_RPER - 1; i >= 0; --i)
-                if (key[i] == gm) cand = (uint32_t)(i * 32 + lane);
-            const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
-#pragma unroll
-            for (int i = 0; i < D2_RPER; ++i)
-                if (i * 32 + lane == bi) key[i] = 0u;
-            const float bp = __uint_as_float(gm - 1u);
-            if (lane == j) { my_p = bp; my_i = bi; }
-            tot = __fadd_rn(tot, bp);
-        }
-    }
+    float my_p, tot;
+    int my_i;
+    topk_select<D2_RPER>(key, p.k, W, my_p, my_i, tot);
     if (lane < p.k) {
         const bf16 wb = f2bf(my_p / tot);
         const int o = t * p.k + lane;
@@ -781,7 +685,7 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
     __shared__ float red[128];
     __shared__ uint64_t full[D2_NS], empty[D2_NS], routing_bar;
     __shared__ DecodeRouting R;
-    __shared__ D2RouteScratch RS[D2_CWARPS];
+    __shared__ TopkScratch RS[D2_CWARPS];
     __shared__ int s_dead;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const D2Shape S = d2_shape(p);

@@ -14,12 +14,138 @@ namespace fnx {
 constexpr int ROUTE_MAX_E = 2048;     // experts per token row handled by one warp
 constexpr int ROUTE_MAX_K = 32;       // top-k slots (one lane each)
 
+// The selection rule on a warp's probability keys (key = bits(p) + 1, 0 for a selected or
+// absent expert; expert i*32 + lane in key[i]): k rounds of (highest key, lowest id on ties).
+// Lane j < k gets slot j's probability and id; `tot` is the slot-order sum of the k
+// probabilities (identical in every lane).
+template <int PER>
+FNX_DEV void topk_rounds(uint32_t (&key)[PER], int k, float& my_p, int& my_i, float& tot) {
+    const int lane = threadIdx.x & 31;
+    my_p = 0.f;
+    tot = 0.f;
+    my_i = 0;
+    for (int j = 0; j < k; ++j) {
+        // a warp max over the keys, then a warp min over the ids of the lanes holding that key
+        // (each lane offers its lowest such id)
+        uint32_t lm = 0;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) lm = max(lm, key[i]);
+        const uint32_t gm = __reduce_max_sync(0xffffffffu, lm);
+        uint32_t cand = 0xffffffffu;
+#pragma unroll
+        for (int i = PER - 1; i >= 0; --i)
+            if (key[i] == gm) cand = (uint32_t)(i * 32 + lane);
+        const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
+#pragma unroll
+        for (int i = 0; i < PER; ++i)
+            if (i * 32 + lane == bi) key[i] = 0u;
+        const float bp = __uint_as_float(gm - 1u);
+        if (lane == j) { my_p = bp; my_i = bi; }
+        tot = __fadd_rn(tot, bp);
+    }
+}
+
+// The same selection, usually without k rounds: the keys within a factor 16 of the largest fall
+// into 64 bins of 2^19 key units (4.4 % in probability); if the smallest set of whole bins holding
+// >= k keys holds at most 32, those candidates are ranked at once (a key's rank is the number of
+// candidates above it, or equal with a lower id), which gives the rounds' selection and order.
+// Otherwise (the k-th key more than a factor 16 below the first, or a crowded last bin) the rounds
+// run.  W: this warp's scratch in shared memory.
+struct TopkScratch {
+    int hist[64];
+    uint32_t ck[32];
+    int ci[32];
+    float prob[ROUTE_MAX_K];
+    int sid[ROUTE_MAX_K];
+};
+template <int PER>
+FNX_DEV void topk_select(uint32_t (&key)[PER], int k, TopkScratch& W, float& my_p, int& my_i, float& tot) {
+    const int lane = threadIdx.x & 31;
+    uint32_t lmax = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) lmax = max(lmax, key[i]);
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, lmax);
+    W.hist[lane] = 0;
+    W.hist[lane + 32] = 0;
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        const uint32_t dist = kmax - key[i];
+        if (key[i] && (dist >> 19) < 64u) atomicAdd(&W.hist[dist >> 19], 1);
+    }
+    __syncwarp();
+    const int c0 = W.hist[2 * lane], c1 = W.hist[2 * lane + 1];
+    int incl = c0 + c1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const int excl = incl - c0 - c1;
+    const bool hit0 = excl + c0 >= k, hit1 = incl >= k;
+    const unsigned bal = __ballot_sync(0xffffffffu, hit0 || hit1);
+    int bstar = -1, cnt = 0;
+    if (bal) {
+        const int l = __ffs(bal) - 1;
+        bstar = __shfl_sync(0xffffffffu, hit0 ? 2 * lane : 2 * lane + 1, l);
+        cnt = __shfl_sync(0xffffffffu, hit0 ? excl + c0 : incl, l);
+    }
+    if (bstar < 0 || cnt > 32) {
+        topk_rounds<PER>(key, k, my_p, my_i, tot);
+        return;
+    }
+    // compact the candidates (bin <= bstar) into slots 0..cnt-1, then rank them all at once
+    int mine = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) mine += (key[i] && ((kmax - key[i]) >> 19) <= (uint32_t)bstar) ? 1 : 0;
+    int off = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, off, o);
+        if (lane >= o) off += y;
+    }
+    off -= mine;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        if (key[i] && ((kmax - key[i]) >> 19) <= (uint32_t)bstar) {
+            W.ck[off] = key[i];
+            W.ci[off] = i * 32 + lane;
+            ++off;
+        }
+    }
+    __syncwarp();
+    const uint32_t mk = lane < cnt ? W.ck[lane] : 0u;
+    const int mi = lane < cnt ? W.ci[lane] : 0x7fffffff;
+    int rank = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const uint32_t kj = __shfl_sync(0xffffffffu, mk, j);
+        const int ij = __shfl_sync(0xffffffffu, mi, j);
+        rank += (kj > mk || (kj == mk && ij < mi)) ? 1 : 0;
+    }
+    if (lane < cnt && rank < k) {
+        W.prob[rank] = __uint_as_float(mk - 1u);
+        W.sid[rank] = mi;
+    }
+    __syncwarp();
+    tot = 0.f;
+    for (int j = 0; j < k; ++j) tot = __fadd_rn(tot, W.prob[j]);
+    my_p = 0.f;
+    my_i = 0;
+    if (lane < k) {
+        my_p = W.prob[lane];
+        my_i = W.sid[lane];
+    }
+    __syncwarp();
+}
+
 // Top-k of one row by one warp; PER = experts per lane (E <= 32*PER).  Returns, in lane
 // j < k, slot j's probability (my_p) and expert id (my_i); `tot` is the slot-order sum of
 // the k probabilities (identical in every lane).  CG reads the row through L2 (rows
-// written by other blocks of the same kernel).
+// written by other blocks of the same kernel).  W: scratch for topk_select (null: the rounds).
 template <int PER, bool CG>
-FNX_DEV void topk_warp(const bf16* row, const float* bias, int E, int k, float& my_p, int& my_i, float& tot) {
+FNX_DEV void topk_warp(const bf16* row, const float* bias, int E, int k, float& my_p, int& my_i, float& tot,
+                       TopkScratch* W = nullptr) {
     const int lane = threadIdx.x & 31;
     float v[PER];
     float mx = -INFINITY;
@@ -59,28 +185,8 @@ FNX_DEV void topk_warp(const bf16* row, const float* bias, int E, int k, float& 
         key[i] = (i * 32 + lane) < E ? __float_as_uint(pr > 0.f ? pr : 0.f) + 1u : 0u;
     }
 
-    my_p = 0.f;
-    tot = 0.f;
-    my_i = 0;
-    for (int j = 0; j < k; ++j) {
-        // highest probability, lowest id on ties: a warp max over the keys, then a warp min
-        // over the ids of the lanes holding that key (each lane offers its lowest such id)
-        uint32_t lm = 0;
-#pragma unroll
-        for (int i = 0; i < PER; ++i) lm = max(lm, key[i]);
-        const uint32_t gm = __reduce_max_sync(0xffffffffu, lm);
-        uint32_t cand = 0xffffffffu;
-#pragma unroll
-        for (int i = PER - 1; i >= 0; --i)
-            if (key[i] == gm) cand = (uint32_t)(i * 32 + lane);
-        const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
-#pragma unroll
-        for (int i = 0; i < PER; ++i)
-            if (i * 32 + lane == bi) key[i] = 0u;
-        const float bp = __uint_as_float(gm - 1u);
-        if (lane == j) { my_p = bp; my_i = bi; }
-        tot = __fadd_rn(tot, bp);
-    }
+    if (W) topk_select<PER>(key, k, *W, my_p, my_i, tot);
+    else topk_rounds<PER>(key, k, my_p, my_i, tot);
 }
 
 // One warp per token.  logits: bf16 [T, ld] (first E columns); bias: fp32 [E] or null.
@@ -89,12 +195,13 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const bf16* __restrict
                                                           const float* __restrict__ bias, bf16* __restrict__ w_out,
                                                           int64_t* __restrict__ idx_out, int32_t* __restrict__ idx32_out,
                                                           float* __restrict__ wf_out, int T, int E, int k) {
+    __shared__ TopkScratch scratch[8];
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= T) return;
     float my_p, tot;
     int my_i;
-    topk_warp<PER, false>(logits + (long long)t * ld, bias, E, k, my_p, my_i, tot);
+    topk_warp<PER, false>(logits + (long long)t * ld, bias, E, k, my_p, my_i, tot, &scratch[threadIdx.x >> 5]);
     if (lane < k) {
         const bf16 wb = f2bf(my_p / tot);
         const long long o = (long long)t * k + lane;
