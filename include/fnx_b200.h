@@ -183,11 +183,21 @@ int fnx_ep_p2p_dedup(const void* desc, const void* order, const void* counts, in
 int fnx_ep_p2p_counts(const void* desc, const void* counts, const void* tcounts, void* stream);
 int fnx_ep_p2p_push(const void* desc, const void* x, int T, const void* order, const void* idx, const void* tok_index,
                     void* stream);
+/* fnx_ep_p2p_push with flags (bit 0: do not copy the rank's own T token rows to its region's
+ * shared-expert rows, for a caller that runs the shared expert from x itself) and a cap on the
+ * launch's blocks (0: the default), so that a GEMM on another stream keeps its SMs. */
+int fnx_ep_p2p_push_ex(const void* desc, const void* x, int T, const void* order, const void* idx,
+                       const void* tok_index, int flags, int max_blocks, void* stream);
 int fnx_ep_p2p_wait(const void* desc, int phase, void* stream);
 int fnx_ep_p2p_signal(const void* desc, int phase, void* stream);
 size_t fnx_ep_p2p_recv_workspace(const void* desc);
 int fnx_ep_p2p_recv_layout(const void* desc, int T, void* order_x, void* ends_x, void* pos, void* rows, void* sh_out,
                            void* workspace, size_t ws_bytes, void* stream);
+/* The received slots alone (no shared-expert rows): order_r [cap] the region row of each slot in
+ * expert-major order, ends_r [Eg] cumulative from 0, pos [cap] each slot's position, rows_r [cap]
+ * each position's down-row destination in its source's return buffer (the sink past the count). */
+int fnx_ep_p2p_recv_layout_routed(const void* desc, void* order_r, void* ends_r, void* pos, void* rows_r,
+                                  void* workspace, size_t ws_bytes, void* stream);
 
 /* The LQP artifact's experts as the int4pack artifact, on the GPU (tools/repack_w4a16.py:41-70,
  * which needs CANN's npu_convert_weight_to_int4pack): v2o uint8 [E, N, K/2] offset-binary
@@ -224,6 +234,11 @@ int fnx_repack_w4_tiles(const void* w4, const void* scales, void* tiles, int E, 
 int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_rows, const void* row_index, int index_div,
                        const void* tiles, const void* ends, void* out, long long ld_out, int E, int M, int K, int Nw,
                        int epilogue, void* stream);
+/* fnx_moe_grouped_w4 on at most max_ctas CTAs (0: all that fit; the CTA-pair kernel rounds down to
+ * whole pairs), leaving SMs to kernels of another stream. */
+int fnx_moe_grouped_w4_lim(const void* act, long long ld_act, long long act_rows, const void* row_index,
+                           int index_div, const void* tiles, const void* ends, void* out, long long ld_out, int E,
+                           int M, int K, int Nw, int epilogue, int max_ctas, void* stream);
 
 /* fnx_moe_grouped_w4 with epilogue 0 whose output row r goes to out_rows[r] (a device array of
  * 16-byte aligned row pointers, bf16 [Nw] each, which may point into peers' memory): the

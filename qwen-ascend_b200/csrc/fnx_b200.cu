@@ -171,7 +171,8 @@ int gemm_launch_t(GemmParams& p, cudaStream_t st) {
                          (unsigned long long)p.E * p.Nw, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (rc) return rc;
-    grouped_gemm_kernel<MODE, EPI><<<num_sms(), G_THREADS, smem, st>>>(p);
+    const int grid = p.max_ctas > 0 && p.max_ctas < num_sms() ? p.max_ctas : num_sms();
+    grouped_gemm_kernel<MODE, EPI><<<grid, G_THREADS, smem, st>>>(p);
     return launch_rc();
 }
 
@@ -202,7 +203,8 @@ int gemm_pair_launch_t(GemmParams& p, cudaStream_t st) {
             return FNX_ELAUNCH;
         clusters = n < num_sms() / 2 ? n : num_sms() / 2;
     }
-    cfg.gridDim = dim3(2 * clusters);
+    const int use = p.max_ctas >= 2 && p.max_ctas / 2 < clusters ? p.max_ctas / 2 : clusters;
+    cfg.gridDim = dim3(2 * use);
     cfg.stream = st;
     if (cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel<EPI>, p) != cudaSuccess) return FNX_ELAUNCH;
     return launch_rc();
@@ -665,18 +667,26 @@ FNX_API int fnx_ep_p2p_counts(const void* desc, const void* counts, const void* 
     return launch_rc();
 }
 
-FNX_API int fnx_ep_p2p_push(const void* desc, const void* x, int T, const void* order, const void* idx,
-                            const void* tok_index, void* stream) {
+FNX_API int fnx_ep_p2p_push_ex(const void* desc, const void* x, int T, const void* order, const void* idx,
+                               const void* tok_index, int flags, int max_blocks, void* stream) {
     const EPDesc* d = ep_desc(desc);
-    if (!d || T < 0 || T > d->T_cap || (T > 0 && (!x || !order || !idx || !tok_index)) || !aligned16(x))
+    if (!d || T < 0 || T > d->T_cap || (T > 0 && (!x || !order || !idx || !tok_index)) || !aligned16(x) ||
+        (flags & ~1) || max_blocks < 0)
         return FNX_EARG;
     const long long rows = (long long)T * d->k + T;
     long long blocks = (rows + 7) / 8;
     if (blocks < 1) blocks = 1;
     if (blocks > (long long)num_sms() * 4) blocks = (long long)num_sms() * 4;
+    if (max_blocks > 0 && blocks > max_blocks) blocks = max_blocks;
     ep_push_kernel<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(*d, (const bf16*)x, T, (const int64_t*)order,
-                                                                  (const int64_t*)idx, (const int*)tok_index);
+                                                                  (const int64_t*)idx, (const int*)tok_index,
+                                                                  (flags & 1) == 0);
     return launch_rc();
+}
+
+FNX_API int fnx_ep_p2p_push(const void* desc, const void* x, int T, const void* order, const void* idx,
+                            const void* tok_index, void* stream) {
+    return fnx_ep_p2p_push_ex(desc, x, T, order, idx, tok_index, 0, 0, stream);
 }
 
 FNX_API int fnx_ep_p2p_wait(const void* desc, int phase, void* stream) {
@@ -715,6 +725,23 @@ FNX_API int fnx_ep_p2p_recv_layout(const void* desc, int T, void* order_x, void*
     return launch_rc();
 }
 
+// The received slots alone (the shared expert computed elsewhere, from the rank's own tokens):
+// order_r [cap] (token row of each slot in the region, expert-major), ends_r [Eg] (from 0), pos
+// [cap] and rows_r [cap] (each slot's down-row destination in its source's return buffer).
+FNX_API int fnx_ep_p2p_recv_layout_routed(const void* desc, void* order_r, void* ends_r, void* pos, void* rows_r,
+                                          void* workspace, size_t ws_bytes, void* stream) {
+    const EPDesc* d = ep_desc(desc);
+    if (!d || !order_r || !ends_r || !pos || !rows_r || d->Eg > PERM_MAX_E) return FNX_EARG;
+    if (ws_bytes < fnx_ep_p2p_recv_workspace(desc)) return FNX_EWORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    ep_sink_rows_kernel<<<num_sms() * 2, 256, 0, st>>>(*d, (bf16**)rows_r);
+    const int rc = permute_launch(d->recv_e[d->rank], order_r, pos, ends_r, nullptr, (int)d->cap, d->Eg, 1, workspace,
+                                  st, d->plan + EP_R, 0, d->recv_row[d->rank]);
+    if (rc) return rc;
+    ep_rows_kernel<<<num_sms() * 2, 256, 0, st>>>(*d, (const int64_t*)pos, 0, (bf16**)rows_r);
+    return launch_rc();
+}
+
 // ======================================================================== grouped GEMMs
 FNX_API int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_rows, const void* row_index,
                                int index_div, const void* tiles, const void* ends, void* out, long long ld_out, int E,
@@ -727,6 +754,29 @@ FNX_API int fnx_moe_grouped_w4(const void* act, long long ld_act, long long act_
     p.E = E; p.M = M; p.K = K; p.Nw = Nw; p.gs = 0;
     if (epilogue < 0 || epilogue > 4) return FNX_EARG;
     // 3: shared expert last (expert E-1), 4: shared expert first (expert 0)
+    p.shared_e = epilogue == 4 ? 0 : E - 1;
+    if (epilogue == 4) epilogue = EPI_SWIGLU_MIXED;
+    p.m_tiles = epilogue == EPI_PLAIN ? Nw / G_BM : (Nw / 2) / 64;
+    const int rc = gemm_check(GEMM_W4, epilogue, p);
+    if (rc) return rc;
+    if (M == 0) return FNX_OK;
+    return gemm_launch(GEMM_W4, epilogue, p, (cudaStream_t)stream);
+}
+
+// fnx_moe_grouped_w4 on at most max_ctas CTAs (0: all that fit), so that kernels of another
+// stream (the expert-parallel exchange) keep SMs while it runs.
+FNX_API int fnx_moe_grouped_w4_lim(const void* act, long long ld_act, long long act_rows, const void* row_index,
+                                   int index_div, const void* tiles, const void* ends, void* out, long long ld_out,
+                                   int E, int M, int K, int Nw, int epilogue, int max_ctas, void* stream) {
+    if (max_ctas < 0) return FNX_EARG;
+    GemmParams p{};
+    p.act = (const bf16*)act; p.ld_act = ld_act; p.row_index = (const int64_t*)row_index; p.index_div = index_div;
+    p.act_rows = act_rows;
+    if (act_rows < 0 || act_rows > 0x7fffffffLL || (!row_index && act_rows < M)) return FNX_EARG;
+    p.w = tiles; p.ends = (const int64_t*)ends; p.out = (bf16*)out; p.ld_out = ld_out;
+    p.E = E; p.M = M; p.K = K; p.Nw = Nw; p.gs = 0;
+    p.max_ctas = max_ctas;
+    if (epilogue < 0 || epilogue > 4) return FNX_EARG;
     p.shared_e = epilogue == 4 ? 0 : E - 1;
     if (epilogue == 4) epilogue = EPI_SWIGLU_MIXED;
     p.m_tiles = epilogue == EPI_PLAIN ? Nw / G_BM : (Nw / 2) / 64;

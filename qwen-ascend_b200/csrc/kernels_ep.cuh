@@ -338,7 +338,7 @@ FNX_DEV void ep_last_block_signal(const EPDesc& d, unsigned* ticket, int phase, 
 __global__ void __launch_bounds__(256) ep_push_kernel(const EPDesc d, const bf16* __restrict__ x, int T,
                                                       const int64_t* __restrict__ order,
                                                       const int64_t* __restrict__ idx,
-                                                      const int* __restrict__ tok_index) {
+                                                      const int* __restrict__ tok_index, bool copy_own) {
     __shared__ long long sp[EP_PLAN_LEN];
     ep_load_plan(d, sp);
     const int G = d.world, H = d.H, k = d.k, lane = threadIdx.x & 31;
@@ -375,8 +375,9 @@ __global__ void __launch_bounds__(256) ep_push_kernel(const EPDesc d, const bf16
             ep_copy_row(d.recv_x[jj] + tr * H, x + sr * H, H, lane);
         }
     }
-    for (long long t = gw; t < T; t += warps)
-        ep_copy_row(d.recv_x[d.rank] + (d.cap_tok + t) * H, x + t * H, H, lane);
+    if (copy_own)
+        for (long long t = gw; t < T; t += warps)
+            ep_copy_row(d.recv_x[d.rank] + (d.cap_tok + t) * H, x + t * H, H, lane);
     ep_last_block_signal(d, d.tickets + 0, EP_PH_DATA, (unsigned)sp[EP_EPOCH]);
 }
 
@@ -415,8 +416,15 @@ __global__ void __launch_bounds__(256) ep_head_kernel(const EPDesc d, int64_t* _
     if (blockIdx.x == 0 && threadIdx.x == 0) ends_x[0] = T;
 }
 
+// Every received slot's down-row destination starts at the sink (rows past this call's count).
+__global__ void __launch_bounds__(256) ep_sink_rows_kernel(const EPDesc d, bf16** __restrict__ rows) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < d.cap; i += (long long)gridDim.x * blockDim.x)
+        rows[i] = d.sink;
+}
+
 // Down-row destinations of the received slots: slot s (from source q, the j-th of q's) at
-// expert-major position pos[s] returns to source q's yb row ret_off[q] + j.
+// expert-major position pos[s] (T + its rank when the rank's own T shared-expert rows come
+// first, else its rank) returns to source q's yb row ret_off[q] + j.
 __global__ void __launch_bounds__(256) ep_rows_kernel(const EPDesc d, const int64_t* __restrict__ pos, int T,
                                                       bf16** __restrict__ rows) {
     __shared__ long long sp[EP_PLAN_LEN];

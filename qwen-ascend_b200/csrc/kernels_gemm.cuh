@@ -104,6 +104,8 @@ struct GemmParams {
     // place of the gathering loader warps
     int b_tma;
     CUtensorMap tmap_b32, tmap_b8;
+    // at most this many CTAs (0: as many as fit), leaving SMs to kernels of another stream
+    int max_ctas;
 };
 
 // The expert whose tile blocks group e reads (an id outside [0, E_w) is flagged, and read as 0).

@@ -57,12 +57,15 @@ SIGNATURES = {
     "fnx_ep_p2p_dedup": ([P, P, P, I, P, P, P], I),
     "fnx_ep_p2p_counts": ([P, P, P, P], I),
     "fnx_ep_p2p_push": ([P, P, I, P, P, P, P], I),
+    "fnx_ep_p2p_push_ex": ([P, P, I, P, P, P, I, I, P], I),
     "fnx_ep_p2p_wait": ([P, I, P], I),
     "fnx_ep_p2p_signal": ([P, I, P], I),
     "fnx_ep_p2p_recv_workspace": ([P], SZ),
     "fnx_ep_p2p_recv_layout": ([P, I, P, P, P, P, P, P, SZ, P], I),
+    "fnx_ep_p2p_recv_layout_routed": ([P, P, P, P, P, P, SZ, P], I),
     "fnx_moe_grouped_w4_rows": ([P, LL, LL, P, I, P, P, P, I, I, I, I, P], I),
     "fnx_moe_grouped_w4": ([P, LL, LL, P, I, P, P, P, LL] + [I] * 5 + [P], I),
+    "fnx_moe_grouped_w4_lim": ([P, LL, LL, P, I, P, P, P, LL] + [I] * 6 + [P], I),
     "fnx_moe_grouped_w4_sel": ([P, LL, LL, P, I, P, I, P, P, P, LL] + [I] * 5 + [P], I),
     "fnx_weighted_sum_f32": ([P, P, P, I, I, P], I),
     "fnx_repack_v2o": ([P, I, I, I, I, P, P], I),

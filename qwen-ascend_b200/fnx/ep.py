@@ -36,12 +36,13 @@ Two transports move the rows:
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 import torch.distributed as dist
 
 from . import _lib
-from .engine import BF16, EPI_PLAIN, EPI_SWIGLU_MIXED, MoELayer, _grouped_w4, repack_w4
+from .engine import BF16, EPI_PLAIN, EPI_SWIGLU_BF16, EPI_SWIGLU_F32, EPI_SWIGLU_MIXED, MoELayer, _grouped_w4, repack_w4
 
 I64 = torch.int64
 EPI_SWIGLU_SHARED_FIRST = 4      # EPI_SWIGLU_MIXED with the shared expert as expert 0
@@ -134,6 +135,13 @@ class ExpertParallelMoE(MoELayer):
         self.max_tokens = max_tokens
         self.last_counts = None
         self._p2p = None
+        # p2p: run the shared expert (which needs only this rank's own tokens) on a second stream
+        # while the exchange kernels run, on all but `reserve_sms` SMs, which the exchange keeps
+        # (FNX_EP_OVERLAP=0: the single-stream form, for comparisons)
+        self.overlap_shared = os.environ.get("FNX_EP_OVERLAP", "1") != "0"
+        self.reserve_sms = int(os.environ.get("FNX_EP_RESERVE_SMS", "64"))
+        self._side = None
+        self._sh_ends = {}
 
     def _arrange(self, tiles):
         """Routed experts then the shared one (collective transport), or the shared expert
@@ -333,6 +341,8 @@ class ExpertParallelMoE(MoELayer):
     __call__ = forward
 
     def _forward_p2p(self, x):
+        if self.overlap_shared:
+            return self._forward_p2p_overlap(x)
         T, H = x.shape
         if T > self.max_tokens:
             raise ValueError(f"ExpertParallelMoE: {T} tokens exceed max_tokens={self.max_tokens}")
@@ -370,6 +380,83 @@ class ExpertParallelMoE(MoELayer):
         _lib.check(L.fnx_ep_p2p_signal(D, 2, st), "EP return signal")
         _lib.check(L.fnx_ep_p2p_wait(D, 2, st), "EP return wait")
         out = torch.empty(T, H, dtype=BF16, device=dev)
+        gate = logits[:, self.E:self.E + 1]
+        _lib.check(L.fnx_moe_combine(ex.yb, wf.data_ptr(), inverse_d.data_ptr(), sh.data_ptr(), gate.data_ptr(),
+                                     logits.stride(0), out.data_ptr(), T, self.k, H, st), "MoE combine")
+        return out
+
+    def _forward_p2p_overlap(self, x):
+        """The p2p call with the shared expert on a second stream: its gate/up and down run from x
+        on all but `reserve_sms` SMs while this stream lays out, deduplicates, exchanges counts
+        and pushes the token rows (on the reserved SMs) and lays out what it received; the routed
+        experts then run over the received slots alone and the streams join before the combine.
+        Every row meets the same kernels and operands as in the single-stream form, so the output
+        is the same bit for bit."""
+        T, H = x.shape
+        if T > self.max_tokens:
+            raise ValueError(f"ExpertParallelMoE: {T} tokens exceed max_tokens={self.max_tokens}")
+        ex = self._p2p
+        dev = x.device
+        L, D = _lib.lib(), ex.desc
+        Eg, I, cap = self.E_local, self.I, ex.cap
+        main = torch.cuda.current_stream(dev)
+        if self._side is None:
+            self._side = torch.cuda.Stream(dev)
+        side = self._side
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        reserve = max(2, min(self.reserve_sms, sms - 2))
+        side_ctas = (sms - reserve) // 2 * 2
+        sh_ends = self._sh_ends.get((T, str(dev)))
+        if sh_ends is None:
+            sh_ends = self._sh_ends[(T, str(dev))] = torch.full((1,), T, dtype=I64, device=dev)
+        x = x.contiguous()
+        logits, w, idx, wf = self.route(x)
+        # buffers of both streams, allocated here (on this stream) before the fork
+        a_sh = torch.empty(max(T, 1), I, dtype=BF16, device=dev)
+        sh = torch.empty(max(T, 1), H, dtype=BF16, device=dev)
+        order_r = torch.empty(max(cap, 1), dtype=I64, device=dev)
+        ends_r = torch.empty(Eg, dtype=I64, device=dev)
+        pos = torch.empty(max(cap, 1), dtype=I64, device=dev)
+        rows = torch.empty(max(cap, 1), dtype=I64, device=dev)
+        wsb = L.fnx_ep_p2p_recv_workspace(D)
+        ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+        a2 = torch.empty(max(cap, 1), I, dtype=BF16, device=dev)
+        out = torch.empty(T, H, dtype=BF16, device=dev)
+        side.wait_stream(main)
+        if T:
+            ss = side.cuda_stream
+            with torch.cuda.stream(side):
+                _lib.check(L.fnx_moe_grouped_w4_lim(x.data_ptr(), H, T, None, 1, self.gu_loc.data_ptr(),
+                                                    sh_ends.data_ptr(), a_sh.data_ptr(), I, 1, T, H, 2 * I,
+                                                    EPI_SWIGLU_BF16, side_ctas, ss), "shared expert gate/up")
+                _lib.check(L.fnx_moe_grouped_w4_lim(a_sh.data_ptr(), I, T, None, 1, self.dn_loc.data_ptr(),
+                                                    sh_ends.data_ptr(), sh.data_ptr(), H, 1, T, I, H, EPI_PLAIN,
+                                                    side_ctas, ss), "shared expert down")
+        st = _lib.stream(dev)
+        order_d, inverse_d, counts = self.dispatch_layout(idx)
+        tok_index = torch.empty(max(idx.numel(), 1), dtype=torch.int32, device=dev)
+        tcounts = torch.empty(self.world, dtype=I64, device=dev)
+        self.last_counts = (counts, tcounts)
+        _lib.check(L.fnx_ep_p2p_dedup(D, order_d.data_ptr(), counts.data_ptr(), T, tok_index.data_ptr(),
+                                      tcounts.data_ptr(), st), "EP token dedup")
+        _lib.check(L.fnx_ep_p2p_counts(D, counts.data_ptr(), tcounts.data_ptr(), st), "EP count exchange")
+        _lib.check(L.fnx_ep_p2p_push_ex(D, x.data_ptr(), T, order_d.data_ptr(), idx.data_ptr(), tok_index.data_ptr(),
+                                        1, 4 * reserve, st), "EP dispatch")
+        _lib.check(L.fnx_ep_p2p_wait(D, 1, st), "EP dispatch wait")
+        _lib.check(L.fnx_ep_p2p_recv_layout_routed(D, order_r.data_ptr(), ends_r.data_ptr(), pos.data_ptr(),
+                                                   rows.data_ptr(), ws.data_ptr(), wsb, st), "EP receive layout")
+        one = self.gu_loc[0].numel() * self.gu_loc.element_size()
+        one_d = self.dn_loc[0].numel() * self.dn_loc.element_size()
+        if cap:
+            _lib.check(L.fnx_moe_grouped_w4(ex.recv_x, H, ex.cap_tok + self.max_tokens, order_r.data_ptr(), 1,
+                                            self.gu_loc.data_ptr() + one, ends_r.data_ptr(), a2.data_ptr(), I, Eg, cap,
+                                            H, 2 * I, EPI_SWIGLU_F32, st), "grouped W4A16 GEMM")
+            _lib.check(L.fnx_moe_grouped_w4_rows(a2.data_ptr(), I, cap, None, 1, self.dn_loc.data_ptr() + one_d,
+                                                 ends_r.data_ptr(), rows.data_ptr(), Eg, cap, I, H, st),
+                       "grouped W4A16 GEMM (return)")
+        _lib.check(L.fnx_ep_p2p_signal(D, 2, st), "EP return signal")
+        _lib.check(L.fnx_ep_p2p_wait(D, 2, st), "EP return wait")
+        main.wait_stream(side)
         gate = logits[:, self.E:self.E + 1]
         _lib.check(L.fnx_moe_combine(ex.yb, wf.data_ptr(), inverse_d.data_ptr(), sh.data_ptr(), gate.data_ptr(),
                                      logits.stride(0), out.data_ptr(), T, self.k, H, st), "MoE combine")

@@ -103,10 +103,13 @@ def test_ep_emulated_bit_identical(cfg2_layer, G, T):
         assert torch.equal(outs[r].view(torch.int16), ref.view(torch.int16)), r
 
 
-@pytest.mark.parametrize("transport", ["p2p", "collective"])
-def test_ep_single_rank_forward(cfg2_layer, transport):
+@pytest.mark.parametrize("transport,overlap", [("p2p", True), ("p2p", False), ("collective", True)])
+def test_ep_single_rank_forward(cfg2_layer, transport, overlap):
+    """Bit-identical to the one-GPU layer; p2p with the shared expert on a second stream (overlap)
+    and in the single-stream form."""
     _, layer = cfg2_layer
     ep = ExpertParallelMoE.from_layer(layer, 0, 1, transport=transport, max_tokens=1024)
+    ep.overlap_shared = overlap
     assert ep.transport == transport
     for T, seed in ((777, 9), (1024, 10), (17, 11), (777, 9)):
         x = synth.make_tokens(T, synth.CFG2.H, seed=seed, device=DEV)
@@ -119,10 +122,13 @@ def test_ep_single_rank_forward(cfg2_layer, transport):
     ep.close()
 
 
-def test_ep_p2p_graph_capture(cfg2_layer):
-    """The p2p layer never waits on the host, so one call captures into a CUDA graph."""
+@pytest.mark.parametrize("overlap", [True, False])
+def test_ep_p2p_graph_capture(cfg2_layer, overlap):
+    """The p2p layer never waits on the host, so one call captures into a CUDA graph (with the
+    shared expert's second stream forked and joined inside the capture)."""
     _, layer = cfg2_layer
     ep = ExpertParallelMoE.from_layer(layer, 0, 1, transport="p2p", max_tokens=512)
+    ep.overlap_shared = overlap
     x = synth.make_tokens(512, synth.CFG2.H, seed=12, device=DEV)
     ref = layer.prefill(x)
     ep(x)
