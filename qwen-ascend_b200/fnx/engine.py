@@ -17,6 +17,8 @@ All tensors live on a CUDA device; nothing here computes on the CPU.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _lib
@@ -28,6 +30,10 @@ DECODE_MAX_EXPERTS = 512         # the fused decode kernel's router width; wider
 
 
 TILE_BLOCK_WORDS = 1088          # 1024 words of int4 + 128 bf16 scales per (tile, k-block)
+# prefill: the shared expert on a second stream while the routing runs (FNX_PREFILL_OVERLAP=0: one
+# stream), leaving SHARED_RESERVE_SMS SMs to the routing kernels
+OVERLAP_SHARED = os.environ.get("FNX_PREFILL_OVERLAP", "1") != "0"
+SHARED_RESERVE_SMS = int(os.environ.get("FNX_PREFILL_RESERVE_SMS", "64"))
 
 
 def repack_w4(w4, scales, swiglu):
@@ -493,7 +499,6 @@ class MoELayer:
         elif logits.dtype != BF16 or logits.dim() != 2 or logits.shape[0] != T or logits.shape[1] <= E \
                 or logits.stride(1) != 1 or logits.device != dev:
             raise ValueError("prefill: logits must be bf16 [T, >= E+1], row-major, on x's device")
-        w, idx, wf = self.topk(logits)
         # expert-major rows of the routed experts, then the shared expert (expert E) over all
         # T tokens: its rows M .. M+T-1 read token t (row index t*k, divided by k)
         key = (T, str(dev))
@@ -505,12 +510,40 @@ class MoELayer:
             ends_x[E] = M + T
             bufs = self._prefill_bufs[key] = (order_x, ends_x)
         order_x, ends_x = bufs
-        order, inverse, ends = self.permute(idx, order=order_x[:M], ends=ends_x[:E])
         act = torch.empty(M + T, I, dtype=BF16, device=dev)
-        _grouped_w4(x, self.gu_all, ends_x, act, E=E + 1, M=M + T, K=H, Nw=2 * I, epilogue=EPI_SWIGLU_MIXED,
-                    row_index=order_x, index_div=k)
         yd = torch.empty(M + T, H, dtype=BF16, device=dev)
-        _grouped_w4(act, self.dn_all, ends_x, yd, E=E + 1, M=M + T, K=I, Nw=H, epilogue=EPI_PLAIN)
+        side = self._shared_side_stream(dev) if T else None
+        if side is not None:
+            # the shared expert (expert E, all T tokens) on a second stream while this one routes
+            # and permutes, on all but SHARED_RESERVE_SMS SMs; then the routed experts alone
+            main = torch.cuda.current_stream(dev)
+            side.wait_stream(main)
+            sh_ends = self._sh_ends_for(T, dev)
+            sms = torch.cuda.get_device_properties(dev).multi_processor_count
+            ctas = max(2, (sms - SHARED_RESERVE_SMS) // 2 * 2)
+            L = _lib.lib()
+            gu_sh = self.gu_all[E:E + 1]
+            dn_sh = self.dn_all[E:E + 1]
+            with torch.cuda.stream(side):
+                ss = side.cuda_stream
+                _lib.check(L.fnx_moe_grouped_w4_lim(x.data_ptr(), x.stride(0), T, None, 1, gu_sh.data_ptr(),
+                                                    sh_ends.data_ptr(), act[M:].data_ptr(), I, 1, T, H, 2 * I,
+                                                    EPI_SWIGLU_BF16, ctas, ss), "shared expert gate/up")
+                _lib.check(L.fnx_moe_grouped_w4_lim(act[M:].data_ptr(), I, T, None, 1, dn_sh.data_ptr(),
+                                                    sh_ends.data_ptr(), yd[M:].data_ptr(), H, 1, T, I, H, EPI_PLAIN,
+                                                    ctas, ss), "shared expert down")
+        w, idx, wf = self.topk(logits)
+        order, inverse, ends = self.permute(idx, order=order_x[:M], ends=ends_x[:E])
+        if side is not None:
+            if M:
+                _grouped_w4(x, self.gu_all, ends_x, act, E=E, M=M, K=H, Nw=2 * I, epilogue=EPI_SWIGLU_F32,
+                            row_index=order_x, index_div=k)
+                _grouped_w4(act, self.dn_all, ends_x, yd, E=E, M=M, K=I, Nw=H, epilogue=EPI_PLAIN)
+            main.wait_stream(side)
+        else:
+            _grouped_w4(x, self.gu_all, ends_x, act, E=E + 1, M=M + T, K=H, Nw=2 * I, epilogue=EPI_SWIGLU_MIXED,
+                        row_index=order_x, index_div=k)
+            _grouped_w4(act, self.dn_all, ends_x, yd, E=E + 1, M=M + T, K=I, Nw=H, epilogue=EPI_PLAIN)
         sh_act, sh = act[M:], yd[M:]
         gate = logits[:, E:E + 1]
         if inject is not None:              # combine + residual inject in one pass
@@ -532,6 +565,23 @@ class MoELayer:
             return out, dict(logits=logits[:, :E], gate=gate, w=w, idx=idx, order=order, inverse=inverse, ends=ends,
                              act=act[:M], yd=yd[:M], sh=sh, sh_act=sh_act)
         return out
+
+    def _shared_side_stream(self, dev):
+        """The second stream of the overlapped prefill (None when `overlap_shared` is off)."""
+        if not getattr(self, "overlap_shared", OVERLAP_SHARED):
+            return None
+        streams = self.__dict__.setdefault("_side_streams", {})
+        st = streams.get(str(dev))
+        if st is None:
+            st = streams[str(dev)] = torch.cuda.Stream(dev)
+        return st
+
+    def _sh_ends_for(self, T, dev):
+        cache = self.__dict__.setdefault("_sh_ends", {})
+        t = cache.get((T, str(dev)))
+        if t is None:
+            t = cache[(T, str(dev))] = torch.full((1,), T, dtype=torch.int64, device=dev)
+        return t
 
     def decode_workspace(self, M, device):
         key = (M, str(device))

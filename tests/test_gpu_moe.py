@@ -283,6 +283,21 @@ def test_weighted_sum_kernel():
     assert torch.equal(W4GemvOp.weighted_sum(y[:0].to(DEV), []).cpu(), torch.zeros(3000))
 
 
+@pytest.mark.parametrize("T", [300, 17])
+def test_prefill_shared_expert_overlap_bit_identical(T):
+    """The shared expert on a second stream (routed experts in their own launches) gives the bits
+    of the single-stream form, which runs both in one launch per projection; captured as well."""
+    t, L, layer = _layer(synth.CFG2, 33)
+    x = synth.make_tokens(T, synth.CFG2.H, seed=5, device=DEV)
+    layer.overlap_shared = False
+    ref = layer.prefill(x).clone()
+    layer.overlap_shared = True
+    got = layer.prefill(x)
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+    cap = layer.capture(T)
+    assert torch.equal(cap(x).view(torch.int16), ref.view(torch.int16))
+
+
 @pytest.mark.parametrize("T", [300, 4])
 def test_captured_layer_replays_the_call(T):
     """MoELayer.capture: the graph replay gives the direct call's bits, on new inputs too."""
