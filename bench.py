@@ -308,10 +308,16 @@ def bench_prefill(args, world, rank, dev):
     torch.cuda.synchronize()
     assert torch.equal(outh.view(torch.int16), ref_out.view(torch.int16)), "host pipeline output differs"
     # this library's kernels per layer: router logits GEMM, top-k, permute (hist, scan, scatter),
-    # gate/up, down, combine.  Expert parallel (peer exchange): router GEMM, top-k, dispatch layout
-    # (3), token dedup (2), count exchange, dispatch push, wait, receive layout (head, permute 3,
-    # row destinations), gate/up, down with the return in its epilogue, signal, wait, combine.
-    launches_per_step = 21 if world > 1 else 8
+    # gate/up, down, combine, with the shared expert's gate/up and down as launches of their own on
+    # the second stream (10; 8 in the single-launch form).  Expert parallel (peer exchange): router
+    # GEMM, top-k, dispatch layout (3), token dedup (2), count exchange, dispatch push, wait, receive
+    # layout (4 + row destinations), routed gate/up, down with the return in its epilogue, signal,
+    # wait, combine, and the shared expert's two launches (23; 21 in the single-stream form).
+    from fnx import engine as _eng
+    if world > 1:
+        launches_per_step = 23 if layers[0].overlap_shared else 21
+    else:
+        launches_per_step = 10 if _eng.OVERLAP_SHARED else 8
     # the host link's ceiling for e2e: both directions at once (the pipeline's copies overlap the
     # replays), so a step takes at least the device step and each direction's copy time
     link = bench_host_link(world, dev, T_PREFILL * H * 2)
