@@ -378,11 +378,13 @@ def bench_host_link(world, dev, nbytes, iters=20):
     return res
 
 
-def bench_ep_stack(args, world, rank, dev, n_layers=48, T=8192, steps=2, warmup=1):
+def bench_ep_stack(args, world, rank, dev, n_layers=48, T=8192, steps=2, warmup=1, balance=None):
     """The expert-parallel stack of the workload definition: 48 independently seeded layers of the
     prefill shape (E=512, top-10, H=2048, I=512, W4 g128), T=8192 tokens per GPU, router logits
     biased by a Zipf(1.1) expert popularity (so the experts, and with them the owner GPUs, are
-    unevenly loaded).  Rank r keeps experts [r*E/N, (r+1)*E/N) of every layer; the layers share one
+    unevenly loaded).  Each layer's experts are first renumbered so that equal contiguous blocks
+    carry equal loads (`balanced_expert_order` on a calibration batch's counts; FNX_EP_BALANCE=0
+    keeps the seeded numbering), then rank r keeps experts [r*E/N, (r+1)*E/N); the layers share one
     peer exchange and run one after another on the rank's tokens (each layer gets the same input:
     the stack times the MoE path, not a model, and the model's residuals and norms are not part of
     it).  Reports tokens/s over the stack, NVLink bytes per GPU per step, and the load imbalance
@@ -390,11 +392,21 @@ def bench_ep_stack(args, world, rank, dev, n_layers=48, T=8192, steps=2, warmup=
     from fnx import synth
     from fnx.engine import MoELayer
     bias = synth.zipf_bias(E, 1.1).to(dev)
+    if balance is None:
+        balance = os.environ.get("FNX_EP_BALANCE", "1") != "0"
     layers, shared = [], None
+    # expert placement: each layer's experts are renumbered so that the ranks' contiguous blocks
+    # carry equal loads by the slot counts of a calibration batch (other tokens than the timed ones)
+    xc = synth.make_tokens(T, H, seed=7000 + rank, device=dev)
     for i in range(n_layers):
         full = MoELayer.from_synth(synth.make_layer(synth.CFG2, seed=5000 + i, device=dev), synth.CFG2, bias=bias)
         if world > 1:
-            from fnx.ep import ExpertParallelMoE
+            from fnx.ep import ExpertParallelMoE, balanced_expert_order
+            if balance:
+                _, idc, _ = full.topk(full.logits(xc))
+                cnt = torch.bincount(idc.reshape(-1), minlength=E).to(torch.float64)
+                torch.distributed.all_reduce(cnt)
+                full.permute_experts(balanced_expert_order(cnt.cpu(), world))
             lay = ExpertParallelMoE.from_layer(full, rank, world, transport="p2p", max_tokens=T, exchange=shared)
             shared = lay.exchange
             del full
@@ -421,6 +433,8 @@ def bench_ep_stack(args, world, rank, dev, n_layers=48, T=8192, steps=2, warmup=
            "inputs": "the same seeded tokens into every layer", "ms_per_step": round(ms, 3),
            "tokens_per_s": round(world * T / (ms * 1e-3), 1), "ms_per_layer": round(ms / n_layers, 4),
            "experts_per_gpu": E // world,
+           "placement": ("experts renumbered per layer for equal rank loads by a calibration batch's slot counts"
+                         if balance and world > 1 else "contiguous blocks of expert ids"),
            "expert_rows_max_over_mean_layer0": round(float(per_expert.max() / per_expert.mean()), 3)}
     if world > 1:
         sends = torch.stack([lay.last_counts[0] for lay in layers]).to(torch.float64)       # [L, world] slots sent

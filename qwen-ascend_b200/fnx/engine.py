@@ -566,6 +566,23 @@ class MoELayer:
                              act=act[:M], yd=yd[:M], sh=sh, sh_act=sh_act)
         return out
 
+    def permute_experts(self, perm):
+        """Renumber the routed experts in place: new expert j is old expert perm[j] (its router row,
+        bias and tile blocks move together), e.g. to give the contiguous expert blocks of an
+        expert-parallel split equal loads.  The layer computes the same function, except where two
+        experts have exactly equal probability: the tie rule orders them by their (new) ids."""
+        E = self.E
+        perm = torch.as_tensor(perm, dtype=torch.int64).reshape(-1)
+        if perm.numel() != E or not torch.equal(torch.sort(perm).values, torch.arange(E)):
+            raise ValueError(f"permute_experts: not a permutation of {E} experts")
+        p = perm.to(self.router_cat.device)
+        self.router_cat[:E] = self.router_cat[:E].index_select(0, p)
+        if self.bias is not None:
+            self.bias = self.bias.index_select(0, p).contiguous()
+        self.gu_all[:E] = self.gu_all[:E].index_select(0, p)
+        self.dn_all[:E] = self.dn_all[:E].index_select(0, p)
+        return self
+
     def _shared_side_stream(self, dev):
         """The second stream of the overlapped prefill (None when `overlap_shared` is off)."""
         if not getattr(self, "overlap_shared", OVERLAP_SHARED):

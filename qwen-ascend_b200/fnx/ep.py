@@ -100,6 +100,27 @@ class _PeerExchange:
         self.base = None
 
 
+def balanced_expert_order(counts, world):
+    """An expert order (new id j = old expert order[j]) whose contiguous blocks of E/world experts,
+    one per rank, carry near-equal loads: experts by descending count (ties by id) each go to the
+    least loaded rank that still has room (longest-processing-time first with equal block sizes).
+    ``counts``: slots per expert from a calibration batch.  The heaviest rank is at most the mean
+    plus the largest single expert; a single expert above the mean share bounds it from below."""
+    c = torch.as_tensor(counts, dtype=torch.float64).reshape(-1).cpu()
+    E = c.numel()
+    if world < 1 or E % world:
+        raise ValueError(f"balanced_expert_order: {E} experts over {world} ranks")
+    per = E // world
+    order = sorted(range(E), key=lambda e: (-float(c[e]), e))
+    load = [0.0] * world
+    blocks = [[] for _ in range(world)]
+    for e in order:
+        r = min((q for q in range(world) if len(blocks[q]) < per), key=lambda q: (load[q], q))
+        blocks[r].append(e)
+        load[r] += float(c[e])
+    return torch.tensor([e for b in blocks for e in sorted(b)], dtype=torch.int64)
+
+
 class ExpertParallelMoE(MoELayer):
     """One MoE layer whose routed experts are sharded over ``world`` ranks.
 

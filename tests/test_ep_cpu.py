@@ -147,3 +147,23 @@ def test_ep_gloo_matches_one_rank(Ts):
     logits, w, idx, _ = one.route(x_all)
     ref2 = O.moe_forward(x_all, L, SHAPE["k"], routing=(w, idx))
     assert O.within_tolerance(ref, ref2)
+
+
+def test_balanced_expert_order():
+    """Equal blocks per rank, every expert once, and the heaviest block within one expert of the
+    mean (LPT bound); a uniform load stays uniform."""
+    from fnx.ep import balanced_expert_order
+    g = torch.Generator().manual_seed(3)
+    for E, G in ((512, 8), (64, 4), (8, 2)):
+        ranks = torch.randperm(E, generator=g)
+        counts = 1.0 / (1.0 + ranks.double()) ** 1.1 * 1e5            # Zipf-like over a random ranking
+        order = balanced_expert_order(counts, G)
+        assert sorted(order.tolist()) == list(range(E))
+        loads = counts[order].view(G, E // G).sum(1)
+        assert float(loads.max()) <= float(loads.mean()) + float(counts.max()) + 1e-6
+        contiguous = counts.view(G, E // G).sum(1)
+        assert float(loads.max()) <= float(contiguous.max()) + 1e-6
+    order = balanced_expert_order(torch.ones(16), 4)
+    assert sorted(order.tolist()) == list(range(16))
+    with pytest.raises(ValueError):
+        balanced_expert_order(torch.ones(10), 4)
