@@ -1109,6 +1109,10 @@ DecodeLayout decode_layout(int M, int H, int I, int E, int k) {
         if (L.ks2 < 2 && M <= 4) L.ks2 = 2;            // 2 to 4 tokens: halves (measured 46.7 against 50.0 us at M = 4)
         if (L.ks2 > cap) L.ks2 = cap;
         if (L.ks2 < 1) L.ks2 = 1;
+        // the shared gate/up does not wait for the routing: a few long items per feature tile
+        // leave the CTAs to the routed items once the routing lands (measured, ks1 = 2M:
+        // M = 1 21.1 against 22.1 us with the slot rule's 15; M = 4 45.5 against 46.4 with its 4)
+        if (M <= 4 && kb / (2 * M) >= 2) L.ks1 = 2 * M;
         const int e1 = env_int("FNX_DEC_KS1", 0), e2 = env_int("FNX_DEC_KS2", 0);
         if (e1 >= 1 && kb / e1 >= 1) L.ks1 = e1;
         if (e2 >= 1 && kb / e2 >= 1) L.ks2 = e2;
