@@ -249,9 +249,10 @@ int fnx_moe_grouped_w4_rows(const void* act, long long ld_act, long long act_row
                             int Nw, void* stream);
 
 /* fnx_moe_grouped_w4 (epilogues 0-2) over a selection of experts read in place, for ExpW4.apply /
- * apply_diag (fnx/engine.py:691-721, whose reference form copies the selected experts out with
- * expert_gather first): group e multiplies the tile blocks of expert expert_ids[e] (int64 [E])
- * of the E_w experts in `tiles`; an id outside [0, E_w) reads expert 0 and sets device error 2. */
+ * apply_diag (fnx/engine.py:691-721, where the selected experts' weights are first gathered,
+ * concatenated or index_select-ed into a copy): group e multiplies the tile blocks of expert
+ * expert_ids[e] (int64 [E]) of the E_w experts in `tiles`; an id outside [0, E_w) reads expert 0
+ * and sets device error 2. */
 int fnx_moe_grouped_w4_sel(const void* act, long long ld_act, long long act_rows, const void* row_index,
                            int index_div, const void* tiles, int E_w, const void* expert_ids, const void* ends,
                            void* out, long long ld_out, int E, int M, int K, int Nw, int epilogue, void* stream);
