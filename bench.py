@@ -11,7 +11,8 @@ per layer) over a CUDA-graphed rotation of 16 distinct layers (13 GB of weights)
 
 With ``--gpus N`` under torchrun each rank brings its own T=4096 tokens (weak scaling); the
 experts are sharded expert-parallel (E/N per GPU, ``fnx.ep``) and token rows go to their
-experts' owners and back with NCCL all-to-all-v.  Decode is reported at N=1 only.
+experts' owners and back over NVLink peer stores (the shared expert runs on a second stream
+meanwhile).  Decode is reported at N=1 only.
 
 ``--impl reference`` times the reference's algorithm on the host CPU (the oracle port of
 ``FnLayer._moe``; the reference itself is Python + torch_npu and cannot run here) on a
@@ -273,9 +274,9 @@ def bench_prefill(args, world, rank, dev):
     roofline = {"kernel": "grouped_gemm_pair_kernel<SwiGLU> (routed gate/up)", "bound": "tensor",
                 "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(achieved / pk["bf16_tflops"], 4), "peak_source": f"{src} bf16 burst",
-                # dram__bytes_read.sum + dram__bytes_write.sum of this launch (587.6 + 8.1 MB) from one
+                # dram__bytes_read.sum + dram__bytes_write.sum of this launch (587.6 + 8.3 MB) from one
                 # ncu capture of `bench.py --profile-case gu`
-                "traffic": 595.7e6, "traffic_unit": "B", "ms_per_launch": round(gu_ms, 4),
+                "traffic": 595.9e6, "traffic_unit": "B", "ms_per_launch": round(gu_ms, 4),
                 "algorithmic_flops_per_launch": gu_flops}
     layer_tflops = prefill_flops(T_PREFILL) / (ms * 1e-3) / 1e12
     # the router + shared-gate logits GEMM ([T, 2048] x [640, 2048]^T): this library's tcgen05 GEMM
