@@ -308,6 +308,21 @@ int fnx_moe_decode_w4(const void* x, const void* router, const void* gu, const v
                       const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H, int I,
                       int E, int k, void* workspace, size_t ws_bytes, void* stream);
 
+/* The step before the decode layer with the router GEMV fused into it (fnx/engine.py:838-845, the
+ * branch mix of gated_residual, then the router GEMV of fnx/engine.py:1786-1790 on its output):
+ * y bf16 [M, H] = bf16(sum_b bf16(bf16(sigmoid(l_b)) * x_b) / HC) of x (hn) and l bf16 [M, HC*H],
+ * and the router + shared-gate logits of y (router bf16 [E+1, H]) written into `workspace`, the
+ * decode workspace of (M, H, I, E, k), tagged for the next decode launch on it.  Follow it with
+ * fnx_moe_decode_w4_ex(..., flags = 1) on the same workspace and stream: that launch has no router
+ * items and routes exactly as fnx_moe_decode_w4 would on y.  M <= 16, the decode shape rules. */
+int fnx_hc_mix_router(const void* x, const void* l, void* y, const void* router, void* workspace, size_t ws_bytes,
+                      int M, int H, int I, int E, int k, int HC, void* stream);
+/* fnx_moe_decode_w4 with flags: bit 0, the router logits are already in the workspace
+ * (fnx_hc_mix_router ran just before on it). */
+int fnx_moe_decode_w4_ex(const void* x, const void* router, const void* gu, const void* dn, const void* sh_gu,
+                         const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H,
+                         int I, int E, int k, void* workspace, size_t ws_bytes, int flags, void* stream);
+
 /* fnx_moe_decode_w4 for callers that cannot allocate device memory (no counterpart in the
  * reference): a plugin host or FFI binding that hands over only input and output buffers,
  * or a serving process that forbids device allocation after start-up.  The scratch is a

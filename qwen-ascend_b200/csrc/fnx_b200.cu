@@ -1164,9 +1164,71 @@ FNX_API size_t fnx_moe_decode_workspace(int M, int H, int I, int E, int k) {
 // the tile blocks of fnx_repack_w4_tiles (gate/up in SwiGLU row order, down plain).
 // workspace must be zero-filled before its first use; every completed call leaves its
 // tickets at zero again.
+namespace {
+int decode_w4_impl(const void* x, const void* router, const void* gu, const void* dn, const void* sh_gu,
+                   const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H, int I,
+                   int E, int k, void* workspace, size_t ws_bytes, int logits_ready, void* stream);
+}
+
 FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu, const void* dn, const void* sh_gu,
                               const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H,
                               int I, int E, int k, void* workspace, size_t ws_bytes, void* stream) {
+    return decode_w4_impl(x, router, gu, dn, sh_gu, sh_dn, bias, out, w_out, idx_out, M, H, I, E, k, workspace,
+                          ws_bytes, 0, stream);
+}
+
+// fnx_moe_decode_w4 whose router logits were already written into the workspace by
+// fnx_hc_mix_router (flags bit 0): the launch skips its router items.
+FNX_API int fnx_moe_decode_w4_ex(const void* x, const void* router, const void* gu, const void* dn, const void* sh_gu,
+                                 const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M,
+                                 int H, int I, int E, int k, void* workspace, size_t ws_bytes, int flags,
+                                 void* stream) {
+    if (flags & ~1) return FNX_EARG;
+    if ((flags & 1) && decode_v1()) return FNX_EARG;            // the first decode kernel has no such mode
+    return decode_w4_impl(x, router, gu, dn, sh_gu, sh_dn, bias, out, w_out, idx_out, M, H, I, E, k, workspace,
+                          ws_bytes, flags & 1, stream);
+}
+
+// The hyper-connection mix of the decode rows with the router GEMV fused behind it: y bf16 [M, H]
+// = the branch mix of x (hn) and l bf16 [M, HC*H], and the router logits of y written, tagged,
+// into the decode workspace for the next fnx_moe_decode_w4_ex(..., flags = 1) on it.
+FNX_API int fnx_hc_mix_router(const void* x, const void* l, void* y, const void* router, void* workspace,
+                              size_t ws_bytes, int M, int H, int I, int E, int k, int HC, void* stream) {
+    if (M < 1 || M > DEC_MAX_M || E < 1 || E > ROUTE_MAX_E || k < 1 || k > 32 || k > E || HC < 1 || HC > 64 ||
+        !x || !l || !y || !router)
+        return FNX_EARG;
+    if (H < 256 || I < 128 || H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K || E > DEC_MAX_E)
+        return FNX_ESHAPE;
+    if (decode_v1()) return FNX_EARG;
+    const DecodeLayout L = decode_layout(M, H, I, E, k);
+    if (!workspace || ws_bytes < L.total) return FNX_EWORKSPACE;
+    if (!aligned16(router) || !aligned16(workspace)) return FNX_EALIGN;
+    uint8_t* ws = (uint8_t*)workspace;
+    StreamParams q{};
+    q.router = (const bf16*)router;
+    q.epoch = (unsigned*)ws;
+    q.tlog = (tword*)(ws + L.tlog);
+    q.M = M; q.H = H; q.I = I; q.E = E; q.k = k; q.R = L.R;
+    const size_t smem = (size_t)M * H * 2;
+    static bool set[FNX_MAX_DEVICES] = {};
+    const int dev = current_device();
+    if (!set[dev]) {
+        if (cudaFuncSetAttribute(hc_mix_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 DEC_MAX_M * DEC_MAX_K * 2) != cudaSuccess)
+            return FNX_ELAUNCH;
+        set[dev] = true;
+    }
+    const int rows = d2_router_rows(H);
+    const int grid = (L.R + rows - 1) / rows;
+    hc_mix_router_kernel<<<grid, D2_CTHREADS, smem, (cudaStream_t)stream>>>((const bf16*)x, (const bf16*)l, HC,
+                                                                           (bf16*)y, q);
+    return launch_rc();
+}
+
+namespace {
+int decode_w4_impl(const void* x, const void* router, const void* gu, const void* dn, const void* sh_gu,
+                   const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H, int I,
+                   int E, int k, void* workspace, size_t ws_bytes, int logits_ready, void* stream) {
     if (M < 1 || M > DEC_MAX_M || E < 1 || E > ROUTE_MAX_E || k < 1 || k > 32 || k > E) return FNX_EARG;
     if (H < 256 || I < 128 || H % 256 || I % 128 || H > DEC_MAX_K || I > DEC_MAX_K || E > DEC_MAX_E)
         return FNX_ESHAPE;
@@ -1187,6 +1249,7 @@ FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu,
         q.tlog = (tword*)(ws + L.tlog); q.tpart = (tword*)(ws + L.tpart); q.tpart2 = (tword*)(ws + L.tpart2);
         q.tyd = (tword*)(ws + L.tyd); q.tsh = (tword*)(ws + L.tsh);
         q.M = M; q.H = H; q.I = I; q.E = E; q.k = k; q.R = L.R; q.ks1 = L.ks1; q.ks2 = L.ks2;
+        q.logits_ready = logits_ready;
         // one cooperative launch of every block that fits at once (work items wait for earlier
         // items of other blocks, so all blocks must be resident)
         static int grid2_of[FNX_MAX_DEVICES] = {};
@@ -1249,6 +1312,7 @@ FNX_API int fnx_moe_decode_w4(const void* x, const void* router, const void* gu,
     if (cudaLaunchKernelEx(&cfg, decode_fused_kernel, p) != cudaSuccess) return FNX_ELAUNCH;
     return launch_rc();
 }
+}  // namespace
 
 // ======================================================================== legacy W4 GEMV
 FNX_API int fnx_w4gemv_launch(void* p4, void* s4t, void* xe, void* xo, void* y, void* dbg, void* ids, int N, int K,

@@ -88,6 +88,8 @@ struct StreamParams {
     tword* tsh;                      // [M][H/2]           bf16x2 shared down row
     int M, H, I, E, k, R;
     int ks1, ks2;                    // K splits of the shared and routed gate/up GEMVs
+    int logits_ready;                // 1: tlog already carries this launch's tagged logits
+                                     // (hc_mix_router_kernel ran before), so there are no router items
 };
 
 FNX_DEV void st_tag(tword* p, uint32_t payload, uint32_t tag) {
@@ -164,7 +166,7 @@ struct D2Shape {
 FNX_DEV D2Shape d2_shape(const StreamParams& p) {
     D2Shape s;
     s.nrow = d2_router_rows(p.H);
-    s.RB = (p.R + s.nrow - 1) / s.nrow;
+    s.RB = p.logits_ready ? 0 : (p.R + s.nrow - 1) / s.nrow;
     s.MT = p.I / 64;
     s.KB = p.H / 64;
     s.MTd = p.H / 128;
@@ -844,6 +846,39 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
             *p.exit = 0;
         }
     }
+}
+
+// The hyper-connection branch mix that produces the decode layer's input (fnx/engine.py:838-845,
+// hc_sigmoid_reduce_kernel's arithmetic) with the router GEMV fused behind it: block b recomputes
+// the M mixed rows in shared memory, block 0 also stores them (y), and every block computes the
+// logits of router rows [b*nrow, b*nrow + nrow) with d2_router's arithmetic, writing them into the
+// decode workspace tagged for the next decode launch on it.  That launch (logits_ready) then has
+// no router items, and routes exactly as if its own router items had produced these logits.
+// x (hn), l bf16 [M, HC*H]; router bf16 [R, H]; dynamic shared memory M*H*2 bytes.
+__global__ void __launch_bounds__(D2_CTHREADS) hc_mix_router_kernel(const bf16* __restrict__ x,
+                                                                   const bf16* __restrict__ l, int HC,
+                                                                   bf16* __restrict__ y, const StreamParams p) {
+    extern __shared__ __align__(16) uint8_t mix_raw[];
+    bf16* xs = reinterpret_cast<bf16*>(mix_raw);            // [M][H]
+    const int H = p.H;
+    const uint32_t tag = *p.epoch + 1u;                       // the next decode launch's tag
+    for (int i = threadIdx.x; i < p.M * H; i += D2_CTHREADS) {
+        const int t = i / H, c = i - t * H;
+        float acc = 0.f;
+        for (int b = 0; b < HC; ++b) {
+            const long long o = ((long long)t * HC + b) * H + c;
+            const float sg = round_bf(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-bf2f(l[o])))));
+            acc = __fadd_rn(acc, round_bf(__fmul_rn(sg, bf2f(x[o]))));
+        }
+        const bf16 v = f2bf(__fdiv_rn(acc, (float)HC));
+        xs[i] = v;
+        if (blockIdx.x == 0) y[i] = v;
+    }
+    __syncthreads();
+    const int nrow = d2_router_rows(H);
+    const int e0 = blockIdx.x * nrow;
+    const int nr = min(nrow, p.R - e0);
+    if (nr > 0) d2_router(p, p.router + (long long)e0 * H, e0, nr, nrow, xs, tag);
 }
 
 }  // namespace fnx

@@ -77,6 +77,8 @@ SIGNATURES = {
     "fnx_bf16_gemm_nt": ([P, LL, P, P, LL, I, I, I, P], I),
     "fnx_moe_decode_workspace": ([I] * 5, SZ),
     "fnx_moe_decode_w4": ([P] * 10 + [I] * 5 + [P, SZ, P], I),
+    "fnx_moe_decode_w4_ex": ([P] * 10 + [I] * 5 + [P, SZ, I, P], I),
+    "fnx_hc_mix_router": ([P] * 5 + [SZ] + [I] * 6 + [P], I),
     "fnx_moe_decode_w4_noalloc": ([P] * 10 + [I] * 5 + [P], I),
     "fnx_w4gemv_launch": ([P] * 7 + [I] * 5 + [P], I),
     "fnx_w4gemv_launch_layers": ([ctypes.POINTER(P)] * 4 + [I] * 6 + [P, P], I),

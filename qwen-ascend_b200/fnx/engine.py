@@ -100,14 +100,16 @@ def mm_nt(x, w):
     return out
 
 
-def gated_residual(h, hc_norm_w, w_down, w_up, w_inj=None, n_inj=0, hc=4, eps=1e-6):
+def gated_residual(h, hc_norm_w, w_down, w_up, w_inj=None, n_inj=0, hc=4, eps=1e-6, moe=None):
     """The hyper-connection mix that produces a layer's MoE input (``fnx/engine.py:818-857``):
     ``h`` bf16 ``[b, 1, hc*H]`` -> ``(mixed [b, 1, H], inj [b, 1, hc])``.  ``w_down`` bf16
     ``[r (+ hc), hc*H]`` (with ``n_inj == hc`` its last rows are the inject weights, as the
     reference's loader concatenates them), ``w_up`` bf16 ``[hc*H, r]``, ``w_inj`` bf16
     ``[hc, hc*H]`` when not concatenated.  RMSNorm, activation and branch mix run on this
     library's kernels with the reference's roundings, the two small GEMMs on its tcgen05 bf16
-    GEMM (``mm_nt``)."""
+    GEMM (``mm_nt``).  ``moe``: the ``MoELayer`` whose decode follows (``b <= 16``): its router
+    GEMV is fused into the mix (``MoELayer.mix_and_route``) and its decode must be called next
+    with ``logits_ready=True``."""
     from . import post_ops
     b, HCH = h.shape[0], h.shape[-1]
     H = HCH // hc
@@ -123,6 +125,11 @@ def gated_residual(h, hc_norm_w, w_down, w_up, w_inj=None, n_inj=0, hc=4, eps=1e
     di = mm_nt(hn, w_down)
     mix, inj = post_ops.activate(di.view(b, 1, -1).contiguous(), hc)
     logits = mm_nt(mix.view(b, -1), w_up)
+    if moe is not None and b <= DECODE_MAX_TOKENS and moe.E <= DECODE_MAX_EXPERTS:
+        # the router GEMV of the MoE layer that follows, fused into the mix; its decode call must
+        # come next on this stream, as moe.decode(mixed, logits_ready=True)
+        mixed = moe.mix_and_route(hn, logits, hc)
+        return mixed.view(b, 1, H), inj
     mixed = post_ops.mix_reduce(hn.view(b, 1, HCH), logits.view(b, 1, HCH).contiguous(), hc)
     return mixed, inj
 
@@ -609,20 +616,43 @@ class MoELayer:
             self._ws[key] = ws
         return ws
 
-    def decode(self, x, out=None, w_out=None, idx_out=None):
-        """Fused decode kernels for ``M <= 16`` tokens; returns ``(out, w, idx)``."""
+    def decode(self, x, out=None, w_out=None, idx_out=None, logits_ready=False):
+        """Fused decode kernels for ``M <= 16`` tokens; returns ``(out, w, idx)``.
+        ``logits_ready``: ``x`` came from ``mix_and_route`` just before, which left its router logits
+        in this layer's decode workspace, so the launch skips its router items."""
         M = x.shape[0]
         dev = x.device
         out = torch.empty(M, self.H, dtype=BF16, device=dev) if out is None else out
         w_out = torch.empty(M, self.k, dtype=BF16, device=dev) if w_out is None else w_out
         idx_out = torch.empty(M, self.k, dtype=torch.int64, device=dev) if idx_out is None else idx_out
         ws = self.decode_workspace(M, dev)
-        rc = _lib.lib().fnx_moe_decode_w4(
+        rc = _lib.lib().fnx_moe_decode_w4_ex(
             x.data_ptr(), self.router_cat.data_ptr(), self.gu_t.data_ptr(), self.dn_t.data_ptr(),
             self.sh_gu_t.data_ptr(), self.sh_dn_t.data_ptr(), _lib.ptr(self.bias), out.data_ptr(), w_out.data_ptr(),
-            idx_out.data_ptr(), M, self.H, self.I, self.E, self.k, ws.data_ptr(), ws.numel(), _lib.stream(dev))
+            idx_out.data_ptr(), M, self.H, self.I, self.E, self.k, ws.data_ptr(), ws.numel(),
+            1 if logits_ready else 0, _lib.stream(dev))
         _lib.check(rc, "MoE decode")
         return out, w_out, idx_out
+
+    def mix_and_route(self, hn, mix_logits, hc=4):
+        """The branch mix that produces this layer's decode input, with the router GEMV fused behind
+        it (``fnx_hc_mix_router``): ``hn``, ``mix_logits`` bf16 ``[M, hc*H]`` -> ``mixed [M, H]``
+        (the bits of ``post_ops.mix_reduce``), the router logits of ``mixed`` left in this layer's
+        decode workspace for the next ``decode(mixed, logits_ready=True)`` on the same stream."""
+        _lib.require_cuda(hn, mix_logits)
+        M = hn.shape[0]
+        dev = hn.device
+        hn = hn.reshape(M, -1).contiguous()
+        mix_logits = mix_logits.reshape(M, -1).contiguous()
+        if hn.shape[1] != hc * self.H or mix_logits.shape != hn.shape:
+            raise ValueError(f"mix_and_route: rows of {hc}*{self.H} expected, got {tuple(hn.shape)}")
+        mixed = torch.empty(M, self.H, dtype=BF16, device=dev)
+        ws = self.decode_workspace(M, dev)
+        rc = _lib.lib().fnx_hc_mix_router(hn.data_ptr(), mix_logits.data_ptr(), mixed.data_ptr(),
+                                          self.router_cat.data_ptr(), ws.data_ptr(), ws.numel(), M, self.H, self.I,
+                                          self.E, self.k, hc, _lib.stream(dev))
+        _lib.check(rc, "hyper-connection mix + router")
+        return mixed
 
 
 class CapturedLayer:

@@ -62,6 +62,12 @@ def test_host_side_rejections(lib):
     assert gs(None, 2048, 64, None, 1, None, 8, 8, None, None, 1024, 8, 64, 2048, 1024, 3, None) == -1
     assert gs(None, 2048, 64, None, 1, None, 8, 8, None, None, 1024, 8, 64, 2048, 1000, 0, None) == -2
     assert lib.fnx_weighted_sum_f32(8, 8, 8, 0, 100, None) == -1                                 # no experts
+    # the fused mix + router: decode shape rules and the decode workspace size; the flagged decode
+    mr = lib.fnx_hc_mix_router
+    assert mr(8, 8, 8, 8, 8, 1 << 30, 0, 2048, 512, 512, 10, 4, None) == -1                    # M = 0
+    assert mr(8, 8, 8, 8, 8, 1 << 30, 1, 2000, 512, 512, 10, 4, None) == -2                    # H % 256
+    assert mr(8, 8, 8, 8, 8, 16, 1, 2048, 512, 512, 10, 4, None) == -5                         # workspace
+    assert lib.fnx_moe_decode_w4_ex(*([8] * 10), 1, 2048, 512, 512, 10, 8, 1 << 30, 2, None) == -1   # flags
     assert lib.fnx_weighted_sum_f32(None, 8, 8, 4, 100, None) == -1                              # no y
     assert lib.fnx_repack_w4_tiles(None, None, None, 8, 2048, 1024, 96, 0, None) == -1          # gs % 64
     assert lib.fnx_repack_v2o(None, 8, 1024, 2048, 0, None, None) == -1                          # no buffers

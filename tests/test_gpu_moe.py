@@ -283,6 +283,28 @@ def test_weighted_sum_kernel():
     assert torch.equal(W4GemvOp.weighted_sum(y[:0].to(DEV), []).cpu(), torch.zeros(3000))
 
 
+@pytest.mark.parametrize("M", [1, 4])
+def test_mix_and_route_matches_unfused_path(M):
+    """The hyper-connection mix with the router GEMV fused behind it: the mixed rows are the bits
+    of the branch-mix kernel, and the decode that reads the logits it left in the workspace gives
+    the bits of the decode that computes its own router logits, on consecutive calls."""
+    from fnx import post_ops
+    t, L, layer = _layer(synth.CFG2, 37)
+    H, hc = synth.CFG2.H, 4
+    g = torch.Generator().manual_seed(M)
+    for call in range(2):
+        hn = (torch.randn(M, hc * H, generator=g) * 2).to(BF16).to(DEV)
+        lg = torch.randn(M, hc * H, generator=g).to(BF16).to(DEV)
+        ref_mixed = post_ops.mix_reduce(hn.view(M, 1, hc * H), lg.view(M, 1, hc * H), hc).view(M, H)
+        ref_out, ref_w, ref_idx = (a.clone() for a in layer.decode(ref_mixed))
+        mixed = layer.mix_and_route(hn, lg, hc)
+        assert torch.equal(mixed.view(torch.int16), ref_mixed.view(torch.int16)), call
+        out, w, idx = layer.decode(mixed, logits_ready=True)
+        assert torch.equal(idx, ref_idx), call
+        assert torch.equal(w.view(torch.int16), ref_w.view(torch.int16)), call
+        assert torch.equal(out.view(torch.int16), ref_out.view(torch.int16)), call
+
+
 def test_permute_experts_keeps_the_layer():
     """Renumbered experts (router rows, bias, tile blocks moved together): every token whose
     selection maps back to the same experts in the same slot order gets the same bits; only
