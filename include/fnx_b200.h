@@ -318,7 +318,8 @@ int fnx_moe_decode_w4(const void* x, const void* router, const void* gu, const v
 int fnx_hc_mix_router(const void* x, const void* l, void* y, const void* router, void* workspace, size_t ws_bytes,
                       int M, int H, int I, int E, int k, int HC, void* stream);
 /* fnx_moe_decode_w4 with flags: bit 0, the router logits are already in the workspace
- * (fnx_hc_mix_router ran just before on it). */
+ * (fnx_hc_mix_router ran just before on it).  Without that call the launch records device error
+ * bit 8 and ends at once, its outputs undefined. */
 int fnx_moe_decode_w4_ex(const void* x, const void* router, const void* gu, const void* dn, const void* sh_gu,
                          const void* sh_dn, const void* bias, void* out, void* w_out, void* idx_out, int M, int H,
                          int I, int E, int k, void* workspace, size_t ws_bytes, int flags, void* stream);
@@ -337,7 +338,9 @@ int fnx_moe_decode_w4_noalloc(const void* x, const void* router, const void* gu,
 /* ---- library ---- */
 const char* fnx_b200_version(void);
 /* device error bits since the last clear: 1 bounded wait expired, 2 expert id out of range,
- * 4 overflow.  Synchronises with the device (cudaMemcpyFromSymbol). */
+ * 4 overflow, 8 a fnx_moe_decode_w4_ex(flags = 1) launch found no fresh router logits (no
+ * fnx_hc_mix_router on its workspace since the last decode; its outputs are then undefined).
+ * Synchronises with the device (cudaMemcpyFromSymbol). */
 unsigned fnx_device_errors(int clear);
 
 #ifdef __cplusplus

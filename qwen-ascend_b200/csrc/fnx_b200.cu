@@ -1209,17 +1209,17 @@ FNX_API int fnx_hc_mix_router(const void* x, const void* l, void* y, const void*
     q.epoch = (unsigned*)ws;
     q.tlog = (tword*)(ws + L.tlog);
     q.M = M; q.H = H; q.I = I; q.E = E; q.k = k; q.R = L.R;
-    const size_t smem = (size_t)M * H * 2;
+    const int rows = d2_router_rows(H);
+    const size_t smem = (size_t)(M + rows) * H * 2;
     static bool set[FNX_MAX_DEVICES] = {};
     const int dev = current_device();
     if (!set[dev]) {
         if (cudaFuncSetAttribute(hc_mix_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 DEC_MAX_M * DEC_MAX_K * 2) != cudaSuccess)
+                                 (DEC_MAX_M + D2_MAX_ROWS) * DEC_MAX_K * 2) != cudaSuccess)
             return FNX_ELAUNCH;
         set[dev] = true;
     }
-    const int rows = d2_router_rows(H);
-    const int grid = (L.R + rows - 1) / rows;
+    const int grid = ((L.R + rows - 1) / rows + HC_MIX_CLUSTER - 1) / HC_MIX_CLUSTER * HC_MIX_CLUSTER;
     hc_mix_router_kernel<<<grid, D2_CTHREADS, smem, (cudaStream_t)stream>>>((const bf16*)x, (const bf16*)l, HC,
                                                                            (bf16*)y, q);
     return launch_rc();

@@ -33,6 +33,7 @@ enum {
     FNX_DEVERR_TIMEOUT = 1u,   // a bounded wait expired
     FNX_DEVERR_BADID = 2u,     // an expert id outside [0, E)
     FNX_DEVERR_OVERFLOW = 4u,  // a count exceeded its buffer
+    FNX_DEVERR_NOLOGITS = 8u,  // a decode with logits_ready found no fresh router logits
 };
 
 __device__ unsigned int g_fnx_errors;

@@ -36,6 +36,7 @@
 // waiting and finishes its items on whatever data is there (the error word records it).
 #pragma once
 #include "kernels_decode.cuh"
+#include "kernels_hc.cuh"
 
 namespace fnx {
 
@@ -89,7 +90,8 @@ struct StreamParams {
     int M, H, I, E, k, R;
     int ks1, ks2;                    // K splits of the shared and routed gate/up GEMVs
     int logits_ready;                // 1: tlog already carries this launch's tagged logits
-                                     // (hc_mix_router_kernel ran before), so there are no router items
+                                     // (hc_mix_router_kernel ran before), so the router items are
+                                     // empty (kept, so every other item runs on the same block)
 };
 
 FNX_DEV void st_tag(tword* p, uint32_t payload, uint32_t tag) {
@@ -166,7 +168,7 @@ struct D2Shape {
 FNX_DEV D2Shape d2_shape(const StreamParams& p) {
     D2Shape s;
     s.nrow = d2_router_rows(p.H);
-    s.RB = p.logits_ready ? 0 : (p.R + s.nrow - 1) / s.nrow;
+    s.RB = (p.R + s.nrow - 1) / s.nrow;              // with logits_ready: empty items, same placement
     s.MT = p.I / 64;
     s.KB = p.H / 64;
     s.MTd = p.H / 128;
@@ -700,6 +702,19 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
         }
         mbar_init(&routing_bar, 1);
         s_dead = 0;
+        if (p.logits_ready) {
+            // the logits were written by the kernel before this one on the stream, so they carry
+            // this launch's tag already; a stale tag means no fnx_hc_mix_router ran on this
+            // workspace since the last decode: record it and end at once instead of by timeouts
+            for (int t = 0; t < p.M; ++t) {
+                const tword* row = p.tlog + (long long)t * p.R;
+                if ((uint32_t)(ld_tag(row) >> 32) != tag || (uint32_t)(ld_tag(row + p.R - 1) >> 32) != tag) {
+                    fnx_flag_error(FNX_DEVERR_NOLOGITS);
+                    s_dead = 1;
+                    break;
+                }
+            }
+        }
         fence_mbar_init();
     }
     __syncthreads();
@@ -717,7 +732,7 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
                     routed = true;
                 }
                 const D2Item d = d2_item(p, S, R, it);
-                const int ns = d2_stages(d);
+                const int ns = (d.type == D2_ROUTER && p.logits_ready) ? 0 : d2_stages(d);
 #ifndef FNX_D2_EAGER_DOWN
                 // a down item's weights are requested once the earlier gate/up stages of this CTA
                 // are consumed: the gate/up bytes, which the critical path waits for, get the HBM
@@ -771,6 +786,7 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
             have_routing = true;
         }
         const D2Item d = d2_item(p, S, R, it);
+        if (d.type == D2_ROUTER && p.logits_ready) continue;
         if (d.type == D2_COMB) {
             d2_combine(p, R, d.t, d.m, tag, dead);
             continue;
@@ -848,37 +864,68 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
     }
 }
 
-// The hyper-connection branch mix that produces the decode layer's input (fnx/engine.py:838-845,
-// hc_sigmoid_reduce_kernel's arithmetic) with the router GEMV fused behind it: block b recomputes
-// the M mixed rows in shared memory, block 0 also stores them (y), and every block computes the
-// logits of router rows [b*nrow, b*nrow + nrow) with d2_router's arithmetic, writing them into the
-// decode workspace tagged for the next decode launch on it.  That launch (logits_ready) then has
-// no router items, and routes exactly as if its own router items had produced these logits.
-// x (hn), l bf16 [M, HC*H]; router bf16 [R, H]; dynamic shared memory M*H*2 bytes.
-__global__ void __launch_bounds__(D2_CTHREADS) hc_mix_router_kernel(const bf16* __restrict__ x,
-                                                                   const bf16* __restrict__ l, int HC,
-                                                                   bf16* __restrict__ y, const StreamParams p) {
+// The hyper-connection branch mix that produces the decode layer's input (fnx/engine.py:838-845;
+// hc_mix_one, the arithmetic of hc_sigmoid_reduce_kernel) with the router GEMV fused behind it.
+// Blocks run in clusters of HC_MIX_CLUSTER: block r of a cluster mixes slice r of the M*H outputs
+// into its shared memory (the first cluster also stores it, y), the slices are exchanged over
+// distributed shared memory, and every block then computes the logits of router rows
+// [b*nrow, b*nrow + nrow) from the full mixed rows with d2_router's arithmetic, writing them into
+// the decode workspace tagged for the next decode launch on it.  That launch (logits_ready) then
+// leaves its router items empty, and routes exactly as if they had produced these logits.  The
+// block's router rows are bulk-loaded into shared memory at entry, under the mix.
+// x (hn), l bf16 [M, HC*H]; router bf16 [R, H]; dynamic shared memory (M + nrow)*H*2 bytes; the
+// grid is a multiple of HC_MIX_CLUSTER (blocks past the last router row only mix).
+constexpr int HC_MIX_CLUSTER = 8;
+
+FNX_DEV uint4 ld_shared_cluster_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
+    return v;
+}
+
+__global__ void __cluster_dims__(HC_MIX_CLUSTER, 1, 1) __launch_bounds__(D2_CTHREADS)
+    hc_mix_router_kernel(const bf16* __restrict__ x, const bf16* __restrict__ l, int HC, bf16* __restrict__ y,
+                         const StreamParams p) {
     extern __shared__ __align__(16) uint8_t mix_raw[];
+    __shared__ uint64_t rows_full;
     bf16* xs = reinterpret_cast<bf16*>(mix_raw);            // [M][H]
     const int H = p.H;
     const uint32_t tag = *p.epoch + 1u;                       // the next decode launch's tag
-    for (int i = threadIdx.x; i < p.M * H; i += D2_CTHREADS) {
-        const int t = i / H, c = i - t * H;
-        float acc = 0.f;
-        for (int b = 0; b < HC; ++b) {
-            const long long o = ((long long)t * HC + b) * H + c;
-            const float sg = round_bf(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-bf2f(l[o])))));
-            acc = __fadd_rn(acc, round_bf(__fmul_rn(sg, bf2f(x[o]))));
-        }
-        const bf16 v = f2bf(__fdiv_rn(acc, (float)HC));
-        xs[i] = v;
-        if (blockIdx.x == 0) y[i] = v;
-    }
-    __syncthreads();
+    const int n = p.M * H;                                    // a multiple of 256 (H is)
+    bf16* rows = xs + n;                                      // [nrow][H] this block's router rows
     const int nrow = d2_router_rows(H);
     const int e0 = blockIdx.x * nrow;
-    const int nr = min(nrow, p.R - e0);
-    if (nr > 0) d2_router(p, p.router + (long long)e0 * H, e0, nr, nrow, xs, tag);
+    const int nr = max(0, min(nrow, p.R - e0));
+    if (threadIdx.x == 0 && nr > 0) {
+        mbar_init(&rows_full, 1);
+        fence_mbar_init();
+        const uint32_t bytes = (uint32_t)nr * H * 2;
+        mbar_arrive_expect_tx(&rows_full, bytes);
+        bulk_load(smem_u32(rows), p.router + (long long)e0 * H, bytes, &rows_full, l2_evict_first());
+    }
+    const int per = n / HC_MIX_CLUSTER;                       // slice length, a multiple of 32
+    const int rank = (int)cluster_rank();
+    const bool store = blockIdx.x < HC_MIX_CLUSTER;
+    for (int i = rank * per + threadIdx.x; i < (rank + 1) * per; i += D2_CTHREADS) {
+        const int t = i / H;
+        const bf16 v = hc_mix_one(x, l, t, i - t * H, H, HC);
+        xs[i] = v;
+        if (store) y[i] = v;
+    }
+    cluster_sync_all();                                       // every slice is in its block's shared memory
+    const int per16 = per / 8;                                // 16-byte words per slice
+    for (int r = 1; r < HC_MIX_CLUSTER; ++r) {
+        const int src = (rank + r) % HC_MIX_CLUSTER;
+        uint4* dst = reinterpret_cast<uint4*>(xs) + src * per16;
+        const uint32_t rem = mapa_rank(dst, (uint32_t)src);
+        for (int j = threadIdx.x; j < per16; j += D2_CTHREADS) dst[j] = ld_shared_cluster_v4(rem + 16u * j);
+    }
+    cluster_sync_all();                                       // peers keep their shared memory until read
+    if (nr > 0) {
+        if (!mbar_wait(&rows_full, 0)) mbar_wait(&rows_full, 0);   // (the copy must land before exit)
+        d2_router(p, rows, e0, nr, nrow, xs, tag);
+    }
 }
 
 }  // namespace fnx

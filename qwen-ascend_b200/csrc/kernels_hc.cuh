@@ -68,20 +68,36 @@ __global__ void __launch_bounds__(256) hc_activation_kernel(const bf16* __restri
 
 // mixed[t, c] = bf16( (sum_b bf16(bf16(sigmoid(l[t, b*H + c])) * x[t, b*H + c])) / HC ), the
 // branch sum in order b = 0..HC-1 in fp32.
+// One output of the branch mix at (t, c): branches in ascending order, the loads of four
+// branches issued before their arithmetic (HC is a runtime value, so the loop is not unrolled).
+FNX_DEV bf16 hc_mix_one(const bf16* __restrict__ x, const bf16* __restrict__ l, long long t, int c, int H, int HC) {
+    float acc = 0.f;
+    for (int b0 = 0; b0 < HC; b0 += 4) {
+        bf16 lv[4] = {}, xv[4] = {};
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (b0 + u < HC) {
+                const long long o = (t * HC + b0 + u) * (long long)H + c;
+                lv[u] = l[o];
+                xv[u] = x[o];
+            }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (b0 + u < HC) {
+                const float sg = round_bf(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-bf2f(lv[u])))));
+                acc = __fadd_rn(acc, round_bf(__fmul_rn(sg, bf2f(xv[u]))));
+            }
+    }
+    return f2bf(__fdiv_rn(acc, (float)HC));
+}
+
 __global__ void __launch_bounds__(256) hc_sigmoid_reduce_kernel(const bf16* __restrict__ x, const bf16* __restrict__ l,
                                                                 bf16* __restrict__ y, int batch, int H, int HC) {
     const long long total = (long long)batch * H;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
         const long long t = i / H;
-        const int c = (int)(i - t * H);
-        float acc = 0.f;
-        for (int b = 0; b < HC; ++b) {
-            const long long o = (t * HC + b) * (long long)H + c;
-            const float sg = round_bf(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-bf2f(l[o])))));
-            acc = __fadd_rn(acc, round_bf(__fmul_rn(sg, bf2f(x[o]))));
-        }
-        y[i] = f2bf(__fdiv_rn(acc, (float)HC));
+        y[i] = hc_mix_one(x, l, t, (int)(i - t * H), H, HC);
     }
 }
 

@@ -128,5 +128,6 @@ def require_cuda(*tensors):
 
 
 def device_errors(clear: bool = True) -> int:
-    """Bits recorded by kernels since the last clear (1 timeout, 2 bad expert id, 4 overflow)."""
+    """Bits recorded by kernels since the last clear (1 timeout, 2 bad expert id, 4 overflow,
+    8 a logits-ready decode without fresh router logits)."""
     return int(lib().fnx_device_errors(1 if clear else 0))

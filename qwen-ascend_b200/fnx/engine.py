@@ -406,6 +406,7 @@ class MoELayer:
         self.router_cat = rc
         self.bias = None if bias is None else bias.to(torch.float32).to(gate_w.device).contiguous()
         self._ws = {}
+        self._routed = set()        # decode workspaces holding logits from mix_and_route
         self._prefill_bufs = {}
 
     @classmethod
@@ -626,6 +627,10 @@ class MoELayer:
         w_out = torch.empty(M, self.k, dtype=BF16, device=dev) if w_out is None else w_out
         idx_out = torch.empty(M, self.k, dtype=torch.int64, device=dev) if idx_out is None else idx_out
         ws = self.decode_workspace(M, dev)
+        key = (M, str(dev))
+        if logits_ready and key not in self._routed:
+            raise RuntimeError("decode(logits_ready=True) needs mix_and_route on the same rows just before")
+        self._routed.discard(key)
         rc = _lib.lib().fnx_moe_decode_w4_ex(
             x.data_ptr(), self.router_cat.data_ptr(), self.gu_t.data_ptr(), self.dn_t.data_ptr(),
             self.sh_gu_t.data_ptr(), self.sh_dn_t.data_ptr(), _lib.ptr(self.bias), out.data_ptr(), w_out.data_ptr(),
@@ -652,6 +657,7 @@ class MoELayer:
                                           self.router_cat.data_ptr(), ws.data_ptr(), ws.numel(), M, self.H, self.I,
                                           self.E, self.k, hc, _lib.stream(dev))
         _lib.check(rc, "hyper-connection mix + router")
+        self._routed.add((M, str(dev)))
         return mixed
 
 

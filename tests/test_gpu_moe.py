@@ -303,6 +303,27 @@ def test_mix_and_route_matches_unfused_path(M):
         assert torch.equal(idx, ref_idx), call
         assert torch.equal(w.view(torch.int16), ref_w.view(torch.int16)), call
         assert torch.equal(out.view(torch.int16), ref_out.view(torch.int16)), call
+    # the decode consumed those logits: a second logits-ready decode is refused on the host, and
+    # through the C ABI it records device error bit 8 and ends at once (no bounded wait runs out)
+    with pytest.raises(RuntimeError):
+        layer.decode(mixed, logits_ready=True)
+    import time
+    ws = layer.decode_workspace(M, DEV)
+    o2, w2 = torch.empty_like(out), torch.empty_like(w)
+    i2 = torch.empty_like(idx)
+    assert _lib.device_errors() == 0
+    torch.cuda.synchronize()
+    t0 = time.monotonic()
+    rc = _lib.lib().fnx_moe_decode_w4_ex(
+        mixed.data_ptr(), layer.router_cat.data_ptr(), layer.gu_t.data_ptr(), layer.dn_t.data_ptr(),
+        layer.sh_gu_t.data_ptr(), layer.sh_dn_t.data_ptr(), _lib.ptr(layer.bias), o2.data_ptr(), w2.data_ptr(),
+        i2.data_ptr(), M, H, layer.I, layer.E, layer.k, ws.data_ptr(), ws.numel(), 1, _lib.stream(mixed.device))
+    torch.cuda.synchronize()
+    assert rc == 0 and time.monotonic() - t0 < 1.0
+    assert _lib.device_errors() == 8
+    # the workspace stays usable: the next plain decode gives the reference bits again
+    out, w, idx = layer.decode(ref_mixed)
+    assert torch.equal(idx, ref_idx) and torch.equal(out.view(torch.int16), ref_out.view(torch.int16))
 
 
 def test_permute_experts_keeps_the_layer():
