@@ -56,7 +56,9 @@ constexpr int D2_THREADS = 32 * (D2_CWARPS + 1);
 constexpr int D2_SK = FNX_D2_SK;                      // tile blocks per stage
 constexpr int D2_NS = FNX_D2_NS;                      // stages in the ring
 constexpr int D2_STAGE_BYTES = D2_SK * TILE_BLOCK_BYTES;
-constexpr int D2_SMEM = D2_NS * D2_STAGE_BYTES;       // 69,632 B at 2 x 8
+constexpr int D2_RING_BYTES = D2_NS * D2_STAGE_BYTES; // 69,632 B at 2 x 8
+constexpr int D2_XRES_BYTES = 16384;                  // the M token rows, resident when M*H*2 fits
+constexpr int D2_SMEM = D2_RING_BYTES + D2_XRES_BYTES;
 constexpr int D2_BAR = 1;                             // named barrier of the compute warps
 constexpr int D2_MAX_ROWS = 4;                        // router rows per item
 
@@ -144,6 +146,32 @@ FNX_DEV void read_tagged(tword (&v)[N], const tword* p0, long long stride, int n
 #pragma unroll
         for (int i = 0; i < N; ++i)
             if ((uint32_t)(v[i] >> 32) != tag) v[i] = ld_tag(p0 + i * stride);
+        if (fnx_globaltimer() - t0 > FNX_WAIT_NS) {
+            fnx_flag_error(FNX_DEVERR_TIMEOUT);
+            *dead = 1;
+            return;
+        }
+    }
+}
+
+// read_tagged over N words at computed addresses (addr(i), for the bits of `valid`): every load is
+// issued before any tag is checked, so words from many producers cost one L2 round trip together.
+template <int N, class F>
+FNX_DEV void read_tagged_fn(tword (&v)[N], F addr, uint32_t valid, uint32_t tag, volatile int* dead) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = ((valid >> i) & 1u) ? ld_tag(addr(i)) : ((tword)tag << 32);
+    const uint64_t t0 = fnx_globaltimer();
+    unsigned ns = 32;
+    while (true) {
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < N; ++i) ok &= (uint32_t)(v[i] >> 32) == tag;
+        if (ok || *dead) return;
+        __nanosleep(ns);
+        if (ns < FNX_D2_BACKOFF_MAX) ns <<= 1;
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+            if ((uint32_t)(v[i] >> 32) != tag) v[i] = ld_tag(addr(i));
         if (fnx_globaltimer() - t0 > FNX_WAIT_NS) {
             fnx_flag_error(FNX_DEVERR_TIMEOUT);
             *dead = 1;
@@ -530,18 +558,19 @@ FNX_DEV void d2_build_act(const tword* part, int MT, int ks, int I, bool shared_
         float g0 = 0.f, u0 = 0.f, g1 = 0.f, u1 = 0.f;
         for (int s0 = 0; s0 < ks; s0 += 8) {
             const int n = min(8, ks - s0);
-            tword va[8], vb[8], vc[8], vd[8];
-            read_tagged<8>(va, base + s0 * 128, 128, n, tag, dead);
-            read_tagged<8>(vb, base + s0 * 128 + 1, 128, n, tag, dead);
-            read_tagged<8>(vc, base + s0 * 128 + 2, 128, n, tag, dead);
-            read_tagged<8>(vd, base + s0 * 128 + 3, 128, n, tag, dead);
+            // v[8r + s]: word r of the 4 (g0, u0, g1, u1) in K part s0 + s; all 4n loads in flight
+            tword v[32];
+            const uint32_t m8 = (1u << n) - 1u;
+            const tword* b0 = base + s0 * 128;
+            read_tagged_fn<32>(v, [&](int i) { return b0 + (i & 7) * 128 + (i >> 3); },
+                               m8 | (m8 << 8) | (m8 << 16) | (m8 << 24), tag, dead);
 #pragma unroll
             for (int s = 0; s < 8; ++s) {
                 if (s < n) {
-                    g0 = __fadd_rn(g0, __uint_as_float((uint32_t)va[s]));
-                    u0 = __fadd_rn(u0, __uint_as_float((uint32_t)vb[s]));
-                    g1 = __fadd_rn(g1, __uint_as_float((uint32_t)vc[s]));
-                    u1 = __fadd_rn(u1, __uint_as_float((uint32_t)vd[s]));
+                    g0 = __fadd_rn(g0, __uint_as_float((uint32_t)v[s]));
+                    u0 = __fadd_rn(u0, __uint_as_float((uint32_t)v[8 + s]));
+                    g1 = __fadd_rn(g1, __uint_as_float((uint32_t)v[16 + s]));
+                    u1 = __fadd_rn(u1, __uint_as_float((uint32_t)v[24 + s]));
                 }
             }
         }
@@ -549,6 +578,38 @@ FNX_DEV void d2_build_act(const tword* part, int MT, int ks, int I, bool shared_
         const float a0 = shared_form ? __fmul_rn(round_bf(silu_f32(g0)), u0) : __fmul_rn(silu_f32(g0), u0);
         const float a1 = shared_form ? __fmul_rn(round_bf(silu_f32(g1)), u1) : __fmul_rn(silu_f32(g1), u1);
         xs2[w] = pack_bf2(a0, a1);
+    }
+}
+
+// All M token rows into shared memory at entry (n16 16-byte words): four loads per thread in
+// flight before their stores.
+FNX_DEV void d2_stage_rows(const bf16* __restrict__ x, int n16, uint32_t* dst32) {
+    const uint4* src = reinterpret_cast<const uint4*>(x);
+    uint4* dst = reinterpret_cast<uint4*>(dst32);
+    for (int i0 = threadIdx.x; i0 < n16; i0 += 4 * D2_CTHREADS) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (i0 + u * D2_CTHREADS < n16) v[u] = __ldg(src + i0 + u * D2_CTHREADS);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (i0 + u * D2_CTHREADS < n16) dst[i0 + u * D2_CTHREADS] = v[u];
+    }
+}
+
+// A token row (H bf16, H % 256 == 0) into shared memory: 16-byte loads, up to two per thread in
+// flight before their stores (the loads may not pass a store through the generic pointer).
+FNX_DEV void d2_stage_row(const bf16* __restrict__ x, int H, uint32_t* xs2) {
+    const uint4* src = reinterpret_cast<const uint4*>(x);
+    uint4* dst = reinterpret_cast<uint4*>(xs2);
+    const int n = H / 8;
+    for (int i = threadIdx.x; i < n; i += 2 * D2_CTHREADS) {
+        const uint4 a = __ldg(src + i);
+        const bool two = i + D2_CTHREADS < n;
+        uint4 b = a;
+        if (two) b = __ldg(src + i + D2_CTHREADS);
+        dst[i] = a;
+        if (two) dst[i + D2_CTHREADS] = b;
     }
 }
 
@@ -617,11 +678,23 @@ FNX_DEV void d2_combine(const StreamParams& p, const DecodeRouting& R, int t, in
     else if (w == p.k + 1) poll_tag(gp, tag, dead);
     named_bar_sync(D2_BAR, D2_CTHREADS);
     if (w < 64) {
-        tword g1[1], s1[1];
-        read_tagged<1>(g1, gp, 0, 1, tag, dead);
-        read_tagged<1>(s1, sp + w, 0, 1, tag, dead);
+        // the gate logit, the shared row's word and the first 16 routed rows' words in one read
+        tword v[18];
+        const int n0 = min(16, p.k);
+        const tword* yw = yrow + w;
+        read_tagged_fn<18>(v, [&](int i) { return i == 0 ? gp : (i == 1 ? sp + w : yw + (long long)(i - 2) * hw); },
+                           (1u << (2 + n0)) - 1u, tag, dead);
         float a0 = 0.f, a1 = 0.f;
-        for (int j0 = 0; j0 < p.k; j0 += 16) {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+            if (jj < n0) {
+                const uint32_t y = (uint32_t)v[2 + jj];
+                const float wf = R.wf[t * p.k + jj];
+                a0 = __fadd_rn(a0, round_bf(__fmul_rn(bf_lo(y), wf)));
+                a1 = __fadd_rn(a1, round_bf(__fmul_rn(bf_hi(y), wf)));
+            }
+        }
+        for (int j0 = 16; j0 < p.k; j0 += 16) {
             tword yv[16];
             read_tagged<16>(yv, yrow + (long long)j0 * hw + w, hw, min(16, p.k - j0), tag, dead);
 #pragma unroll
@@ -636,9 +709,9 @@ FNX_DEV void d2_combine(const StreamParams& p, const DecodeRouting& R, int t, in
         }
         a0 = round_bf(a0);
         a1 = round_bf(a1);
-        const float g = __uint_as_float((uint32_t)g1[0] << 16);
+        const float g = __uint_as_float((uint32_t)v[0] << 16);
         const float sg = round_bf(sigmoid_f32(g));
-        const uint32_t sh = (uint32_t)s1[0];
+        const uint32_t sh = (uint32_t)v[1];
         const uint32_t o = pack_bf2(__fadd_rn(a0, round_bf(__fmul_rn(bf_lo(sh), sg))),
                                     __fadd_rn(a1, round_bf(__fmul_rn(bf_hi(sh), sg))));
         *reinterpret_cast<uint32_t*>(p.out + (long long)t * p.H + 2 * (m * 64 + w)) = o;
@@ -764,6 +837,14 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
     }
 
     // ---------------------------------------------------- compute warps
+    // the token rows stay in shared memory for the whole launch when they fit (router and gate/up
+    // items then stage nothing); loaded while the copy warp's first stages are in flight
+    uint32_t* xres = reinterpret_cast<uint32_t*>(ring + D2_RING_BYTES);
+    const bool resident = p.M * p.H * 2 <= D2_XRES_BYTES;
+    if (resident) {
+        d2_stage_rows(p.x, p.M * p.H / 8, xres);
+        named_bar_sync(D2_BAR, D2_CTHREADS);
+    }
     int j = 0;
     bool have_routing = false;
     for (int it = blockIdx.x; it < S.total; it += gridDim.x) {
@@ -792,14 +873,12 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
             continue;
         }
         // ---- the item's input row into shared memory
+        const uint32_t* xrow = xs2;
         if (d.type == D2_ROUTER) {
-            if (p.M == 1) {
-                const uint32_t* src = reinterpret_cast<const uint32_t*>(p.x);
-                for (int i = tid; i < p.H / 2; i += D2_CTHREADS) xs2[i] = src[i];
-            }
+            if (p.M == 1 && !resident) d2_stage_row(p.x, p.H, xs2);
         } else if (d.type == D2_SHGU || d.type == D2_GU) {
-            const uint32_t* src = reinterpret_cast<const uint32_t*>(p.x + (long long)d.t * p.H);
-            for (int i = tid; i < p.H / 2; i += D2_CTHREADS) xs2[i] = src[i];
+            if (resident) xrow = xres + (long long)d.t * (p.H / 2);
+            else d2_stage_row(p.x + (long long)d.t * p.H, p.H, xs2);
         } else if (d.type == D2_SHDN) {
             d2_build_act(p.tpart + (long long)d.t * S.MT * p.ks1 * 128, S.MT, p.ks1, p.I, true, tag, dead, xs2);
         } else {
@@ -811,7 +890,8 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
             const int slot = j % D2_NS;
             mbar_wait(&full[slot], (j / D2_NS) & 1);
             d2_router(p, reinterpret_cast<const bf16*>(ring + slot * D2_STAGE_BYTES), d.kb0, d.kb1 - d.kb0, S.nrow,
-                      p.M == 1 ? reinterpret_cast<const bf16*>(xs2) : p.x, tag);
+                      resident ? reinterpret_cast<const bf16*>(xres)
+                               : (p.M == 1 ? reinterpret_cast<const bf16*>(xs2) : p.x), tag);
             // every warp is past its reads of the stage (d2_router's barrier)
             if (lane == 0) mbar_arrive(&empty[slot]);
             ++j;
@@ -827,7 +907,7 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
             mbar_wait(&full[slot], (j / D2_NS) & 1);
             const int kb = d.kb0 + s * D2_SK;
             d2_mma_stage(reinterpret_cast<const uint32_t*>(ring + slot * D2_STAGE_BYTES), min(D2_SK, d.kb1 - kb), kb,
-                         xs2, acc);
+                         xrow, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
