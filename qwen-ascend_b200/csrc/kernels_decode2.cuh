@@ -663,9 +663,9 @@ FNX_DEV void d2_router(const StreamParams& p, const bf16* rows, int e0, int nr, 
 
 // out[t, 128m .. 128m+127]: the slot-order weighted reduce of the k routed rows and the
 // sigmoid-gated shared row (kernels/reduce/reduce.cpp + kernels/post_ops/post_ops.cpp rounding).
-// One thread per producing item (k down items, the shared down item, the router row of the gate)
-// first waits for one of its words; then thread w < 64 reads the column pair 128m + 2w, 2w + 1 of
-// every row at once.
+// Thread w < 64 waits on and reads the column pair 128m + 2w, 2w + 1 of every row at once (its
+// words of the k down items, the shared down item and the gate's router row): one L2 round trip
+// after the last word lands, no separate poll.  The other warps go on to their next item.
 FNX_DEV void d2_combine(const StreamParams& p, const DecodeRouting& R, int t, int m, uint32_t tag,
                         volatile int* dead) {
     const int hw = p.H / 2;
@@ -673,10 +673,6 @@ FNX_DEV void d2_combine(const StreamParams& p, const DecodeRouting& R, int t, in
     const tword* gp = p.tlog + (long long)t * p.R + p.E;
     const tword* sp = p.tsh + (long long)t * hw + m * 64;
     const int w = threadIdx.x;
-    if (w < p.k) poll_tag(yrow + (long long)w * hw, tag, dead);
-    else if (w == p.k) poll_tag(sp, tag, dead);
-    else if (w == p.k + 1) poll_tag(gp, tag, dead);
-    named_bar_sync(D2_BAR, D2_CTHREADS);
     if (w < 64) {
         // the gate logit, the shared row's word and the first 16 routed rows' words in one read
         tword v[18];
