@@ -1263,16 +1263,22 @@ int decode_w4_impl(const void* x, const void* router, const void* gu, const void
                 return FNX_ELAUNCH;
             grid2 = per_sm * num_sms();
         }
-        cudaLaunchAttribute attr2[1];
+        // programmatic dependent launch: the blocks may start while the kernel before this one
+        // on the stream finishes (their copy warps stream weights; the rest waits for it);
+        // FNX_DECODE_PDL=0 launches after it as usual
+        static const bool pdl = env_int("FNX_DECODE_PDL", 1) != 0;
+        cudaLaunchAttribute attr2[2];
         attr2[0].id = cudaLaunchAttributeCooperative;
         attr2[0].val.cooperative = 1;
+        attr2[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr2[1].val.programmaticStreamSerializationAllowed = 1;
         cudaLaunchConfig_t cfg2 = {};
         cfg2.gridDim = dim3(grid2);
         cfg2.blockDim = dim3(D2_THREADS);
         cfg2.dynamicSmemBytes = D2_SMEM;
         cfg2.stream = (cudaStream_t)stream;
         cfg2.attrs = attr2;
-        cfg2.numAttrs = 1;
+        cfg2.numAttrs = pdl ? 2 : 1;
         if (cudaLaunchKernelEx(&cfg2, decode_stream_kernel, q) != cudaSuccess) return FNX_ELAUNCH;
         return launch_rc();
     }

@@ -763,7 +763,6 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const D2Shape S = d2_shape(p);
     const int first_routed = S.RB + S.nsh;
-    const uint32_t tag = *p.epoch + 1u;          // this launch's tag (the counter is bumped at the end)
     if (tid == 0) {
         for (int s = 0; s < D2_NS; ++s) {
             mbar_init(&full[s], 1);
@@ -771,20 +770,10 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
         }
         mbar_init(&routing_bar, 1);
         s_dead = 0;
-        if (p.logits_ready) {
-            // the logits were written by the kernel before this one on the stream, so they carry
-            // this launch's tag already; a stale tag means no fnx_hc_mix_router ran on this
-            // workspace since the last decode: record it and end at once instead of by timeouts
-            for (int t = 0; t < p.M; ++t) {
-                const tword* row = p.tlog + (long long)t * p.R;
-                if ((uint32_t)(ld_tag(row) >> 32) != tag || (uint32_t)(ld_tag(row + p.R - 1) >> 32) != tag) {
-                    fnx_flag_error(FNX_DEVERR_NOLOGITS);
-                    s_dead = 1;
-                    break;
-                }
-            }
-        }
         fence_mbar_init();
+        // a decode launched behind this one (programmatic dependent launch) may start as this
+        // grid's blocks leave: its copy warps stream weights, its compute warps wait below
+        pdl_launch_dependents();
     }
     __syncthreads();
     volatile int* dead = &s_dead;
@@ -833,6 +822,26 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
     }
 
     // ---------------------------------------------------- compute warps
+    // The input rows, the workspace (launch counter, tags) and the logits of a logits-ready launch
+    // may come from the kernel before this one on the stream, which may still be running when this
+    // grid starts (programmatic dependent launch): wait for it here.  The copy warp above reads
+    // weights only and runs ahead.
+    pdl_wait();
+    const uint32_t tag = *p.epoch + 1u;          // this launch's tag (the counter is bumped at the end)
+    if (tid == 0 && p.logits_ready) {
+        // the logits were written by the kernel before this one on the stream, so they carry
+        // this launch's tag already; a stale tag means no fnx_hc_mix_router ran on this
+        // workspace since the last decode: record it and end at once instead of by timeouts
+        for (int t = 0; t < p.M; ++t) {
+            const tword* row = p.tlog + (long long)t * p.R;
+            if ((uint32_t)(ld_tag(row) >> 32) != tag || (uint32_t)(ld_tag(row + p.R - 1) >> 32) != tag) {
+                fnx_flag_error(FNX_DEVERR_NOLOGITS);
+                s_dead = 1;
+                break;
+            }
+        }
+    }
+    named_bar_sync(D2_BAR, D2_CTHREADS);
     // the token rows stay in shared memory for the whole launch when they fit (router and gate/up
     // items then stage nothing); loaded while the copy warp's first stages are in flight
     uint32_t* xres = reinterpret_cast<uint32_t*>(ring + D2_RING_BYTES);
