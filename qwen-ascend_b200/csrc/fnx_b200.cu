@@ -1264,8 +1264,8 @@ int decode_w4_impl(const void* x, const void* router, const void* gu, const void
             grid2 = per_sm * num_sms();
         }
         // programmatic dependent launch: the blocks may start while the kernel before this one
-        // on the stream finishes (their copy warps stream weights; the rest waits for it);
-        // FNX_DECODE_PDL=0 launches after it as usual
+        // on the stream finishes (their copy warps prefetch the first weights into L2, then all
+        // warps wait for it); FNX_DECODE_PDL=0 launches after it as usual
         static const bool pdl = env_int("FNX_DECODE_PDL", 1) != 0;
         cudaLaunchAttribute attr2[2];
         attr2[0].id = cudaLaunchAttributeCooperative;

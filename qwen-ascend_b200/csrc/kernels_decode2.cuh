@@ -772,7 +772,7 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
         s_dead = 0;
         fence_mbar_init();
         // a decode launched behind this one (programmatic dependent launch) may start as this
-        // grid's blocks leave: its copy warps stream weights, its compute warps wait below
+        // grid's blocks leave: its copy warps prefetch weights into L2, then everything waits
         pdl_launch_dependents();
     }
     __syncthreads();
@@ -781,6 +781,26 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
     if (warp == D2_COPY_WARP) {
         // ------------------------------------------------ copy warp: every stage of every item, in order
         if (lane == 0) {
+            // Until the kernel before this one on the stream is complete (programmatic dependent
+            // launch), its writes may not be visible: that kernel may have written the weights
+            // (a repack, an expert renumbering).  So before the wait only the first stages' weights
+            // are prefetched into L2, which is coherent (lines still being written are read again
+            // by the copies after the wait).
+            int pre = 0;
+            for (int it = blockIdx.x; it < first_routed && pre < D2_NS; it += gridDim.x) {
+                const D2Item d = d2_item(p, S, R, it);          // router / shared items: no routing read
+                const int ns = (d.type == D2_ROUTER && p.logits_ready) ? 0 : d2_stages(d);
+                for (int s2 = 0; s2 < ns && pre < D2_NS; ++s2, ++pre) {
+                    if (d.type == D2_ROUTER) {
+                        l2_prefetch(d.src, (uint32_t)(d.kb1 - d.kb0) * p.H * 2);
+                    } else {
+                        const int kb = d.kb0 + s2 * D2_SK;
+                        l2_prefetch(d.src + (long long)kb * TILE_BLOCK_WORDS,
+                                    (uint32_t)min(D2_SK, d.kb1 - kb) * TILE_BLOCK_BYTES);
+                    }
+                }
+            }
+            pdl_wait();
             const uint64_t once = l2_evict_first();
             bool routed = false;
             int j = 0, prev_type = D2_ROUTER;
@@ -824,8 +844,7 @@ __global__ void __launch_bounds__(D2_THREADS, 2) decode_stream_kernel(const Stre
     // ---------------------------------------------------- compute warps
     // The input rows, the workspace (launch counter, tags) and the logits of a logits-ready launch
     // may come from the kernel before this one on the stream, which may still be running when this
-    // grid starts (programmatic dependent launch): wait for it here.  The copy warp above reads
-    // weights only and runs ahead.
+    // grid starts (programmatic dependent launch): wait for it here.
     pdl_wait();
     const uint32_t tag = *p.epoch + 1u;          // this launch's tag (the counter is bumped at the end)
     if (tid == 0 && p.logits_ready) {
