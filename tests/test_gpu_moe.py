@@ -326,6 +326,27 @@ def test_mix_and_route_matches_unfused_path(M):
     assert torch.equal(idx, ref_idx) and torch.equal(out.view(torch.int16), ref_out.view(torch.int16))
 
 
+def test_gated_residual_with_moe_fuses_the_router():
+    """engine.gated_residual(..., moe=layer) returns the bits of the plain call, and the layer's
+    logits-ready decode that follows gives the bits of the decode that routes itself."""
+    from fnx.engine import gated_residual
+    t, L, layer = _layer(synth.CFG2, 38)
+    H, hc, lr, b = synth.CFG2.H, 4, 32, 2
+    g = torch.Generator().manual_seed(9)
+    h = torch.randn(b, 1, hc * H, generator=g).to(BF16).to(DEV)
+    norm_w = (torch.randn(hc * H, generator=g) * 0.1).to(BF16).to(DEV)
+    w_di = (torch.randn(lr + hc, hc * H, generator=g) * 0.02).to(BF16).to(DEV)
+    w_up = (torch.randn(hc * H, lr, generator=g) * 0.2).to(BF16).to(DEV)
+    mixed0, inj0 = gated_residual(h, norm_w, w_di, w_up, n_inj=hc, hc=hc)
+    ref = [a.clone() for a in layer.decode(mixed0.view(b, H))]
+    mixed1, inj1 = gated_residual(h, norm_w, w_di, w_up, n_inj=hc, hc=hc, moe=layer)
+    assert torch.equal(mixed1.view(torch.int16), mixed0.view(torch.int16))
+    assert torch.equal(inj1.view(torch.int16), inj0.view(torch.int16))
+    out, w, idx = layer.decode(mixed1.view(b, H), logits_ready=True)
+    assert torch.equal(idx, ref[2]) and torch.equal(w.view(torch.int16), ref[1].view(torch.int16))
+    assert torch.equal(out.view(torch.int16), ref[0].view(torch.int16))
+
+
 def test_permute_experts_keeps_the_layer():
     """Renumbered experts (router rows, bias, tile blocks moved together): every token whose
     selection maps back to the same experts in the same slot order gets the same bits; only
