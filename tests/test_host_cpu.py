@@ -1,5 +1,6 @@
-"""Host-side placement of the pinned buffers (fnx.hostmem), on the CPU: the sysfs CPU-list
-parser and the binding rule, with the device's locality and the process affinity faked."""
+"""Host-side logic on the CPU: the placement of the pinned buffers (fnx.hostmem: the sysfs
+CPU-list parser and the binding rule, with the device's locality and the process affinity
+faked) and bench.py's clock record from nvidia-smi samples."""
 import pytest
 
 from fnx import hostmem
@@ -45,3 +46,20 @@ def test_bind_is_a_no_op_without_locality(monkeypatch):
     assert calls == [] and r == {"pci": "0000:9c:00.0", "numa_node": None, "cpus": 16, "bound": False}
     calls = _fake(monkeypatch, local={100, 101}, allowed=range(16))
     assert hostmem.bind_to_device("cuda:0")["bound"] is False and calls == []
+
+
+def test_clock_sampler_summary():
+    """bench.py's clock record: the median SM clock under load, the max clock, and the throttle
+    reasons seen active in any sample (a run with a slowdown reason is re-measured)."""
+    import bench
+    c = bench.ClockSampler(0)
+    c.rows = [["0", "1965", "1965", "700.1", "0x0", "Not Active", "Not Active", "Not Active", "Not Active"],
+              ["0", "1920", "1965", "990.0", "0x4", "Not Active", "Not Active", "Not Active", "Active"],
+              ["0", "1965", "1965", "800.5", "0x0", "Not Active", "Not Active", "Not Active", "Not Active"]]
+    s = c.summary()
+    assert s == {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 3}
+    c.rows = [["0", "[N/A]", "1965", "1.0", "0x8", "Active", "Not Active", "Active", "Not Active"]]
+    s = c.summary()
+    assert s["sm_mhz"] is None and s["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"]
+    c.rows = []
+    assert c.summary()["reasons"] == ["unsampled"]
