@@ -107,14 +107,18 @@ def gated_residual(h, hc_norm_w, w_down, w_up, w_inj=None, n_inj=0, hc=4, eps=1e
     reference's loader concatenates them), ``w_up`` bf16 ``[hc*H, r]``, ``w_inj`` bf16
     ``[hc, hc*H]`` when not concatenated.  RMSNorm, activation and branch mix run on this
     library's kernels with the reference's roundings, the two small GEMMs on its tcgen05 bf16
-    GEMM (``mm_nt``).  ``moe``: the ``MoELayer`` whose decode follows (``b <= 16``): its router
-    GEMV is fused into the mix (``MoELayer.mix_and_route``) and its decode must be called next
-    with ``logits_ready=True``.  Same bits either way; on B200 the fused pair is the slower one
-    (25.6 against 23.0 us per layer at b = 1), because the decode kernel already overlaps its own
-    router GEMV with the expert-weight stream."""
+    GEMM (``mm_nt``).  ``moe``: the ``MoELayer`` whose decode follows (``b <= 16``, ``moe.H == H``;
+    ``ValueError`` otherwise, before any launch): its router GEMV is fused into the mix
+    (``MoELayer.mix_and_route``) and its decode must be called next with ``logits_ready=True``.
+    Same bits either way; on B200 the fused pair is the slower one (25.6 against 23.0 us per layer
+    at b = 1), because the decode kernel already overlaps its own router GEMV with the
+    expert-weight stream."""
     from . import post_ops
     b, HCH = h.shape[0], h.shape[-1]
     H = HCH // hc
+    if moe is not None and (b > DECODE_MAX_TOKENS or moe.E > DECODE_MAX_EXPERTS or moe.H != H):
+        raise ValueError(f"gated_residual: the fused router needs b <= {DECODE_MAX_TOKENS}, E <= "
+                         f"{DECODE_MAX_EXPERTS} and the layer's H = {H} (got b={b}, E={moe.E}, H={moe.H})")
     h2 = h.reshape(b, HCH).contiguous()
     hn = torch.empty_like(h2)
     rc = _lib.lib().fnx_hc_rms_norm(h2.data_ptr(), hc_norm_w.contiguous().data_ptr(), hn.data_ptr(), b, H, hc, eps,
@@ -127,7 +131,7 @@ def gated_residual(h, hc_norm_w, w_down, w_up, w_inj=None, n_inj=0, hc=4, eps=1e
     di = mm_nt(hn, w_down)
     mix, inj = post_ops.activate(di.view(b, 1, -1).contiguous(), hc)
     logits = mm_nt(mix.view(b, -1), w_up)
-    if moe is not None and b <= DECODE_MAX_TOKENS and moe.E <= DECODE_MAX_EXPERTS:
+    if moe is not None:
         # the router GEMV of the MoE layer that follows, fused into the mix; its decode call must
         # come next on this stream, as moe.decode(mixed, logits_ready=True)
         mixed = moe.mix_and_route(hn, logits, hc)

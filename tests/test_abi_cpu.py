@@ -161,6 +161,21 @@ def test_python_wrappers_return_none_for_unsupported():
     assert expert_gather.gather(P(), torch.zeros(10, dtype=torch.int64)) is None
 
 
+def test_gated_residual_rejects_an_unsupported_fused_router():
+    """gated_residual(..., moe=layer) refuses, before any launch, a batch or layer the fused mix +
+    router kernel cannot take, instead of falling back to the unfused mix, after which the
+    logits-ready decode the caller runs next would have no logits."""
+    import torch
+    from types import SimpleNamespace
+    from fnx.engine import gated_residual
+    H, hc = 256, 4
+    w = torch.zeros(hc * H, dtype=torch.bfloat16)
+    for b, moe in [(17, SimpleNamespace(E=64, H=H)), (2, SimpleNamespace(E=1024, H=H)),
+                   (2, SimpleNamespace(E=64, H=2 * H))]:
+        with pytest.raises(ValueError):
+            gated_residual(torch.zeros(b, 1, hc * H, dtype=torch.bfloat16), w, None, None, moe=moe)
+
+
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     from fnx import _lib
     monkeypatch.setattr(_lib, "_lib", None)
